@@ -1,0 +1,171 @@
+/*
+ * lai_kernels.h - device-pointer C ABI of the B200 (sm_100a) per-layer kernels.
+ *
+ * Library: local-ai-server_b200/liblai_kernels.so. Plain C types only: device
+ * pointers, element counts, a cudaStream_t (passed as void *; NULL = the legacy
+ * default stream). Every entry returns LAI_OK (0) or a negative LAI_ERR_* code
+ * and never synchronises the stream. Launch failures are reported from the
+ * launch itself; data-dependent faults (an out-of-range token id or RoPE
+ * position) never trap: the kernel skips that row and ORs a LAI_DEVERR_* bit
+ * into the caller's device word `err` (may be NULL), which the caller reads
+ * after synchronising.
+ *
+ * BF16 tensors are raw bit patterns (lai_bf16 = uint16_t). All arithmetic is
+ * FP32; BF16 stores round to nearest even. Norm weights and RoPE tables are
+ * FP32, as the reference keeps them (src/tts_native.c:125-133 load_f32,
+ * src/tts_native.c:377-417).
+ *
+ * Reference functions replaced (their C source lives in the un-vendored qwen-asr
+ * submodule; prototypes inferred from the call sites cited on each entry). The
+ * exact reference-named, host-or-device FP32 drop-ins are in lai_qwen_dropin.h.
+ */
+#ifndef LAI_KERNELS_H
+#define LAI_KERNELS_H
+
+#include <stdint.h>
+
+#ifndef LAI_API
+#if defined(__GNUC__)
+#define LAI_API __attribute__((visibility("default")))
+#else
+#define LAI_API
+#endif
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef uint16_t lai_bf16;
+typedef void *lai_stream_t; /* a cudaStream_t */
+
+enum {
+    LAI_OK = 0,
+    LAI_ERR_INVALID = -1, /* bad size, NULL required pointer, unsupported head_dim */
+    LAI_ERR_CUDA = -2,    /* a CUDA call or kernel launch failed */
+    LAI_ERR_RANGE = -3,   /* an id / position was out of range (host-checked path) */
+    LAI_ERR_ALIAS = -4,   /* output overlaps an input in an unsupported way */
+    LAI_ERR_NOMEM = -5,   /* staging allocation failed (drop-in host path) */
+    LAI_ERR_TOOBIG = -6   /* size beyond a stated maximum */
+};
+
+/* Bits ORed into the caller's device error word. */
+enum { LAI_DEVERR_TOKEN_ID = 1, LAI_DEVERR_POSITION = 2 };
+
+LAI_API const char *lai_status_string(int status);
+LAI_API int lai_version(void); /* major*10000 + minor*100 + patch */
+
+/* ---- RMSNorm -------------------------------------------------------------
+ * y[r,:] = x[r,:] / sqrt(mean(x[r,:]^2) + eps) * w      x,y [rows, dim], w [dim]
+ * Replaces qwen_rms_norm(out, x, w, seq, dim, eps): src/tts_native.c:556, 584,
+ * 637, 661, 674; src/tts_vocoder_xfmr.c:163, 189, 211. y == x is allowed.
+ */
+LAI_API int lai_rmsnorm_bf16(lai_bf16 *y, const lai_bf16 *x, const float *w, int64_t rows, int dim,
+                     float eps, lai_stream_t stream);
+LAI_API int lai_rmsnorm_f32(float *y, const float *x, const float *w, int64_t rows, int dim, float eps,
+                    lai_stream_t stream);
+
+/* ---- fused residual add + RMSNorm ------------------------------------------
+ * x[r,:] += delta[r,:] (stored, BF16-rounded for the BF16 entry); y = RMSNorm(x).
+ * Replaces the pair qwen_add_inplace(x, delta, seq*dim); qwen_rms_norm(y, x, w, ...)
+ * at src/tts_native.c:582-584, 659-661, 738-740 (and the residual add at :591 /
+ * :668 fused into the next layer's input norm at :556 / :637).
+ * y must not overlap x or delta.
+ */
+LAI_API int lai_add_rmsnorm_bf16(lai_bf16 *x, const lai_bf16 *delta, const float *w, lai_bf16 *y,
+                         int64_t rows, int dim, float eps, lai_stream_t stream);
+LAI_API int lai_add_rmsnorm_f32(float *x, const float *delta, const float *w, float *y, int64_t rows,
+                        int dim, float eps, lai_stream_t stream);
+
+/* ---- fused per-head q/k RMSNorm + NeoX RoPE (in place) ----------------------
+ * q [rows, n_q_heads*head_dim], k [rows, n_kv_heads*head_dim] (k may be NULL).
+ * Per head: RMSNorm with wq / wk [head_dim] (NULL skips that norm), then NeoX
+ * rotate-half with table row p = pos ? pos[r] : r of cos_t/sin_t [table_rows,
+ * head_dim] (cos_t NULL skips RoPE). A row whose p is outside [0, table_rows) is
+ * left unmodified and sets LAI_DEVERR_POSITION in *err.
+ * Replaces qwen_rms_norm_per_head(q|k, w, seq, heads, hd, eps) x2 followed by
+ * qwen_apply_rope_neox(q|k, cos, sin, seq, heads, hd) x2: src/tts_native.c:562-568,
+ * 644-648, 724-730; src/tts_vocoder_xfmr.c:172-175 (RoPE only). head_dim even.
+ */
+LAI_API int lai_qk_norm_rope_bf16(lai_bf16 *q, lai_bf16 *k, const float *wq, const float *wk,
+                          const float *cos_t, const float *sin_t, const int32_t *pos,
+                          int64_t table_rows, int64_t rows, int n_q_heads, int n_kv_heads,
+                          int head_dim, float eps, int *err, lai_stream_t stream);
+LAI_API int lai_qk_norm_rope_f32(float *q, float *k, const float *wq, const float *wk,
+                         const float *cos_t, const float *sin_t, const int32_t *pos,
+                         int64_t table_rows, int64_t rows, int n_q_heads, int n_kv_heads,
+                         int head_dim, float eps, int *err, lai_stream_t stream);
+
+/* ---- RoPE table ---------------------------------------------------------------
+ * cos_t/sin_t [n, head_dim]: row i holds cos/sin(p_i * inv_freq[d]) in both halves,
+ * p_i = pos ? pos[i] : i, inv_freq[d] = 1/powf(theta, 2d/head_dim) computed on the
+ * host exactly as ensure_rope_cache does (src/tts_native.c:377-417). Replaces
+ * qwen_compute_rope_neox(cos, sin, pos, n, hd, theta): src/tts_vocoder_xfmr.c:150-156.
+ * head_dim even, <= 512.
+ */
+LAI_API int lai_rope_table_f32(float *cos_t, float *sin_t, const int32_t *pos, int64_t n, int head_dim,
+                       float theta, lai_stream_t stream);
+
+/* ---- SwiGLU over the interleaved gate/up GEMM output ---------------------------
+ * gate_up [rows, 2*inter] with rows interleaved [g0,u0,g1,u1,...] (fused weight,
+ * src/tts_native.c:149-161); out[r,j] = silu(g[r,j]) * u[r,j], out [rows, inter].
+ * out == gate_up compacts in place (the reference's call form, src/tts_native.c:588,
+ * 665, 744) without scratch memory, using ordered passes; any other overlap is
+ * LAI_ERR_ALIAS. Replaces qwen_swiglu_multiply(out, gate_up, seq, inter).
+ */
+LAI_API int lai_swiglu_bf16(lai_bf16 *out, const lai_bf16 *gate_up, int64_t rows, int inter,
+                    lai_stream_t stream);
+LAI_API int lai_swiglu_f32(float *out, const float *gate_up, int64_t rows, int inter,
+                   lai_stream_t stream);
+
+/* out[i] = silu(gate[i]) * up[i]: swiglu_separate, src/tts_vocoder_xfmr.c:73-80, 203. */
+LAI_API int lai_swiglu_separate_f32(float *out, const float *gate, const float *up, int64_t n,
+                            lai_stream_t stream);
+/* x[i] = silu(x[i]) in place: qwen_silu(x, n), src/tts_native.c:504. */
+LAI_API int lai_silu_f32(float *x, int64_t n, lai_stream_t stream);
+
+/* ---- residual add: x[i] += y[i] ---------------------------------------------------
+ * Replaces qwen_add_inplace(x, y, n): src/tts_native.c:582, 591, 659, 668, 738, 747,
+ * 1142; src/tts_vocoder_xfmr.c:186, 206.
+ */
+LAI_API int lai_add_bf16(lai_bf16 *x, const lai_bf16 *y, int64_t n, lai_stream_t stream);
+LAI_API int lai_add_f32(float *x, const float *y, int64_t n, lai_stream_t stream);
+
+/* ---- BF16 token-embedding gather ----------------------------------------------------
+ * out[r,:] = table[ids[r],:], table [vocab, dim] BF16; widened to F32 by the bit
+ * shift of bf16_to_f32_row (bit-exact) or copied as BF16. An id outside [0, vocab)
+ * zero-fills its row and sets LAI_DEVERR_TOKEN_ID in *err.
+ * Replaces embed_lookup_bf16 / codec_embed_lookup (static, src/tts_native.c:35-40,
+ * 473-476, 518-520; uses at :490-493, :930, :1121, :1138-1139).
+ */
+LAI_API int lai_embed_gather_bf16(lai_bf16 *out, const lai_bf16 *table, const int32_t *ids, int64_t n,
+                          int dim, int64_t vocab, int *err, lai_stream_t stream);
+LAI_API int lai_embed_gather_bf16_to_f32(float *out, const lai_bf16 *table, const int32_t *ids,
+                                 int64_t n, int dim, int64_t vocab, int *err,
+                                 lai_stream_t stream);
+
+/* ---- SnakeBeta (in place, FP32) ---------------------------------------------------------
+ * x [batch, channels, T]: x += inv_exp_beta[c] * sin(exp_alpha[c] * x)^2, params
+ * pre-exponentiated (src/tts_vocoder.c:221-227). Replaces voc_snake_beta(x, ea, ieb,
+ * channels, T) (src/tts_vocoder_ops.c:279-305; call sites src/tts_vocoder.c:548, 556,
+ * 715, 745) for batch == 1, and a batch of such calls otherwise.
+ */
+LAI_API int lai_snake_beta_f32(float *x, const float *exp_alpha, const float *inv_exp_beta,
+                       int64_t batch, int channels, int64_t T, lai_stream_t stream);
+
+/* ---- seeded synthetic inputs (bench and test support) ------------------------------------
+ * Counter-based: element i of a fill is a pure function of (seed, offset + i), so a
+ * row-sharded fill on G devices equals the single-device fill of the same rows.
+ * normal: mean + std * N(0,1); uniform ints in [lo, hi).
+ */
+LAI_API int lai_synth_normal_bf16(lai_bf16 *out, int64_t n, uint64_t seed, int64_t offset, float mean,
+                          float std, lai_stream_t stream);
+LAI_API int lai_synth_normal_f32(float *out, int64_t n, uint64_t seed, int64_t offset, float mean,
+                         float std, lai_stream_t stream);
+LAI_API int lai_synth_uniform_i32(int32_t *out, int64_t n, uint64_t seed, int64_t offset, int32_t lo,
+                          int32_t hi, lai_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LAI_KERNELS_H */

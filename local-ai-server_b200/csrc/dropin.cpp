@@ -1,0 +1,449 @@
+// dropin.cpp - the reference's qwen_* / voc_snake_beta names over the B200 kernels.
+//
+// Each drop-in call is described as a list of arguments (pointer, bytes per row
+// or whole size, in/out) plus a launcher that runs one lai_* kernel on a row
+// range. If every pointer is device-accessible the launcher runs once on the
+// drop-in stream. Otherwise host rows are staged: rows are cut into chunks of
+// about kChunkBytes host bytes, chunk c runs on pipeline stream c % 3 as
+// copy-in -> kernel -> copy-out using that stream's device slot, so the copy-in
+// of one chunk, the kernel of the next and the copy-out of a third overlap. When
+// a host output aliases a host input with another row size (SwiGLU compaction,
+// out == gate_up) the copy-out of chunk c first waits for the copy-in events of
+// every earlier chunk whose input bytes it overwrites.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/lai_kernels.h"
+#include "../../include/lai_qwen_dropin.h"
+
+namespace {
+
+constexpr int kSlots = 3;
+constexpr size_t kChunkBytes = 16u << 20;
+
+struct Ctx {
+    int device = -1;
+    cudaStream_t pipe[kSlots] = {};
+    void *slot[kSlots] = {};
+    size_t slot_cap[kSlots] = {};
+    void *whole = nullptr;
+    size_t whole_cap = 0;
+    int *derr = nullptr;        // device error word of staged calls
+    int *derr_direct = nullptr; // device error word of device-pointer calls
+    int32_t *zero_id = nullptr; // a device int holding 0 (single-row gathers)
+    std::vector<cudaEvent_t> events;
+    cudaEvent_t start_ev = nullptr;
+};
+
+thread_local std::unordered_map<int, Ctx> t_ctx;
+thread_local int t_last_error = LAI_OK;
+thread_local cudaStream_t t_stream = nullptr;
+
+int fail(const char *fn, int status, const char *what) {
+    t_last_error = status;
+    std::fprintf(stderr, "lai: %s: %s (%s)\n", fn, lai_status_string(status), what ? what : "");
+    return status;
+}
+
+int cuda_fail(const char *fn, cudaError_t e) {
+    return fail(fn, LAI_ERR_CUDA, cudaGetErrorString(e));
+}
+
+Ctx *get_ctx(const char *fn) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        cuda_fail(fn, e);
+        return nullptr;
+    }
+    Ctx &c = t_ctx[dev];
+    if (c.device < 0) {
+        c.device = dev;
+        for (int i = 0; i < kSlots; i++)
+            if ((e = cudaStreamCreateWithFlags(&c.pipe[i], cudaStreamNonBlocking)) != cudaSuccess) break;
+        if (e == cudaSuccess) e = cudaMalloc(&c.derr, 4 * sizeof(int));
+        if (e == cudaSuccess) e = cudaMemset(c.derr, 0, 4 * sizeof(int));
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c.start_ev, cudaEventDisableTiming);
+        if (e != cudaSuccess) {
+            cuda_fail(fn, e);
+            t_ctx.erase(dev);
+            return nullptr;
+        }
+        c.derr_direct = c.derr + 1;
+        c.zero_id = reinterpret_cast<int32_t *>(c.derr + 2);
+    }
+    return &c;
+}
+
+bool grow(void **p, size_t *cap, size_t need) {
+    if (need <= *cap) return true;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    size_t n = need + need / 4;
+    if (cudaMalloc(p, n) != cudaSuccess) {
+        cudaGetLastError();
+        *p = nullptr;
+        return false;
+    }
+    *cap = n;
+    return true;
+}
+
+bool device_accessible(const void *p) {
+    if (!p) return true;
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+// Host memory registered (pinned and mapped): the device address to read it with.
+const void *mapped_device_ptr(const void *p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) return p;
+    if (a.type == cudaMemoryTypeHost) return a.devicePointer;
+    return nullptr;
+}
+
+struct Arg {
+    const void *ptr;  // user pointer (may be NULL for optional args)
+    size_t row_bytes; // > 0: chunked by rows; 0: whole argument of whole_bytes
+    size_t whole_bytes;
+    bool in, out;
+    // filled by the engine
+    bool host = false;
+    size_t whole_off = 0;
+    size_t slot_off = 0;
+};
+
+// launcher(stream, row0, nrows, device pointers per arg, err word) -> LAI status
+using Launcher = std::function<int(cudaStream_t, int64_t, int64_t, void **, int *)>;
+
+int run_op(const char *fn, std::vector<Arg> &args, int64_t rows, const Launcher &launch) {
+    Ctx *c = get_ctx(fn);
+    if (!c) return LAI_ERR_CUDA;
+    if (rows <= 0) return LAI_OK;
+    std::vector<void *> dptr(args.size());
+    bool all_dev = true;
+    for (auto &a : args) {
+        a.host = a.ptr && !device_accessible(a.ptr);
+        all_dev = all_dev && !a.host;
+    }
+    if (all_dev) {
+        for (size_t i = 0; i < args.size(); i++) dptr[i] = const_cast<void *>(args[i].ptr);
+        int st = launch(t_stream, 0, rows, dptr.data(), c->derr_direct);
+        return st == LAI_OK ? LAI_OK : fail(fn, st, "launch");
+    }
+
+    // ---- staged path ----
+    cudaError_t e;
+    size_t whole = 0, per_row = 0;
+    for (auto &a : args) {
+        if (!a.host) continue;
+        if (a.row_bytes == 0) {
+            a.whole_off = whole;
+            whole += (a.whole_bytes + 255) & ~size_t(255);
+        } else {
+            per_row += a.row_bytes;
+        }
+    }
+    int64_t chunk = per_row ? (int64_t)(kChunkBytes / per_row) : rows;
+    if (chunk < 1) chunk = 1;
+    if (chunk > rows) chunk = rows;
+    size_t off = 0;
+    for (auto &a : args)
+        if (a.host && a.row_bytes) {
+            a.slot_off = off;
+            off += ((size_t)chunk * a.row_bytes + 255) & ~size_t(255);
+        }
+    for (int s = 0; s < kSlots; s++)
+        if (off && !grow(&c->slot[s], &c->slot_cap[s], off)) return fail(fn, LAI_ERR_NOMEM, "staging");
+    if (whole && !grow(&c->whole, &c->whole_cap, whole)) return fail(fn, LAI_ERR_NOMEM, "staging");
+
+    // order after prior work on the drop-in stream (device-pointer args)
+    if ((e = cudaEventRecord(c->start_ev, t_stream)) != cudaSuccess) return cuda_fail(fn, e);
+    for (int s = 0; s < kSlots; s++) cudaStreamWaitEvent(c->pipe[s], c->start_ev, 0);
+    cudaMemsetAsync(c->derr, 0, sizeof(int), c->pipe[0]);
+    for (auto &a : args)
+        if (a.host && a.row_bytes == 0 && a.in)
+            cudaMemcpyAsync(static_cast<char *>(c->whole) + a.whole_off, a.ptr, a.whole_bytes,
+                            cudaMemcpyHostToDevice, c->pipe[0]);
+    // the other pipeline streams start after the whole-argument copies and the reset
+    if ((e = cudaEventRecord(c->start_ev, c->pipe[0])) != cudaSuccess) return cuda_fail(fn, e);
+    for (int s = 1; s < kSlots; s++) cudaStreamWaitEvent(c->pipe[s], c->start_ev, 0);
+
+    // aliasing host output/input pairs with different row sizes need ordering
+    bool alias = false;
+    for (auto &o : args)
+        for (auto &i : args)
+            if (&o != &i && o.host && i.host && o.out && i.in && o.row_bytes && i.row_bytes &&
+                o.row_bytes != i.row_bytes && o.ptr == i.ptr)
+                alias = true;
+    const int64_t nchunks = (rows + chunk - 1) / chunk;
+    if (alias) {
+        while ((int64_t)c->events.size() < nchunks) {
+            cudaEvent_t ev;
+            if ((e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming)) != cudaSuccess)
+                return cuda_fail(fn, e);
+            c->events.push_back(ev);
+        }
+    }
+
+    int status = LAI_OK;
+    for (int64_t ci = 0; ci < nchunks && status == LAI_OK; ci++) {
+        const int64_t r0 = ci * chunk, nr = (r0 + chunk <= rows) ? chunk : rows - r0;
+        const int s = (int)(ci % kSlots);
+        cudaStream_t st = c->pipe[s];
+        for (size_t i = 0; i < args.size(); i++) {
+            Arg &a = args[i];
+            if (!a.ptr) { dptr[i] = nullptr; continue; }
+            if (!a.host) {
+                dptr[i] = const_cast<char *>(static_cast<const char *>(a.ptr)) +
+                          (a.row_bytes ? (size_t)r0 * a.row_bytes : 0);
+                continue;
+            }
+            if (a.row_bytes == 0) {
+                dptr[i] = static_cast<char *>(c->whole) + a.whole_off;
+                continue;
+            }
+            dptr[i] = static_cast<char *>(c->slot[s]) + a.slot_off;
+            if (a.in)
+                cudaMemcpyAsync(dptr[i], static_cast<const char *>(a.ptr) + (size_t)r0 * a.row_bytes,
+                                (size_t)nr * a.row_bytes, cudaMemcpyHostToDevice, st);
+        }
+        if (alias) cudaEventRecord(c->events[ci], st);
+        status = launch(st, r0, nr, dptr.data(), c->derr);
+        for (size_t i = 0; i < args.size() && status == LAI_OK; i++) {
+            Arg &a = args[i];
+            if (!a.ptr || !a.host || !a.out || a.row_bytes == 0) continue;
+            char *hdst = const_cast<char *>(static_cast<const char *>(a.ptr)) + (size_t)r0 * a.row_bytes;
+            const size_t nb = (size_t)nr * a.row_bytes;
+            if (alias) {
+                // wait for every earlier chunk whose host input bytes this copy-out overwrites
+                for (const Arg &b : args) {
+                    if (&b == &a || !b.host || !b.in || b.ptr != a.ptr || !b.row_bytes) continue;
+                    for (int64_t cj = 0; cj < ci; cj++) {
+                        const char *lo = static_cast<const char *>(b.ptr) + (size_t)(cj * chunk) * b.row_bytes;
+                        const int64_t nj = (cj * chunk + chunk <= rows) ? chunk : rows - cj * chunk;
+                        const char *hi = lo + (size_t)nj * b.row_bytes;
+                        if (lo < hdst + nb && hdst < hi) cudaStreamWaitEvent(st, c->events[cj], 0);
+                    }
+                }
+            }
+            cudaMemcpyAsync(hdst, dptr[i], nb, cudaMemcpyDeviceToHost, st);
+        }
+    }
+    cudaError_t sync_err = cudaSuccess;
+    for (int s = 0; s < kSlots; s++) {
+        cudaError_t es = cudaStreamSynchronize(c->pipe[s]);
+        if (es != cudaSuccess && sync_err == cudaSuccess) sync_err = es;
+    }
+    const cudaError_t last = cudaGetLastError();
+    if (sync_err != cudaSuccess) return cuda_fail(fn, sync_err);
+    if (last != cudaSuccess) return cuda_fail(fn, last);
+    int flags = 0;
+    if ((e = cudaMemcpy(&flags, c->derr, sizeof(int), cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return cuda_fail(fn, e);
+    if (status != LAI_OK) return fail(fn, status, "launch");
+    if (flags) return fail(fn, LAI_ERR_RANGE, "index out of range");
+    return LAI_OK;
+}
+
+template <typename T> T *P(void **d, int i) { return static_cast<T *>(d[i]); }
+
+}  // namespace
+
+extern "C" {
+
+void qwen_rms_norm(float *out, const float *x, const float *w, int seq, int dim, float eps) {
+    const char *fn = "qwen_rms_norm";
+    if (!out || !x || !w || seq < 0 || dim <= 0) { fail(fn, LAI_ERR_INVALID, "arguments"); return; }
+    std::vector<Arg> a = {{out, (size_t)dim * 4, 0, false, true},
+                          {x, (size_t)dim * 4, 0, true, false},
+                          {w, 0, (size_t)dim * 4, true, false}};
+    run_op(fn, a, seq, [&](cudaStream_t s, int64_t, int64_t n, void **d, int *) {
+        return lai_rmsnorm_f32(P<float>(d, 0), P<float>(d, 1), P<float>(d, 2), n, dim, eps, s);
+    });
+}
+
+void qwen_rms_norm_per_head(float *x, const float *w, int seq, int n_heads, int head_dim,
+                            float eps) {
+    const char *fn = "qwen_rms_norm_per_head";
+    if (!x || !w || seq < 0 || n_heads <= 0 || head_dim <= 0 || (head_dim & 1)) {
+        fail(fn, LAI_ERR_INVALID, "arguments");
+        return;
+    }
+    std::vector<Arg> a = {{x, (size_t)n_heads * head_dim * 4, 0, true, true},
+                          {w, 0, (size_t)head_dim * 4, true, false}};
+    run_op(fn, a, seq, [&](cudaStream_t s, int64_t, int64_t n, void **d, int *err) {
+        return lai_qk_norm_rope_f32(P<float>(d, 0), nullptr, P<float>(d, 1), nullptr, nullptr,
+                                    nullptr, nullptr, 0, n, n_heads, 0, head_dim, eps, err, s);
+    });
+}
+
+void qwen_apply_rope_neox(float *x, const float *cos, const float *sin, int seq, int n_heads,
+                          int head_dim) {
+    const char *fn = "qwen_apply_rope_neox";
+    if (!x || !cos || !sin || seq < 0 || n_heads <= 0 || head_dim <= 0 || (head_dim & 1)) {
+        fail(fn, LAI_ERR_INVALID, "arguments");
+        return;
+    }
+    const size_t hb = (size_t)head_dim * 4;
+    std::vector<Arg> a = {{x, (size_t)n_heads * hb, 0, true, true},
+                          {cos, hb, 0, true, false},
+                          {sin, hb, 0, true, false}};
+    run_op(fn, a, seq, [&](cudaStream_t s, int64_t, int64_t n, void **d, int *err) {
+        return lai_qk_norm_rope_f32(P<float>(d, 0), nullptr, nullptr, nullptr, P<float>(d, 1),
+                                    P<float>(d, 2), nullptr, n, n, n_heads, 0, head_dim, 0.f,
+                                    err, s);
+    });
+}
+
+void qwen_compute_rope_neox(float *cos, float *sin, const int *pos, int n, int head_dim,
+                            float theta) {
+    const char *fn = "qwen_compute_rope_neox";
+    if (!cos || !sin || !pos || n < 0 || head_dim <= 0 || (head_dim & 1) || head_dim > 512) {
+        fail(fn, LAI_ERR_INVALID, "arguments");
+        return;
+    }
+    const size_t hb = (size_t)head_dim * 4;
+    std::vector<Arg> a = {{cos, hb, 0, false, true}, {sin, hb, 0, false, true},
+                          {pos, 4, 0, true, false}};
+    run_op(fn, a, n, [&](cudaStream_t s, int64_t, int64_t m, void **d, int *) {
+        return lai_rope_table_f32(P<float>(d, 0), P<float>(d, 1), P<int32_t>(d, 2), m, head_dim,
+                                  theta, s);
+    });
+}
+
+void qwen_swiglu_multiply(float *out, const float *gate_up, int seq, int inter) {
+    const char *fn = "qwen_swiglu_multiply";
+    if (!out || !gate_up || seq < 0 || inter <= 0) { fail(fn, LAI_ERR_INVALID, "arguments"); return; }
+    std::vector<Arg> a = {{out, (size_t)inter * 4, 0, false, true},
+                          {gate_up, (size_t)inter * 8, 0, true, false}};
+    run_op(fn, a, seq, [&](cudaStream_t s, int64_t, int64_t n, void **d, int *) {
+        return lai_swiglu_f32(P<float>(d, 0), P<float>(d, 1), n, inter, s);
+    });
+}
+
+void qwen_add_inplace(float *x, const float *y, int n) {
+    const char *fn = "qwen_add_inplace";
+    if (!x || !y || n < 0) { fail(fn, LAI_ERR_INVALID, "arguments"); return; }
+    std::vector<Arg> a = {{x, 4, 0, true, true}, {y, 4, 0, true, false}};
+    run_op(fn, a, n, [&](cudaStream_t s, int64_t, int64_t m, void **d, int *) {
+        return lai_add_f32(P<float>(d, 0), P<float>(d, 1), m, s);
+    });
+}
+
+void qwen_silu(float *x, int n) {
+    const char *fn = "qwen_silu";
+    if (!x || n < 0) { fail(fn, LAI_ERR_INVALID, "arguments"); return; }
+    std::vector<Arg> a = {{x, 4, 0, true, true}};
+    run_op(fn, a, n, [&](cudaStream_t s, int64_t, int64_t m, void **d, int *) {
+        return lai_silu_f32(P<float>(d, 0), m, s);
+    });
+}
+
+void voc_snake_beta(float *x, const float *exp_alpha, const float *inv_exp_beta, int channels,
+                    int T) {
+    const char *fn = "voc_snake_beta";
+    if (!x || !exp_alpha || !inv_exp_beta || channels < 0 || T < 0) {
+        fail(fn, LAI_ERR_INVALID, "arguments");
+        return;
+    }
+    if (T == 0) return;
+    // rows are channels: the per-channel parameters are chunked with their rows
+    std::vector<Arg> a = {{x, (size_t)T * 4, 0, true, true},
+                          {exp_alpha, 4, 0, true, false},
+                          {inv_exp_beta, 4, 0, true, false}};
+    run_op(fn, a, channels, [&](cudaStream_t s, int64_t, int64_t n, void **d, int *) {
+        return lai_snake_beta_f32(P<float>(d, 0), P<float>(d, 1), P<float>(d, 2), 1, (int)n, T, s);
+    });
+}
+
+void lai_embed_lookup_bf16(float *dst, const uint16_t *table, int token_id, int dim,
+                           int64_t vocab) {
+    const char *fn = "lai_embed_lookup_bf16";
+    if (!dst || !table || dim <= 0 || token_id < 0 || (vocab > 0 && token_id >= vocab)) {
+        fail(fn, vocab > 0 && token_id >= vocab ? LAI_ERR_RANGE : LAI_ERR_INVALID, "arguments");
+        return;
+    }
+    const void *tdev = mapped_device_ptr(table);
+    if (!tdev) {
+        fail(fn, LAI_ERR_INVALID, "table must be device memory or registered host memory");
+        return;
+    }
+    // Gather row 0 of the one-row view that starts at the requested row.
+    const uint16_t *row = static_cast<const uint16_t *>(tdev) + (size_t)token_id * dim;
+    Ctx *c = get_ctx(fn);
+    if (!c) return;
+    const int32_t *ids = c->zero_id;
+    std::vector<Arg> a = {{dst, (size_t)dim * 4, 0, false, true}};
+    run_op(fn, a, 1, [&](cudaStream_t s, int64_t, int64_t, void **d, int *) {
+        return lai_embed_gather_bf16_to_f32(P<float>(d, 0), row, ids, 1, dim, 1, nullptr, s);
+    });
+}
+
+int lai_register_host_table(const void *table, size_t bytes) {
+    if (!table || !bytes) return fail("lai_register_host_table", LAI_ERR_INVALID, "arguments");
+    cudaError_t e = cudaHostRegister(const_cast<void *>(table), bytes,
+                                     cudaHostRegisterMapped | cudaHostRegisterPortable);
+    return e == cudaSuccess ? LAI_OK : cuda_fail("lai_register_host_table", e);
+}
+
+int lai_unregister_host_table(const void *table) {
+    cudaError_t e = cudaHostUnregister(const_cast<void *>(table));
+    return e == cudaSuccess ? LAI_OK : cuda_fail("lai_unregister_host_table", e);
+}
+
+int lai_last_error(void) {
+    int e = t_last_error;
+    t_last_error = LAI_OK;
+    return e;
+}
+
+void lai_set_stream(void *stream) { t_stream = static_cast<cudaStream_t>(stream); }
+void *lai_get_stream(void) { return t_stream; }
+
+int lai_device_error_flags(void) {
+    Ctx *c = get_ctx("lai_device_error_flags");
+    if (!c) return LAI_ERR_CUDA;
+    int flags = 0;
+    if (cudaStreamSynchronize(t_stream) != cudaSuccess ||
+        cudaMemcpy(&flags, c->derr_direct, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemset(c->derr_direct, 0, sizeof(int)) != cudaSuccess)
+        return cuda_fail("lai_device_error_flags", cudaGetLastError());
+    return flags;
+}
+
+void lai_shutdown(void) {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    for (auto &kv : t_ctx) {
+        Ctx &c = kv.second;
+        cudaSetDevice(c.device);
+        for (int s = 0; s < kSlots; s++) {
+            if (c.pipe[s]) cudaStreamSynchronize(c.pipe[s]), cudaStreamDestroy(c.pipe[s]);
+            if (c.slot[s]) cudaFree(c.slot[s]);
+        }
+        if (c.whole) cudaFree(c.whole);
+        if (c.derr) cudaFree(c.derr);
+        for (cudaEvent_t ev : c.events) cudaEventDestroy(ev);
+        if (c.start_ev) cudaEventDestroy(c.start_ev);
+    }
+    t_ctx.clear();
+    cudaSetDevice(cur);
+}
+
+}  // extern "C"

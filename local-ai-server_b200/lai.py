@@ -1,0 +1,221 @@
+"""Python binding of liblai_kernels.so (ctypes over the C ABI in include/*.h).
+
+The library is the product; this module only marshals torch tensors (device
+memory, streams) into the C entry points and raises on a non-zero status. There
+is no fallback: if the shared library is missing or CUDA is unavailable the
+calls fail loudly.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(HERE)
+LIB_PATH = os.path.join(HERE, "liblai_kernels.so")
+
+LAI_OK, LAI_ERR_INVALID, LAI_ERR_CUDA, LAI_ERR_RANGE, LAI_ERR_ALIAS, LAI_ERR_NOMEM, LAI_ERR_TOOBIG = \
+    0, -1, -2, -3, -4, -5, -6
+LAI_DEVERR_TOKEN_ID, LAI_DEVERR_POSITION = 1, 2
+
+_vp, _i32, _i64, _f32, _u64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_uint64
+
+# name -> (restype, argtypes); every exported symbol of include/*.h
+SIGNATURES: dict[str, tuple] = {
+    "lai_status_string": (ctypes.c_char_p, [_i32]),
+    "lai_version": (_i32, []),
+    "lai_rmsnorm_bf16": (_i32, [_vp, _vp, _vp, _i64, _i32, _f32, _vp]),
+    "lai_rmsnorm_f32": (_i32, [_vp, _vp, _vp, _i64, _i32, _f32, _vp]),
+    "lai_add_rmsnorm_bf16": (_i32, [_vp, _vp, _vp, _vp, _i64, _i32, _f32, _vp]),
+    "lai_add_rmsnorm_f32": (_i32, [_vp, _vp, _vp, _vp, _i64, _i32, _f32, _vp]),
+    "lai_qk_norm_rope_bf16": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32,
+                                     _i32, _f32, _vp, _vp]),
+    "lai_qk_norm_rope_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32,
+                                    _i32, _f32, _vp, _vp]),
+    "lai_rope_table_f32": (_i32, [_vp, _vp, _vp, _i64, _i32, _f32, _vp]),
+    "lai_swiglu_bf16": (_i32, [_vp, _vp, _i64, _i32, _vp]),
+    "lai_swiglu_f32": (_i32, [_vp, _vp, _i64, _i32, _vp]),
+    "lai_swiglu_separate_f32": (_i32, [_vp, _vp, _vp, _i64, _vp]),
+    "lai_silu_f32": (_i32, [_vp, _i64, _vp]),
+    "lai_add_bf16": (_i32, [_vp, _vp, _i64, _vp]),
+    "lai_add_f32": (_i32, [_vp, _vp, _i64, _vp]),
+    "lai_embed_gather_bf16": (_i32, [_vp, _vp, _vp, _i64, _i32, _i64, _vp, _vp]),
+    "lai_embed_gather_bf16_to_f32": (_i32, [_vp, _vp, _vp, _i64, _i32, _i64, _vp, _vp]),
+    "lai_snake_beta_f32": (_i32, [_vp, _vp, _vp, _i64, _i32, _i64, _vp]),
+    "lai_synth_normal_bf16": (_i32, [_vp, _i64, _u64, _i64, _f32, _f32, _vp]),
+    "lai_synth_normal_f32": (_i32, [_vp, _i64, _u64, _i64, _f32, _f32, _vp]),
+    "lai_synth_uniform_i32": (_i32, [_vp, _i64, _u64, _i64, _i32, _i32, _vp]),
+    # reference-named drop-ins (lai_qwen_dropin.h)
+    "qwen_rms_norm": (None, [_vp, _vp, _vp, _i32, _i32, _f32]),
+    "qwen_rms_norm_per_head": (None, [_vp, _vp, _i32, _i32, _i32, _f32]),
+    "qwen_apply_rope_neox": (None, [_vp, _vp, _vp, _i32, _i32, _i32]),
+    "qwen_compute_rope_neox": (None, [_vp, _vp, _vp, _i32, _i32, _f32]),
+    "qwen_swiglu_multiply": (None, [_vp, _vp, _i32, _i32]),
+    "qwen_add_inplace": (None, [_vp, _vp, _i32]),
+    "qwen_silu": (None, [_vp, _i32]),
+    "voc_snake_beta": (None, [_vp, _vp, _vp, _i32, _i32]),
+    "lai_embed_lookup_bf16": (None, [_vp, _vp, _i32, _i32, _i64]),
+    "lai_register_host_table": (_i32, [_vp, ctypes.c_size_t]),
+    "lai_unregister_host_table": (_i32, [_vp]),
+    "lai_last_error": (_i32, []),
+    "lai_set_stream": (None, [_vp]),
+    "lai_get_stream": (_vp, []),
+    "lai_device_error_flags": (_i32, []),
+    "lai_shutdown": (None, []),
+}
+
+
+class LaiError(RuntimeError):
+    def __init__(self, fn: str, status: int):
+        self.status = status
+        super().__init__(f"{fn} failed: {status_string(status)} ({status})")
+
+
+_LIB: ctypes.CDLL | None = None
+
+
+def header_symbols() -> list[str]:
+    """Function names declared with LAI_API in include/*.h."""
+    names = []
+    inc = os.path.join(REPO, "include")
+    for fn in sorted(os.listdir(inc)):
+        if fn.endswith(".h"):
+            with open(os.path.join(inc, fn)) as f:
+                names += re.findall(r"LAI_API\s+[\w\s\*]+?\b(\w+)\s*\(", f.read())
+    return names
+
+
+def load() -> ctypes.CDLL:
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not os.path.exists(LIB_PATH):
+        raise FileNotFoundError(
+            f"{LIB_PATH} is not built; run `python local-ai-server_b200/build.py` "
+            "(there is no CPU fallback)")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _LIB = lib
+    return lib
+
+
+def status_string(status: int) -> str:
+    return load().lai_status_string(status).decode()
+
+
+def check(fn: str, status: int) -> None:
+    if status != LAI_OK:
+        raise LaiError(fn, status)
+
+
+# ---- torch helpers -------------------------------------------------------------
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _s(stream):
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+def _bf16(t):
+    import torch
+    assert t.dtype in (torch.bfloat16, torch.int16, torch.uint16), t.dtype
+    return _p(t)
+
+
+def call(name: str, *args) -> int:
+    st = getattr(load(), name)(*args)
+    check(name, st)
+    return st
+
+
+def rmsnorm(x, w, eps, y=None, stream=None):
+    import torch
+    y = torch.empty_like(x) if y is None else y
+    fn = "lai_rmsnorm_bf16" if x.dtype == torch.bfloat16 else "lai_rmsnorm_f32"
+    call(fn, _p(y), _p(x), _p(w), x.shape[0], x.shape[-1], eps, _s(stream))
+    return y
+
+
+def add_rmsnorm(x, delta, w, eps, y=None, stream=None):
+    import torch
+    y = torch.empty_like(x) if y is None else y
+    fn = "lai_add_rmsnorm_bf16" if x.dtype == torch.bfloat16 else "lai_add_rmsnorm_f32"
+    call(fn, _p(x), _p(delta), _p(w), _p(y), x.shape[0], x.shape[-1], eps, _s(stream))
+    return y
+
+
+def qk_norm_rope(q, k, wq, wk, cos_t, sin_t, pos, n_q, n_kv, head_dim, eps, err=None,
+                 stream=None):
+    import torch
+    fn = "lai_qk_norm_rope_bf16" if q.dtype == torch.bfloat16 else "lai_qk_norm_rope_f32"
+    table_rows = 0 if cos_t is None else cos_t.shape[0]
+    call(fn, _p(q), _p(k), _p(wq), _p(wk), _p(cos_t), _p(sin_t), _p(pos), table_rows,
+         q.shape[0], n_q, n_kv, head_dim, eps, _p(err), _s(stream))
+
+
+def rope_table(pos, n, head_dim, theta, stream=None, device="cuda"):
+    import torch
+    c = torch.empty((n, head_dim), dtype=torch.float32, device=device)
+    s = torch.empty_like(c)
+    call("lai_rope_table_f32", _p(c), _p(s), _p(pos), n, head_dim, theta, _s(stream))
+    return c, s
+
+
+def swiglu(gate_up, inter, out=None, stream=None):
+    import torch
+    rows = gate_up.shape[0]
+    out = torch.empty((rows, inter), dtype=gate_up.dtype, device=gate_up.device) if out is None else out
+    fn = "lai_swiglu_bf16" if gate_up.dtype == torch.bfloat16 else "lai_swiglu_f32"
+    call(fn, _p(out), _p(gate_up), rows, inter, _s(stream))
+    return out
+
+
+def swiglu_inplace(gate_up, inter, stream=None):
+    """Compact [rows, 2*inter] into its own first rows*inter elements (reference call form)."""
+    import torch
+    fn = "lai_swiglu_bf16" if gate_up.dtype == torch.bfloat16 else "lai_swiglu_f32"
+    call(fn, _p(gate_up), _p(gate_up), gate_up.shape[0], inter, _s(stream))
+    return gate_up.view(-1)[: gate_up.shape[0] * inter].view(gate_up.shape[0], inter)
+
+
+def add(x, y, stream=None):
+    import torch
+    fn = "lai_add_bf16" if x.dtype == torch.bfloat16 else "lai_add_f32"
+    call(fn, _p(x), _p(y), x.numel(), _s(stream))
+    return x
+
+
+def embed_gather(table, ids, to_f32: bool, err=None, stream=None):
+    import torch
+    n, dim = ids.shape[0], table.shape[1]
+    out = torch.empty((n, dim), dtype=torch.float32 if to_f32 else table.dtype, device=ids.device)
+    fn = "lai_embed_gather_bf16_to_f32" if to_f32 else "lai_embed_gather_bf16"
+    call(fn, _p(out), _p(table), _p(ids), n, dim, table.shape[0], _p(err), _s(stream))
+    return out
+
+
+def snake_beta(x, ea, ieb, stream=None):
+    b, c, t = (1, *x.shape) if x.dim() == 2 else x.shape
+    call("lai_snake_beta_f32", _p(x), _p(ea), _p(ieb), b, c, t, _s(stream))
+    return x
+
+
+def synth_normal(t, seed, offset=0, mean=0.0, std=1.0, stream=None):
+    import torch
+    fn = "lai_synth_normal_bf16" if t.dtype == torch.bfloat16 else "lai_synth_normal_f32"
+    call(fn, _p(t), t.numel(), seed, offset, mean, std, _s(stream))
+    return t
+
+
+def synth_uniform_i32(t, seed, lo, hi, offset=0, stream=None):
+    call("lai_synth_uniform_i32", _p(t), t.numel(), seed, offset, lo, hi, _s(stream))
+    return t

@@ -1,0 +1,135 @@
+"""Workloads and the row-sharded runner for the per-layer kernels.
+
+A decoder layer's elementwise chain over `tokens` rows (BF16 activations, FP32
+norm weights and RoPE table), laid out as the reference's buffers are
+(src/tts_native.c:314-338, ensure_prefill_buffers):
+    x [T, D] residual, delta_attn / delta_ffn [T, D] (o_proj / down_proj outputs),
+    y [T, D] normed, q [T, Hq*hd], k [T, Hkv*hd], gate_up [T, 2I] interleaved,
+    act [T, I] SwiGLU output, positions [T] int32, cos/sin [P, hd] FP32.
+One step launches, in the reference's per-layer order (src/tts_native.c:553-592):
+    add_rmsnorm(x += delta_ffn, y = norm(x; input_norm))   (prev. layer residual fused)
+    qk_norm_rope(q, k)
+    add_rmsnorm(x += delta_attn, y = norm(x; post_attn_norm))
+    swiglu(gate_up -> act)
+Rows are independent, so G devices each run their own contiguous row block
+(`shard_range`) with no collective; inputs are generated on each device from a
+counter-based generator keyed by global element index, so a shard's contents do
+not depend on G.
+"""
+from __future__ import annotations
+
+import dataclasses
+
+import lai
+
+BF16_BYTES = 2
+
+
+@dataclasses.dataclass(frozen=True)
+class LayerConfig:
+    name: str
+    tokens: int
+    dim: int
+    inter: int
+    n_q: int = 16
+    n_kv: int = 8
+    head_dim: int = 128
+    pos_mode: str = "seq"      # "seq": positions t % pos_period; "random": U[0, pos_period)
+    pos_period: int = 1024
+    theta: float = 1e6
+    eps: float = 1e-6
+    vocab: int = 0             # embedding table rows for the gather (0 = no gather)
+
+    # Algorithmic HBM bytes per token (BF16 storage), per kernel.
+    def bytes_per_token(self) -> dict[str, int]:
+        s = BF16_BYTES
+        return {
+            "add_rmsnorm": 4 * self.dim * s,                       # read x, delta; write x', y
+            "qk_norm_rope": 2 * (self.n_q + self.n_kv) * self.head_dim * s,  # q, k in place
+            "swiglu": 3 * self.inter * s,                          # read 2I, write I
+        }
+
+    def step_bytes_per_token(self) -> int:
+        b = self.bytes_per_token()
+        return 2 * b["add_rmsnorm"] + b["qk_norm_rope"] + b["swiglu"]
+
+
+# BASELINE configs (SURVEY 8a naming: C1..C5).
+CONFIGS = {
+    "c1": LayerConfig("qwen3-asr-0.6b-decoder-layer", tokens=512, dim=1024, inter=3072,
+                      pos_period=512, vocab=151936),
+    "c2": LayerConfig("qwen3-asr-1.7b-decoder-layer", tokens=64 * 1024, dim=2048, inter=6144,
+                      pos_period=1024),
+    "c3": LayerConfig("qwen3-tts-0.6b-talker-decode", tokens=256, dim=1024, inter=3072,
+                      pos_mode="random", pos_period=4096, vocab=3072),
+    "c5": LayerConfig("qwen3-1.7b-chain-2m", tokens=1 << 21, dim=2048, inter=6144,
+                      pos_period=1024),
+}
+
+# Vocoder SnakeBeta stages (channels, T) x batch 8 (config 4).
+SNAKE_STAGES = [(1536, 2000), (768, 16000), (384, 48000), (192, 96000), (96, 192000)]
+SNAKE_BATCH = 8
+
+
+def shard_range(n: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous balanced block [start, stop) of n rows for `rank` of `world`."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of {world}")
+    base, extra = divmod(n, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+class LayerChain:
+    """Device buffers and launches for one shard of a LayerConfig."""
+
+    KERNELS = ("add_rmsnorm", "qk_norm_rope", "add_rmsnorm", "swiglu")
+
+    def __init__(self, cfg: LayerConfig, rows: int, row0: int = 0, seed: int = 1234,
+                 device: str = "cuda"):
+        import torch
+        self.cfg, self.rows, self.row0, self.device = cfg, rows, row0, device
+        T, D, I = rows, cfg.dim, cfg.inter
+        bf = torch.bfloat16
+        e = lambda *s, dt=bf: torch.empty(s, dtype=dt, device=device)  # noqa: E731
+        self.x, self.d_attn, self.d_ffn, self.y = e(T, D), e(T, D), e(T, D), e(T, D)
+        self.q, self.k = e(T, cfg.n_q * cfg.head_dim), e(T, cfg.n_kv * cfg.head_dim)
+        self.gate_up, self.act = e(T, 2 * I), e(T, I)
+        f32 = torch.float32
+        self.w_in, self.w_post = e(D, dt=f32), e(D, dt=f32)
+        self.wq, self.wk = e(cfg.head_dim, dt=f32), e(cfg.head_dim, dt=f32)
+        self.pos = e(T, dt=torch.int32)
+        # global element offsets make each shard's data independent of the shard count
+        for i, (t, width) in enumerate([(self.x, D), (self.d_attn, D), (self.d_ffn, D),
+                                        (self.q, cfg.n_q * cfg.head_dim),
+                                        (self.k, cfg.n_kv * cfg.head_dim), (self.gate_up, 2 * I)]):
+            lai.synth_normal(t, seed=seed + i, offset=row0 * width)
+        for i, w in enumerate([self.w_in, self.w_post, self.wq, self.wk]):
+            lai.synth_normal(w, seed=seed + 100 + i, mean=1.0, std=0.02)
+        if cfg.pos_mode == "random":
+            lai.synth_uniform_i32(self.pos, seed=seed + 200, lo=0, hi=cfg.pos_period, offset=row0)
+        else:
+            self.pos.copy_((torch.arange(row0, row0 + T, device=device) % cfg.pos_period).to(torch.int32))
+        table_pos = torch.arange(cfg.pos_period, dtype=torch.int32, device=device)
+        self.cos, self.sin = lai.rope_table(table_pos, cfg.pos_period, cfg.head_dim, cfg.theta,
+                                            device=device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def launches(self, stream=None):
+        """The step as a list of callables, one kernel launch each."""
+        c = self.cfg
+        return [
+            lambda: lai.add_rmsnorm(self.x, self.d_ffn, self.w_in, c.eps, y=self.y, stream=stream),
+            lambda: lai.qk_norm_rope(self.q, self.k, self.wq, self.wk, self.cos, self.sin, self.pos,
+                                     c.n_q, c.n_kv, c.head_dim, c.eps, err=self.err, stream=stream),
+            lambda: lai.add_rmsnorm(self.x, self.d_attn, self.w_post, c.eps, y=self.y, stream=stream),
+            lambda: lai.swiglu(self.gate_up, c.inter, out=self.act, stream=stream),
+        ]
+
+    def step(self, stream=None) -> None:
+        for f in self.launches(stream):
+            f()
+
+    def bytes_per_launch(self) -> list[int]:
+        b = self.cfg.bytes_per_token()
+        return [b[k] * self.rows for k in self.KERNELS]

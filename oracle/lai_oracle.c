@@ -1,0 +1,359 @@
+/*
+ * lai_oracle.c - CPU restatement of local-ai-server's per-layer kernels.
+ *
+ * TEST INFRASTRUCTURE ONLY: the checker for the CUDA kernels and the timed CPU
+ * baseline. The product library never links or calls it.
+ *
+ * Provenance. The reference's own C for qwen_rms_norm, qwen_rms_norm_per_head,
+ * qwen_apply_rope_neox, qwen_compute_rope_neox, qwen_swiglu_multiply,
+ * qwen_add_inplace and qwen_silu lives in the un-vendored git submodule
+ * `qwen-asr` (https://github.com/rmtew/qwen-asr.git, .gitmodules:1-3, pinned
+ * commit unknown), which is empty in the mounted reference. Those functions are
+ * restated here from
+ *   - their call sites (argument order, in-place conventions):
+ *       src/tts_native.c:553-592, 634-669, 711-748; src/tts_vocoder_xfmr.c:150-211
+ *   - the repo's own numpy specification of the same math:
+ *       tools/verify_xfmr.py:32-35 (RMSNorm), :37-55 (NeoX RoPE), :79-80 (SiLU)
+ *   - the C that is present for the neighbouring code:
+ *       src/tts_native.c:377-417 (RoPE table), :149-161 (gate/up row interleave),
+ *       :35-40 (BF16 -> F32), src/tts_vocoder_xfmr.c:73-80 (SiLU * up).
+ * The parity of these restatements is pinned to the reference's numpy
+ * functions (tests/golden/make_golden.py extracts them from tools/verify_*.py),
+ * not to the absent C. SnakeBeta (src/tts_vocoder_ops.c:279-305) is present and
+ * oracle/Makefile compiles the reference's own function into oracle/_ref/; the
+ * restatement below is checked against it.
+ *
+ * LAI_ACC selects the accumulator of sums of squares: double in the checker
+ * build (so that the oracle's own rounding stays far below the 1e-5 tolerance),
+ * float in the timed baseline build (what a C implementation would do).
+ */
+#include "lai_oracle.h"
+
+#include <math.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#ifndef LAI_ACC
+#define LAI_ACC double
+#endif
+
+typedef LAI_ACC acc_t;
+
+int oracle_num_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
+
+/* ---------------------------------------------------------------------------
+ * BF16 <-> F32. Widening is the bit shift of src/tts_native.c:35-40 (exact).
+ * Narrowing is round-to-nearest-even, the rounding of every BF16 store
+ * (NaN becomes the canonical 0x7fff, as the GPU's cvt.rn.bf16.f32 makes it).
+ * ------------------------------------------------------------------------- */
+float oracle_bf16_to_f32(uint16_t h) {
+    uint32_t bits = ((uint32_t)h) << 16;
+    float f;
+    memcpy(&f, &bits, sizeof(f));
+    return f;
+}
+
+uint16_t oracle_f32_to_bf16(float f) {
+    uint32_t u;
+    memcpy(&u, &f, sizeof(u));
+    if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7fffu; /* canonical NaN, as cvt.rn.bf16 */
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+/* ---------------------------------------------------------------------------
+ * RMSNorm: out[s,:] = (x[s,:] / sqrt(mean(x[s,:]^2) + eps)) * w
+ * Spec: tools/verify_xfmr.py:32-35. Call sites: src/tts_native.c:556, 584, 637,
+ * 661, 674 (out == x), src/tts_vocoder_xfmr.c:163, 189, 211. Row-wise, so
+ * out == x is safe.
+ * ------------------------------------------------------------------------- */
+static void rms_norm_row(float *out, const float *x, const float *w, int dim, float eps) {
+    acc_t ss = 0;
+    for (int i = 0; i < dim; i++) ss += (acc_t)x[i] * (acc_t)x[i];
+    float rms = sqrtf((float)(ss / (acc_t)dim) + eps);
+    for (int i = 0; i < dim; i++) out[i] = (x[i] / rms) * w[i];
+}
+
+void oracle_rms_norm(float *out, const float *x, const float *w, int seq, int dim, float eps) {
+#pragma omp parallel for schedule(static)
+    for (int s = 0; s < seq; s++)
+        rms_norm_row(out + (size_t)s * dim, x + (size_t)s * dim, w, dim, eps);
+}
+
+/* Per-head RMSNorm in place; w [head_dim] shared by all heads (q_norm / k_norm,
+ * src/tts_native.c:125-128). Call sites src/tts_native.c:562-563, 644-645. */
+void oracle_rms_norm_per_head(float *x, const float *w, int seq, int n_heads, int head_dim,
+                              float eps) {
+#pragma omp parallel for schedule(static)
+    for (int s = 0; s < seq; s++)
+        for (int h = 0; h < n_heads; h++) {
+            float *xh = x + ((size_t)s * n_heads + h) * head_dim;
+            rms_norm_row(xh, xh, w, head_dim, eps);
+        }
+}
+
+/* ---------------------------------------------------------------------------
+ * NeoX RoPE (rotate-half) in place. Row s uses row s of the cos/sin table;
+ * decode call sites offset the table pointer to row `pos`
+ * (src/tts_native.c:565-568, 647-648). Table rows are [head_dim] with
+ * duplicated halves (src/tts_native.c:402-412), and the formula follows
+ * tools/verify_xfmr.py:49-53: (x1*c - x2*s, x1*s + x2*c).
+ * ------------------------------------------------------------------------- */
+static void rope_head(float *xh, const float *c, const float *sn, int head_dim) {
+    int half = head_dim / 2;
+    for (int d = 0; d < half; d++) {
+        float x1 = xh[d], x2 = xh[d + half];
+        xh[d] = x1 * c[d] - x2 * sn[d];
+        xh[d + half] = x1 * sn[d + half] + x2 * c[d + half];
+    }
+}
+
+void oracle_apply_rope_neox(float *x, const float *cos_t, const float *sin_t, int seq,
+                            int n_heads, int head_dim) {
+#pragma omp parallel for schedule(static)
+    for (int s = 0; s < seq; s++)
+        for (int h = 0; h < n_heads; h++)
+            rope_head(x + ((size_t)s * n_heads + h) * head_dim, cos_t + (size_t)s * head_dim,
+                      sin_t + (size_t)s * head_dim, head_dim);
+}
+
+void oracle_apply_rope_neox_pos(float *x, const float *cos_t, const float *sin_t,
+                                const int32_t *pos, int seq, int n_heads, int head_dim) {
+    for (int s = 0; s < seq; s++) {
+        size_t p = pos ? (size_t)pos[s] : (size_t)s;
+        for (int h = 0; h < n_heads; h++)
+            rope_head(x + ((size_t)s * n_heads + h) * head_dim, cos_t + p * head_dim,
+                      sin_t + p * head_dim, head_dim);
+    }
+}
+
+/* inv_freq[d] = 1 / theta^(2d/hd), exactly as ensure_rope_cache computes it
+ * (src/tts_native.c:383-388). */
+void oracle_rope_inv_freq(float *inv_freq, int head_dim, float theta) {
+    for (int d = 0; d < head_dim / 2; d++)
+        inv_freq[d] = 1.0f / powf(theta, (float)(2 * d) / (float)head_dim);
+}
+
+/* cos/sin rows for arbitrary positions: qwen_compute_rope_neox's contract
+ * (src/tts_vocoder_xfmr.c:150-156), row layout of src/tts_native.c:402-412. */
+void oracle_compute_rope_neox(float *cos_t, float *sin_t, const int *pos, int n, int head_dim,
+                              float theta) {
+    int half = head_dim / 2;
+    float inv_freq[1024];
+    if (half > 1024) return;
+    oracle_rope_inv_freq(inv_freq, head_dim, theta);
+    for (int i = 0; i < n; i++) {
+        float *cr = cos_t + (size_t)i * head_dim, *sr = sin_t + (size_t)i * head_dim;
+        for (int d = 0; d < half; d++) {
+            float angle = (float)pos[i] * inv_freq[d];
+            float c = cosf(angle), s = sinf(angle);
+            cr[d] = c;
+            cr[half + d] = c;
+            sr[d] = s;
+            sr[half + d] = s;
+        }
+    }
+}
+
+/* ---------------------------------------------------------------------------
+ * SwiGLU over the interleaved GEMM output. The gate/up weight rows are
+ * interleaved [g0,u0,g1,u1,...] (src/tts_native.c:149-161), so row s of
+ * gate_up is [g(s,0), u(s,0), g(s,1), u(s,1), ...] and, flattened,
+ * out[k] = silu(in[2k]) * in[2k+1] for k < seq*inter. The call sites pass
+ * out == gate_up (src/tts_native.c:588, 665, 744); increasing k is safe in place
+ * because write k only clobbers inputs already consumed by k/2.
+ * SiLU*up is written as src/tts_vocoder_xfmr.c:76-78 writes it.
+ * ------------------------------------------------------------------------- */
+static inline float silu_mul(float g, float u) {
+    float sig = 1.0f / (1.0f + expf(-g));
+    return (g * sig) * u;
+}
+
+void oracle_swiglu_multiply(float *out, const float *gate_up, int seq, int inter) {
+    size_t n = (size_t)seq * (size_t)inter;
+    for (size_t k = 0; k < n; k++) out[k] = silu_mul(gate_up[2 * k], gate_up[2 * k + 1]);
+}
+
+/* swiglu_separate (src/tts_vocoder_xfmr.c:73-80). */
+void oracle_swiglu_separate(float *out, const float *gate, const float *up, int n) {
+#pragma omp parallel for schedule(static)
+    for (int i = 0; i < n; i++) out[i] = silu_mul(gate[i], up[i]);
+}
+
+/* qwen_silu(x, n) in place (src/tts_native.c:504); spec tools/verify_xfmr.py:79-80. */
+void oracle_silu(float *x, int n) {
+#pragma omp parallel for schedule(static)
+    for (int i = 0; i < n; i++) {
+        float g = x[i];
+        float sig = 1.0f / (1.0f + expf(-g));
+        x[i] = g * sig;
+    }
+}
+
+/* qwen_add_inplace(x, y, n): x += y (src/tts_native.c:582, 591, 1142). */
+void oracle_add_inplace(float *x, const float *y, int n) {
+#pragma omp parallel for schedule(static)
+    for (int i = 0; i < n; i++) x[i] += y[i];
+}
+
+/* ---------------------------------------------------------------------------
+ * SnakeBeta, scalar branch of voc_snake_beta (src/tts_vocoder_ops.c:298-303):
+ * x[c,t] += ieb[c] * sin(ea[c]*x[c,t])^2, params pre-exponentiated
+ * (src/tts_vocoder.c:221-227).
+ * ------------------------------------------------------------------------- */
+void oracle_snake_beta(float *x, const float *exp_alpha, const float *inv_exp_beta,
+                       int channels, int T) {
+#pragma omp parallel for schedule(static)
+    for (int ch = 0; ch < channels; ch++) {
+        float *row = x + (size_t)ch * T;
+        float ea = exp_alpha[ch], ieb = inv_exp_beta[ch];
+        for (int t = 0; t < T; t++) {
+            float s = sinf(ea * row[t]);
+            row[t] += ieb * s * s;
+        }
+    }
+}
+
+/* ---------------------------------------------------------------------------
+ * BF16 embedding gather (src/tts_native.c:35-40, 473-476): row id of a
+ * [vocab, dim] BF16 table, widened to F32 by the bit shift, or copied as BF16.
+ * ------------------------------------------------------------------------- */
+void oracle_embed_gather_bf16_to_f32(float *out, const uint16_t *table, const int32_t *ids,
+                                     int n, int dim) {
+    for (int r = 0; r < n; r++) {
+        const uint16_t *src = table + (size_t)ids[r] * dim;
+        float *dst = out + (size_t)r * dim;
+        for (int i = 0; i < dim; i++) {
+            uint32_t bits = ((uint32_t)src[i]) << 16;
+            memcpy(&dst[i], &bits, sizeof(float));
+        }
+    }
+}
+
+void oracle_embed_gather_bf16(uint16_t *out, const uint16_t *table, const int32_t *ids, int n,
+                              int dim) {
+    for (int r = 0; r < n; r++)
+        memcpy(out + (size_t)r * dim, table + (size_t)ids[r] * dim, (size_t)dim * 2);
+}
+
+/* ---------------------------------------------------------------------------
+ * Fused compositions. Each is the reference's own call sequence on one row
+ * (src/tts_native.c:582-584: qwen_add_inplace then qwen_rms_norm;
+ * :562-568: per-head norms then RoPE), which is what the fused kernels must
+ * reproduce. BF16 variants round to BF16 wherever the kernel stores BF16: the
+ * updated residual x' is rounded before it is normalised, so the fused kernel
+ * equals the unfused BF16 add followed by the BF16 RMSNorm.
+ * ------------------------------------------------------------------------- */
+void oracle_add_rms_norm_f32(float *x, const float *delta, const float *w, float *y, int seq,
+                             int dim, float eps) {
+    for (int s = 0; s < seq; s++) {
+        float *xr = x + (size_t)s * dim;
+        const float *dr = delta + (size_t)s * dim;
+        for (int i = 0; i < dim; i++) xr[i] += dr[i];
+        rms_norm_row(y + (size_t)s * dim, xr, w, dim, eps);
+    }
+}
+
+void oracle_add_bf16(uint16_t *x, const uint16_t *y, int64_t n) {
+    for (int64_t i = 0; i < n; i++)
+        x[i] = oracle_f32_to_bf16(oracle_bf16_to_f32(x[i]) + oracle_bf16_to_f32(y[i]));
+}
+
+void oracle_rms_norm_bf16(uint16_t *out, const uint16_t *x, const float *w, int seq, int dim,
+                          float eps) {
+    float row[16384], o[16384];
+    if (dim > 16384) return;
+    for (int s = 0; s < seq; s++) {
+        for (int i = 0; i < dim; i++) row[i] = oracle_bf16_to_f32(x[(size_t)s * dim + i]);
+        rms_norm_row(o, row, w, dim, eps);
+        for (int i = 0; i < dim; i++) out[(size_t)s * dim + i] = oracle_f32_to_bf16(o[i]);
+    }
+}
+
+void oracle_add_rms_norm_bf16(uint16_t *x, const uint16_t *delta, const float *w, uint16_t *y,
+                              int seq, int dim, float eps) {
+    oracle_add_bf16(x, delta, (int64_t)seq * dim);
+    oracle_rms_norm_bf16(y, x, w, seq, dim, eps);
+}
+
+void oracle_qk_norm_rope_f32(float *q, float *k, const float *wq, const float *wk,
+                             const float *cos_t, const float *sin_t, const int32_t *pos,
+                             int seq, int n_q_heads, int n_kv_heads, int head_dim, float eps) {
+    if (wq) oracle_rms_norm_per_head(q, wq, seq, n_q_heads, head_dim, eps);
+    if (wk && k) oracle_rms_norm_per_head(k, wk, seq, n_kv_heads, head_dim, eps);
+    if (cos_t) {
+        oracle_apply_rope_neox_pos(q, cos_t, sin_t, pos, seq, n_q_heads, head_dim);
+        if (k) oracle_apply_rope_neox_pos(k, cos_t, sin_t, pos, seq, n_kv_heads, head_dim);
+    }
+}
+
+static void qk_bf16_one(uint16_t *t, const float *w, const float *cos_t, const float *sin_t,
+                        const int32_t *pos, int seq, int heads, int head_dim, float eps) {
+    size_t n = (size_t)seq * heads * head_dim;
+    for (size_t base = 0; base < n; base += (size_t)heads * head_dim) {
+        int s = (int)(base / ((size_t)heads * head_dim));
+        float buf[8192];
+        int row = heads * head_dim;
+        if (row > 8192) return;
+        for (int i = 0; i < row; i++) buf[i] = oracle_bf16_to_f32(t[base + i]);
+        if (w) oracle_rms_norm_per_head(buf, w, 1, heads, head_dim, eps);
+        if (cos_t) {
+            int32_t p = pos ? pos[s] : s;
+            oracle_apply_rope_neox_pos(buf, cos_t, sin_t, &p, 1, heads, head_dim);
+        }
+        for (int i = 0; i < row; i++) t[base + i] = oracle_f32_to_bf16(buf[i]);
+    }
+}
+
+void oracle_qk_norm_rope_bf16(uint16_t *q, uint16_t *k, const float *wq, const float *wk,
+                              const float *cos_t, const float *sin_t, const int32_t *pos,
+                              int seq, int n_q_heads, int n_kv_heads, int head_dim, float eps) {
+    qk_bf16_one(q, wq, cos_t, sin_t, pos, seq, n_q_heads, head_dim, eps);
+    if (k) qk_bf16_one(k, wk, cos_t, sin_t, pos, seq, n_kv_heads, head_dim, eps);
+}
+
+void oracle_swiglu_bf16(uint16_t *out, const uint16_t *gate_up, int seq, int inter) {
+    size_t n = (size_t)seq * (size_t)inter;
+    for (size_t k = 0; k < n; k++)
+        out[k] = oracle_f32_to_bf16(
+            silu_mul(oracle_bf16_to_f32(gate_up[2 * k]), oracle_bf16_to_f32(gate_up[2 * k + 1])));
+}
+
+/* ---------------------------------------------------------------------------
+ * Timed CPU reference: the elementwise ops of one decoder layer, FP32, in the
+ * order talker_prefill calls them (src/tts_native.c:553-592), with the GEMM and
+ * attention outputs supplied as inputs:
+ *   add(x, ffn residual) ; rms_norm ; per-head q, k ; rope q, k ;
+ *   add(x, attn residual) ; rms_norm ; swiglu
+ * The reference compacts SwiGLU in place; in place is only safe serially, so
+ * the multi-threaded timing writes it to gate_up's first half row by row
+ * within each thread's rows (same bytes moved as in place).
+ * ------------------------------------------------------------------------- */
+void oracle_layer_chain_f32(float *x, const float *delta_attn, const float *delta_ffn,
+                            float *x_norm, float *q, float *k, float *gate_up,
+                            const float *w_in, const float *w_post, const float *wq,
+                            const float *wk, const float *cos_t, const float *sin_t, int seq,
+                            int dim, int n_q_heads, int n_kv_heads, int head_dim, int inter,
+                            float eps) {
+    oracle_add_inplace(x, delta_ffn, seq * dim);
+    oracle_rms_norm(x_norm, x, w_in, seq, dim, eps);
+    oracle_rms_norm_per_head(q, wq, seq, n_q_heads, head_dim, eps);
+    oracle_rms_norm_per_head(k, wk, seq, n_kv_heads, head_dim, eps);
+    oracle_apply_rope_neox(q, cos_t, sin_t, seq, n_q_heads, head_dim);
+    oracle_apply_rope_neox(k, cos_t, sin_t, seq, n_kv_heads, head_dim);
+    oracle_add_inplace(x, delta_attn, seq * dim);
+    oracle_rms_norm(x_norm, x, w_post, seq, dim, eps);
+#pragma omp parallel for schedule(static)
+    for (int s = 0; s < seq; s++) {
+        float *row = gate_up + (size_t)s * 2 * inter;
+        for (int j = 0; j < inter; j++) row[j] = silu_mul(row[2 * j], row[2 * j + 1]);
+    }
+}

@@ -1,0 +1,83 @@
+/*
+ * lai_oracle.h - CPU restatement of local-ai-server's per-layer kernels.
+ *
+ * TEST INFRASTRUCTURE ONLY. Nothing in the product library links, loads or
+ * calls this code; only tests/, __graft_entry__.smoke() and bench.py's CPU
+ * baseline leg do, as the checker or as the timed CPU reference.
+ *
+ * The same source (lai_oracle.c) is compiled twice:
+ *   liblai_oracle.so  - the parity checker: -O2 -ffp-contract=off, double
+ *                       accumulation of sums of squares, single thread.
+ *   liblai_cpuref.so  - the timed CPU baseline: the reference's optimisation
+ *                       tier (Makefile:7, -O2 -march=native -ffast-math, here
+ *                       -mavx2 -mfma so it runs on any x86-64 GPU host),
+ *                       float accumulation, OpenMP over rows.
+ *
+ * Function names keep the reference's names with an "oracle_" prefix; argument
+ * order and meaning follow the call sites cited in lai_oracle.c.
+ */
+#ifndef LAI_ORACLE_H
+#define LAI_ORACLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- reference signatures (FP32, host memory) ---- */
+void oracle_rms_norm(float *out, const float *x, const float *w, int seq, int dim, float eps);
+void oracle_rms_norm_per_head(float *x, const float *w, int seq, int n_heads, int head_dim,
+                              float eps);
+void oracle_apply_rope_neox(float *x, const float *cos_t, const float *sin_t, int seq,
+                            int n_heads, int head_dim);
+void oracle_compute_rope_neox(float *cos_t, float *sin_t, const int *pos, int n, int head_dim,
+                              float theta);
+void oracle_rope_inv_freq(float *inv_freq, int head_dim, float theta);
+void oracle_swiglu_multiply(float *out, const float *gate_up, int seq, int inter);
+void oracle_swiglu_separate(float *out, const float *gate, const float *up, int n);
+void oracle_add_inplace(float *x, const float *y, int n);
+void oracle_silu(float *x, int n);
+void oracle_snake_beta(float *x, const float *exp_alpha, const float *inv_exp_beta,
+                       int channels, int T);
+void oracle_embed_gather_bf16_to_f32(float *out, const uint16_t *table, const int32_t *ids,
+                                     int n, int dim);
+void oracle_embed_gather_bf16(uint16_t *out, const uint16_t *table, const int32_t *ids, int n,
+                              int dim);
+
+/* ---- position-indexed RoPE (device API semantics: row r uses table row pos[r]) ---- */
+void oracle_apply_rope_neox_pos(float *x, const float *cos_t, const float *sin_t,
+                                const int32_t *pos, int seq, int n_heads, int head_dim);
+
+/* ---- BF16 storage variants: BF16 in/out, FP32 arithmetic, RNE rounding on store ---- */
+uint16_t oracle_f32_to_bf16(float f);
+float oracle_bf16_to_f32(uint16_t h);
+void oracle_rms_norm_bf16(uint16_t *out, const uint16_t *x, const float *w, int seq, int dim,
+                          float eps);
+void oracle_add_rms_norm_bf16(uint16_t *x, const uint16_t *delta, const float *w, uint16_t *y,
+                              int seq, int dim, float eps);
+void oracle_add_rms_norm_f32(float *x, const float *delta, const float *w, float *y, int seq,
+                             int dim, float eps);
+void oracle_qk_norm_rope_bf16(uint16_t *q, uint16_t *k, const float *wq, const float *wk,
+                              const float *cos_t, const float *sin_t, const int32_t *pos,
+                              int seq, int n_q_heads, int n_kv_heads, int head_dim, float eps);
+void oracle_qk_norm_rope_f32(float *q, float *k, const float *wq, const float *wk,
+                             const float *cos_t, const float *sin_t, const int32_t *pos,
+                             int seq, int n_q_heads, int n_kv_heads, int head_dim, float eps);
+void oracle_swiglu_bf16(uint16_t *out, const uint16_t *gate_up, int seq, int inter);
+void oracle_add_bf16(uint16_t *x, const uint16_t *y, int64_t n);
+
+/* ---- timed CPU reference: one decoder layer's elementwise chain, FP32, called in
+ * the reference's own order (talker_prefill, src/tts_native.c:553-592) ---- */
+void oracle_layer_chain_f32(float *x, const float *delta_attn, const float *delta_ffn,
+                            float *x_norm, float *q, float *k, float *gate_up,
+                            const float *w_in, const float *w_post, const float *wq,
+                            const float *wk, const float *cos_t, const float *sin_t, int seq,
+                            int dim, int n_q_heads, int n_kv_heads, int head_dim, int inter,
+                            float eps);
+int oracle_num_threads(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,306 @@
+"""ctypes access to the CPU oracle (test infrastructure only).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import this
+module, as the parity checker or as the timed CPU reference. The product library
+(local-ai-server_b200/liblai_kernels.so) never loads anything under oracle/.
+
+Libraries (built by oracle/Makefile):
+  _build/liblai_oracle.so    restatement of the reference ops, checker flags
+  _build/liblai_cpuref.so    the same restatement, reference optimisation tier + OpenMP
+  _ref/libvoc_ref_scalar.so  the reference's own voc_snake_beta (src/tts_vocoder_ops.c),
+                             scalar sinf build: the SnakeBeta parity oracle
+  _ref/libvoc_ref_avx2.so    the same function as shipped (AVX2 fast sin)
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_F = ctypes.POINTER(ctypes.c_float)
+_U16 = ctypes.POINTER(ctypes.c_uint16)
+_I32 = ctypes.POINTER(ctypes.c_int32)
+_c_int, _c_float, _c_i64 = ctypes.c_int, ctypes.c_float, ctypes.c_int64
+
+
+def build() -> None:
+    """Compile the oracle and (when the reference source is present) oracle/_ref."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def _lib_path(name: str) -> str:
+    sub = "_ref" if name.startswith("libvoc_ref") else "_build"
+    return os.path.join(HERE, sub, name)
+
+
+_LIBS: dict[str, ctypes.CDLL] = {}
+
+
+def load(name: str = "liblai_oracle.so") -> ctypes.CDLL:
+    if name in _LIBS:
+        return _LIBS[name]
+    path = _lib_path(name)
+    if not os.path.exists(path):
+        build()
+    lib = ctypes.CDLL(path)
+    if name.startswith("liblai_"):
+        _declare(lib)
+    else:
+        lib.voc_snake_beta.argtypes = [_F, _F, _F, _c_int, _c_int]
+        lib.voc_snake_beta.restype = None
+    _LIBS[name] = lib
+    return lib
+
+
+def have_ref() -> bool:
+    return os.path.exists(_lib_path("libvoc_ref_scalar.so"))
+
+
+def _declare(lib: ctypes.CDLL) -> None:
+    sig = {
+        "oracle_rms_norm": [_F, _F, _F, _c_int, _c_int, _c_float],
+        "oracle_rms_norm_per_head": [_F, _F, _c_int, _c_int, _c_int, _c_float],
+        "oracle_apply_rope_neox": [_F, _F, _F, _c_int, _c_int, _c_int],
+        "oracle_apply_rope_neox_pos": [_F, _F, _F, _I32, _c_int, _c_int, _c_int],
+        "oracle_compute_rope_neox": [_F, _F, _I32, _c_int, _c_int, _c_float],
+        "oracle_rope_inv_freq": [_F, _c_int, _c_float],
+        "oracle_swiglu_multiply": [_F, _F, _c_int, _c_int],
+        "oracle_swiglu_separate": [_F, _F, _F, _c_int],
+        "oracle_add_inplace": [_F, _F, _c_int],
+        "oracle_silu": [_F, _c_int],
+        "oracle_snake_beta": [_F, _F, _F, _c_int, _c_int],
+        "oracle_embed_gather_bf16_to_f32": [_F, _U16, _I32, _c_int, _c_int],
+        "oracle_embed_gather_bf16": [_U16, _U16, _I32, _c_int, _c_int],
+        "oracle_rms_norm_bf16": [_U16, _U16, _F, _c_int, _c_int, _c_float],
+        "oracle_add_rms_norm_bf16": [_U16, _U16, _F, _U16, _c_int, _c_int, _c_float],
+        "oracle_add_rms_norm_f32": [_F, _F, _F, _F, _c_int, _c_int, _c_float],
+        "oracle_qk_norm_rope_bf16": [_U16, _U16, _F, _F, _F, _F, _I32, _c_int, _c_int,
+                                     _c_int, _c_int, _c_float],
+        "oracle_qk_norm_rope_f32": [_F, _F, _F, _F, _F, _F, _I32, _c_int, _c_int, _c_int,
+                                    _c_int, _c_float],
+        "oracle_swiglu_bf16": [_U16, _U16, _c_int, _c_int],
+        "oracle_add_bf16": [_U16, _U16, _c_i64],
+        "oracle_layer_chain_f32": [_F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _F,
+                                   _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float],
+        "oracle_num_threads": [],
+    }
+    for name, args in sig.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = _c_int if name == "oracle_num_threads" else None
+    lib.oracle_f32_to_bf16.argtypes = [_c_float]
+    lib.oracle_f32_to_bf16.restype = ctypes.c_uint16
+
+
+def ptr(a: np.ndarray | None, kind=_F):
+    """Pointer to a C-contiguous numpy array (None -> NULL)."""
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(kind)
+
+
+# ---- numpy helpers for BF16 as uint16 bit patterns ----
+
+def bf16_bits_to_f32(h: np.ndarray) -> np.ndarray:
+    return (h.astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16_bits(f: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even F32 -> BF16 bit patterns (same rule as the oracle's C)."""
+    u = np.ascontiguousarray(f, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    r[nan] = 0x7FFF
+    return r
+
+
+# ---- thin wrappers (arrays in, arrays out; inputs are never modified) ----
+
+def rms_norm(x, w, eps, lib=None):
+    lib = lib or load()
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    seq, dim = x.shape
+    lib.oracle_rms_norm(ptr(out), ptr(x), ptr(np.ascontiguousarray(w, np.float32)), seq, dim,
+                        eps)
+    return out
+
+
+def rms_norm_per_head(x, w, n_heads, head_dim, eps, lib=None):
+    lib = lib or load()
+    y = np.array(x, np.float32, copy=True, order="C")
+    lib.oracle_rms_norm_per_head(ptr(y), ptr(np.ascontiguousarray(w, np.float32)), y.shape[0],
+                                 n_heads, head_dim, eps)
+    return y
+
+
+def apply_rope_neox(x, cos_t, sin_t, n_heads, head_dim, lib=None):
+    lib = lib or load()
+    y = np.array(x, np.float32, copy=True, order="C")
+    lib.oracle_apply_rope_neox(ptr(y), ptr(np.ascontiguousarray(cos_t, np.float32)),
+                               ptr(np.ascontiguousarray(sin_t, np.float32)), y.shape[0],
+                               n_heads, head_dim)
+    return y
+
+
+def compute_rope_neox(pos, head_dim, theta, lib=None):
+    lib = lib or load()
+    pos = np.ascontiguousarray(pos, np.int32)
+    n = pos.shape[0]
+    c = np.empty((n, head_dim), np.float32)
+    s = np.empty((n, head_dim), np.float32)
+    lib.oracle_compute_rope_neox(ptr(c), ptr(s), ptr(pos, _I32), n, head_dim, theta)
+    return c, s
+
+
+def rope_inv_freq(head_dim, theta, lib=None):
+    lib = lib or load()
+    f = np.empty(head_dim // 2, np.float32)
+    lib.oracle_rope_inv_freq(ptr(f), head_dim, theta)
+    return f
+
+
+def swiglu_multiply(gate_up, inter, lib=None):
+    lib = lib or load()
+    g = np.ascontiguousarray(gate_up, np.float32)
+    seq = g.shape[0]
+    out = np.empty((seq, inter), np.float32)
+    lib.oracle_swiglu_multiply(ptr(out), ptr(g), seq, inter)
+    return out
+
+
+def swiglu_separate(gate, up, lib=None):
+    lib = lib or load()
+    g = np.ascontiguousarray(gate, np.float32)
+    u = np.ascontiguousarray(up, np.float32)
+    out = np.empty_like(g)
+    lib.oracle_swiglu_separate(ptr(out), ptr(g), ptr(u), g.size)
+    return out
+
+
+def silu(x, lib=None):
+    lib = lib or load()
+    y = np.array(x, np.float32, copy=True, order="C")
+    lib.oracle_silu(ptr(y), y.size)
+    return y
+
+
+def add_inplace(x, y, lib=None):
+    lib = lib or load()
+    r = np.array(x, np.float32, copy=True, order="C")
+    lib.oracle_add_inplace(ptr(r), ptr(np.ascontiguousarray(y, np.float32)), r.size)
+    return r
+
+
+def snake_beta(x, ea, ieb, lib=None):
+    lib = lib or load()
+    y = np.array(x, np.float32, copy=True, order="C")
+    C, T = y.shape[-2], y.shape[-1]
+    rows = y.reshape(-1, C, T)
+    for b in range(rows.shape[0]):
+        lib.oracle_snake_beta(ptr(rows[b]), ptr(np.ascontiguousarray(ea, np.float32)),
+                              ptr(np.ascontiguousarray(ieb, np.float32)), C, T)
+    return y
+
+
+def ref_snake_beta(x, ea, ieb, build: str = "scalar"):
+    """The reference's own voc_snake_beta (compiled from src/tts_vocoder_ops.c)."""
+    lib = load(f"libvoc_ref_{build}.so")
+    y = np.array(x, np.float32, copy=True, order="C")
+    C, T = y.shape[-2], y.shape[-1]
+    rows = y.reshape(-1, C, T)
+    ea = np.ascontiguousarray(ea, np.float32)
+    ieb = np.ascontiguousarray(ieb, np.float32)
+    for b in range(rows.shape[0]):
+        lib.voc_snake_beta(ptr(rows[b]), ptr(ea), ptr(ieb), C, T)
+    return y
+
+
+def gather_bf16_to_f32(table, ids, lib=None):
+    lib = lib or load()
+    table = np.ascontiguousarray(table, np.uint16)
+    ids = np.ascontiguousarray(ids, np.int32)
+    out = np.empty((ids.shape[0], table.shape[1]), np.float32)
+    lib.oracle_embed_gather_bf16_to_f32(ptr(out), ptr(table, _U16), ptr(ids, _I32), ids.shape[0],
+                                        table.shape[1])
+    return out
+
+
+def gather_bf16(table, ids, lib=None):
+    lib = lib or load()
+    table = np.ascontiguousarray(table, np.uint16)
+    ids = np.ascontiguousarray(ids, np.int32)
+    out = np.empty((ids.shape[0], table.shape[1]), np.uint16)
+    lib.oracle_embed_gather_bf16(ptr(out, _U16), ptr(table, _U16), ptr(ids, _I32), ids.shape[0],
+                                 table.shape[1])
+    return out
+
+
+def add_rms_norm_bf16(x, delta, w, eps, lib=None):
+    lib = lib or load()
+    xo = np.array(x, np.uint16, copy=True, order="C")
+    y = np.empty_like(xo)
+    seq, dim = xo.shape
+    lib.oracle_add_rms_norm_bf16(ptr(xo, _U16), ptr(np.ascontiguousarray(delta, np.uint16), _U16),
+                                 ptr(np.ascontiguousarray(w, np.float32)), ptr(y, _U16), seq, dim,
+                                 eps)
+    return xo, y
+
+
+def add_rms_norm_f32(x, delta, w, eps, lib=None):
+    lib = lib or load()
+    xo = np.array(x, np.float32, copy=True, order="C")
+    y = np.empty_like(xo)
+    seq, dim = xo.shape
+    lib.oracle_add_rms_norm_f32(ptr(xo), ptr(np.ascontiguousarray(delta, np.float32)),
+                                ptr(np.ascontiguousarray(w, np.float32)), ptr(y), seq, dim, eps)
+    return xo, y
+
+
+def rms_norm_bf16(x, w, eps, lib=None):
+    lib = lib or load()
+    x = np.ascontiguousarray(x, np.uint16)
+    y = np.empty_like(x)
+    seq, dim = x.shape
+    lib.oracle_rms_norm_bf16(ptr(y, _U16), ptr(x, _U16), ptr(np.ascontiguousarray(w, np.float32)),
+                             seq, dim, eps)
+    return y
+
+
+def qk_norm_rope(q, k, wq, wk, cos_t, sin_t, pos, n_q, n_kv, hd, eps, bf16: bool, lib=None):
+    """Per-head RMSNorm of q and k, then NeoX RoPE at table row pos[r] (None -> r).
+    wq/wk None skip the norm; cos_t None skips RoPE."""
+    lib = lib or load()
+    kind = _U16 if bf16 else _F
+    dt = np.uint16 if bf16 else np.float32
+    qo = np.array(q, dt, copy=True, order="C")
+    ko = None if k is None else np.array(k, dt, copy=True, order="C")
+    c = None if cos_t is None else np.ascontiguousarray(cos_t, np.float32)
+    s = None if sin_t is None else np.ascontiguousarray(sin_t, np.float32)
+    p = None if pos is None else np.ascontiguousarray(pos, np.int32)
+    wqa = None if wq is None else np.ascontiguousarray(wq, np.float32)
+    wka = None if wk is None else np.ascontiguousarray(wk, np.float32)
+    fn = lib.oracle_qk_norm_rope_bf16 if bf16 else lib.oracle_qk_norm_rope_f32
+    fn(ptr(qo, kind), ptr(ko, kind), ptr(wqa), ptr(wka), ptr(c), ptr(s), ptr(p, _I32),
+       qo.shape[0], n_q, n_kv, hd, eps)
+    return qo, ko
+
+
+def swiglu_bf16(gate_up, inter, lib=None):
+    lib = lib or load()
+    g = np.ascontiguousarray(gate_up, np.uint16)
+    seq = g.shape[0]
+    out = np.empty((seq, inter), np.uint16)
+    lib.oracle_swiglu_bf16(ptr(out, _U16), ptr(g, _U16), seq, inter)
+    return out
+
+
+def add_bf16(x, y, lib=None):
+    lib = lib or load()
+    r = np.array(x, np.uint16, copy=True, order="C")
+    lib.oracle_add_bf16(ptr(r, _U16), ptr(np.ascontiguousarray(y, np.uint16), _U16), r.size)
+    return r

@@ -1,0 +1,81 @@
+"""The C ABI library: loads, exports what include/*.h declares, rejects bad arguments.
+
+CPU only. The argument checks below return before any CUDA call, so they run
+without a GPU; no kernel is launched here.
+"""
+import ctypes
+import subprocess
+
+import pytest
+
+import lai
+
+V = ctypes.c_void_p
+
+
+def test_library_loads_and_reports_version():
+    lib = lai.load()
+    assert lib.lai_version() >= 100
+    assert lai.status_string(lai.LAI_ERR_ALIAS) == "unsupported overlap of output and input"
+
+
+def test_exports_every_header_symbol():
+    declared = set(lai.header_symbols())
+    assert len(declared) >= 30
+    out = subprocess.run(["nm", "-D", "--defined-only", lai.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    assert declared <= exported, sorted(declared - exported)
+    # the binding covers exactly the header
+    assert declared == set(lai.SIGNATURES), sorted(declared ^ set(lai.SIGNATURES))
+
+
+def test_no_internal_symbols_leak():
+    out = subprocess.run(["nm", "-D", "--defined-only", lai.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    assert not [s for s in exported if s.startswith("_ZN3lai")]
+
+
+def test_oracle_is_not_linked_into_the_product():
+    out = subprocess.run(["nm", "-D", lai.LIB_PATH], capture_output=True, text=True,
+                         check=True).stdout
+    assert "oracle_" not in out
+    deps = subprocess.run(["ldd", lai.LIB_PATH], capture_output=True, text=True).stdout
+    assert "lai_oracle" not in deps and "cpuref" not in deps
+
+
+P = V(16)  # a non-NULL dummy pointer: never dereferenced, the checks fail first
+
+
+@pytest.mark.parametrize("call, want", [
+    (lambda l: l.lai_rmsnorm_bf16(P, P, P, -1, 1024, 1e-6, None), lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_rmsnorm_f32(P, None, P, 4, 1024, 1e-6, None), lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_rmsnorm_f32(P, P, P, 4, 0, 1e-6, None), lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_add_rmsnorm_bf16(V(4096), P, P, V(4096), 4, 256, 1e-6, None), lai.LAI_ERR_ALIAS),
+    (lambda l: l.lai_qk_norm_rope_bf16(P, None, None, None, None, None, None, 0, 4, 16, 8, 128,
+                                       1e-6, None, None), lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_qk_norm_rope_f32(P, None, P, None, None, None, None, 0, 4, 16, 8, 127,
+                                      1e-6, None, None), lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_qk_norm_rope_f32(P, None, None, None, P, None, None, 8, 4, 16, 8, 128,
+                                      1e-6, None, None), lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_swiglu_bf16(V(4096 + 2), V(4096), 4, 64, None), lai.LAI_ERR_ALIAS),
+    (lambda l: l.lai_swiglu_f32(P, P, 4, 0, None), lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_add_f32(V(4096), V(4096 + 4), 64, None), lai.LAI_ERR_ALIAS),
+    (lambda l: l.lai_embed_gather_bf16(P, P, P, 4, 1024, 0, None, None), lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_snake_beta_f32(P, P, None, 1, 4, 16, None), lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_rope_table_f32(P, P, None, 4, 1024, 1e6, None), lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_synth_uniform_i32(P, 4, 1, 0, 5, 5, None), lai.LAI_ERR_INVALID),
+])
+def test_argument_checks(call, want):
+    assert call(lai.load()) == want
+
+
+@pytest.mark.parametrize("call", [
+    lambda l: l.lai_rmsnorm_bf16(P, P, P, 0, 1024, 1e-6, None),
+    lambda l: l.lai_swiglu_f32(P, P, 0, 64, None),
+    lambda l: l.lai_add_bf16(P, P, 0, None),
+    lambda l: l.lai_snake_beta_f32(P, P, P, 0, 4, 16, None),
+])
+def test_empty_inputs_are_no_ops(call):
+    assert call(lai.load()) == lai.LAI_OK

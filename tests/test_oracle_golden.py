@@ -1,0 +1,119 @@
+"""The CPU oracle against the reference's own golden vectors (CPU only).
+
+Fixtures in tests/golden/ were produced by tests/golden/make_golden.py from the
+reference: its numpy specification functions (tools/verify_xfmr.py,
+tools/verify_vocoder.py) and its compiled voc_snake_beta (src/tts_vocoder_ops.c).
+"""
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import TOL_F32, max_rel_err
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def g(name):
+    return np.load(os.path.join(GOLD, f"{name}.npz"))
+
+
+@pytest.mark.parametrize("tag", ["d1024", "d2048", "d512", "d200"])
+def test_rmsnorm_matches_reference_numpy(tag):
+    d = g(f"rmsnorm_{tag}")
+    y = oracle.rms_norm(d["x"], d["w"], float(d["eps"]))
+    assert max_rel_err(y, d["y"]) <= TOL_F32
+
+
+@pytest.mark.parametrize("tag", ["hd128", "hd64"])
+def test_rope_matches_reference_numpy(tag):
+    d = g(f"rope_{tag}")
+    T, hd, heads = d["x"].shape[0], int(d["hd"]), int(d["heads"])
+    c, s = oracle.compute_rope_neox(np.arange(T), hd, float(d["theta"]))
+    y = oracle.apply_rope_neox(d["x"], c, s, heads, hd)
+    assert max_rel_err(y, d["y"]) <= TOL_F32
+
+
+def test_rope_position_zero_is_identity():
+    x = np.random.default_rng(1).standard_normal((1, 4 * 128), dtype=np.float32)
+    c, s = oracle.compute_rope_neox(np.array([0]), 128, 1e6)
+    assert np.array_equal(oracle.apply_rope_neox(x, c, s, 4, 128), x)
+
+
+def test_swiglu_matches_reference_numpy():
+    d = g("swiglu")
+    y = oracle.swiglu_multiply(d["gate_up"], int(d["inter"]))
+    assert max_rel_err(y, d["y"]) <= TOL_F32
+
+
+def test_swiglu_in_place_matches_out_of_place():
+    rng = np.random.default_rng(2)
+    gu = rng.standard_normal((7, 2 * 96), dtype=np.float32)
+    ref = oracle.swiglu_multiply(gu, 96)
+    buf = gu.copy()
+    lib = oracle.load()
+    lib.oracle_swiglu_multiply(oracle.ptr(buf), oracle.ptr(buf), 7, 96)
+    assert np.array_equal(buf.reshape(-1)[: 7 * 96].reshape(7, 96), ref)
+
+
+def test_silu_matches_reference_numpy():
+    d = g("silu")
+    assert max_rel_err(oracle.silu(d["x"]), d["y"]) <= TOL_F32
+
+
+def test_snake_restatement_is_bit_exact_with_reference_build():
+    d = g("snake")
+    y = oracle.snake_beta(d["x"], d["ea"], d["ieb"])
+    assert np.array_equal(y, d["y_ref_scalar"])
+    assert max_rel_err(y, d["y_numpy"]) <= TOL_F32
+
+
+def test_reference_avx2_snake_error_is_the_known_approximation():
+    # The shipped AVX2 fast sin is the reference's approximation, ~2e-4 * ieb at most.
+    d = g("snake")
+    err = np.max(np.abs(d["y_ref_avx2"] - d["y_ref_scalar"]))
+    assert 1e-6 < err < 1e-3
+
+
+@pytest.mark.skipif(not oracle.have_ref(), reason="oracle/_ref not built (reference absent)")
+def test_snake_against_live_reference_build_ragged():
+    rng = np.random.default_rng(3)
+    for C, T in [(3, 1), (5, 7), (2, 1001)]:
+        x = (3 * rng.standard_normal((C, T))).astype(np.float32)
+        ea = np.exp(0.1 * rng.standard_normal(C)).astype(np.float32)
+        ieb = (1 / np.exp(0.1 * rng.standard_normal(C))).astype(np.float32)
+        assert np.array_equal(oracle.snake_beta(x, ea, ieb), oracle.ref_snake_beta(x, ea, ieb))
+
+
+def test_bf16_widening_known_answers():
+    d = g("bf16_widen")
+    table = d["bf16"].reshape(1, -1)
+    out = oracle.gather_bf16_to_f32(table, np.array([0], np.int32))
+    assert np.array_equal(out.view(np.uint32).reshape(-1), d["f32_bits"])
+
+
+def test_bf16_rounding_is_rne():
+    f = np.array([1.0, 1.00390625, 1.01171875, -2.5, 3.0e38, np.inf, -0.0], np.float32)
+    # 1+2^-8 is a tie -> even (1.0); 1+3*2^-8 is a tie -> even (1+2^-6)
+    want = np.array([0x3F80, 0x3F80, 0x3F82, 0xC020, 0x7F62, 0x7F80, 0x8000], np.uint16)
+    assert np.array_equal(oracle.f32_to_bf16_bits(f), want)
+    lib = oracle.load()
+    assert [lib.oracle_f32_to_bf16(float(v)) for v in f] == want.tolist()
+    assert lib.oracle_f32_to_bf16(float("nan")) == 0x7FFF
+
+
+def test_fused_oracles_equal_reference_call_sequences():
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((4, 256), dtype=np.float32)
+    dl = rng.standard_normal((4, 256), dtype=np.float32)
+    w = (1 + 0.02 * rng.standard_normal(256)).astype(np.float32)
+    xo, y = oracle.add_rms_norm_f32(x, dl, w, 1e-6)
+    assert np.array_equal(xo, oracle.add_inplace(x, dl))
+    assert np.array_equal(y, oracle.rms_norm(xo, w, 1e-6))
+    q = rng.standard_normal((3, 4 * 128), dtype=np.float32)
+    wq = (1 + 0.02 * rng.standard_normal(128)).astype(np.float32)
+    c, s = oracle.compute_rope_neox(np.arange(3), 128, 1e6)
+    qo, _ = oracle.qk_norm_rope(q, None, wq, None, c, s, None, 4, 0, 128, 1e-6, bf16=False)
+    ref = oracle.apply_rope_neox(oracle.rms_norm_per_head(q, wq, 4, 128, 1e-6), c, s, 4, 128)
+    assert np.array_equal(qo, ref)
