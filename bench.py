@@ -275,7 +275,8 @@ def run_ours(args) -> None:
     if strong:
         row0, row1 = runner.shard_range(cfg.tokens, world, rank)
     else:
-        row0, row1 = rank * cfg.tokens, (rank + 1) * cfg.tokens
+        per = args.rows or cfg.tokens
+        row0, row1 = rank * per, (rank + 1) * per
     rows = row1 - row0
     chain = runner.LayerChain(cfg, rows, row0=row0, seed=args.seed)
     stream = torch.cuda.current_stream()
@@ -319,7 +320,7 @@ def run_ours(args) -> None:
     assert int(chain.err.item()) == 0, "position out of range in the chain"
 
     peak, peak_kind = measured_peaks()
-    total_rows = (cfg.tokens if strong else rows * world)
+    total_rows = cfg.tokens if strong else rows * world
     value = total_rows * args.steps / (max_ms / 1000.0)
     bpl = chain.bytes_per_launch()
     kernels = {}
@@ -400,6 +401,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=["c1", "c2", "c3", "c5"], default="c2")
     ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--rows", type=int, default=0,
+                    help="rows per GPU instead of the config's batch (small profiling cases)")
     ap.add_argument("--e2e-rows", type=int, default=16384)
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-e2e", action="store_true")
@@ -407,8 +410,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
-    if args.warmup < 3:
-        ap.error("--warmup must be >= 3")
+    args.warmup = max(args.warmup, 3)  # timing rule: at least 3 untimed warm-up steps
     if args.impl == "reference":
         run_reference(args)
     else:
