@@ -40,6 +40,19 @@ extern "C" {
 
 /* src/tts_native.c:556, 584, 637, 661, 674 (out == x); src/tts_vocoder_xfmr.c:163, 189, 211 */
 LAI_API void qwen_rms_norm(float *out, const float *x, const float *w, int seq, int dim, float eps);
+/* No counterpart in the reference. qwen_rms_norm's host-buffer semantics (out may
+ * equal x; host or device pointers) for callers that cannot let a library
+ * allocate device memory -- a process whose memory belongs to its own pool
+ * allocator, or a loop that must not meet cudaMalloc/cudaFree's device-wide
+ * synchronisation. It stages through a fixed 8 MiB array compiled into the
+ * library (held on every GPU that loads it) and calls no allocator: seq*dim*4
+ * plus dim*4 bytes (each rounded up to 256) must fit in 8 MiB, else
+ * LAI_ERR_TOOBIG. The first call on a device looks up the array's address, so
+ * make it before any stream capture. Calls share the array: calls whose GPU work
+ * overlaps (several threads or streams on one device) race; the call
+ * synchronises `stream` before it returns. Returns a LAI_* status. */
+LAI_API int lai_rmsnorm_f32_host_noalloc(float *out, const float *x, const float *w, int seq,
+                                         int dim, float eps, void *stream);
 /* src/tts_native.c:562-563, 644-645, 724-725 (in place) */
 LAI_API void qwen_rms_norm_per_head(float *x, const float *w, int seq, int n_heads, int head_dim,
                             float eps);

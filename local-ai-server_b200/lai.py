@@ -48,6 +48,7 @@ SIGNATURES: dict[str, tuple] = {
     "lai_synth_uniform_i32": (_i32, [_vp, _i64, _u64, _i64, _i32, _i32, _vp]),
     # reference-named drop-ins (lai_qwen_dropin.h)
     "qwen_rms_norm": (None, [_vp, _vp, _vp, _i32, _i32, _f32]),
+    "lai_rmsnorm_f32_host_noalloc": (_i32, [_vp, _vp, _vp, _i32, _i32, _f32, _vp]),
     "qwen_rms_norm_per_head": (None, [_vp, _vp, _i32, _i32, _i32, _f32]),
     "qwen_apply_rope_neox": (None, [_vp, _vp, _vp, _i32, _i32, _i32]),
     "qwen_compute_rope_neox": (None, [_vp, _vp, _vp, _i32, _i32, _f32]),
