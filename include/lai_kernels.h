@@ -49,8 +49,10 @@ enum {
     LAI_ERR_TOOBIG = -6   /* size beyond a stated maximum */
 };
 
-/* Bits ORed into the caller's device error word. */
-enum { LAI_DEVERR_TOKEN_ID = 1, LAI_DEVERR_POSITION = 2 };
+/* Bits ORed into the caller's device error word. LAI_DEVERR_TIMEOUT: a kernel's
+ * bounded wait on its own asynchronous copies ran out (never expected; the kernel
+ * drains what it issued and returns instead of hanging). */
+enum { LAI_DEVERR_TOKEN_ID = 1, LAI_DEVERR_POSITION = 2, LAI_DEVERR_TIMEOUT = 4 };
 
 LAI_API const char *lai_status_string(int status);
 LAI_API int lai_version(void); /* major*10000 + minor*100 + patch */

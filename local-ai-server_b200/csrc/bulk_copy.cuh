@@ -1,0 +1,97 @@
+// bulk_copy.cuh - mbarrier + bulk asynchronous copy (TMA engine) helpers, sm_90+/sm_100a.
+//
+// Plain (non-multicast, non-tensor) cp.async.bulk between this GPU's global memory
+// and the issuing CTA's shared memory. Addresses and sizes must be 16-byte
+// multiples. Every wait is bounded by %globaltimer so a lost completion can never
+// hang the GPU: the caller sees `false` and takes its error path.
+#pragma once
+
+#include <stdint.h>
+
+namespace lai {
+namespace bulk {
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+                 : "memory");
+}
+
+// Make initialised barriers visible to the async proxy before any copy uses them.
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    uint64_t state;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 %0, [%1], %2;"
+                 : "=l"(state)
+                 : "r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+    (void)state;
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Wait for phase `parity` of `bar`; false if `limit_ns` passes first.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
+                                                  uint64_t limit_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t n = 1;; n++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((n & 255u) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
+    }
+}
+
+// global -> shared, completion counted in bytes on `bar`.
+__device__ __forceinline__ void load(void *smem_dst, const void *gsrc, uint32_t bytes,
+                                     uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(smem_dst)),
+        "l"(gsrc), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// shared -> global, tracked by bulk async-groups of the issuing thread.
+__device__ __forceinline__ void store(void *gdst, const void *smem_src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst),
+                 "r"(smem_addr(smem_src)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// All but the most recent N groups have finished reading shared memory.
+template <int N>
+__device__ __forceinline__ void wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// All groups complete (writes performed).
+__device__ __forceinline__ void wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Generic-proxy shared-memory writes -> visible to a following bulk store.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+}  // namespace bulk
+}  // namespace lai

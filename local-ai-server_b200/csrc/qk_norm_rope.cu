@@ -18,6 +18,7 @@
 // Each lane loads its hd/LPH weights and its cos/sin entries once per segment.
 // RoPE uses separately rounded products (no contraction), so with identical
 // inputs it reproduces the reference's scalar C bit for bit.
+#include "bulk_copy.cuh"
 #include "lai_common.cuh"
 
 #include <math.h>
@@ -118,6 +119,201 @@ qk_warp_kernel(T *q, T *k, const float *__restrict__ wq, const float *__restrict
     }
 }
 
+// ---- pipelined BF16 hd=128 kernel: bulk async copies through a shared-memory ring ----
+//
+// Persistent CTAs (2 per SM). A tile is kTileTok consecutive tokens: their q rows
+// and their k rows are each one contiguous range, fetched by two bulk copies into
+// one of kStages shared-memory stages (completion counted on the stage's mbarrier).
+// kStages-1 tiles are in flight while one is computed in place in shared memory and
+// written back by two bulk stores; a stage is refilled only after its stores have
+// finished reading it. Memory parallelism therefore comes from the copy engine,
+// not from registers. Work split: 16 half-warps per CTA, 16/kTileTok per token, a
+// half-warp per head (pipe_heads).
+__device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
+
+constexpr int kTileTok = 4;
+constexpr int kStages = 4;
+constexpr int kPipeThreads = 256;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far beyond any real copy
+
+// One token's heads (q or k) in shared memory, BF16 hd=128: a half-warp per head,
+// lane owns elements d0..d0+3 (first half) and their RoPE partners 64+d0..64+d0+3,
+// so the rotation needs no shuffle; the sum of squares is a 4-step xor tree. The
+// trip count is the same in every half-warp (shuffles need the whole warp); `valid`
+// and h < nheads predicate the shared-memory traffic.
+template <int HW, int TRIPS>
+__device__ __forceinline__ void pipe_heads(uint16_t *base, int nheads, int sub, int d0, bool valid,
+                                           const float (&w)[8], bool norm, bool rope,
+                                           const float (&cs)[8], const float (&sn)[8], float eps) {
+    // TRIPS > 0: the trip count is known at compile time, the loop unrolls fully and
+    // independent heads interleave; TRIPS == 0: any head count.
+    const int trips = TRIPS > 0 ? TRIPS : (nheads + HW - 1) / HW;
+#pragma unroll
+    for (int j = 0; j < (TRIPS > 0 ? TRIPS : trips); j++) {
+        const int h = sub + j * HW;
+        const bool hv = valid && h < nheads;
+        uint16_t *hp = base + (size_t)h * 128;
+        const uint2 lo = hv ? *reinterpret_cast<const uint2 *>(hp + d0) : make_uint2(0, 0);
+        const uint2 hi = hv ? *reinterpret_cast<const uint2 *>(hp + 64 + d0) : make_uint2(0, 0);
+        float a[8] = {bf16_lo(lo.x), bf16_hi(lo.x), bf16_lo(lo.y), bf16_hi(lo.y),
+                      bf16_lo(hi.x), bf16_hi(hi.x), bf16_lo(hi.y), bf16_hi(hi.y)};
+        // pairwise tree: 3 dependent levels instead of 8
+        float ss = ((a[0] * a[0] + a[1] * a[1]) + (a[2] * a[2] + a[3] * a[3])) +
+                   ((a[4] * a[4] + a[5] * a[5]) + (a[6] * a[6] + a[7] * a[7]));
+        ss = group_sum<16>(ss);
+        // BF16 output keeps 8 significant bits, so the approximate reciprocal square
+        // root and the fused multiply-adds (FP32 ulp-level departures from the
+        // separately rounded reference form) cannot show in the result.
+        if (norm) {
+            const float inv = rsqrtf(ss * (1.0f / 128) + eps);
+#pragma unroll
+            for (int e = 0; e < 8; e++) a[e] = a[e] * inv * w[e];
+        }
+        if (rope) {
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float x1 = a[e], x2 = a[4 + e];
+                a[e] = fmaf(-x2, sn[e], x1 * cs[e]);         // x1*c - x2*s
+                a[4 + e] = fmaf(x1, sn[4 + e], x2 * cs[4 + e]);  // x1*s + x2*c
+            }
+        }
+        if (hv) {
+            *reinterpret_cast<uint2 *>(hp + d0) = make_uint2(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]));
+            *reinterpret_cast<uint2 *>(hp + 64 + d0) =
+                make_uint2(pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
+        }
+    }
+}
+
+template <int QT, int KT>  // head trips per half-warp for q and k (0: runtime)
+__global__ void __launch_bounds__(kPipeThreads, 2)
+qk_pipe_kernel(uint16_t *q, uint16_t *k, const float *__restrict__ wq,
+               const float *__restrict__ wk, const float *__restrict__ cos_t,
+               const float *__restrict__ sin_t, const int32_t *__restrict__ pos,
+               int64_t table_rows, int64_t rows, int nq, int nkv, float eps, int *err) {
+    constexpr int HD = 128;
+    constexpr int HW_PER_TOK = 16 / kTileTok;
+    extern __shared__ __align__(128) unsigned char smem[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    unsigned char *ring = smem + 128;
+    const uint32_t q_tok = (uint32_t)nq * HD * 2, k_tok = (uint32_t)nkv * HD * 2;
+    const uint32_t stage_bytes = kTileTok * (q_tok + k_tok);
+    const int H = nq + nkv;
+    const int64_t ntiles = (rows + kTileTok - 1) / kTileTok;
+    const int64_t my_n = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int tid = threadIdx.x, lane = tid & 31;
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; s++) bulk::mbar_init(&full[s], 1);
+        bulk::fence_barrier_init();
+    }
+    __syncthreads();
+
+    auto issue = [&](int64_t i) {  // tile i of this CTA into stage i % kStages (thread 0)
+        const int64_t r0 = (blockIdx.x + i * gridDim.x) * kTileTok;
+        const uint32_t gt = (uint32_t)imin64((int64_t)kTileTok, rows - r0);
+        unsigned char *st = ring + (size_t)(i % kStages) * stage_bytes;
+        uint64_t *bar = &full[i % kStages];
+        bulk::mbar_arrive_expect_tx(bar, gt * (q_tok + k_tok));
+        bulk::load(st, q + (size_t)r0 * nq * HD, gt * q_tok, bar);
+        if (k_tok) bulk::load(st + kTileTok * q_tok, k + (size_t)r0 * nkv * HD, gt * k_tok, bar);
+    };
+    int64_t issued = 0;
+    if (tid == 0)
+        for (; issued < imin64((int64_t)kStages - 1, my_n); issued++) issue(issued);
+
+    const int hw = tid >> 4;          // half-warp 0..15
+    const int tok = hw / HW_PER_TOK;  // token within the tile
+    const int sub = hw % HW_PER_TOK;  // this half-warp's share of the token's heads
+    const int d0 = (lane & 15) * 4;   // lane owns elements d0..d0+3 and 64+d0..64+d0+3
+    const bool rope = cos_t != nullptr;
+    float wqv[8], wkv[8];  // [0..3] first half, [4..7] second half
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        wqv[e] = wq ? wq[d0 + e] : 1.f;
+        wqv[4 + e] = wq ? wq[64 + d0 + e] : 1.f;
+        wkv[e] = wk ? wk[d0 + e] : 1.f;
+        wkv[4 + e] = wk ? wk[64 + d0 + e] : 1.f;
+    }
+    // Table position of this half-warp's token in tile i (-1 when there is no token).
+    auto tile_pos = [&](int64_t t) -> int64_t {
+        if (t >= my_n) return -1;
+        const int64_t row = (blockIdx.x + t * gridDim.x) * kTileTok + tok;
+        if (row >= rows) return -1;
+        return pos ? (int64_t)pos[row] : row;
+    };
+    auto load_table = [&](int64_t p, float (&c)[8], float (&sgn)[8]) {
+        if (!rope || p < 0 || p >= table_rows) return;
+        const float *cr = cos_t + (size_t)p * HD, *sr = sin_t + (size_t)p * HD;
+        const float4 c1 = ld_f4(cr + d0), c2 = ld_f4(cr + 64 + d0);
+        const float4 s1 = ld_f4(sr + d0), s2 = ld_f4(sr + 64 + d0);
+        c[0] = c1.x; c[1] = c1.y; c[2] = c1.z; c[3] = c1.w;
+        c[4] = c2.x; c[5] = c2.y; c[6] = c2.z; c[7] = c2.w;
+        sgn[0] = s1.x; sgn[1] = s1.y; sgn[2] = s1.z; sgn[3] = s1.w;
+        sgn[4] = s2.x; sgn[5] = s2.y; sgn[6] = s2.z; sgn[7] = s2.w;
+    };
+    // positions run two tiles ahead and table rows one tile ahead of the compute, so
+    // their global-load latency overlaps the wait for the tile's copy
+    int64_t p_cur = tile_pos(0), p_nxt = tile_pos(1);
+    float cs[8] = {}, sn[8] = {}, csn[8] = {}, snn[8] = {};
+    load_table(p_cur, cs, sn);
+
+    bool stopped = false;
+    int64_t i = 0;
+    for (; i < my_n; i++) {
+        const int s = (int)(i % kStages);
+        const uint32_t parity = (uint32_t)((i / kStages) & 1);
+        const int64_t r0 = (blockIdx.x + i * gridDim.x) * kTileTok;
+        const int gt = (int)imin64((int64_t)kTileTok, rows - r0);
+        unsigned char *st = ring + (size_t)s * stage_bytes;
+        load_table(p_nxt, csn, snn);
+        const int64_t p_far = tile_pos(i + 2);
+        const bool ok = bulk::mbar_wait_bounded(&full[s], parity, kWaitLimitNs);
+        if (ok) {
+            bool valid = tok < gt;
+            if (rope && valid && (p_cur < 0 || p_cur >= table_rows)) {
+                valid = false;
+                if (sub == 0 && (lane & 15) == 0 && err) atomicOr(err, LAI_DEVERR_POSITION);
+            }
+            uint16_t *qb = reinterpret_cast<uint16_t *>(st + (size_t)tok * q_tok);
+            uint16_t *kb = reinterpret_cast<uint16_t *>(st + (size_t)kTileTok * q_tok + (size_t)tok * k_tok);
+            pipe_heads<HW_PER_TOK, QT>(qb, nq, sub, d0, valid, wqv, wq != nullptr, rope, cs, sn, eps);
+            pipe_heads<HW_PER_TOK, KT>(kb, nkv, sub, d0, valid, wkv, wk != nullptr, rope, cs, sn, eps);
+        }
+        p_cur = p_nxt;
+        p_nxt = p_far;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            cs[e] = csn[e];
+            sn[e] = snn[e];
+        }
+        bulk::fence_proxy_async_smem();
+        if (__syncthreads_or(!ok)) {  // CTA-uniform: a lost copy ends this CTA's work
+            stopped = true;
+            break;
+        }
+        if (tid == 0) {
+            bulk::store(q + (size_t)r0 * nq * HD, st, (uint32_t)gt * q_tok);
+            if (k_tok)
+                bulk::store(k + (size_t)r0 * nkv * HD, st + kTileTok * q_tok, (uint32_t)gt * k_tok);
+            bulk::commit();
+            if (issued < my_n) {
+                bulk::wait_read<1>();  // stage of tile i-1 has been read out by its stores
+                issue(issued++);
+            }
+        }
+    }
+    if (tid == 0) {
+        bulk::wait_all();
+        if (stopped) {
+            if (err) atomicOr(err, LAI_DEVERR_TIMEOUT);
+            // drain loads still in flight into this CTA's shared memory, each bounded
+            for (int64_t j = i; j < issued; j++)
+                bulk::mbar_wait_bounded(&full[j % kStages], (uint32_t)((j / kStages) & 1), kWaitLimitNs);
+        }
+    }
+}
+
 // Any even head_dim / alignment / head count: one warp per (token, head).
 template <typename T>
 __global__ void __launch_bounds__(256)
@@ -187,6 +383,56 @@ bool try_fast(T *q, T *k, const float *wq, const float *wk, const float *cos_t,
     }
 }
 
+// Shared memory of the pipelined kernel, and whether it fits two CTAs per SM.
+inline size_t pipe_smem_bytes(int nq, int nkv) {
+    return 128 + (size_t)kStages * kTileTok * (size_t)(nq + nkv) * 128 * 2;
+}
+
+struct DeviceInfo {
+    int sms = 0;
+    bool attr_set = false;
+};
+
+bool try_pipe(uint16_t *q, uint16_t *k, const float *wq, const float *wk, const float *cos_t,
+              const float *sin_t, const int32_t *pos, int64_t table_rows, int64_t rows, int nq,
+              int nkv, float eps, int *err, cudaStream_t s) {
+    constexpr size_t kMaxSmem = 110 * 1024;  // two CTAs per SM
+    const size_t smem = pipe_smem_bytes(nq, nkv);
+    if (smem > kMaxSmem || !aligned16(q) || (k && !aligned16(k)) ||
+        (cos_t && (!aligned16(cos_t) || !aligned16(sin_t))))
+        return false;
+    static DeviceInfo info[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+    DeviceInfo &d = info[dev];
+    // Qwen3's 16 q / 8 kv heads get fully unrolled head loops; other counts the generic one.
+    constexpr int HW = 16 / kTileTok;
+    const bool qwen = nq == 4 * HW && (nkv == 2 * HW || nkv == 0);
+    auto kern = qwen ? (nkv ? qk_pipe_kernel<4, 2> : qk_pipe_kernel<4, 0>) : qk_pipe_kernel<0, 0>;
+    if (!d.attr_set) {
+        if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        for (auto f : {qk_pipe_kernel<4, 2>, qk_pipe_kernel<4, 0>, qk_pipe_kernel<0, 0>}) {
+            if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kMaxSmem) != cudaSuccess ||
+                // the largest carveout, so that two CTAs' rings are resident per SM
+                cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, 100) !=
+                    cudaSuccess) {
+                cudaGetLastError();
+                return false;
+            }
+        }
+        d.attr_set = true;
+    }
+    const int64_t ntiles = (rows + kTileTok - 1) / kTileTok;
+    const int64_t grid = ntiles < 2 * (int64_t)d.sms ? ntiles : 2 * (int64_t)d.sms;
+    kern<<<(unsigned)grid, kPipeThreads, smem, s>>>(q, k, wq, wk, cos_t, sin_t, pos, table_rows,
+                                                    rows, nq, nkv, eps, err);
+    return true;
+}
+
 template <typename T>
 int run(T *q, T *k, const float *wq, const float *wk, const float *cos_t, const float *sin_t,
         const int32_t *pos, int64_t table_rows, int64_t rows, int nq, int nkv, int hd, float eps,
@@ -199,7 +445,11 @@ int run(T *q, T *k, const float *wq, const float *wk, const float *cos_t, const 
         return LAI_ERR_ALIAS;
     cudaStream_t s = as_stream(stream);
     bool done = false;
-    switch (hd) {
+    if constexpr (sizeof(T) == 2) {
+        if (hd == 128) done = try_pipe(q, k, wq, wk, cos_t, sin_t, pos, table_rows, rows, nq,
+                                       k ? nkv : 0, eps, err, s);
+    }
+    if (!done) switch (hd) {
         case 64: done = try_fast<T, 64>(q, k, wq, wk, cos_t, sin_t, pos, table_rows, rows, nq, nkv, eps, err, s); break;
         case 128: done = try_fast<T, 128>(q, k, wq, wk, cos_t, sin_t, pos, table_rows, rows, nq, nkv, eps, err, s); break;
         case 256: done = try_fast<T, 256>(q, k, wq, wk, cos_t, sin_t, pos, table_rows, rows, nq, nkv, eps, err, s); break;

@@ -119,6 +119,7 @@ def table(rows, hd, theta):
 @pytest.mark.parametrize("rows,nq,nkv,hd,posmode", [
     (512, 16, 8, 128, "seq"),      # config 1 prefill, positions 0..511
     (256, 16, 8, 128, "random"),   # config 3 decode, positions U[0, 4095]
+    (5003, 16, 8, 128, "random"),  # several tiles per persistent CTA, partial last tile
     (64, 16, 16, 64, "seq"),       # vocoder pre-transformer heads (hd 64)
     (7, 3, 1, 128, "random"),      # odd head counts -> generic kernel
     (5, 2, 2, 96, "seq"),          # head_dim without a fast path
