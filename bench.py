@@ -193,12 +193,73 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-# ------------------------------------------------------------------ e2e path
-def e2e_dropin(cfg, rows: int, steps: int, warmup: int) -> dict:
-    """The reference-facing drop-ins (qwen_*) on pinned host FP32 buffers.
+# ------------------------------------------------------------------ e2e paths
+def _pinned(shape, dtype, gen, fill="normal"):
+    import torch
+    t = torch.empty(shape, dtype=torch.float32).pin_memory() if dtype is None else \
+        torch.empty(shape, dtype=dtype).pin_memory()
+    if fill == "normal":
+        src = torch.randn(shape, generator=gen)
+        t.copy_(src if dtype is None else src.to(dtype))
+    return t
 
-    Per step, the layer's calls in the reference's order; each call copies its
-    host inputs in and its outputs back before returning (pipelined chunks).
+
+def e2e_staged_bf16(cfg, rows: int, steps: int, warmup: int) -> dict:
+    """The layer chain through the synchronous BF16 entry points on pinned host buffers.
+
+    Per step: lai_staged_add_rmsnorm_bf16, lai_staged_qk_norm_rope_bf16,
+    lai_staged_add_rmsnorm_bf16, lai_staged_swiglu_bf16 -- each copies its host inputs
+    to the GPU and its outputs back (pipelined chunks) before returning.
+    """
+    import torch
+    import lai
+    lib = lai.load()
+    D, I, hd, nq, nkv, P = cfg.dim, cfg.inter, cfg.head_dim, cfg.n_q, cfg.n_kv, cfg.pos_period
+    g = torch.Generator().manual_seed(9)
+    bf = torch.bfloat16
+    x, da, df = _pinned((rows, D), bf, g), _pinned((rows, D), bf, g), _pinned((rows, D), bf, g)
+    y = _pinned((rows, D), bf, g, fill=None)
+    q, k = _pinned((rows, nq * hd), bf, g), _pinned((rows, nkv * hd), bf, g)
+    gu, act = _pinned((rows, 2 * I), bf, g), _pinned((rows, I), bf, g, fill=None)
+    w_in, w_post = _pinned((D,), None, g), _pinned((D,), None, g)
+    wq, wk = _pinned((hd,), None, g), _pinned((hd,), None, g)
+    pos = (torch.arange(rows, dtype=torch.int32) % P).pin_memory()
+    inv = 1.0 / torch.pow(torch.tensor(cfg.theta, dtype=torch.float32),
+                          torch.arange(0, hd, 2, dtype=torch.float32) / hd)
+    ang = torch.arange(P, dtype=torch.float32)[:, None] * inv[None, :]
+    cos_t = torch.cat([ang.cos(), ang.cos()], 1).contiguous().pin_memory()
+    sin_t = torch.cat([ang.sin(), ang.sin()], 1).contiguous().pin_memory()
+    V = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def step():
+        st = [lib.lai_staged_add_rmsnorm_bf16(V(x), V(df), V(w_in), V(y), rows, D, cfg.eps),
+              lib.lai_staged_qk_norm_rope_bf16(V(q), V(k), V(wq), V(wk), V(cos_t), V(sin_t), V(pos),
+                                               P, rows, nq, nkv, hd, cfg.eps),
+              lib.lai_staged_add_rmsnorm_bf16(V(x), V(da), V(w_post), V(y), rows, D, cfg.eps),
+              lib.lai_staged_swiglu_bf16(V(act), V(gu), rows, I)]
+        if any(st):
+            raise RuntimeError(f"staged chain failed: {[lai.status_string(s) for s in st]}")
+
+    b = 2
+    h2d = rows * (2 * D * b + (nq + nkv) * hd * b + 4 + 2 * D * b + 2 * I * b) \
+        + (2 * D + 2 * hd + 2 * P * hd) * 4
+    d2h = rows * (2 * D * b + (nq + nkv) * hd * b + 2 * D * b + I * b)
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    torch.cuda.synchronize()
+    return {"seconds": time.perf_counter() - t0, "rows": rows, "steps": steps, "h2d": h2d,
+            "d2h": d2h}
+
+
+def e2e_dropin_f32(cfg, rows: int, steps: int, warmup: int) -> dict:
+    """The reference-named FP32 drop-ins (qwen_*) on pinned host FP32 buffers.
+
+    Per step, the layer's 9 calls in the reference's order; each copies its host
+    inputs in and its outputs back before returning.
     """
     import numpy as np
     import torch
@@ -206,21 +267,16 @@ def e2e_dropin(cfg, rows: int, steps: int, warmup: int) -> dict:
     lib = lai.load()
     D, I, hd, nq, nkv = cfg.dim, cfg.inter, cfg.head_dim, cfg.n_q, cfg.n_kv
     g = torch.Generator().manual_seed(9)
-
-    def pinned(*shape):
-        t = torch.empty(shape, dtype=torch.float32).pin_memory()
-        t.normal_(generator=g)
-        return t
-
-    x, da, df, y = pinned(rows, D), pinned(rows, D), pinned(rows, D), pinned(rows, D)
-    q, k, gu = pinned(rows, nq * hd), pinned(rows, nkv * hd), pinned(rows, 2 * I)
-    w_in, w_post, wq, wk = pinned(D), pinned(D), pinned(hd), pinned(hd)
-    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    x, da, df = _pinned((rows, D), None, g), _pinned((rows, D), None, g), _pinned((rows, D), None, g)
+    y = _pinned((rows, D), None, g, fill=None)
+    q, k, gu = _pinned((rows, nq * hd), None, g), _pinned((rows, nkv * hd), None, g), \
+        _pinned((rows, 2 * I), None, g)
+    w_in, w_post, wq, wk = (_pinned((n,), None, g) for n in (D, D, hd, hd))
     pos = np.arange(rows) % cfg.pos_period
     inv = 1.0 / np.power(np.float32(cfg.theta), np.arange(0, hd, 2, dtype=np.float32) / hd)
     ang = pos[:, None].astype(np.float32) * inv[None, :].astype(np.float32)
-    c_rows = torch.from_numpy(np.concatenate([np.cos(ang), np.cos(ang)], 1).astype(np.float32)).pin_memory()
-    s_rows = torch.from_numpy(np.concatenate([np.sin(ang), np.sin(ang)], 1).astype(np.float32)).pin_memory()
+    c_rows = torch.from_numpy(np.concatenate([np.cos(ang)] * 2, 1).astype(np.float32)).pin_memory()
+    s_rows = torch.from_numpy(np.concatenate([np.sin(ang)] * 2, 1).astype(np.float32)).pin_memory()
     V = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
     T = rows
 
@@ -250,8 +306,7 @@ def e2e_dropin(cfg, rows: int, steps: int, warmup: int) -> dict:
     err = lib.lai_last_error()
     if err != 0:
         raise RuntimeError(f"drop-in chain failed: {lai.status_string(err)}")
-    return {"seconds": el, "rows": rows, "steps": steps, "h2d": h2d, "d2h": d2h,
-            "kernels_per_step": 9}
+    return {"seconds": el, "rows": rows, "steps": steps, "h2d": h2d, "d2h": d2h}
 
 
 # ------------------------------------------------------------------ our path
@@ -318,6 +373,7 @@ def run_ours(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     max_ms = float(t.item())
     assert int(chain.err.item()) == 0, "position out of range in the chain"
+    swiglu_tail = 1 if (rows * cfg.inter) % 4 else 0
 
     peak, peak_kind = measured_peaks()
     total_rows = cfg.tokens if strong else rows * world
@@ -346,18 +402,29 @@ def run_ours(args) -> None:
                 "traffic": traffic, "algorithmic_bytes_per_launch": d["bytes_per_launch"],
                 "step_gbs": round(step_gbs, 1), "step_frac": round(step_gbs / peak, 4)}
 
-    # e2e through the reference-facing drop-ins (pinned host buffers)
-    e2e = None
+    # e2e: the same chain on pinned host buffers through the C ABI's synchronous entries
+    e2e = e2e_f32 = None
     if not args.no_e2e:
-        e_rows = min(rows, args.e2e_rows)
-        r = e2e_dropin(cfg, e_rows, args.e2e_steps, 1)
-        et = torch.tensor([r["seconds"]], device="cuda", dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(et, op=dist.ReduceOp.MAX)
-        e2e = {"value": round(e_rows * world * r["steps"] / float(et.item()), 1), "unit": "rows/s",
-               "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"],
-               "rows_per_step": e_rows, "dtype": "f32",
-               "api": "qwen_* drop-ins (lai_qwen_dropin.h) on pinned host buffers, 9 calls/step"}
+        def max_time(sec):
+            et = torch.tensor([sec], device="cuda", dtype=torch.float64)
+            if world > 1:
+                dist.all_reduce(et, op=dist.ReduceOp.MAX)
+            return float(et.item())
+        del chain  # free the device-resident workload before the staged runs
+        torch.cuda.empty_cache()
+        r = e2e_staged_bf16(cfg, rows, args.e2e_steps, 1)
+        e2e = {"value": round(rows * world * r["steps"] / max_time(r["seconds"]), 1),
+               "unit": "rows/s", "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"],
+               "rows_per_step": rows, "dtype": "bf16",
+               "api": "lai_staged_{add_rmsnorm,qk_norm_rope,swiglu}_bf16 on pinned host buffers, "
+                      "4 synchronous calls/step"}
+        fr = min(rows, args.e2e_rows)
+        r = e2e_dropin_f32(cfg, fr, args.e2e_steps, 1)
+        e2e_f32 = {"value": round(fr * world * r["steps"] / max_time(r["seconds"]), 1),
+                   "unit": "rows/s", "h2d_bytes_per_step": r["h2d"],
+                   "d2h_bytes_per_step": r["d2h"], "rows_per_step": fr, "dtype": "f32",
+                   "api": "reference-named qwen_* drop-ins on pinned host FP32 buffers, "
+                          "9 calls/step"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -372,7 +439,6 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
     if rank != 0:
         return
-    swiglu_tail = 1 if (rows * cfg.inter) % 4 else 0
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "rows/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup,
@@ -387,6 +453,7 @@ def run_ours(args) -> None:
                    "l2": f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB per step per GPU)"},
         "hbm_gbs": round(step_gbs * (world if not strong else 1), 1),
         "per_kernel": per_kernel, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+        "e2e_dropin_f32": e2e_f32,
         "gpu_launches": args.steps * (3 + 1 + swiglu_tail),
         "clocks": clocks,
     }
@@ -404,7 +471,7 @@ def main():
     ap.add_argument("--rows", type=int, default=0,
                     help="rows per GPU instead of the config's batch (small profiling cases)")
     ap.add_argument("--e2e-rows", type=int, default=16384)
-    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-rows", type=int, default=8192)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

@@ -73,6 +73,23 @@ LAI_API void qwen_silu(float *x, int n);
 LAI_API void voc_snake_beta(float *x, const float *exp_alpha, const float *inv_exp_beta, int channels,
                     int T);
 
+/* Synchronous, pointer-agnostic BF16 fused ops: the lai_kernels.h entries of the same
+ * name without "_staged", for callers whose rows live in host memory. Every argument
+ * may be host (pinned or pageable) or device memory; host rows go through the same
+ * 3-stream staging pipeline as the qwen_* drop-ins, and the call returns when the
+ * outputs are in place (LAI_* status). For the qk entry the cos/sin tables
+ * [table_rows, head_dim] are copied whole and pos per row; pos NULL means row index.
+ * Replace, on BF16 activations, the call pairs / quadruples cited in lai_kernels.h. */
+LAI_API int lai_staged_add_rmsnorm_bf16(uint16_t *x, const uint16_t *delta, const float *w,
+                                        uint16_t *y, int64_t rows, int dim, float eps);
+LAI_API int lai_staged_qk_norm_rope_bf16(uint16_t *q, uint16_t *k, const float *wq,
+                                         const float *wk, const float *cos_t,
+                                         const float *sin_t, const int32_t *pos,
+                                         int64_t table_rows, int64_t rows, int n_q_heads,
+                                         int n_kv_heads, int head_dim, float eps);
+LAI_API int lai_staged_swiglu_bf16(uint16_t *out, const uint16_t *gate_up, int64_t rows,
+                                   int inter);
+
 /* The static helper embed_lookup_bf16(dst, table, token_id, dim) of
  * src/tts_native.c:473-476 (a call-site one-liner forwards to this). The table
  * must be device memory, managed memory or host memory registered with

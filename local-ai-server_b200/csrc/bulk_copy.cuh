@@ -26,12 +26,11 @@ __device__ __forceinline__ void fence_barrier_init() {
 }
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
-    uint64_t state;
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 %0, [%1], %2;"
-                 : "=l"(state)
-                 : "r"(smem_addr(bar)), "r"(bytes)
-                 : "memory");
-    (void)state;
+    asm volatile(
+        "{\n\t.reg .b64 state;\n\t"
+        "mbarrier.arrive.expect_tx.shared::cta.b64 state, [%0], %1;\n\t}" ::"r"(smem_addr(bar)),
+        "r"(bytes)
+        : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {

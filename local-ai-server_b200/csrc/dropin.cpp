@@ -372,6 +372,61 @@ void voc_snake_beta(float *x, const float *exp_alpha, const float *inv_exp_beta,
     });
 }
 
+int lai_staged_add_rmsnorm_bf16(uint16_t *x, const uint16_t *delta, const float *w,
+                                uint16_t *y, int64_t rows, int dim, float eps) {
+    const char *fn = "lai_staged_add_rmsnorm_bf16";
+    if (!x || !delta || !w || !y || rows < 0 || dim <= 0) return fail(fn, LAI_ERR_INVALID, "arguments");
+    const size_t rb = (size_t)dim * 2;
+    std::vector<Arg> a = {{x, rb, 0, true, true}, {delta, rb, 0, true, false},
+                          {w, 0, (size_t)dim * 4, true, false}, {y, rb, 0, false, true}};
+    return run_op(fn, a, rows, [&](cudaStream_t s, int64_t, int64_t n, void **d, int *) {
+        return lai_add_rmsnorm_bf16(P<uint16_t>(d, 0), P<uint16_t>(d, 1), P<float>(d, 2),
+                                    P<uint16_t>(d, 3), n, dim, eps, s);
+    });
+}
+
+int lai_staged_qk_norm_rope_bf16(uint16_t *q, uint16_t *k, const float *wq, const float *wk,
+                                 const float *cos_t, const float *sin_t, const int32_t *pos,
+                                 int64_t table_rows, int64_t rows, int n_q_heads, int n_kv_heads,
+                                 int head_dim, float eps) {
+    const char *fn = "lai_staged_qk_norm_rope_bf16";
+    if (!q || rows < 0 || n_q_heads <= 0 || head_dim <= 0 || (head_dim & 1) ||
+        (k && n_kv_heads <= 0) || (cos_t && (!sin_t || table_rows <= 0)) ||
+        (!cos_t && !wq && !wk))
+        return fail(fn, LAI_ERR_INVALID, "arguments");
+    const size_t hb = (size_t)head_dim;
+    const size_t tb = cos_t ? (size_t)table_rows * hb * 4 : 0;
+    std::vector<Arg> a = {{q, (size_t)n_q_heads * hb * 2, 0, true, true},
+                          {k, (size_t)(k ? n_kv_heads : 0) * hb * 2, 0, true, true},
+                          {wq, 0, hb * 4, true, false},
+                          {wk, 0, hb * 4, true, false},
+                          {cos_t, 0, tb, true, false},
+                          {sin_t, 0, tb, true, false},
+                          {pos, 4, 0, true, false}};
+    return run_op(fn, a, rows, [&](cudaStream_t s, int64_t r0, int64_t n, void **d, int *err) {
+        const float *c = P<float>(d, 4), *sn = P<float>(d, 5);
+        int64_t trows = table_rows;
+        if (!pos && c) {  // row index is the position: shift the table to this chunk's rows
+            c += r0 * head_dim;
+            sn += r0 * head_dim;
+            trows -= r0;
+        }
+        return lai_qk_norm_rope_bf16(P<uint16_t>(d, 0), P<uint16_t>(d, 1), P<float>(d, 2),
+                                     P<float>(d, 3), c, sn, P<int32_t>(d, 6), trows, n,
+                                     n_q_heads, k ? n_kv_heads : 0, head_dim, eps, err, s);
+    });
+}
+
+int lai_staged_swiglu_bf16(uint16_t *out, const uint16_t *gate_up, int64_t rows, int inter) {
+    const char *fn = "lai_staged_swiglu_bf16";
+    if (!out || !gate_up || rows < 0 || inter <= 0) return fail(fn, LAI_ERR_INVALID, "arguments");
+    std::vector<Arg> a = {{out, (size_t)inter * 2, 0, false, true},
+                          {gate_up, (size_t)inter * 4, 0, true, false}};
+    return run_op(fn, a, rows, [&](cudaStream_t s, int64_t, int64_t n, void **d, int *) {
+        return lai_swiglu_bf16(P<uint16_t>(d, 0), P<uint16_t>(d, 1), n, inter, s);
+    });
+}
+
 void lai_embed_lookup_bf16(float *dst, const uint16_t *table, int token_id, int dim,
                            int64_t vocab) {
     const char *fn = "lai_embed_lookup_bf16";

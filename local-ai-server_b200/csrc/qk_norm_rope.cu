@@ -198,7 +198,6 @@ qk_pipe_kernel(uint16_t *q, uint16_t *k, const float *__restrict__ wq,
     unsigned char *ring = smem + 128;
     const uint32_t q_tok = (uint32_t)nq * HD * 2, k_tok = (uint32_t)nkv * HD * 2;
     const uint32_t stage_bytes = kTileTok * (q_tok + k_tok);
-    const int H = nq + nkv;
     const int64_t ntiles = (rows + kTileTok - 1) / kTileTok;
     const int64_t my_n = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
     const int tid = threadIdx.x, lane = tid & 31;

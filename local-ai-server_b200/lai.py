@@ -56,6 +56,10 @@ SIGNATURES: dict[str, tuple] = {
     "qwen_add_inplace": (None, [_vp, _vp, _i32]),
     "qwen_silu": (None, [_vp, _i32]),
     "voc_snake_beta": (None, [_vp, _vp, _vp, _i32, _i32]),
+    "lai_staged_add_rmsnorm_bf16": (_i32, [_vp, _vp, _vp, _vp, _i64, _i32, _f32]),
+    "lai_staged_qk_norm_rope_bf16": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32,
+                                            _i32, _i32, _f32]),
+    "lai_staged_swiglu_bf16": (_i32, [_vp, _vp, _i64, _i32]),
     "lai_embed_lookup_bf16": (None, [_vp, _vp, _i32, _i32, _i64]),
     "lai_register_host_table": (_i32, [_vp, ctypes.c_size_t]),
     "lai_unregister_host_table": (_i32, [_vp]),

@@ -183,6 +183,71 @@ def test_embed_lookup_registered_host_table_and_device_table():
     assert np.array_equal(dst.view(np.uint32), want.view(np.uint32))
 
 
+def _bits(t):
+    return t.view(torch.int16).numpy().view(np.uint16)
+
+
+@pytest.mark.parametrize("pinned", [True, False])
+def test_staged_bf16_chain_equals_device_api(pinned):
+    """Host-buffer BF16 entries give the device API's bytes (same kernels, staged rows)."""
+    g = torch.Generator().manual_seed(21)
+    T, D, I, nq, nkv, hd, P = 3000, 2048, 6144, 16, 8, 128, 1024
+    bf = torch.bfloat16
+
+    def host(*shape, dtype=bf):
+        t = torch.randn(shape, generator=g).to(dtype)
+        return t.pin_memory() if pinned else t
+
+    x, dl, q, k, gu = host(T, D), host(T, D), host(T, nq * hd), host(T, nkv * hd), host(T, 2 * I)
+    w, wq, wk = (1 + 0.02 * torch.randn(n, generator=g) for n in (D, hd, hd))
+    pos = torch.randint(0, P, (T,), generator=g, dtype=torch.int32)
+    ct, st = lai.rope_table(torch.arange(P, dtype=torch.int32, device="cuda"), P, hd, 1e6)
+    ct_h, st_h = ct.cpu(), st.cpu()
+    # device reference results
+    xd, dd, qd, kd, gd = (t.cuda() for t in (x, dl, q, k, gu))
+    yd = lai.add_rmsnorm(xd, dd, w.cuda(), 1e-6)
+    lai.qk_norm_rope(qd, kd, wq.cuda(), wk.cuda(), ct, st, pos.cuda(), nq, nkv, hd, 1e-6)
+    ad = lai.swiglu(gd, I)
+    torch.cuda.synchronize()
+    # staged host calls
+    y = torch.empty_like(x)
+    act = torch.empty(T, I, dtype=bf)
+    L = lib()
+    assert L.lai_staged_add_rmsnorm_bf16(V(x.data_ptr()), V(dl.data_ptr()), V(w.data_ptr()),
+                                         V(y.data_ptr()), T, D, 1e-6) == lai.LAI_OK
+    assert L.lai_staged_qk_norm_rope_bf16(V(q.data_ptr()), V(k.data_ptr()), V(wq.data_ptr()),
+                                          V(wk.data_ptr()), V(ct_h.data_ptr()), V(st_h.data_ptr()),
+                                          V(pos.data_ptr()), P, T, nq, nkv, hd, 1e-6) == lai.LAI_OK
+    assert L.lai_staged_swiglu_bf16(V(act.data_ptr()), V(gu.data_ptr()), T, I) == lai.LAI_OK
+    for got, want in [(x, xd), (y, yd), (q, qd), (k, kd), (act, ad)]:
+        assert np.array_equal(_bits(got), _bits(want.cpu()))
+
+
+def test_staged_qk_without_positions_uses_row_index_across_chunks():
+    # pos NULL: row r uses table row r, also in chunks after the first
+    g = torch.Generator().manual_seed(22)
+    T, nq, hd = 20000, 16, 128
+    q = torch.randn(T, nq * hd, generator=g).to(torch.bfloat16)
+    ct, st = lai.rope_table(torch.arange(T, dtype=torch.int32, device="cuda"), T, hd, 1e6)
+    qd = q.cuda()
+    lai.qk_norm_rope(qd, None, None, None, ct, st, None, nq, 0, hd, 0.0)
+    ct_h, st_h = ct.cpu(), st.cpu()
+    assert lib().lai_staged_qk_norm_rope_bf16(V(q.data_ptr()), None, None, None, V(ct_h.data_ptr()),
+                                              V(st_h.data_ptr()), None, T, T, nq, 0, hd,
+                                              0.0) == lai.LAI_OK
+    assert np.array_equal(_bits(q), _bits(qd.cpu()))
+
+
+def test_staged_swiglu_in_place_host():
+    g = torch.Generator().manual_seed(23)
+    T, I = 2500, 6144  # several staging chunks; out aliases gate_up
+    gu = (2 * torch.randn(T, 2 * I, generator=g)).to(torch.bfloat16)
+    want = lai.swiglu(gu.cuda(), I).cpu()
+    assert lib().lai_staged_swiglu_bf16(V(gu.data_ptr()), V(gu.data_ptr()), T, I) == lai.LAI_OK
+    got = gu.view(-1)[: T * I].view(T, I)
+    assert np.array_equal(_bits(got), _bits(want))
+
+
 def test_invalid_arguments_report_without_launching():
     x = np.zeros(8, np.float32)
     lib().qwen_rms_norm(hp(x), hp(x), None, 1, 8, 1e-6)
