@@ -130,6 +130,7 @@ def cpu_chain_rate(cfg, rows: int, min_seconds: float, steps: int | None = None,
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     import oracle
     lib = oracle.load("liblai_cpuref.so")
+    lib.oracle_set_threads(len(os.sched_getaffinity(0)))  # all host cores, whatever OMP_* says
     rng = np.random.default_rng(5)
     D, I, hd = cfg.dim, cfg.inter, cfg.head_dim
     f = lambda *s: rng.standard_normal(s, dtype=np.float32)  # noqa: E731

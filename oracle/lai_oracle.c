@@ -49,6 +49,16 @@ int oracle_num_threads(void) {
 #endif
 }
 
+/* Thread count of the timed build's parallel loops (launchers such as torchrun
+ * export OMP_NUM_THREADS=1; the CPU baseline is meant to use every host core). */
+void oracle_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 /* ---------------------------------------------------------------------------
  * BF16 <-> F32. Widening is the bit shift of src/tts_native.c:35-40 (exact).
  * Narrowing is round-to-nearest-even, the rounding of every BF16 store

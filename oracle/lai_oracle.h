@@ -76,6 +76,7 @@ void oracle_layer_chain_f32(float *x, const float *delta_attn, const float *delt
                             int dim, int n_q_heads, int n_kv_heads, int head_dim, int inter,
                             float eps);
 int oracle_num_threads(void);
+void oracle_set_threads(int n);
 
 #ifdef __cplusplus
 }

@@ -86,6 +86,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         "oracle_layer_chain_f32": [_F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _F,
                                    _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float],
         "oracle_num_threads": [],
+        "oracle_set_threads": [_c_int],
     }
     for name, args in sig.items():
         fn = getattr(lib, name)
