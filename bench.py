@@ -2,7 +2,7 @@
 """Benchmark of the B200 per-layer kernels (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c1|c3|c5] [--e2e-rows R]
+                    [--config c2|c1|c3|c4|c5] [--graph auto|on|off]
 
 A step is one decoder layer's elementwise chain over one batch (runner.LayerChain):
 fused residual-add+RMSNorm, fused q/k RMSNorm+RoPE, fused residual-add+RMSNorm,
@@ -170,27 +170,95 @@ def cpu_model() -> str:
     return "unknown"
 
 
+def cpu_snake_rate(stages, batch: int, min_seconds: float, steps: int | None = None,
+                   warmup: int = 1, build: str = "avx2") -> dict:
+    """The reference's own voc_snake_beta (oracle/_ref, built from src/tts_vocoder_ops.c as
+    shipped: AVX2 fast sin) on host cores: channel ranges of each stage run on a thread
+    pool (ctypes releases the GIL). Returns channel-rows/s over one sweep of `stages`."""
+    import concurrent.futures as cf
+
+    import numpy as np
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle
+    lib = oracle.load(f"libvoc_ref_{build}.so")
+    nthreads = len(os.sched_getaffinity(0))
+    rng = np.random.default_rng(6)
+    data = []
+    for c, t in stages:
+        x = rng.standard_normal((batch * c, t), dtype=np.float32)
+        ea = np.exp(0.1 * rng.standard_normal(c)).astype(np.float32)
+        ieb = (1 / np.exp(0.1 * rng.standard_normal(c))).astype(np.float32)
+        data.append((x, ea, ieb, c, t))
+    F = ctypes.POINTER(ctypes.c_float)
+
+    jobs = []  # (x row pointer, ea pointer, ieb pointer, channels, T): one per (item, chunk)
+    for x, ea, ieb, c, t in data:
+        per = max(1, c // max(1, nthreads // batch))
+        for b_ in range(batch):
+            for c0 in range(0, c, per):
+                n = min(per, c - c0)
+                row = x[b_ * c + c0]
+                jobs.append((row.ctypes.data_as(F), ea[c0:].ctypes.data_as(F),
+                             ieb[c0:].ctypes.data_as(F), n, t))
+    rows = sum(batch * c for _, _, _, c, _ in data)
+    with cf.ThreadPoolExecutor(nthreads) as ex:
+        def sweep():
+            list(ex.map(lambda j: lib.voc_snake_beta(*j), jobs))
+        for _ in range(warmup):
+            sweep()
+        n, t0 = 0, time.perf_counter()
+        while True:
+            sweep()
+            n += 1
+            el = time.perf_counter() - t0
+            if (steps is not None and n >= steps) or (steps is None and el >= min_seconds):
+                break
+    return {"rows_per_s": rows * n / el, "threads": nthreads, "passes": n, "seconds": el,
+            "rows": rows}
+
+
 def run_reference(args) -> None:
     rank = env_int("RANK", 0)
     if rank != 0:
         return
     import runner
-    cfg = runner.CONFIGS[args.config]
-    rows = min(cfg.tokens, args.cpu_rows)
-    r = cpu_chain_rate(cfg, rows, 0.0, steps=args.steps, warmup=args.warmup)
-    cb = {"value": r["rows_per_s"], "unit": "rows/s", "cores": r["threads"], "kind": "port",
-          "sample": f"{rows} of {cfg.tokens} tokens of {cfg.name} per step, FP32, "
-                    f"OpenMP over rows, host {cpu_model()} x {os.cpu_count()}"}
-    line = {"metric": METRIC, "impl": "reference", "value": r["rows_per_s"], "unit": "rows/s",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1000.0 * r["seconds"] / r["passes"], "higher_is_better": True,
-            "scaling": "weak" if args.config != "c5" else "strong", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"{cfg.name} layer elementwise chain", "config": args.config,
-                       "rows_per_step": rows, "dim": cfg.dim, "ffn": cfg.inter},
-            "cpu_baseline": cb,
-            "e2e": {"value": r["rows_per_s"], "unit": "rows/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+    common = {"metric": METRIC, "impl": "reference", "n_gpus": args.gpus, "steps": args.steps,
+              "warmup": args.warmup, "higher_is_better": True, "vs_baseline": None,
+              "data": "synthetic"}
+    # each step is a bounded sample sized so that warm-up + timed steps take about
+    # args.ref_budget seconds in total, whatever K and W the caller passes
+    per_step_s = args.ref_budget / (args.steps + args.warmup)
+    if args.config == "c4":
+        # every stage (rows/s depends on the stage mix), items scaled to the budget
+        probe = cpu_snake_rate(runner.SNAKE_STAGES, 1, 0.0, steps=1, warmup=0)
+        batch = int(max(1, min(runner.SNAKE_BATCH, per_step_s / probe["seconds"])))
+        r = cpu_snake_rate(runner.SNAKE_STAGES, batch, 0.0, steps=args.steps, warmup=args.warmup)
+        cb = {"value": r["rows_per_s"], "unit": "rows/s", "cores": r["threads"],
+              "kind": "reference",
+              "sample": f"all stages x batch {batch} (of {runner.SNAKE_BATCH}) per step; the "
+                        f"reference's voc_snake_beta (AVX2 build) on {r['threads']} threads, "
+                        f"host {cpu_model()}"}
+        line = dict(common, value=r["rows_per_s"], unit="rows/s",
+                    ms_per_step=1000.0 * r["seconds"] / r["passes"], scaling="weak",
+                    dtype="f32", config={"workload": "vocoder SnakeBeta stages", "config": "c4",
+                                         "stages": runner.SNAKE_STAGES, "batch": batch})
+    else:
+        cfg = runner.CONFIGS[args.config]
+        probe = cpu_chain_rate(cfg, min(cfg.tokens, 1024), 0.0, steps=2, warmup=1)
+        rows = int(max(64, min(cfg.tokens, args.cpu_rows, probe["rows_per_s"] * per_step_s)))
+        r = cpu_chain_rate(cfg, rows, 0.0, steps=args.steps, warmup=args.warmup)
+        cb = {"value": r["rows_per_s"], "unit": "rows/s", "cores": r["threads"], "kind": "port",
+              "sample": f"{rows} of {cfg.tokens} tokens of {cfg.name} per step, FP32, "
+                        f"OpenMP over rows, host {cpu_model()}"}
+        line = dict(common, value=r["rows_per_s"], unit="rows/s",
+                    ms_per_step=1000.0 * r["seconds"] / r["passes"],
+                    scaling="weak" if args.config != "c5" else "strong", dtype="f32",
+                    config={"workload": f"{cfg.name} layer elementwise chain",
+                            "config": args.config, "rows_per_step": rows, "dim": cfg.dim,
+                            "ffn": cfg.inter})
+    line["cpu_baseline"] = cb
+    line["e2e"] = {"value": line["value"], "unit": "rows/s", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}
     print(json.dumps(line), flush=True)
 
 
@@ -310,34 +378,123 @@ def e2e_dropin_f32(cfg, rows: int, steps: int, warmup: int) -> dict:
     return {"seconds": el, "rows": rows, "steps": steps, "h2d": h2d, "d2h": d2h}
 
 
+def e2e_snake_dropin(stages, batch: int, steps: int, warmup: int) -> dict:
+    """voc_snake_beta (reference name, FP32) on pinned host buffers, one call per (item, stage)."""
+    import torch
+    import lai
+    lib = lai.load()
+    g = torch.Generator().manual_seed(12)
+    bufs = [(_pinned((batch, c, t), None, g), _pinned((c,), None, g), _pinned((c,), None, g), c, t)
+            for c, t in stages]
+    V = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def step():
+        for x, ea, ieb, c, t in bufs:
+            for b_ in range(batch):
+                lib.voc_snake_beta(ctypes.c_void_p(x.data_ptr() + b_ * c * t * 4), V(ea), V(ieb), c, t)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    torch.cuda.synchronize()
+    if lib.lai_last_error() != 0:
+        raise RuntimeError("voc_snake_beta drop-in failed")
+    nbytes = sum(batch * c * t * 4 + 8 * c for _, _, _, c, t in bufs)
+    return {"seconds": time.perf_counter() - t0, "steps": steps, "h2d": nbytes,
+            "d2h": sum(batch * c * t * 4 for _, _, _, c, t in bufs)}
+
+
 # ------------------------------------------------------------------ our path
+def time_launches(launches, steps: int, graph: bool):
+    """Time `steps` steps. Returns (total ms, per-launch lists of ms).
+
+    Direct mode records a CUDA event after every launch on the launching stream.
+    Graph mode (launch-bound small configs) replays one captured graph per step for
+    the total, and, for the per-launch times, one graph per kernel holding 20
+    back-to-back launches of it (a kernel reading the same L2-resident inputs)."""
+    import torch
+    stream = torch.cuda.current_stream()
+    nk = len(launches)
+    if not graph:
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps * nk + 1)]
+        evs[0].record(stream)
+        i = 1
+        for _ in range(steps):
+            for f in launches:
+                f()
+                evs[i].record(stream)
+                i += 1
+        torch.cuda.synchronize()
+        per = [[evs[s * nk + j].elapsed_time(evs[s * nk + j + 1]) for s in range(steps)]
+               for j in range(nk)]
+        return evs[0].elapsed_time(evs[-1]), per
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for f in launches:
+            f()
+    reps = 20  # launches of one kernel per graph, so a replay's launch cost is amortised
+    singles = []
+    for f in launches:
+        gs = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gs):
+            for _ in range(reps):
+                f()
+        singles.append(gs)
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        g.replay()
+    b.record(stream)
+    torch.cuda.synchronize()
+    total = a.elapsed_time(b)
+    per = []
+    n_rep = max(1, steps // reps)
+    for gs in singles:
+        gs.replay()
+        a.record(stream)
+        for _ in range(n_rep):
+            gs.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
+        per.append([a.elapsed_time(b) / (n_rep * reps)] * steps)
+    return total, per
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
-    import lai
     import runner
 
     world = env_int("WORLD_SIZE", 1)
     rank = env_int("RANK", 0)
     local = env_int("LOCAL_RANK", 0)
-    if world != args.gpus:
-        args.gpus = world
+    args.gpus = world
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-    cfg = runner.CONFIGS[args.config]
+    snake = args.config == "c4"
     strong = args.config == "c5"
-    if strong:
-        row0, row1 = runner.shard_range(cfg.tokens, world, rank)
+    if snake:
+        work = runner.SnakeSweep(seed=args.seed + 1000 * rank)
+        rows = sum(work.rows_per_launch())
+        cfg = None
     else:
-        per = args.rows or cfg.tokens
-        row0, row1 = rank * per, (rank + 1) * per
-    rows = row1 - row0
-    chain = runner.LayerChain(cfg, rows, row0=row0, seed=args.seed)
-    stream = torch.cuda.current_stream()
-    launches = chain.launches(stream)
-    nk = len(launches)
+        cfg = runner.CONFIGS[args.config]
+        if strong:
+            row0, row1 = runner.shard_range(cfg.tokens, world, rank)
+        else:
+            per = args.rows or cfg.tokens
+            row0, row1 = rank * per, (rank + 1) * per
+        rows = row1 - row0
+        work = runner.LayerChain(cfg, rows, row0=row0, seed=args.seed)
+    launches = work.launches(None)  # each launch goes to the current stream when called
+    graph = args.graph == "on" or (args.graph == "auto" and not snake and rows <= 4096)
 
     for _ in range(args.warmup):
         for f in launches:
@@ -347,42 +504,31 @@ def run_ours(args) -> None:
     phys = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
     gpu_index = phys[local] if local < len(phys) and phys[local] != "" else str(local)
     sampler = ClockSampler(gpu_index)
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps * nk + 1)]
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     sampler.start()
     time.sleep(0.3)  # let the sampler attach before the timed region
-    evs[0].record(stream)
-    i = 1
-    for _ in range(args.steps):
-        for f in launches:
-            f()
-            evs[i].record(stream)
-            i += 1
+    total_ms, per = time_launches(launches, args.steps, graph)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clocks = sampler.stop()
-    total_ms = evs[0].elapsed_time(evs[-1])
-    per = [[] for _ in range(nk)]
-    for s in range(args.steps):
-        for j in range(nk):
-            per[j].append(evs[s * nk + j].elapsed_time(evs[s * nk + j + 1]))
     t = torch.tensor([total_ms], device="cuda", dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     max_ms = float(t.item())
-    assert int(chain.err.item()) == 0, "position out of range in the chain"
-    swiglu_tail = 1 if (rows * cfg.inter) % 4 else 0
+    if not snake:
+        assert int(work.err.item()) == 0, "an id or position was out of range in the chain"
 
     peak, peak_kind = measured_peaks()
     total_rows = cfg.tokens if strong else rows * world
     value = total_rows * args.steps / (max_ms / 1000.0)
-    bpl = chain.bytes_per_launch()
+    bpl = work.bytes_per_launch()
+    rows_pl = work.rows_per_launch() if snake else [rows] * len(bpl)
     kernels = {}
-    for j, name in enumerate(runner.LayerChain.KERNELS):
-        k = kernels.setdefault(name, {"ms": [], "bytes": bpl[j]})
+    for j, name in enumerate(work.kernel_names):
+        k = kernels.setdefault(name, {"ms": [], "bytes": bpl[j], "rows": rows_pl[j]})
         k["ms"] += per[j]
     per_kernel, dominant, dom_total = {}, None, -1.0
     for name, k in kernels.items():
@@ -390,72 +536,104 @@ def run_ours(args) -> None:
         gbs = k["bytes"] / (avg_ms / 1000.0) / 1e9
         per_kernel[name] = {"avg_us": round(avg_ms * 1000, 2), "gbs": round(gbs, 1),
                             "frac_of_peak": round(gbs / peak, 4),
-                            "rows_per_s": round(rows / (avg_ms / 1000.0), 1),
+                            "rows_per_s": round(k["rows"] / (avg_ms / 1000.0), 1),
                             "bytes_per_launch": k["bytes"], "launches": len(k["ms"])}
         if sum(k["ms"]) > dom_total:
             dominant, dom_total = name, sum(k["ms"])
-    step_bytes = cfg.step_bytes_per_token() * rows
+    step_bytes = sum(bpl)
     step_gbs = step_bytes * args.steps / (total_ms / 1000.0) / 1e9
-    traffic = load_traffic().get(f"{dominant}@{args.config}")
     d = per_kernel[dominant]
     roofline = {"bound": "hbm", "kernel": dominant, "achieved": d["gbs"], "peak": peak,
-                "unit": "GB/s", "frac": round(d["gbs"] / peak, 4), "peak_source": peak_kind,
-                "traffic": traffic, "algorithmic_bytes_per_launch": d["bytes_per_launch"],
+                "unit": "GB/s", "frac": round(d["gbs"] / peak, 4),
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                               else "fallback 6650 GB/s",
+                "traffic": load_traffic().get(f"{dominant}@{args.config}"),
+                "algorithmic_bytes_per_launch": d["bytes_per_launch"],
                 "step_gbs": round(step_gbs, 1), "step_frac": round(step_gbs / peak, 4)}
 
-    # e2e: the same chain on pinned host buffers through the C ABI's synchronous entries
+    def max_time(sec):
+        et = torch.tensor([sec], device="cuda", dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        return float(et.item())
+
     e2e = e2e_f32 = None
     if not args.no_e2e:
-        def max_time(sec):
-            et = torch.tensor([sec], device="cuda", dtype=torch.float64)
-            if world > 1:
-                dist.all_reduce(et, op=dist.ReduceOp.MAX)
-            return float(et.item())
-        del chain  # free the device-resident workload before the staged runs
+        del work, launches  # free the device-resident workload before the staged runs
         torch.cuda.empty_cache()
-        r = e2e_staged_bf16(cfg, rows, args.e2e_steps, 1)
-        e2e = {"value": round(rows * world * r["steps"] / max_time(r["seconds"]), 1),
-               "unit": "rows/s", "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"],
-               "rows_per_step": rows, "dtype": "bf16",
-               "api": "lai_staged_{add_rmsnorm,qk_norm_rope,swiglu}_bf16 on pinned host buffers, "
-                      "4 synchronous calls/step"}
-        fr = min(rows, args.e2e_rows)
-        r = e2e_dropin_f32(cfg, fr, args.e2e_steps, 1)
-        e2e_f32 = {"value": round(fr * world * r["steps"] / max_time(r["seconds"]), 1),
+        if snake:
+            r = e2e_snake_dropin(runner.SNAKE_STAGES, runner.SNAKE_BATCH, args.e2e_steps, 1)
+            e2e = {"value": round(rows * world * r["steps"] / max_time(r["seconds"]), 1),
                    "unit": "rows/s", "h2d_bytes_per_step": r["h2d"],
-                   "d2h_bytes_per_step": r["d2h"], "rows_per_step": fr, "dtype": "f32",
-                   "api": "reference-named qwen_* drop-ins on pinned host FP32 buffers, "
-                          "9 calls/step"}
+                   "d2h_bytes_per_step": r["d2h"], "dtype": "f32",
+                   "api": "voc_snake_beta drop-in on pinned host buffers, one call per item and stage"}
+        else:
+            er = min(rows, args.e2e_rows_bf16)
+            r = e2e_staged_bf16(cfg, er, args.e2e_steps, 1)
+            e2e = {"value": round(er * world * r["steps"] / max_time(r["seconds"]), 1),
+                   "unit": "rows/s", "h2d_bytes_per_step": r["h2d"],
+                   "d2h_bytes_per_step": r["d2h"], "rows_per_step": er, "dtype": "bf16",
+                   "api": "lai_staged_{add_rmsnorm,qk_norm_rope,swiglu}_bf16 on pinned host "
+                          "buffers, 4 synchronous calls/step"}
+            fr = min(rows, args.e2e_rows)
+            r = e2e_dropin_f32(cfg, fr, args.e2e_steps, 1)
+            e2e_f32 = {"value": round(fr * world * r["steps"] / max_time(r["seconds"]), 1),
+                       "unit": "rows/s", "h2d_bytes_per_step": r["h2d"],
+                       "d2h_bytes_per_step": r["d2h"], "rows_per_step": fr, "dtype": "f32",
+                       "api": "reference-named qwen_* drop-ins on pinned host FP32 buffers, "
+                              "9 calls/step"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        r = cpu_chain_rate(cfg, min(rows, args.cpu_rows), args.cpu_seconds)
-        cpu = {"value": round(r["rows_per_s"], 1), "unit": "rows/s", "cores": r["threads"],
-               "kind": "port",
-               "sample": f"{min(rows, args.cpu_rows)} tokens x {r['passes']} passes "
-                         f"({r['seconds']:.1f} s) of the FP32 chain, host {cpu_model()}"}
+        if snake:
+            r = cpu_snake_rate(runner.SNAKE_STAGES, args.cpu_batch, args.cpu_seconds)
+            cpu = {"value": round(r["rows_per_s"], 1), "unit": "rows/s", "cores": r["threads"],
+                   "kind": "reference",
+                   "sample": f"{r['passes']} sweeps of all stages x batch {args.cpu_batch} "
+                             f"({r['seconds']:.1f} s) through the reference's voc_snake_beta "
+                             f"(AVX2 build), host {cpu_model()}"}
+        else:
+            r = cpu_chain_rate(cfg, min(rows, args.cpu_rows), args.cpu_seconds)
+            cpu = {"value": round(r["rows_per_s"], 1), "unit": "rows/s", "cores": r["threads"],
+                   "kind": "port",
+                   "sample": f"{min(rows, args.cpu_rows)} tokens x {r['passes']} passes "
+                             f"({r['seconds']:.1f} s) of the FP32 chain, host {cpu_model()}"}
 
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
+    if snake:
+        config = {"workload": "vocoder SnakeBeta over the BigVGAN stages, FP32 in place",
+                  "config": "c4", "stages": runner.SNAKE_STAGES, "batch": runner.SNAKE_BATCH,
+                  "rows": "channel rows (batch x channels) per sweep",
+                  "parallelism": f"replicas x{world}, no collective",
+                  "l2": f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB per step per GPU)"}
+        launches_per_step = len(runner.SNAKE_STAGES)
+    else:
+        config = {"workload": f"{cfg.name} layer elementwise chain ("
+                              + ", ".join(work_names := list(cfg.kernels())) + ")",
+                  "config": args.config, "rows_per_gpu": rows, "dim": cfg.dim, "ffn": cfg.inter,
+                  "heads": [cfg.n_q, cfg.n_kv, cfg.head_dim], "positions": cfg.pos_mode,
+                  "parallelism": f"row-sharded x{world}, no collective",
+                  "timing": "CUDA graph replay" if graph else "direct launches",
+                  "l2": (f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB per step per GPU)"
+                         if step_bytes > 126e6 else
+                         f"L2-resident working set ({step_bytes / 1e6:.1f} MB per step): hot-cache numbers")}
+        launches_per_step = len(work_names) + (1 if (rows * cfg.inter) % 4 else 0)
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "rows/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(max_ms / args.steps, 4), "higher_is_better": True,
-        "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "bf16",
+        "scaling": "strong" if strong else "weak", "vs_baseline": None,
+        "dtype": "f32" if snake else "bf16",
         "data": "synthetic (seeded counter-based N(0,1) on device; norm weights 1+N(0,0.02))",
-        "config": {"workload": f"{cfg.name} layer elementwise chain "
-                               "(add+RMSNorm, qk-norm+RoPE, add+RMSNorm, SwiGLU)",
-                   "config": args.config, "rows_per_gpu": rows, "dim": cfg.dim, "ffn": cfg.inter,
-                   "heads": [cfg.n_q, cfg.n_kv, cfg.head_dim], "positions": cfg.pos_mode,
-                   "parallelism": f"row-sharded x{world}, no collective",
-                   "l2": f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB per step per GPU)"},
-        "hbm_gbs": round(step_gbs * (world if not strong else 1), 1),
+        "config": config,
+        "hbm_gbs": round(step_gbs * (1 if strong else world), 1),
         "per_kernel": per_kernel, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
         "e2e_dropin_f32": e2e_f32,
-        "gpu_launches": args.steps * (3 + 1 + swiglu_tail),
+        "gpu_launches": args.steps * launches_per_step,
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
@@ -467,14 +645,21 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c1", "c2", "c3", "c5"], default="c2")
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5"], default="c2")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--rows", type=int, default=0,
                     help="rows per GPU instead of the config's batch (small profiling cases)")
-    ap.add_argument("--e2e-rows", type=int, default=16384)
+    ap.add_argument("--graph", choices=["auto", "on", "off"], default="auto",
+                    help="CUDA-graph replay (auto: for launch-bound configs of <= 4096 rows)")
+    ap.add_argument("--e2e-rows", type=int, default=16384, help="rows of the FP32 drop-in e2e")
+    ap.add_argument("--e2e-rows-bf16", type=int, default=65536, help="rows of the BF16 e2e")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-rows", type=int, default=8192)
+    ap.add_argument("--cpu-batch", type=int, default=2,
+                    help="SnakeBeta batch items in the CPU baseline sample (c4)")
+    ap.add_argument("--ref-budget", type=float, default=90.0,
+                    help="seconds the --impl reference run should take in total")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()

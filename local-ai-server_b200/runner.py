@@ -44,14 +44,19 @@ class LayerConfig:
     def bytes_per_token(self) -> dict[str, int]:
         s = BF16_BYTES
         return {
+            "embed_gather": 2 * self.dim * s + 4,                  # table row, id, output row
             "add_rmsnorm": 4 * self.dim * s,                       # read x, delta; write x', y
             "qk_norm_rope": 2 * (self.n_q + self.n_kv) * self.head_dim * s,  # q, k in place
             "swiglu": 3 * self.inter * s,                          # read 2I, write I
         }
 
+    def kernels(self) -> tuple[str, ...]:
+        k = ("add_rmsnorm", "qk_norm_rope", "add_rmsnorm", "swiglu")
+        return (("embed_gather",) + k) if self.vocab else k
+
     def step_bytes_per_token(self) -> int:
         b = self.bytes_per_token()
-        return 2 * b["add_rmsnorm"] + b["qk_norm_rope"] + b["swiglu"]
+        return sum(b[k] for k in self.kernels())
 
 
 # BASELINE configs (SURVEY 8a naming: C1..C5).
@@ -81,9 +86,11 @@ def shard_range(n: int, world: int, rank: int) -> tuple[int, int]:
 
 
 class LayerChain:
-    """Device buffers and launches for one shard of a LayerConfig."""
+    """Device buffers and launches for one shard of a LayerConfig.
 
-    KERNELS = ("add_rmsnorm", "qk_norm_rope", "add_rmsnorm", "swiglu")
+    With cfg.vocab > 0 the step starts with the BF16 token-embedding gather
+    (src/tts_native.c:490-493, 518-520) into its own output rows.
+    """
 
     def __init__(self, cfg: LayerConfig, rows: int, row0: int = 0, seed: int = 1234,
                  device: str = "cuda"):
@@ -114,11 +121,21 @@ class LayerChain:
         self.cos, self.sin = lai.rope_table(table_pos, cfg.pos_period, cfg.head_dim, cfg.theta,
                                             device=device)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        if cfg.vocab:
+            self.table = e(cfg.vocab, D)
+            lai.synth_normal(self.table, seed=seed + 300)
+            self.ids = e(T, dt=torch.int32)
+            lai.synth_uniform_i32(self.ids, seed=seed + 301, lo=0, hi=cfg.vocab, offset=row0)
+            self.emb = e(T, D)
+        self.kernel_names = cfg.kernels()
 
     def launches(self, stream=None):
         """The step as a list of callables, one kernel launch each."""
         c = self.cfg
-        return [
+        gather = [lambda: lai.call("lai_embed_gather_bf16", lai._p(self.emb), lai._p(self.table),
+                                   lai._p(self.ids), self.rows, c.dim, c.vocab,
+                                   lai._p(self.err), lai._s(stream))] if c.vocab else []
+        return gather + [
             lambda: lai.add_rmsnorm(self.x, self.d_ffn, self.w_in, c.eps, y=self.y, stream=stream),
             lambda: lai.qk_norm_rope(self.q, self.k, self.wq, self.wk, self.cos, self.sin, self.pos,
                                      c.n_q, c.n_kv, c.head_dim, c.eps, err=self.err, stream=stream),
@@ -132,4 +149,36 @@ class LayerChain:
 
     def bytes_per_launch(self) -> list[int]:
         b = self.cfg.bytes_per_token()
-        return [b[k] * self.rows for k in self.KERNELS]
+        return [b[k] * self.rows for k in self.kernel_names]
+
+
+class SnakeSweep:
+    """Vocoder SnakeBeta over the BigVGAN stages (config 4): x [batch, C, T] FP32 per
+    stage, per-channel exp(alpha) / 1/exp(beta) pre-exponentiated as the reference
+    does at load (src/tts_vocoder.c:221-227). One step = one launch per stage."""
+
+    def __init__(self, stages=SNAKE_STAGES, batch=SNAKE_BATCH, seed: int = 77, device="cuda"):
+        import torch
+        self.stages, self.batch = list(stages), batch
+        self.x, self.ea, self.ieb = [], [], []
+        for i, (c, t) in enumerate(self.stages):
+            x = torch.empty((batch, c, t), dtype=torch.float32, device=device)
+            lai.synth_normal(x, seed=seed + i)
+            a = torch.empty(c, dtype=torch.float32, device=device)
+            b = torch.empty(c, dtype=torch.float32, device=device)
+            lai.synth_normal(a, seed=seed + 100 + i, std=0.1)
+            lai.synth_normal(b, seed=seed + 200 + i, std=0.1)
+            self.x.append(x)
+            self.ea.append(torch.exp(a))
+            self.ieb.append(1.0 / torch.exp(b))
+        self.kernel_names = tuple(f"snake_beta_{c}x{t}" for c, t in self.stages)
+
+    def launches(self, stream=None):
+        return [(lambda i=i: lai.snake_beta(self.x[i], self.ea[i], self.ieb[i], stream=stream))
+                for i in range(len(self.stages))]
+
+    def bytes_per_launch(self) -> list[int]:
+        return [8 * self.batch * c * t for c, t in self.stages]  # FP32 read + write
+
+    def rows_per_launch(self) -> list[int]:
+        return [self.batch * c for c, _ in self.stages]
