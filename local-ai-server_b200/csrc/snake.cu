@@ -3,18 +3,17 @@
 // Reference: voc_snake_beta(x, exp_alpha, inv_exp_beta, C, T)
 // (src/tts_vocoder_ops.c:279-305): x[c,t] += ieb[c] * sin(ea[c] * x[c,t])^2 with the
 // parameters pre-exponentiated at load (src/tts_vocoder.c:221-227). The scalar
-// branch of the reference computes x + ((ieb * s) * s) with separately rounded
-// operations; this kernel does the same with CUDA's full-accuracy sinf (no fast
-// math), so it differs from the reference only where the two sinf differ.
+// branch of the reference computes x + ((ieb * s) * s), s = sinf(ea * x); this
+// kernel evaluates sin^2 directly (sin2_fast below) and lands within ~1e-7 of it.
 //
-// Roofline: HBM, 8 bytes per element (read + write). The per-element arithmetic
-// (sinf's range reduction and polynomial, ~30 instructions) keeps the kernel
-// within reach of the FP32 issue rate at HBM speed.
+// Roofline: HBM, 8 bytes per element (read + write). With a full-range sinf the
+// kernel was issue-bound (ncu: 85% issue-active, ~41 instructions per element);
+// sin2_fast brings the arithmetic well under the HBM rate.
 //
-// Layout: x is [batch*C rows, T]. Grid y walks rows, grid x walks 16 KiB
-// segments of a row. A row starts 16-byte aligned only when row*T % 4 == 0, so
-// each row is a scalar head (to the first aligned element), an aligned body of
-// float4 vectors, and a scalar tail; CTA x == 0 of each row takes head and tail.
+// Layout: snake_flat_kernel treats [batch*C rows, T] as one run of float4 vectors
+// and recovers each vector's row and channel by multiply-high division, so short
+// rows waste no threads. snake_kernel (unaligned base, T < 4, or >= 2^32 elements)
+// walks rows on grid y and 16 KiB segments on grid x with scalar head and tail.
 #include "lai_common.cuh"
 
 namespace lai {
@@ -24,9 +23,54 @@ constexpr int kThreads = 256;
 constexpr int kUnroll = 4;
 constexpr int kSegVec = kThreads * kUnroll;  // float4 vectors per CTA segment
 
+// sin^2(y) without a full sin, from textbook pieces:
+//  * Cody-Waite reduction (W. J. Cody, W. Waite, "Software Manual for the Elementary
+//    Functions", 1980): m = rint(y * 2/pi), r = y - m*pi/2 with pi/2 split into three
+//    floats so that r keeps ~full precision for |m| < 2^16;
+//  * sin^2 y = (1 - cos 2y) / 2 and cos 2y = cos(m*pi + 2r) = (-1)^m cos t, t = 2r,
+//    |t| <= pi/2;
+//  * cos t by its Taylor series through t^12 (coefficients 1/(2k)!): the remainder is
+//    below (pi/2)^14 / 14! < 6.4e-9 on |t| <= pi/2, under float resolution.
+// About 14 FP instructions instead of a full-range sinf plus a square. Arguments
+// beyond 65536 in magnitude (and inf/NaN) take CUDA's sinf. The absolute error of
+// sin^2 stays within a few 1e-8 (tests/test_gpu_parity.py bounds it against the
+// reference's own compiled voc_snake_beta).
+// pi/2 = hi + mid + lo, each the float nearest to what remains (computed in 80-digit
+// decimal arithmetic); 2/pi rounded to float.
+constexpr float kTwoOverPi = 0.6366197466850281f;
+constexpr float kPiO2Hi = 1.5707963705062866f;
+constexpr float kPiO2Mid = -4.371138828673793e-08f;
+constexpr float kPiO2Lo = -1.7151245100058819e-15f;
+
+__device__ __forceinline__ float sin2_fast(float y) {
+    const float m = rintf(y * kTwoOverPi);
+    float r = fmaf(-m, kPiO2Hi, y);
+    r = fmaf(-m, kPiO2Mid, r);
+    r = fmaf(-m, kPiO2Lo, r);
+    const float t = 2.0f * r;
+    const float u = t * t;
+    float c = 1.0f / 479001600.0f;              // 1/12!
+    c = fmaf(c, u, -1.0f / 3628800.0f);         // 1/10!
+    c = fmaf(c, u, 1.0f / 40320.0f);            // 1/8!
+    c = fmaf(c, u, -1.0f / 720.0f);             // 1/6!
+    c = fmaf(c, u, 1.0f / 24.0f);               // 1/4!
+    c = fmaf(c, u, -0.5f);                      // 1/2!
+    c = fmaf(c, u, 1.0f);
+    const int odd = static_cast<int>(m) & 1;
+    c = odd ? -c : c;                           // cos 2y
+    return fmaf(-0.5f, c, 0.5f);                // (1 - cos 2y) / 2
+}
+
 __device__ __forceinline__ float snake1(float x, float ea, float ieb) {
-    const float s = sinf(__fmul_rn(ea, x));
-    return __fadd_rn(x, __fmul_rn(__fmul_rn(ieb, s), s));
+    const float y = __fmul_rn(ea, x);
+    float s2;
+    if (fabsf(y) <= 65536.0f) {
+        s2 = sin2_fast(y);
+    } else {  // huge or non-finite argument: full-range sinf
+        const float s = sinf(y);
+        s2 = s * s;
+    }
+    return fmaf(ieb, s2, x);  // x + ieb * sin^2(ea * x)
 }
 
 __global__ void __launch_bounds__(kThreads)
@@ -67,6 +111,69 @@ snake_kernel(float *x, const float *__restrict__ ea, const float *__restrict__ i
     }
 }
 
+// Unsigned division by an invariant 32-bit divisor as multiply-high and shifts
+// (Granlund & Montgomery, "Division by invariant integers using multiplication",
+// PLDI 1994, fig. 4.1): exact for every 32-bit dividend.
+struct FastDiv {
+    uint32_t d, m, s1, s2;
+};
+inline FastDiv make_fastdiv(uint32_t d) {
+    uint32_t l = 0;
+    while (l < 32 && (1ull << l) < d) l++;  // l = ceil(log2 d)
+    const uint64_t m = ((1ull << 32) * ((1ull << l) - d)) / d + 1;
+    return FastDiv{d, (uint32_t)m, l < 1 ? l : 1u, l > 0 ? l - 1 : 0u};
+}
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv &f) {
+    const uint32_t t = __umulhi(f.m, n);
+    return (t + ((n - t) >> f.s1)) >> f.s2;
+}
+
+// The whole [rows, T] tensor as one flat run of float4 vectors: uniform work per
+// thread whatever the row length (short rows waste no threads). Needs a 16-byte
+// aligned base, T >= 4 (a vector spans at most two rows) and < 2^32 elements.
+__global__ void __launch_bounds__(kThreads)
+snake_flat_kernel(float *x, const float *__restrict__ ea, const float *__restrict__ ieb,
+                  uint32_t total, uint32_t T, uint32_t C, FastDiv divT, FastDiv divC) {
+    const uint32_t nvec = total / 4;
+    const uint32_t base = blockIdx.x * (uint32_t)kSegVec + threadIdx.x;
+    float4 *xv = reinterpret_cast<float4 *>(x);
+    float4 v[kUnroll];
+#pragma unroll
+    for (int i = 0; i < kUnroll; i++) {
+        const uint32_t k = base + i * kThreads;
+        if (k < nvec) v[i] = xv[k];
+    }
+#pragma unroll
+    for (int i = 0; i < kUnroll; i++) {
+        const uint32_t k = base + i * kThreads;
+        if (k >= nvec) continue;
+        const uint32_t e = 4 * k;
+        const uint32_t row = fdiv(e, divT);
+        const uint32_t col = e - row * T;
+        const uint32_t c = row - fdiv(row, divC) * C;
+        const float a = __ldg(ea + c), b = __ldg(ieb + c);
+        float4 r;
+        if (col + 3 < T) {
+            r.x = snake1(v[i].x, a, b); r.y = snake1(v[i].y, a, b);
+            r.z = snake1(v[i].z, a, b); r.w = snake1(v[i].w, a, b);
+        } else {  // the vector crosses into the next row (T % 4 != 0)
+            const uint32_t c2 = c + 1 == C ? 0 : c + 1;
+            const float a2 = __ldg(ea + c2), b2 = __ldg(ieb + c2);
+            r.x = col + 0 < T ? snake1(v[i].x, a, b) : snake1(v[i].x, a2, b2);
+            r.y = col + 1 < T ? snake1(v[i].y, a, b) : snake1(v[i].y, a2, b2);
+            r.z = col + 2 < T ? snake1(v[i].z, a, b) : snake1(v[i].z, a2, b2);
+            r.w = snake1(v[i].w, a2, b2);
+        }
+        xv[k] = r;
+    }
+    if (blockIdx.x == 0 && threadIdx.x < total - 4 * nvec) {  // the last 1-3 elements
+        const uint32_t e = 4 * nvec + threadIdx.x;
+        const uint32_t row = fdiv(e, divT);
+        const uint32_t c = row - fdiv(row, divC) * C;
+        x[e] = snake1(x[e], __ldg(ea + c), __ldg(ieb + c));
+    }
+}
+
 }  // namespace
 }  // namespace lai
 
@@ -77,6 +184,15 @@ extern "C" int lai_snake_beta_f32(float *x, const float *exp_alpha, const float 
     const int64_t rows = batch * channels;
     if (rows == 0 || T == 0) return LAI_OK;
     const bool vec = lai::aligned16(x);
+    const int64_t total = rows * T;
+    if (vec && T >= 4 && total < (int64_t)0xffffffffll) {
+        const int64_t nvec = total / 4;
+        lai::snake_flat_kernel<<<lai::grid_for(nvec > 0 ? nvec : 1, lai::kSegVec), lai::kThreads, 0,
+                                 lai::as_stream(stream)>>>(
+            x, exp_alpha, inv_exp_beta, (uint32_t)total, (uint32_t)T, (uint32_t)channels,
+            lai::make_fastdiv((uint32_t)T), lai::make_fastdiv((uint32_t)channels));
+        return lai::launch_status();
+    }
     const int64_t nv_max = vec ? T / 4 + 1 : 0;
     const unsigned gx = lai::grid_for(nv_max, lai::kSegVec);
     const unsigned gy = (unsigned)(rows < 65535 ? rows : 65535);
