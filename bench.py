@@ -540,6 +540,19 @@ def run_ours(args) -> None:
                             "bytes_per_launch": k["bytes"], "launches": len(k["ms"])}
         if sum(k["ms"]) > dom_total:
             dominant, dom_total = name, sum(k["ms"])
+    # each distinct kernel also timed alone: `steps` back-to-back launches of it (outside
+    # the chain, so no neighbour's leftover L2 write-back is charged to it)
+    isolated = {}
+    if not args.no_isolate and not graph:
+        seen = {}
+        for j, name in enumerate(work.kernel_names):
+            seen.setdefault(name, j)
+        for name, j in seen.items():
+            iso_ms, _ = time_launches([launches[j]], args.steps, False)
+            avg_ms = iso_ms / args.steps
+            isolated[name] = {"avg_us": round(avg_ms * 1000, 2),
+                              "gbs": round(bpl[j] / (avg_ms / 1000.0) / 1e9, 1),
+                              "frac_of_peak": round(bpl[j] / (avg_ms / 1000.0) / 1e9 / peak, 4)}
     step_bytes = sum(bpl)
     step_gbs = step_bytes * args.steps / (total_ms / 1000.0) / 1e9
     d = per_kernel[dominant]
@@ -631,7 +644,7 @@ def run_ours(args) -> None:
         "data": "synthetic (seeded counter-based N(0,1) on device; norm weights 1+N(0,0.02))",
         "config": config,
         "hbm_gbs": round(step_gbs * (1 if strong else world), 1),
-        "per_kernel": per_kernel, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+        "per_kernel": per_kernel, "per_kernel_isolated": isolated, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
         "e2e_dropin_f32": e2e_f32,
         "gpu_launches": args.steps * launches_per_step,
         "clocks": clocks,
@@ -655,6 +668,8 @@ def main():
     ap.add_argument("--e2e-rows-bf16", type=int, default=65536, help="rows of the BF16 e2e")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-isolate", action="store_true",
+                    help="skip timing each kernel alone after the chain")
     ap.add_argument("--cpu-rows", type=int, default=8192)
     ap.add_argument("--cpu-batch", type=int, default=2,
                     help="SnakeBeta batch items in the CPU baseline sample (c4)")
