@@ -492,7 +492,7 @@ def run_ours(args) -> None:
             per = args.rows or cfg.tokens
             row0, row1 = rank * per, (rank + 1) * per
         rows = row1 - row0
-        work = runner.LayerChain(cfg, rows, row0=row0, seed=args.seed)
+        work = runner.LayerChain(cfg, rows, row0=row0, seed=args.seed, dtype=args.dtype)
     launches = work.launches(None)  # each launch goes to the current stream when called
     graph = args.graph == "on" or (args.graph == "auto" and not snake and rows <= 4096)
 
@@ -640,7 +640,7 @@ def run_ours(args) -> None:
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(max_ms / args.steps, 4), "higher_is_better": True,
         "scaling": "strong" if strong else "weak", "vs_baseline": None,
-        "dtype": "f32" if snake else "bf16",
+        "dtype": "f32" if snake else args.dtype,
         "data": "synthetic (seeded counter-based N(0,1) on device; norm weights 1+N(0,0.02))",
         "config": config,
         "hbm_gbs": round(step_gbs * (1 if strong else world), 1),
@@ -660,6 +660,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5"], default="c2")
     ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--dtype", choices=["bf16", "f32"], default="bf16",
+                    help="activation storage of the layer chain (f32: the drop-ins' type)")
     ap.add_argument("--rows", type=int, default=0,
                     help="rows per GPU instead of the config's batch (small profiling cases)")
     ap.add_argument("--graph", choices=["auto", "on", "off"], default="auto",

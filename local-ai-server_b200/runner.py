@@ -40,11 +40,11 @@ class LayerConfig:
     eps: float = 1e-6
     vocab: int = 0             # embedding table rows for the gather (0 = no gather)
 
-    # Algorithmic HBM bytes per token (BF16 storage), per kernel.
-    def bytes_per_token(self) -> dict[str, int]:
-        s = BF16_BYTES
+    # Algorithmic HBM bytes per token per kernel; s = activation element size
+    # (2 for BF16 storage, 4 for the FP32 drop-in path).
+    def bytes_per_token(self, s: int = BF16_BYTES) -> dict[str, int]:
         return {
-            "embed_gather": 2 * self.dim * s + 4,                  # table row, id, output row
+            "embed_gather": 2 * self.dim * 2 + 4,                  # BF16 table row, id, output row
             "add_rmsnorm": 4 * self.dim * s,                       # read x, delta; write x', y
             "qk_norm_rope": 2 * (self.n_q + self.n_kv) * self.head_dim * s,  # q, k in place
             "swiglu": 3 * self.inter * s,                          # read 2I, write I
@@ -54,8 +54,8 @@ class LayerConfig:
         k = ("add_rmsnorm", "qk_norm_rope", "add_rmsnorm", "swiglu")
         return (("embed_gather",) + k) if self.vocab else k
 
-    def step_bytes_per_token(self) -> int:
-        b = self.bytes_per_token()
+    def step_bytes_per_token(self, s: int = BF16_BYTES) -> int:
+        b = self.bytes_per_token(s)
         return sum(b[k] for k in self.kernels())
 
 
@@ -93,11 +93,12 @@ class LayerChain:
     """
 
     def __init__(self, cfg: LayerConfig, rows: int, row0: int = 0, seed: int = 1234,
-                 device: str = "cuda"):
+                 device: str = "cuda", dtype: str = "bf16"):
         import torch
         self.cfg, self.rows, self.row0, self.device = cfg, rows, row0, device
+        self.elem = 2 if dtype == "bf16" else 4
         T, D, I = rows, cfg.dim, cfg.inter
-        bf = torch.bfloat16
+        bf = torch.bfloat16 if dtype == "bf16" else torch.float32
         e = lambda *s, dt=bf: torch.empty(s, dtype=dt, device=device)  # noqa: E731
         self.x, self.d_attn, self.d_ffn, self.y = e(T, D), e(T, D), e(T, D), e(T, D)
         self.q, self.k = e(T, cfg.n_q * cfg.head_dim), e(T, cfg.n_kv * cfg.head_dim)
@@ -122,7 +123,7 @@ class LayerChain:
                                             device=device)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
         if cfg.vocab:
-            self.table = e(cfg.vocab, D)
+            self.table = e(cfg.vocab, D, dt=torch.bfloat16)
             lai.synth_normal(self.table, seed=seed + 300)
             self.ids = e(T, dt=torch.int32)
             lai.synth_uniform_i32(self.ids, seed=seed + 301, lo=0, hi=cfg.vocab, offset=row0)
@@ -132,7 +133,8 @@ class LayerChain:
     def launches(self, stream=None):
         """The step as a list of callables, one kernel launch each."""
         c = self.cfg
-        gather = [lambda: lai.call("lai_embed_gather_bf16", lai._p(self.emb), lai._p(self.table),
+        gfn = "lai_embed_gather_bf16" if self.elem == 2 else "lai_embed_gather_bf16_to_f32"
+        gather = [lambda: lai.call(gfn, lai._p(self.emb), lai._p(self.table),
                                    lai._p(self.ids), self.rows, c.dim, c.vocab,
                                    lai._p(self.err), lai._s(stream))] if c.vocab else []
         return gather + [
@@ -148,7 +150,9 @@ class LayerChain:
             f()
 
     def bytes_per_launch(self) -> list[int]:
-        b = self.cfg.bytes_per_token()
+        b = self.cfg.bytes_per_token(self.elem)
+        if self.elem == 4 and self.cfg.vocab:  # BF16 table row in, FP32 row out
+            b = dict(b, embed_gather=2 * self.cfg.dim + 4 * self.cfg.dim + 4)
         return [b[k] * self.rows for k in self.kernel_names]
 
 
