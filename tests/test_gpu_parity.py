@@ -148,6 +148,23 @@ def test_qk_norm_rope(dtype, rows, nq, nkv, hd, posmode):
         assert max_rel_err(f32(k), kr) <= TOL_F32
 
 
+def test_qk_result_does_not_depend_on_batch_size():
+    # one large call (persistent ring kernel) vs 100-row calls (warp-per-token kernel)
+    rows, nq, nkv, hd = 5000, 16, 8, 128
+    q, k = rand((rows, nq * hd), 27, torch.bfloat16), rand((rows, nkv * hd), 28, torch.bfloat16)
+    wq, wk = norm_w(hd, 29), norm_w(hd, 30)
+    cos_t, sin_t = table(4096, hd, 1e6)
+    g = torch.Generator(device="cpu").manual_seed(31)
+    pos = torch.randint(0, 4096, (rows,), generator=g, dtype=torch.int32).to(DEV)
+    q2, k2 = q.clone(), k.clone()
+    lai.qk_norm_rope(q, k, wq, wk, cos_t, sin_t, pos, nq, nkv, hd, 1e-6)
+    for r0 in range(0, rows, 100):
+        lai.qk_norm_rope(q2[r0:r0 + 100], k2[r0:r0 + 100], wq, wk, cos_t, sin_t, pos[r0:r0 + 100],
+                         nq, nkv, hd, 1e-6)
+    torch.cuda.synchronize()
+    assert torch.equal(q, q2) and torch.equal(k, k2)
+
+
 def test_rope_only_is_bit_exact_f32():
     # separately rounded products, same as the reference's scalar C: bit-exact
     q = rand((64, 16 * 128), 25)
