@@ -9,15 +9,17 @@
 // read once, written once in place); the [hd] weights and the table rows are
 // shared (L1/L2-resident) and not counted.
 //
-// Layout of the fast path. One warp owns one (token, q-or-k) segment. A head of
-// hd elements spans LPH = hd*s/16 lanes (16 for BF16 hd=128), each lane one
-// 16-byte vector, so a warp-wide 16-byte load covers 32/LPH heads and the whole
-// segment is `slots` such loads, issued back to back before any arithmetic. The
-// per-head sum of squares is an xor-shuffle tree over the LPH lanes; the RoPE
-// partner element (d <-> d + hd/2) sits in lane ^ LPH/2, one shuffle per element.
-// Each lane loads its hd/LPH weights and its cos/sin entries once per segment.
-// RoPE uses separately rounded products (no contraction), so with identical
-// inputs it reproduces the reference's scalar C bit for bit.
+// Kernels. BF16 with hd=128 (every Qwen3 decoder shape) runs qk_pipe_kernel: a
+// persistent kernel that streams token tiles through a shared-memory ring filled
+// by bulk async copies (described at the kernel), used for every batch size so a
+// token's result never depends on the batch it arrives in. FP32 and hd=64/256 run
+// qk_warp_kernel: one warp owns one (token, q-or-k) segment; a head of hd elements
+// spans LPH = hd*s/16 lanes, each lane one 16-byte vector, all of the segment's
+// loads issued before any arithmetic; the per-head sum of squares is an xor-shuffle
+// tree over the LPH lanes and the RoPE partner (d <-> d + hd/2) sits in lane ^ LPH/2.
+// The FP32 path uses separately rounded products (no contraction), so with
+// identical inputs it reproduces the reference's scalar C RoPE bit for bit.
+// Anything else (odd head counts per warp, unaligned rows) runs qk_generic_kernel.
 #include "bulk_copy.cuh"
 #include "lai_common.cuh"
 
