@@ -155,6 +155,28 @@ LAI_API int lai_embed_gather_bf16_to_f32(float *out, const lai_bf16 *table, cons
 LAI_API int lai_snake_beta_f32(float *x, const float *exp_alpha, const float *inv_exp_beta,
                        int64_t batch, int channels, int64_t T, lai_stream_t stream);
 
+/* ---- decode-time linear layers with the layer's elementwise ops fused in -------------------
+ * linear_bf16(out, in, W, M, K, N) computes out[M,N] = in[M,K] @ W[N,K]^T with BF16
+ * weights and FP32 activations (src/tts_native.c:66-79). At decode (M = 1,
+ * src/tts_native.c:637-667) the ops around it fuse in:
+ *   lai_gemv_bf16w_f32:          y = W @ x, or W @ RMSNorm(x; norm_w, eps) when norm_w is
+ *                                given  (qwen_rms_norm + q/k/v linear_bf16, :637-642)
+ *   lai_gemv_residual_bf16w_f32: x_res += W @ a  (o_proj / down_proj linear_bf16 +
+ *                                qwen_add_inplace, :658-659, :666-668)
+ *   lai_gemv_swiglu_bf16w_f32:   out[m,j] = silu(W_gu[2j].xn) * (W_gu[2j+1].xn), xn = x or
+ *                                RMSNorm(x)  (qwen_rms_norm + gate_up linear_bf16 +
+ *                                qwen_swiglu_multiply, :661-665; rows interleaved :149-161)
+ * x/a [M, K], outputs [M, N] (or [M, inter]); any M (passes of up to 8 rows); K*4 bytes
+ * <= 200 KiB. Outputs must not overlap the inputs.
+ */
+LAI_API int lai_gemv_bf16w_f32(float *y, const float *x, const float *norm_w, float eps,
+                               const lai_bf16 *W, int64_t M, int K, int N, lai_stream_t stream);
+LAI_API int lai_gemv_residual_bf16w_f32(float *x_res, const float *a, const lai_bf16 *W,
+                                        int64_t M, int K, int N, lai_stream_t stream);
+LAI_API int lai_gemv_swiglu_bf16w_f32(float *out, const float *x, const float *norm_w, float eps,
+                                      const lai_bf16 *W_gu, int64_t M, int K, int inter,
+                                      lai_stream_t stream);
+
 /* ---- seeded synthetic inputs (bench and test support) ------------------------------------
  * Counter-based: element i of a fill is a pure function of (seed, offset + i), so a
  * row-sharded fill on G devices equals the single-device fill of the same rows.

@@ -1,0 +1,250 @@
+// gemv.cu - decode-time linear layers with the layer's elementwise ops fused in.
+//
+// Reference: linear_bf16(ctx, out, in, W, M, K, N) = in[M,K] @ W[N,K]^T with BF16
+// weights and FP32 activations (src/tts_native.c:66-79), called at decode with M = 1
+// (talker_forward, src/tts_native.c:637-667) between the per-layer elementwise ops:
+//   qwen_rms_norm -> q/k/v projections            (:637-642)   -> lai_gemv_bf16w_f32 (norm prologue)
+//   o_proj -> qwen_add_inplace                    (:658-659)   -> lai_gemv_residual_bf16w_f32
+//   qwen_rms_norm -> gate_up -> qwen_swiglu_multiply (:661-665) -> lai_gemv_swiglu_bf16w_f32
+//   down_proj -> qwen_add_inplace                 (:666-668)   -> lai_gemv_residual_bf16w_f32
+// so the normalised, activated and projected vectors never make an HBM round trip.
+//
+// Roofline: HBM on the weights. Algorithmic bytes per launch: N*K*2 (weights, read
+// once) + M*(K + N)*4 (activations; the residual epilogue reads and writes its
+// output). At M <= 8 the FLOPs (2*M*N*K) are far below what the weights' bytes cost
+// at HBM speed, so CUDA cores are the right unit; a batched (large-M) projection
+// would be a tensor-core GEMM, which this file does not attempt.
+//
+// Layout: each CTA first stages the M input rows in shared memory (normalising
+// them when a norm weight is given: every CTA recomputes the norm of the <= 8 short
+// rows, cheaper than a separate launch and its HBM round trip). Each warp then owns
+// RPW output rows (2 for SwiGLU: the interleaved gate row 2j and up row 2j+1,
+// src/tts_native.c:149-161) and streams them in 16-byte vectors, 4 per lane in
+// flight, against the staged inputs; a warp-shuffle tree reduces each dot product.
+#include "lai_common.cuh"
+
+#include <math.h>
+
+namespace lai {
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxM = 8;
+constexpr int kUnrollK = 4;
+constexpr size_t kMaxSmem = 200 * 1024;
+
+enum Epi { kStore = 0, kResidual = 1, kSwiglu = 2 };
+
+// Stage x[M,K] in shared memory as FP32, normalised by RMSNorm when norm_w != NULL.
+template <int M>
+__device__ __forceinline__ void stage_inputs(float *xs, const float *x, const float *norm_w,
+                                             float eps, int K) {
+    __shared__ float red[M][kWarps];
+    float ss[M];
+#pragma unroll
+    for (int m = 0; m < M; m++) ss[m] = 0.f;
+    for (int i = threadIdx.x; i < K; i += kThreads) {
+#pragma unroll
+        for (int m = 0; m < M; m++) {
+            const float v = x[(size_t)m * K + i];
+            xs[m * K + i] = v;
+            ss[m] = fmaf(v, v, ss[m]);
+        }
+    }
+    if (norm_w) {
+        const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+        for (int m = 0; m < M; m++) {
+            const float t = group_sum<32>(ss[m]);
+            if (lane == 0) red[m][wid] = t;
+        }
+        __syncthreads();
+        float inv[M];
+#pragma unroll
+        for (int m = 0; m < M; m++) {
+            float t = 0.f;
+#pragma unroll
+            for (int w = 0; w < kWarps; w++) t += red[m][w];
+            inv[m] = 1.0f / sqrtf(t / (float)K + eps);
+        }
+        for (int i = threadIdx.x; i < K; i += kThreads) {
+            const float wi = norm_w[i];
+#pragma unroll
+            for (int m = 0; m < M; m++) xs[m * K + i] = __fmul_rn(__fmul_rn(xs[m * K + i], inv[m]), wi);
+        }
+    }
+    __syncthreads();
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
+    return __fmul_rn(__fmul_rn(g, sig), u);
+}
+
+// K % 8 == 0 and W 16-byte aligned: 16-byte weight vectors.
+template <int M, int EPI>
+__global__ void __launch_bounds__(kThreads)
+gemv_vec_kernel(float *y, const float *x, const float *norm_w, float eps,
+                const uint16_t *__restrict__ W, int K, int N, int ldy) {
+    constexpr int RPW = EPI == kSwiglu ? 2 : 1;
+    extern __shared__ __align__(16) float xs[];
+    stage_inputs<M>(xs, x, norm_w, eps, K);
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int row0 = (blockIdx.x * kWarps + warp) * RPW;
+    if (row0 >= N) return;
+    float acc[RPW][M];
+#pragma unroll
+    for (int r = 0; r < RPW; r++)
+#pragma unroll
+        for (int m = 0; m < M; m++) acc[r][m] = 0.f;
+
+    const uint16_t *wr[RPW];
+#pragma unroll
+    for (int r = 0; r < RPW; r++) wr[r] = W + (size_t)(row0 + r) * K;
+    for (int kb = 0; kb < K; kb += 256 * kUnrollK) {
+        uint4 wv[kUnrollK][RPW];
+#pragma unroll
+        for (int u = 0; u < kUnrollK; u++) {
+            const int k0 = kb + u * 256 + lane * 8;
+#pragma unroll
+            for (int r = 0; r < RPW; r++)
+                if (k0 < K) wv[u][r] = ld_stream(wr[r] + k0);
+        }
+#pragma unroll
+        for (int u = 0; u < kUnrollK; u++) {
+            const int k0 = kb + u * 256 + lane * 8;
+            if (k0 >= K) break;
+#pragma unroll
+            for (int m = 0; m < M; m++) {
+                const float4 a = *reinterpret_cast<const float4 *>(xs + m * K + k0);
+                const float4 b = *reinterpret_cast<const float4 *>(xs + m * K + k0 + 4);
+                const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int r = 0; r < RPW; r++) {
+                    float wf[8];
+                    unpack<uint16_t>(wv[u][r], wf);
+#pragma unroll
+                    for (int e = 0; e < 8; e++) acc[r][m] = fmaf(wf[e], xv[e], acc[r][m]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < RPW; r++)
+#pragma unroll
+        for (int m = 0; m < M; m++) acc[r][m] = group_sum<32>(acc[r][m]);
+    // lane m writes input m's result (all lanes hold every total after the tree)
+#pragma unroll
+    for (int m = 0; m < M; m++) {
+        if (lane != m) continue;
+        if constexpr (EPI == kStore) y[(size_t)m * ldy + row0] = acc[0][m];
+        if constexpr (EPI == kResidual) y[(size_t)m * ldy + row0] += acc[0][m];
+        if constexpr (EPI == kSwiglu) y[(size_t)m * ldy + row0 / 2] = silu_mul(acc[0][m], acc[1][m]);
+    }
+}
+
+// Any K / alignment: scalar weight reads, same structure.
+template <int M, int EPI>
+__global__ void __launch_bounds__(kThreads)
+gemv_scalar_kernel(float *y, const float *x, const float *norm_w, float eps, const uint16_t *W,
+                   int K, int N, int ldy) {
+    constexpr int RPW = EPI == kSwiglu ? 2 : 1;
+    extern __shared__ __align__(16) float xs[];
+    stage_inputs<M>(xs, x, norm_w, eps, K);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int row0 = (blockIdx.x * kWarps + warp) * RPW;
+    if (row0 >= N) return;
+    float acc[RPW][M] = {};
+    for (int k = lane; k < K; k += 32)
+#pragma unroll
+        for (int r = 0; r < RPW; r++) {
+            const float wf = to_f(W[(size_t)(row0 + r) * K + k]);
+#pragma unroll
+            for (int m = 0; m < M; m++) acc[r][m] = fmaf(wf, xs[m * K + k], acc[r][m]);
+        }
+#pragma unroll
+    for (int r = 0; r < RPW; r++)
+#pragma unroll
+        for (int m = 0; m < M; m++) acc[r][m] = group_sum<32>(acc[r][m]);
+#pragma unroll
+    for (int m = 0; m < M; m++) {
+        if (lane != m) continue;
+        if constexpr (EPI == kStore) y[(size_t)m * ldy + row0] = acc[0][m];
+        if constexpr (EPI == kResidual) y[(size_t)m * ldy + row0] += acc[0][m];
+        if constexpr (EPI == kSwiglu) y[(size_t)m * ldy + row0 / 2] = silu_mul(acc[0][m], acc[1][m]);
+    }
+}
+
+template <int M, int EPI>
+int launch(float *y, const float *x, const float *norm_w, float eps, const uint16_t *W, int K, int N,
+           int ldy, bool vec, cudaStream_t s) {
+    constexpr int RPW = EPI == kSwiglu ? 2 : 1;
+    const size_t smem = (size_t)M * K * sizeof(float);
+    auto kern = vec ? gemv_vec_kernel<M, EPI> : gemv_scalar_kernel<M, EPI>;
+    // opt in above 47 KiB: the default 48 KiB limit also covers the kernel's small static array
+    if (smem > 47 * 1024 &&
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+        cudaGetLastError();
+        return LAI_ERR_CUDA;
+    }
+    kern<<<grid_for(N, kWarps * RPW), kThreads, smem, s>>>(y, x, norm_w, eps, W, K, N, ldy);
+    return launch_status();
+}
+
+template <int EPI>
+int run(float *y, const float *x, const float *norm_w, float eps, const uint16_t *W, int64_t M,
+        int K, int N, lai_stream_t stream) {
+    if (!y || !x || !W || M < 0 || K <= 0 || N <= 0 || (EPI == kSwiglu && (N & 1)))
+        return LAI_ERR_INVALID;
+    if (M == 0) return LAI_OK;
+    const int ny = EPI == kSwiglu ? N / 2 : N;  // output row length
+    if (overlaps(y, (size_t)M * ny * 4, x, (size_t)M * K * 4)) return LAI_ERR_ALIAS;
+    // inputs per pass: as many rows (<= 8) as fit in shared memory
+    int64_t per = kMaxM;
+    while (per > 1 && (size_t)per * K * 4 > kMaxSmem) per /= 2;
+    if ((size_t)K * 4 > kMaxSmem) return LAI_ERR_TOOBIG;
+    const bool vec = K % 8 == 0 && aligned16(W);
+    cudaStream_t s = as_stream(stream);
+    for (int64_t m0 = 0; m0 < M;) {
+        const int64_t cap = M - m0 < per ? M - m0 : per;
+        const int take = cap >= 8 ? 8 : cap >= 4 ? 4 : cap >= 2 ? 2 : 1;  // rows this pass
+        float *yp = y + m0 * ny;
+        const float *xp = x + m0 * K;
+        int st;
+        switch (take) {
+            case 8: st = launch<8, EPI>(yp, xp, norm_w, eps, W, K, N, ny, vec, s); break;
+            case 4: st = launch<4, EPI>(yp, xp, norm_w, eps, W, K, N, ny, vec, s); break;
+            case 2: st = launch<2, EPI>(yp, xp, norm_w, eps, W, K, N, ny, vec, s); break;
+            default: st = launch<1, EPI>(yp, xp, norm_w, eps, W, K, N, ny, vec, s); break;
+        }
+        if (st != LAI_OK) return st;
+        m0 += take;
+    }
+    return LAI_OK;
+}
+
+}  // namespace
+}  // namespace lai
+
+extern "C" {
+
+int lai_gemv_bf16w_f32(float *y, const float *x, const float *norm_w, float eps, const lai_bf16 *W,
+                       int64_t M, int K, int N, lai_stream_t stream) {
+    return lai::run<lai::kStore>(y, x, norm_w, eps, W, M, K, N, stream);
+}
+
+int lai_gemv_residual_bf16w_f32(float *x_res, const float *a, const lai_bf16 *W, int64_t M, int K,
+                                int N, lai_stream_t stream) {
+    return lai::run<lai::kResidual>(x_res, a, nullptr, 0.f, W, M, K, N, stream);
+}
+
+int lai_gemv_swiglu_bf16w_f32(float *out, const float *x, const float *norm_w, float eps,
+                              const lai_bf16 *W_gu, int64_t M, int K, int inter,
+                              lai_stream_t stream) {
+    if (inter <= 0 || inter > (1 << 29)) return LAI_ERR_INVALID;
+    return lai::run<lai::kSwiglu>(out, x, norm_w, eps, W_gu, M, K, 2 * inter, stream);
+}
+
+}  // extern "C"

@@ -43,6 +43,9 @@ SIGNATURES: dict[str, tuple] = {
     "lai_embed_gather_bf16": (_i32, [_vp, _vp, _vp, _i64, _i32, _i64, _vp, _vp]),
     "lai_embed_gather_bf16_to_f32": (_i32, [_vp, _vp, _vp, _i64, _i32, _i64, _vp, _vp]),
     "lai_snake_beta_f32": (_i32, [_vp, _vp, _vp, _i64, _i32, _i64, _vp]),
+    "lai_gemv_bf16w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
+    "lai_gemv_residual_bf16w_f32": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _vp]),
+    "lai_gemv_swiglu_bf16w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
     "lai_synth_normal_bf16": (_i32, [_vp, _i64, _u64, _i64, _f32, _f32, _vp]),
     "lai_synth_normal_f32": (_i32, [_vp, _i64, _u64, _i64, _f32, _f32, _vp]),
     "lai_synth_uniform_i32": (_i32, [_vp, _i64, _u64, _i64, _i32, _i32, _vp]),
@@ -212,6 +215,34 @@ def snake_beta(x, ea, ieb, stream=None):
     b, c, t = (1, *x.shape) if x.dim() == 2 else x.shape
     call("lai_snake_beta_f32", _p(x), _p(ea), _p(ieb), b, c, t, _s(stream))
     return x
+
+
+def gemv(x, W, norm_w=None, eps=1e-6, y=None, stream=None):
+    """y[M,N] = W[N,K] @ (RMSNorm(x) if norm_w is given else x), x [M,K] FP32, W BF16."""
+    import torch
+    M, K = x.shape
+    N = W.shape[0]
+    y = torch.empty((M, N), dtype=torch.float32, device=x.device) if y is None else y
+    call("lai_gemv_bf16w_f32", _p(y), _p(x), _p(norm_w), eps, _p(W), M, K, N, _s(stream))
+    return y
+
+
+def gemv_residual(x_res, a, W, stream=None):
+    """x_res[M,N] += W[N,K] @ a[M,K]."""
+    call("lai_gemv_residual_bf16w_f32", _p(x_res), _p(a), _p(W), a.shape[0], a.shape[1],
+         W.shape[0], _s(stream))
+    return x_res
+
+
+def gemv_swiglu(x, W_gu, norm_w=None, eps=1e-6, out=None, stream=None):
+    """out[M,I] = silu(W_gu[2j].xn) * W_gu[2j+1].xn, W_gu [2I, K] rows interleaved."""
+    import torch
+    M, K = x.shape
+    inter = W_gu.shape[0] // 2
+    out = torch.empty((M, inter), dtype=torch.float32, device=x.device) if out is None else out
+    call("lai_gemv_swiglu_bf16w_f32", _p(out), _p(x), _p(norm_w), eps, _p(W_gu), M, K, inter,
+         _s(stream))
+    return out
 
 
 def synth_normal(t, seed, offset=0, mean=0.0, std=1.0, stream=None):

@@ -338,6 +338,24 @@ void oracle_swiglu_bf16(uint16_t *out, const uint16_t *gate_up, int seq, int int
 }
 
 /* ---------------------------------------------------------------------------
+ * linear_bf16 / qwen_linear_nobias_bf16 (src/tts_native.c:66-79; the CPU body is in
+ * the absent qwen-asr submodule): out[m,n] = sum_k in[m,k] * W[n,k], W row-major
+ * [N, K] BF16 widened exactly to F32 (bits << 16).
+ * ------------------------------------------------------------------------- */
+void oracle_linear_bf16(float *out, const float *in, const uint16_t *W, int M, int K, int N) {
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; n++) {
+        const uint16_t *wr = W + (size_t)n * K;
+        for (int m = 0; m < M; m++) {
+            const float *xr = in + (size_t)m * K;
+            acc_t s = 0;
+            for (int k = 0; k < K; k++) s += (acc_t)oracle_bf16_to_f32(wr[k]) * (acc_t)xr[k];
+            out[(size_t)m * N + n] = (float)s;
+        }
+    }
+}
+
+/* ---------------------------------------------------------------------------
  * Timed CPU reference: the elementwise ops of one decoder layer, FP32, in the
  * order talker_prefill calls them (src/tts_native.c:553-592), with the GEMM and
  * attention outputs supplied as inputs:

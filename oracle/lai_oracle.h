@@ -67,6 +67,9 @@ void oracle_qk_norm_rope_f32(float *q, float *k, const float *wq, const float *w
 void oracle_swiglu_bf16(uint16_t *out, const uint16_t *gate_up, int seq, int inter);
 void oracle_add_bf16(uint16_t *x, const uint16_t *y, int64_t n);
 
+/* ---- linear_bf16 (src/tts_native.c:66-79): out[M,N] = in[M,K] @ W[N,K]^T, W BF16 ---- */
+void oracle_linear_bf16(float *out, const float *in, const uint16_t *W, int M, int K, int N);
+
 /* ---- timed CPU reference: one decoder layer's elementwise chain, FP32, called in
  * the reference's own order (talker_prefill, src/tts_native.c:553-592) ---- */
 void oracle_layer_chain_f32(float *x, const float *delta_attn, const float *delta_ffn,

@@ -85,6 +85,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         "oracle_add_bf16": [_U16, _U16, _c_i64],
         "oracle_layer_chain_f32": [_F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _F,
                                    _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float],
+        "oracle_linear_bf16": [_F, _F, _U16, _c_int, _c_int, _c_int],
         "oracle_num_threads": [],
         "oracle_set_threads": [_c_int],
     }
@@ -297,6 +298,18 @@ def swiglu_bf16(gate_up, inter, lib=None):
     seq = g.shape[0]
     out = np.empty((seq, inter), np.uint16)
     lib.oracle_swiglu_bf16(ptr(out, _U16), ptr(g, _U16), seq, inter)
+    return out
+
+
+def linear_bf16(x, W, lib=None):
+    """out[M,N] = x[M,K] @ W[N,K]^T with W as BF16 bit patterns (linear_bf16's contract)."""
+    lib = lib or load()
+    x = np.ascontiguousarray(x, np.float32)
+    W = np.ascontiguousarray(W, np.uint16)
+    M, K = x.shape
+    N = W.shape[0]
+    out = np.empty((M, N), np.float32)
+    lib.oracle_linear_bf16(ptr(out), ptr(x), ptr(W, _U16), M, K, N)
     return out
 
 

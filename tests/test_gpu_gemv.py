@@ -1,0 +1,108 @@
+"""Decode-time fused linear layers against the oracle and a plain PyTorch FP32 matmul.
+
+linear_bf16 (src/tts_native.c:66-79) with the ops the decode step runs around it
+(src/tts_native.c:637-668): RMSNorm prologue, residual-add epilogue, SwiGLU epilogue
+over interleaved gate/up rows. FP32 tolerance: max |d| / max(1, |ref|) <= 1e-5.
+"""
+import numpy as np
+import pytest
+
+import lai
+import oracle
+from conftest import TOL_F32, max_rel_err
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+# (M, K, N): talker-0.6B q / k,v / o / gate_up / down projections, 1.7B gate_up,
+# small batches, multi-pass M, and shapes without a 16-byte weight path
+SHAPES = [(1, 1024, 2048), (1, 1024, 1024), (1, 2048, 1024), (1, 1024, 6144), (1, 3072, 1024),
+          (1, 2048, 12288), (3, 1024, 512), (8, 2048, 64), (13, 512, 96), (1, 100, 37),
+          (2, 6144, 2048)]
+
+
+def make(M, K, N, seed):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = torch.randn(M, K, generator=g)
+    W = (torch.randn(N, K, generator=g) / np.sqrt(K)).to(torch.bfloat16)
+    w = 1 + 0.02 * torch.randn(K, generator=g)
+    return x, W, w
+
+
+def wbits(W):
+    return W.view(torch.int16).numpy().view(np.uint16)
+
+
+@pytest.mark.parametrize("M,K,N", SHAPES)
+@pytest.mark.parametrize("norm", [False, True])
+def test_gemv(M, K, N, norm):
+    x, W, w = make(M, K, N, 1)
+    y = lai.gemv(x.to(DEV), W.to(DEV), w.to(DEV) if norm else None, 1e-6)
+    torch.cuda.synchronize()
+    xn = oracle.rms_norm(x.numpy(), w.numpy(), 1e-6) if norm else x.numpy()
+    assert max_rel_err(y.cpu().numpy(), oracle.linear_bf16(xn, wbits(W))) <= TOL_F32
+    ref = torch.from_numpy(xn).to(DEV) @ W.to(DEV).float().T  # plain FP32 matmul
+    assert max_rel_err(y.cpu().numpy(), ref.cpu().numpy()) <= TOL_F32
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 2048, 1024), (1, 3072, 1024), (4, 1024, 512), (9, 100, 37)])
+def test_gemv_residual(M, K, N):
+    a, W, _ = make(M, K, N, 2)
+    x = torch.randn(M, N)
+    xd = x.to(DEV)
+    lai.gemv_residual(xd, a.to(DEV), W.to(DEV))
+    torch.cuda.synchronize()
+    ref = oracle.add_inplace(x.numpy(), oracle.linear_bf16(a.numpy(), wbits(W)))
+    assert max_rel_err(xd.cpu().numpy(), ref) <= TOL_F32
+
+
+@pytest.mark.parametrize("M,K,inter", [(1, 1024, 3072), (1, 2048, 6144), (5, 512, 96), (1, 40, 7)])
+@pytest.mark.parametrize("norm", [False, True])
+def test_gemv_swiglu(M, K, inter, norm):
+    x, W, w = make(M, K, 2 * inter, 3)
+    out = lai.gemv_swiglu(x.to(DEV), W.to(DEV), w.to(DEV) if norm else None, 1e-6)
+    torch.cuda.synchronize()
+    xn = oracle.rms_norm(x.numpy(), w.numpy(), 1e-6) if norm else x.numpy()
+    gate_up = oracle.linear_bf16(xn, wbits(W))  # [M, 2I], interleaved as the fused weight is
+    assert max_rel_err(out.cpu().numpy(), oracle.swiglu_multiply(gate_up, inter)) <= TOL_F32
+
+
+def test_gemv_decode_layer_equals_unfused_sequence():
+    # one talker decode layer's linear + elementwise sequence (src/tts_native.c:637-668),
+    # fused kernels vs the unfused device kernels (RMSNorm, GEMV, SwiGLU, add)
+    D, I, QKV = 1024, 3072, 2048 + 2 * 1024
+    g = torch.Generator(device="cpu").manual_seed(4)
+    x = torch.randn(1, D, generator=g).to(DEV)
+    w_in, w_post = (1 + 0.02 * torch.randn(D, generator=g)).to(DEV), (1 + 0.02 * torch.randn(D, generator=g)).to(DEV)
+    Wqkv = (torch.randn(QKV, D, generator=g) / 32).to(torch.bfloat16).to(DEV)
+    Wo = (torch.randn(D, 2048, generator=g) / 45).to(torch.bfloat16).to(DEV)
+    Wgu = (torch.randn(2 * I, D, generator=g) / 32).to(torch.bfloat16).to(DEV)
+    Wd = (torch.randn(D, I, generator=g) / 55).to(torch.bfloat16).to(DEV)
+    attn = torch.randn(1, 2048, generator=g).to(DEV)  # stands in for attention's output
+    # fused
+    xf = x.clone()
+    qkv_f = lai.gemv(xf, Wqkv, w_in, 1e-6)
+    lai.gemv_residual(xf, attn, Wo)
+    act_f = lai.gemv_swiglu(xf, Wgu, w_post, 1e-6)
+    lai.gemv_residual(xf, act_f, Wd)
+    # unfused: every intermediate through HBM
+    xu = x.clone()
+    qkv_u = lai.gemv(lai.rmsnorm(xu, w_in, 1e-6), Wqkv)
+    lai.add(xu, lai.gemv(attn, Wo))
+    act_u = lai.swiglu(lai.gemv(lai.rmsnorm(xu, w_post, 1e-6), Wgu), I)
+    lai.add(xu, lai.gemv(act_u, Wd))
+    torch.cuda.synchronize()
+    for f, u in [(qkv_f, qkv_u), (act_f, act_u), (xf, xu)]:
+        assert max_rel_err(f.cpu().numpy(), u.cpu().numpy()) <= TOL_F32
+
+
+def test_gemv_argument_checks():
+    L = lai.load()
+    import ctypes
+    P = ctypes.c_void_p(256)
+    assert L.lai_gemv_bf16w_f32(P, P, None, 1e-6, P, 1, 64, 8, None) == lai.LAI_ERR_ALIAS
+    assert L.lai_gemv_swiglu_bf16w_f32(P, ctypes.c_void_p(1 << 20), None, 1e-6, P, 1, 64, 0,
+                                       None) == lai.LAI_ERR_INVALID
+    assert L.lai_gemv_bf16w_f32(P, ctypes.c_void_p(1 << 30), None, 1e-6, P, 1, 60000, 8,
+                                None) == lai.LAI_ERR_TOOBIG
