@@ -159,6 +159,47 @@ def cpu_chain_rate(cfg, rows: int, min_seconds: float, steps: int | None = None,
             "seconds": el}
 
 
+def cpu_decode_rate(cfg, min_seconds: float) -> dict:
+    """One layer's decode linear path on host cores (oracle/_build/liblai_cpuref.so: the
+    restated linear_bf16 and elementwise ops, OpenMP), M = cfg.m tokens per pass."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle
+    lib = oracle.load("liblai_cpuref.so")
+    lib.oracle_set_threads(len(os.sched_getaffinity(0)))
+    rng = np.random.default_rng(8)
+    D, I, M = cfg.dim, cfg.inter, cfg.m
+    qkv_n = cfg.q_dim + 2 * cfg.kv_dim
+    wb = lambda n, k: oracle.f32_to_bf16_bits((rng.standard_normal((n, k)) / np.sqrt(k)).astype(np.float32))  # noqa: E731
+    Wqkv, Wo, Wgu, Wd = wb(qkv_n, D), wb(D, cfg.q_dim), wb(2 * I, D), wb(D, I)
+    x = rng.standard_normal((M, D), dtype=np.float32)
+    attn = rng.standard_normal((M, cfg.q_dim), dtype=np.float32)
+    w_in = (1 + 0.02 * rng.standard_normal(D)).astype(np.float32)
+    w_post = (1 + 0.02 * rng.standard_normal(D)).astype(np.float32)
+
+    def step():
+        xn = oracle.rms_norm(x, w_in, cfg.eps, lib)
+        oracle.linear_bf16(xn, Wqkv, lib)
+        o = oracle.linear_bf16(attn, Wo, lib)
+        x2 = oracle.add_inplace(x, o, lib)
+        gu = oracle.linear_bf16(oracle.rms_norm(x2, w_post, cfg.eps, lib), Wgu, lib)
+        act = oracle.swiglu_multiply(gu, I, lib)
+        oracle.add_inplace(x2, oracle.linear_bf16(act, Wd, lib), lib)
+
+    step()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        step()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    # one layer per pass (its weights stay cache-warm, favouring the CPU); a decode
+    # step runs cfg.layers of them
+    return {"rows_per_s": M * n / el / cfg.layers, "threads": lib.oracle_num_threads(),
+            "passes": n, "seconds": el}
+
+
 def cpu_model() -> str:
     try:
         with open("/proc/cpuinfo") as f:
@@ -408,13 +449,14 @@ def e2e_snake_dropin(stages, batch: int, steps: int, warmup: int) -> dict:
 
 
 # ------------------------------------------------------------------ our path
-def time_launches(launches, steps: int, graph: bool):
+def time_launches(launches, steps: int, graph: bool, names=None):
     """Time `steps` steps. Returns (total ms, per-launch lists of ms).
 
     Direct mode records a CUDA event after every launch on the launching stream.
-    Graph mode (launch-bound small configs) replays one captured graph per step for
-    the total, and, for the per-launch times, one graph per kernel holding 20
-    back-to-back launches of it (a kernel reading the same L2-resident inputs)."""
+    Graph mode (launch-bound configs) replays one captured graph per step for the
+    total; for the per-launch times, every kernel name gets one graph holding all of
+    that name's launches of a step (each layer's weights read once per replay),
+    replayed until about `steps` launches, and its launches share the average."""
     import torch
     stream = torch.cuda.current_stream()
     nk = len(launches)
@@ -435,14 +477,6 @@ def time_launches(launches, steps: int, graph: bool):
     with torch.cuda.graph(g):
         for f in launches:
             f()
-    reps = 20  # launches of one kernel per graph, so a replay's launch cost is amortised
-    singles = []
-    for f in launches:
-        gs = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gs):
-            for _ in range(reps):
-                f()
-        singles.append(gs)
     g.replay()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -452,16 +486,30 @@ def time_launches(launches, steps: int, graph: bool):
     b.record(stream)
     torch.cuda.synchronize()
     total = a.elapsed_time(b)
-    per = []
-    n_rep = max(1, steps // reps)
-    for gs in singles:
+    names = list(names) if names is not None else [str(j) for j in range(nk)]
+    groups: dict[str, list[int]] = {}
+    for j, n in enumerate(names):
+        groups.setdefault(n, []).append(j)
+    per = [None] * nk
+    for idx in groups.values():
+        reps = max(1, 20 // len(idx))  # ~20 launches per replay
+        gs = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gs):
+            for _ in range(reps):
+                for j in idx:
+                    launches[j]()
         gs.replay()
+        torch.cuda.synchronize()
+        n_rep = max(1, steps * len(idx) // (reps * len(idx)) // 1)
+        n_rep = max(1, min(n_rep, 2000))
         a.record(stream)
         for _ in range(n_rep):
             gs.replay()
         b.record(stream)
         torch.cuda.synchronize()
-        per.append([a.elapsed_time(b) / (n_rep * reps)] * steps)
+        avg = a.elapsed_time(b) / (n_rep * reps * len(idx))
+        for j in idx:
+            per[j] = [avg] * steps
     return total, per
 
 
@@ -479,11 +527,16 @@ def run_ours(args) -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     snake = args.config == "c4"
+    decode = args.config in runner.DECODE_CONFIGS
     strong = args.config == "c5"
     if snake:
         work = runner.SnakeSweep(seed=args.seed + 1000 * rank)
         rows = sum(work.rows_per_launch())
         cfg = None
+    elif decode:
+        cfg = runner.DECODE_CONFIGS[args.config]
+        work = runner.DecodeLinear(cfg, seed=args.seed + 1000 * rank)
+        rows = cfg.m
     else:
         cfg = runner.CONFIGS[args.config]
         if strong:
@@ -495,6 +548,15 @@ def run_ours(args) -> None:
         work = runner.LayerChain(cfg, rows, row0=row0, seed=args.seed, dtype=args.dtype)
     launches = work.launches(None)  # each launch goes to the current stream when called
     graph = args.graph == "on" or (args.graph == "auto" and not snake and rows <= 4096)
+    unfused_us = None
+    if decode:  # the same step as separate kernels around cuBLAS GEMMs, for comparison
+        ul = work.unfused_library_launches()
+        for _ in range(args.warmup):
+            for f in ul:
+                f()
+        torch.cuda.synchronize()
+        u_ms, _ = time_launches(ul, args.steps, graph, [str(j) for j in range(len(ul))])
+        unfused_us = round(1000.0 * u_ms / args.steps, 2)
 
     for _ in range(args.warmup):
         for f in launches:
@@ -509,7 +571,7 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
     sampler.start()
     time.sleep(0.3)  # let the sampler attach before the timed region
-    total_ms, per = time_launches(launches, args.steps, graph)
+    total_ms, per = time_launches(launches, args.steps, graph, work.kernel_names)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -518,14 +580,14 @@ def run_ours(args) -> None:
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     max_ms = float(t.item())
-    if not snake:
+    if not snake and not decode:
         assert int(work.err.item()) == 0, "an id or position was out of range in the chain"
 
     peak, peak_kind = measured_peaks()
     total_rows = cfg.tokens if strong else rows * world
     value = total_rows * args.steps / (max_ms / 1000.0)
     bpl = work.bytes_per_launch()
-    rows_pl = work.rows_per_launch() if snake else [rows] * len(bpl)
+    rows_pl = work.rows_per_launch() if (snake or decode) else [rows] * len(bpl)
     kernels = {}
     for j, name in enumerate(work.kernel_names):
         k = kernels.setdefault(name, {"ms": [], "bytes": bpl[j], "rows": rows_pl[j]})
@@ -571,7 +633,7 @@ def run_ours(args) -> None:
         return float(et.item())
 
     e2e = e2e_f32 = None
-    if not args.no_e2e:
+    if not args.no_e2e and not decode:
         del work, launches  # free the device-resident workload before the staged runs
         torch.cuda.empty_cache()
         if snake:
@@ -598,7 +660,14 @@ def run_ours(args) -> None:
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        if snake:
+        if decode:
+            r = cpu_decode_rate(cfg, args.cpu_seconds)
+            cpu = {"value": round(r["rows_per_s"], 1), "unit": "rows/s", "cores": r["threads"],
+                   "kind": "port",
+                   "sample": f"{r['passes']} single-layer linear paths ({r['seconds']:.1f} s, "
+                             f"rate divided by {cfg.layers} layers): RMSNorm, linear_bf16 x4, "
+                             f"SwiGLU, adds, FP32, host {cpu_model()}"}
+        elif snake:
             r = cpu_snake_rate(runner.SNAKE_STAGES, args.cpu_batch, args.cpu_seconds)
             cpu = {"value": round(r["rows_per_s"], 1), "unit": "rows/s", "cores": r["threads"],
                    "kind": "reference",
@@ -617,7 +686,17 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
     if rank != 0:
         return
-    if snake:
+    if decode:
+        config = {"workload": f"{cfg.name}: the decode step's linear path through "
+                              f"{cfg.layers} layers (per layer RMSNorm+QKV GEMV, O GEMV+residual, "
+                              "RMSNorm+gate/up GEMV+SwiGLU, down GEMV+residual)",
+                  "config": args.config, "m": cfg.m, "dim": cfg.dim, "ffn": cfg.inter,
+                  "layers": cfg.layers, "bytes_per_step": step_bytes,
+                  "timing": "CUDA graph replay" if graph else "direct launches",
+                  "unfused_library_us_per_step": unfused_us,
+                  "l2": f"weights larger than L2 ({step_bytes / 1e9:.2f} GB per step)"}
+        launches_per_step = 4 * cfg.layers
+    elif snake:
         config = {"workload": "vocoder SnakeBeta over the BigVGAN stages, FP32 in place",
                   "config": "c4", "stages": runner.SNAKE_STAGES, "batch": runner.SNAKE_BATCH,
                   "rows": "channel rows (batch x channels) per sweep",
@@ -640,7 +719,7 @@ def run_ours(args) -> None:
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(max_ms / args.steps, 4), "higher_is_better": True,
         "scaling": "strong" if strong else "weak", "vs_baseline": None,
-        "dtype": "f32" if snake else args.dtype,
+        "dtype": "f32" if snake else ("bf16 weights / f32 activations" if decode else args.dtype),
         "data": "synthetic (seeded counter-based N(0,1) on device; norm weights 1+N(0,0.02))",
         "config": config,
         "hbm_gbs": round(step_gbs * (1 if strong else world), 1),
@@ -658,7 +737,7 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5"], default="c2")
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "g1", "g2"], default="c2")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--dtype", choices=["bf16", "f32"], default="bf16",
                     help="activation storage of the layer chain (f32: the drop-ins' type)")

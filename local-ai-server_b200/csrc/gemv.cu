@@ -15,11 +15,16 @@
 // at HBM speed, so CUDA cores are the right unit; a batched (large-M) projection
 // would be a tensor-core GEMM, which this file does not attempt.
 //
+// Launch: programmatic dependent launch. A GEMV issues its first weight loads before
+// it waits (griddepcontrol.wait) for the previous kernel's results, and lets the next
+// kernel start launching once its own weight stream has been read, so one layer's
+// weight stream overlaps the previous kernel's tail.
+//
 // Layout: each CTA first stages the M input rows in shared memory (normalising
 // them when a norm weight is given: every CTA recomputes the norm of the <= 8 short
 // rows, cheaper than a separate launch and its HBM round trip). Each warp then owns
 // RPW output rows (2 for SwiGLU: the interleaved gate row 2j and up row 2j+1,
-// src/tts_native.c:149-161) and streams them in 16-byte vectors, 4 per lane in
+// src/tts_native.c:149-161) and streams them in 16-byte vectors, 8 per lane in
 // flight, against the staged inputs; a warp-shuffle tree reduces each dot product.
 #include "lai_common.cuh"
 
@@ -31,10 +36,18 @@ namespace {
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxM = 8;
-constexpr int kUnrollK = 4;
+constexpr int kUnrollK = 8;  // 16-byte weight vectors in flight per lane per row (K <= 2048: one trip)
 constexpr size_t kMaxSmem = 200 * 1024;
 
 enum Epi { kStore = 0, kResidual = 1, kSwiglu = 2 };
+
+// Programmatic dependent launch: let the next kernel on the stream start launching
+// now, and wait for the previous kernel's results only where they are first read.
+// Without the launch attribute both are no-ops.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait_prior() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // Stage x[M,K] in shared memory as FP32, normalised by RMSNorm when norm_w != NULL.
 template <int M>
@@ -89,28 +102,43 @@ gemv_vec_kernel(float *y, const float *x, const float *norm_w, float eps,
                 const uint16_t *__restrict__ W, int K, int N, int ldy) {
     constexpr int RPW = EPI == kSwiglu ? 2 : 1;
     extern __shared__ __align__(16) float xs[];
-    stage_inputs<M>(xs, x, norm_w, eps, K);
-
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int row0 = (blockIdx.x * kWarps + warp) * RPW;
-    if (row0 >= N) return;
+    const bool active = row0 < N;
+    const uint16_t *wr[RPW];
+#pragma unroll
+    for (int r = 0; r < RPW; r++) wr[r] = W + (size_t)(active ? row0 + r : 0) * K;
+    // the weights depend on nothing earlier on the stream: their first chunk is in
+    // flight before this kernel waits for the previous one and stages its inputs
+    uint4 wv[kUnrollK][RPW];
+#pragma unroll
+    for (int u = 0; u < kUnrollK; u++) {
+        const int k0 = u * 256 + lane * 8;
+#pragma unroll
+        for (int r = 0; r < RPW; r++)
+            if (active && k0 < K) wv[u][r] = ld_stream(wr[r] + k0);
+    }
+    pdl_wait_prior();
+    stage_inputs<M>(xs, x, norm_w, eps, K);
+    if (!active) {
+        pdl_launch_dependents();
+        return;
+    }
     float acc[RPW][M];
 #pragma unroll
     for (int r = 0; r < RPW; r++)
 #pragma unroll
         for (int m = 0; m < M; m++) acc[r][m] = 0.f;
 
-    const uint16_t *wr[RPW];
-#pragma unroll
-    for (int r = 0; r < RPW; r++) wr[r] = W + (size_t)(row0 + r) * K;
     for (int kb = 0; kb < K; kb += 256 * kUnrollK) {
-        uint4 wv[kUnrollK][RPW];
+        if (kb > 0) {
 #pragma unroll
-        for (int u = 0; u < kUnrollK; u++) {
-            const int k0 = kb + u * 256 + lane * 8;
+            for (int u = 0; u < kUnrollK; u++) {
+                const int k0 = kb + u * 256 + lane * 8;
 #pragma unroll
-            for (int r = 0; r < RPW; r++)
-                if (k0 < K) wv[u][r] = ld_stream(wr[r] + k0);
+                for (int r = 0; r < RPW; r++)
+                    if (k0 < K) wv[u][r] = ld_stream(wr[r] + k0);
+            }
         }
 #pragma unroll
         for (int u = 0; u < kUnrollK; u++) {
@@ -131,6 +159,9 @@ gemv_vec_kernel(float *y, const float *x, const float *norm_w, float eps,
             }
         }
     }
+    // this warp's weights are read: the next kernel may start launching (its CTAs
+    // stream their own weights, then wait for this grid before reading activations)
+    pdl_launch_dependents();
 #pragma unroll
     for (int r = 0; r < RPW; r++)
 #pragma unroll
@@ -152,6 +183,8 @@ gemv_scalar_kernel(float *y, const float *x, const float *norm_w, float eps, con
                    int K, int N, int ldy) {
     constexpr int RPW = EPI == kSwiglu ? 2 : 1;
     extern __shared__ __align__(16) float xs[];
+    pdl_launch_dependents();
+    pdl_wait_prior();
     stage_inputs<M>(xs, x, norm_w, eps, K);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int row0 = (blockIdx.x * kWarps + warp) * RPW;
@@ -189,7 +222,20 @@ int launch(float *y, const float *x, const float *norm_w, float eps, const uint1
         cudaGetLastError();
         return LAI_ERR_CUDA;
     }
-    kern<<<grid_for(N, kWarps * RPW), kThreads, smem, s>>>(y, x, norm_w, eps, W, K, N, ldy);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid_for(N, kWarps * RPW));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see pdl_wait_prior
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, y, x, norm_w, eps, W, K, N, ldy) != cudaSuccess) {
+        cudaGetLastError();
+        return LAI_ERR_CUDA;
+    }
     return launch_status();
 }
 

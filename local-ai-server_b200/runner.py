@@ -71,6 +71,24 @@ CONFIGS = {
                       pos_period=1024),
 }
 
+# Decode-step linear path of one layer (fused GEMVs), M tokens per step.
+@dataclasses.dataclass(frozen=True)
+class DecodeConfig:
+    name: str
+    dim: int
+    inter: int
+    q_dim: int = 16 * 128
+    kv_dim: int = 8 * 128
+    m: int = 1
+    layers: int = 28  # talker depth (src/tts_native.h:28): a step streams every layer's weights
+    eps: float = 1e-6
+
+
+DECODE_CONFIGS = {
+    "g1": DecodeConfig("qwen3-tts-0.6b-talker-decode-linear", dim=1024, inter=3072),
+    "g2": DecodeConfig("qwen3-1.7b-decode-linear", dim=2048, inter=6144),
+}
+
 # Vocoder SnakeBeta stages (channels, T) x batch 8 (config 4).
 SNAKE_STAGES = [(1536, 2000), (768, 16000), (384, 48000), (192, 96000), (96, 192000)]
 SNAKE_BATCH = 8
@@ -186,3 +204,90 @@ class SnakeSweep:
 
     def rows_per_launch(self) -> list[int]:
         return [self.batch * c for c, _ in self.stages]
+
+
+class DecodeLinear:
+    """The decode step's linear path through `layers` decoder layers
+    (src/tts_native.c:637-668 per layer), fused per layer: RMSNorm+QKV GEMV, O GEMV +
+    residual, RMSNorm + gate/up GEMV + SwiGLU, down GEMV + residual. FP32 activations,
+    BF16 weights (q, k, v rows concatenated into one matrix, gate/up rows interleaved
+    as the reference's fused weight), every layer its own weights so a step streams
+    them all from HBM. The attention output is a fixed stand-in (attention is not part
+    of this path)."""
+
+    def __init__(self, cfg: DecodeConfig, seed: int = 4321, device: str = "cuda"):
+        import torch
+        self.cfg, self.rows = cfg, cfg.m
+        D, I, M = cfg.dim, cfg.inter, cfg.m
+        self.qkv_n = cfg.q_dim + 2 * cfg.kv_dim
+        f32, bf = torch.float32, torch.bfloat16
+
+        def w(n, k, s):
+            t = torch.empty((n, k), dtype=bf, device=device)
+            return lai.synth_normal(t, seed=seed + s, std=float(k) ** -0.5)
+
+        L = cfg.layers
+        self.Wqkv = [w(self.qkv_n, D, 10 * l + 1) for l in range(L)]
+        self.Wo = [w(D, cfg.q_dim, 10 * l + 2) for l in range(L)]
+        self.Wgu = [w(2 * I, D, 10 * l + 3) for l in range(L)]
+        self.Wd = [w(D, I, 10 * l + 4) for l in range(L)]
+        self.w_in = lai.synth_normal(torch.empty(D, dtype=f32, device=device), seed=seed + 5,
+                                     mean=1.0, std=0.02)
+        self.w_post = lai.synth_normal(torch.empty(D, dtype=f32, device=device), seed=seed + 6,
+                                       mean=1.0, std=0.02)
+        self.x = lai.synth_normal(torch.empty((M, D), dtype=f32, device=device), seed=seed + 7)
+        self.attn = lai.synth_normal(torch.empty((M, cfg.q_dim), dtype=f32, device=device),
+                                     seed=seed + 8)
+        self.qkv = torch.empty((M, self.qkv_n), dtype=f32, device=device)
+        self.act = torch.empty((M, I), dtype=f32, device=device)
+        self.kernel_names = ("rmsnorm_qkv_gemv", "o_gemv_residual", "rmsnorm_gate_up_gemv_swiglu",
+                             "down_gemv_residual") * L
+
+    def launches(self, stream=None):
+        c = self.cfg
+        out = []
+        for l in range(c.layers):
+            out += [
+                lambda l=l: lai.gemv(self.x, self.Wqkv[l], self.w_in, c.eps, y=self.qkv, stream=stream),
+                lambda l=l: lai.gemv_residual(self.x, self.attn, self.Wo[l], stream=stream),
+                lambda l=l: lai.gemv_swiglu(self.x, self.Wgu[l], self.w_post, c.eps, out=self.act,
+                                            stream=stream),
+                lambda l=l: lai.gemv_residual(self.x, self.act, self.Wd[l], stream=stream),
+            ]
+        return out
+
+    def unfused_library_launches(self):
+        """The same step as separate kernels around cuBLAS BF16 GEMMs (torch), every
+        intermediate through HBM: the library baseline the fusion is measured against."""
+        import torch
+        import torch.nn.functional as F
+        c = self.cfg
+
+        def layer(l):
+            def qkv():
+                xn = lai.rmsnorm(self.x, self.w_in, c.eps)
+                self.qkv.copy_(F.linear(xn.to(torch.bfloat16), self.Wqkv[l]))
+
+            def o():
+                lai.add(self.x, F.linear(self.attn.to(torch.bfloat16), self.Wo[l]).float())
+
+            def gu():
+                xn = lai.rmsnorm(self.x, self.w_post, c.eps)
+                lai.swiglu(F.linear(xn.to(torch.bfloat16), self.Wgu[l]).float(), c.inter,
+                           out=self.act)
+
+            def down():
+                lai.add(self.x, F.linear(self.act.to(torch.bfloat16), self.Wd[l]).float())
+            return [qkv, o, gu, down]
+        return [f for l in range(c.layers) for f in layer(l)]
+
+    def bytes_per_launch(self) -> list[int]:
+        c, M = self.cfg, self.cfg.m
+        D, I = c.dim, c.inter
+        return [self.qkv_n * D * 2 + M * D * 4 + M * self.qkv_n * 4 + D * 4,
+                D * c.q_dim * 2 + M * c.q_dim * 4 + 2 * M * D * 4,
+                2 * I * D * 2 + M * D * 4 + M * I * 4 + D * 4,
+                D * I * 2 + M * I * 4 + 2 * M * D * 4] * c.layers
+
+    def rows_per_launch(self) -> list[int]:
+        return [self.cfg.m] * 4 * self.cfg.layers
