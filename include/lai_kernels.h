@@ -177,6 +177,39 @@ LAI_API int lai_gemv_swiglu_bf16w_f32(float *out, const float *x, const float *n
                                       const lai_bf16 *W_gu, int64_t M, int K, int inter,
                                       lai_stream_t stream);
 
+/* ---- vocoder BigVGAN ResUnits on tensor cores ------------------------------------------------
+ * run_resunit(x, ru, C, T, scratch) (src/tts_vocoder.c:540-583) for n_units consecutive
+ * units, as tts_vocoder_run calls them per block (src/tts_vocoder.c:725-728):
+ *   x = x + conv1x1(snake2(conv1d_causal(snake1(x), dilation))) with the biases
+ * Activations are CHANNELS-LAST [batch, T, C] F32 (the reference stores [C, T]; convert
+ * with lai_voc_transpose_f32). Snake parameters are pre-exponentiated as the reference
+ * loads them (src/tts_vocoder.c:221-227). conv1_w / conv2_w are lai_voc_pack_conv_f32
+ * images of the reference weights [C, C, 7] / [C, C, 1] (16-byte aligned).
+ * scratch: 4 * batch * T * C floats (16-byte aligned, not overlapping x).
+ * passes = 3: F32-faithful products (TF32 hi/lo split); passes = 1: plain TF32.
+ * C must be a multiple of 32. A stalled pipeline wait ORs LAI_DEVERR_TIMEOUT into *err.
+ */
+typedef struct {
+    const float *snake1_ea, *snake1_ieb; /* [C] exp(alpha), 1/exp(beta) of act1 */
+    const float *conv1_w;                /* packed, 2 * 7 * C * C floats */
+    const float *conv1_b;                /* [C] */
+    const float *snake2_ea, *snake2_ieb; /* [C] of act2 */
+    const float *conv2_w;                /* packed, 2 * C * C floats */
+    const float *conv2_b;                /* [C] */
+    int dilation;                        /* 1, 3, 9 in the reference (src/tts_vocoder.c:269) */
+} lai_voc_resunit_t;
+
+LAI_API int lai_voc_resunits_f32(float *x, float *scratch, const lai_voc_resunit_t *units,
+                                 int n_units, int batch, int channels, int T, int passes,
+                                 int *err, lai_stream_t stream);
+/* dst (2 * c_out * c_in * kernel floats) <- reference conv weight w [c_out, c_in, kernel]
+ * regrouped per tap as [2][kernel][c_out][c_in]: TF32 high parts, then the remainders. */
+LAI_API int lai_voc_pack_conv_f32(float *dst, const float *w, int c_out, int c_in, int kernel,
+                                  lai_stream_t stream);
+/* dst[b][j][i] = src[b][i][j] for src [batch, rows, cols]: [C, T] <-> [T, C]. */
+LAI_API int lai_voc_transpose_f32(float *dst, const float *src, int batch, int rows, int cols,
+                                  lai_stream_t stream);
+
 /* ---- seeded synthetic inputs (bench and test support) ------------------------------------
  * Counter-based: element i of a fill is a pure function of (seed, offset + i), so a
  * row-sharded fill on G devices equals the single-device fill of the same rows.

@@ -15,6 +15,7 @@
 // rows waste no threads. snake_kernel (unaligned base, T < 4, or >= 2^32 elements)
 // walks rows on grid y and 16 KiB segments on grid x with scalar head and tail.
 #include "lai_common.cuh"
+#include "snake_math.cuh"
 
 namespace lai {
 namespace {
@@ -22,56 +23,6 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kUnroll = 4;
 constexpr int kSegVec = kThreads * kUnroll;  // float4 vectors per CTA segment
-
-// sin^2(y) without a full sin, from textbook pieces:
-//  * Cody-Waite reduction (W. J. Cody, W. Waite, "Software Manual for the Elementary
-//    Functions", 1980): m = rint(y * 2/pi), r = y - m*pi/2 with pi/2 split into three
-//    floats so that r keeps ~full precision for |m| < 2^16;
-//  * sin^2 y = (1 - cos 2y) / 2 and cos 2y = cos(m*pi + 2r) = (-1)^m cos t, t = 2r,
-//    |t| <= pi/2;
-//  * cos t by its Taylor series through t^12 (coefficients 1/(2k)!): the remainder is
-//    below (pi/2)^14 / 14! < 6.4e-9 on |t| <= pi/2, under float resolution.
-// About 14 FP instructions instead of a full-range sinf plus a square. Arguments
-// beyond 65536 in magnitude (and inf/NaN) take CUDA's sinf. The absolute error of
-// sin^2 stays within a few 1e-8 (tests/test_gpu_parity.py bounds it against the
-// reference's own compiled voc_snake_beta).
-// pi/2 = hi + mid + lo, each the float nearest to what remains (computed in 80-digit
-// decimal arithmetic); 2/pi rounded to float.
-constexpr float kTwoOverPi = 0.6366197466850281f;
-constexpr float kPiO2Hi = 1.5707963705062866f;
-constexpr float kPiO2Mid = -4.371138828673793e-08f;
-constexpr float kPiO2Lo = -1.7151245100058819e-15f;
-
-__device__ __forceinline__ float sin2_fast(float y) {
-    const float m = rintf(y * kTwoOverPi);
-    float r = fmaf(-m, kPiO2Hi, y);
-    r = fmaf(-m, kPiO2Mid, r);
-    r = fmaf(-m, kPiO2Lo, r);
-    const float t = 2.0f * r;
-    const float u = t * t;
-    float c = 1.0f / 479001600.0f;              // 1/12!
-    c = fmaf(c, u, -1.0f / 3628800.0f);         // 1/10!
-    c = fmaf(c, u, 1.0f / 40320.0f);            // 1/8!
-    c = fmaf(c, u, -1.0f / 720.0f);             // 1/6!
-    c = fmaf(c, u, 1.0f / 24.0f);               // 1/4!
-    c = fmaf(c, u, -0.5f);                      // 1/2!
-    c = fmaf(c, u, 1.0f);
-    const int odd = static_cast<int>(m) & 1;
-    c = odd ? -c : c;                           // cos 2y
-    return fmaf(-0.5f, c, 0.5f);                // (1 - cos 2y) / 2
-}
-
-__device__ __forceinline__ float snake1(float x, float ea, float ieb) {
-    const float y = __fmul_rn(ea, x);
-    float s2;
-    if (fabsf(y) <= 65536.0f) {
-        s2 = sin2_fast(y);
-    } else {  // huge or non-finite argument: full-range sinf
-        const float s = sinf(y);
-        s2 = s * s;
-    }
-    return fmaf(ieb, s2, x);  // x + ieb * sin^2(ea * x)
-}
 
 __global__ void __launch_bounds__(kThreads)
 snake_kernel(float *x, const float *__restrict__ ea, const float *__restrict__ ieb,

@@ -46,6 +46,9 @@ SIGNATURES: dict[str, tuple] = {
     "lai_gemv_bf16w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
     "lai_gemv_residual_bf16w_f32": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _vp]),
     "lai_gemv_swiglu_bf16w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
+    "lai_voc_resunits_f32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
+    "lai_voc_pack_conv_f32": (_i32, [_vp, _vp, _i32, _i32, _i32, _vp]),
+    "lai_voc_transpose_f32": (_i32, [_vp, _vp, _i32, _i32, _i32, _vp]),
     "lai_synth_normal_bf16": (_i32, [_vp, _i64, _u64, _i64, _f32, _f32, _vp]),
     "lai_synth_normal_f32": (_i32, [_vp, _i64, _u64, _i64, _f32, _f32, _vp]),
     "lai_synth_uniform_i32": (_i32, [_vp, _i64, _u64, _i64, _i32, _i32, _vp]),
@@ -243,6 +246,59 @@ def gemv_swiglu(x, W_gu, norm_w=None, eps=1e-6, out=None, stream=None):
     call("lai_gemv_swiglu_bf16w_f32", _p(out), _p(x), _p(norm_w), eps, _p(W_gu), M, K, inter,
          _s(stream))
     return out
+
+
+class VocResUnit(ctypes.Structure):
+    """lai_voc_resunit_t: device pointers of one ResUnit's parameters."""
+    _fields_ = [("snake1_ea", _vp), ("snake1_ieb", _vp), ("conv1_w", _vp), ("conv1_b", _vp),
+                ("snake2_ea", _vp), ("snake2_ieb", _vp), ("conv2_w", _vp), ("conv2_b", _vp),
+                ("dilation", _i32)]
+
+
+def voc_pack_conv(w, stream=None):
+    """Reference conv weight [c_out, c_in, k] -> packed [2, k, c_out, c_in] (TF32 hi, lo)."""
+    import torch
+    c_out, c_in, k = w.shape
+    dst = torch.empty((2, k, c_out, c_in), dtype=torch.float32, device=w.device)
+    call("lai_voc_pack_conv_f32", _p(dst), _p(w), c_out, c_in, k, _s(stream))
+    return dst
+
+
+def voc_transpose(src, stream=None):
+    """[batch, R, C] -> [batch, C, R] (a 2-D tensor is batch 1)."""
+    import torch
+    b, r, c = (1, *src.shape) if src.dim() == 2 else src.shape
+    shape = (c, r) if src.dim() == 2 else (b, c, r)
+    dst = torch.empty(shape, dtype=torch.float32, device=src.device)
+    call("lai_voc_transpose_f32", _p(dst), _p(src), b, r, c, _s(stream))
+    return dst
+
+
+def voc_units(params, packed=None):
+    """params: list of dicts (ea1, ieb1, w1 [C,C,7], b1, ea2, ieb2, w2 [C,C,1], b2, dilation)
+    of CUDA tensors. Returns (ctypes array of lai_voc_resunit_t, tensors kept alive)."""
+    keep = []
+    arr = (VocResUnit * len(params))()
+    for i, p in enumerate(params):
+        w1 = packed[i][0] if packed else voc_pack_conv(p["w1"])
+        w2 = packed[i][1] if packed else voc_pack_conv(p["w2"])
+        keep += [w1, w2]
+        arr[i] = VocResUnit(p["ea1"].data_ptr(), p["ieb1"].data_ptr(), w1.data_ptr(),
+                            p["b1"].data_ptr(), p["ea2"].data_ptr(), p["ieb2"].data_ptr(),
+                            w2.data_ptr(), p["b2"].data_ptr(), int(p["dilation"]))
+    return arr, keep
+
+
+def voc_resunits(x, units, scratch=None, passes=3, err=None, stream=None):
+    """In place on x [batch, T, C] (channels-last); units from voc_units()."""
+    import torch
+    b, t, c = (1, *x.shape) if x.dim() == 2 else x.shape
+    if scratch is None:
+        scratch = torch.empty(4 * b * t * c, dtype=torch.float32, device=x.device)
+    arr = units[0] if isinstance(units, tuple) else units
+    call("lai_voc_resunits_f32", _p(x), _p(scratch), ctypes.cast(arr, _vp), len(arr), b, c, t,
+         passes, _p(err), _s(stream))
+    return x
 
 
 def synth_normal(t, seed, offset=0, mean=0.0, std=1.0, stream=None):

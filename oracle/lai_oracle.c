@@ -356,6 +356,53 @@ void oracle_linear_bf16(float *out, const float *in, const uint16_t *W, int M, i
 }
 
 /* ---------------------------------------------------------------------------
+ * Causal dilated conv1d, channels-first, groups == 1 (voc_conv1d_causal,
+ * src/tts_vocoder_ops.c:44-147): the input is left-padded with
+ * dilation * (kernel - 1) zeros, so tap k of output t reads
+ * in[c, t - (kernel - 1 - k) * dilation] (zero before t = 0); weight
+ * [c_out, c_in, kernel] row-major; bias may be NULL. The reference sums through
+ * im2col and SGEMM in float; this restatement sums each output in acc_t.
+ * ------------------------------------------------------------------------- */
+void oracle_voc_conv1d_causal(float *out, const float *in, const float *w, const float *bias,
+                              int c_in, int c_out, int T, int kernel, int dilation) {
+#pragma omp parallel for schedule(static)
+    for (int o = 0; o < c_out; o++) {
+        const float *wo = w + (size_t)o * c_in * kernel;
+        for (int t = 0; t < T; t++) {
+            acc_t s = 0;
+            for (int c = 0; c < c_in; c++) {
+                const float *row = in + (size_t)c * T;
+                for (int k = 0; k < kernel; k++) {
+                    int src = t - (kernel - 1 - k) * dilation;
+                    if (src >= 0) s += (acc_t)wo[(size_t)c * kernel + k] * (acc_t)row[src];
+                }
+            }
+            out[(size_t)o * T + t] = (float)s + (bias ? bias[o] : 0.0f);
+        }
+    }
+}
+
+/* ---------------------------------------------------------------------------
+ * BigVGAN ResUnit (run_resunit, src/tts_vocoder.c:540-583), in place on x [C, T]:
+ *   r = x ; x = snake1(x) ; h = conv1(x) (k = 7, dilation d) + b1 ; h = snake2(h)
+ *   x = conv2(h) (k = 1) + b2 + r
+ * Snake parameters are pre-exponentiated (src/tts_vocoder.c:221-227).
+ * scratch: 2 * C * T floats (the residual copy and h).
+ * ------------------------------------------------------------------------- */
+void oracle_voc_resunit(float *x, const float *ea1, const float *ieb1, const float *w1,
+                        const float *b1, const float *ea2, const float *ieb2, const float *w2,
+                        const float *b2, int C, int T, int dilation, float *scratch) {
+    size_t cT = (size_t)C * T;
+    float *res = scratch, *h = scratch + cT;
+    memcpy(res, x, cT * sizeof(float));
+    oracle_snake_beta(x, ea1, ieb1, C, T);
+    oracle_voc_conv1d_causal(h, x, w1, b1, C, C, T, 7, dilation);
+    oracle_snake_beta(h, ea2, ieb2, C, T);
+    oracle_voc_conv1d_causal(x, h, w2, b2, C, C, T, 1, 1);
+    for (size_t i = 0; i < cT; i++) x[i] += res[i];
+}
+
+/* ---------------------------------------------------------------------------
  * Timed CPU reference: the elementwise ops of one decoder layer, FP32, in the
  * order talker_prefill calls them (src/tts_native.c:553-592), with the GEMM and
  * attention outputs supplied as inputs:

@@ -70,6 +70,15 @@ void oracle_add_bf16(uint16_t *x, const uint16_t *y, int64_t n);
 /* ---- linear_bf16 (src/tts_native.c:66-79): out[M,N] = in[M,K] @ W[N,K]^T, W BF16 ---- */
 void oracle_linear_bf16(float *out, const float *in, const uint16_t *W, int M, int K, int N);
 
+/* ---- vocoder ResUnit, channels-first [C, T] F32 as the reference stores it ----
+ * voc_conv1d_causal (src/tts_vocoder_ops.c:44-147, groups == 1): w [c_out, c_in, kernel] */
+void oracle_voc_conv1d_causal(float *out, const float *in, const float *w, const float *bias,
+                              int c_in, int c_out, int T, int kernel, int dilation);
+/* run_resunit (src/tts_vocoder.c:540-583), in place on x; scratch holds 2 * C * T floats */
+void oracle_voc_resunit(float *x, const float *ea1, const float *ieb1, const float *w1,
+                        const float *b1, const float *ea2, const float *ieb2, const float *w2,
+                        const float *b2, int C, int T, int dilation, float *scratch);
+
 /* ---- timed CPU reference: one decoder layer's elementwise chain, FP32, called in
  * the reference's own order (talker_prefill, src/tts_native.c:553-592) ---- */
 void oracle_layer_chain_f32(float *x, const float *delta_attn, const float *delta_ffn,

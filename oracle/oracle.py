@@ -51,6 +51,9 @@ def load(name: str = "liblai_oracle.so") -> ctypes.CDLL:
     else:
         lib.voc_snake_beta.argtypes = [_F, _F, _F, _c_int, _c_int]
         lib.voc_snake_beta.restype = None
+        lib.voc_conv1d_causal.argtypes = [_F, _F, _F, _F, _c_int, _c_int, _c_int, _c_int,
+                                          _c_int, _c_int, _F]
+        lib.voc_conv1d_causal.restype = None
     _LIBS[name] = lib
     return lib
 
@@ -86,6 +89,8 @@ def _declare(lib: ctypes.CDLL) -> None:
         "oracle_layer_chain_f32": [_F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _F,
                                    _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float],
         "oracle_linear_bf16": [_F, _F, _U16, _c_int, _c_int, _c_int],
+        "oracle_voc_conv1d_causal": [_F, _F, _F, _F, _c_int, _c_int, _c_int, _c_int, _c_int],
+        "oracle_voc_resunit": [_F, _F, _F, _F, _F, _F, _F, _F, _F, _c_int, _c_int, _c_int, _F],
         "oracle_num_threads": [],
         "oracle_set_threads": [_c_int],
     }
@@ -318,3 +323,68 @@ def add_bf16(x, y, lib=None):
     r = np.array(x, np.uint16, copy=True, order="C")
     lib.oracle_add_bf16(ptr(r, _U16), ptr(np.ascontiguousarray(y, np.uint16), _U16), r.size)
     return r
+
+
+# ---- vocoder ResUnit, channels-first [C, T] (per batch item) ----
+
+def voc_conv1d_causal(x, w, bias, dilation=1, lib=None):
+    """out[o,t] = bias[o] + sum_{c,k} w[o,c,k] * x[c, t - (K-1-k)*dilation] (zero before 0)."""
+    lib = lib or load()
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    c_out, c_in, kernel = w.shape
+    T = x.shape[-1]
+    out = np.empty((c_out, T), np.float32)
+    lib.oracle_voc_conv1d_causal(ptr(out), ptr(x), ptr(w),
+                                 ptr(None if bias is None else np.ascontiguousarray(bias, np.float32)),
+                                 c_in, c_out, T, kernel, dilation)
+    return out
+
+
+def ref_voc_conv1d_causal(x, w, bias, dilation=1, build: str = "scalar"):
+    """The reference's own voc_conv1d_causal (compiled from src/tts_vocoder_ops.c, no BLAS:
+    left padding, im2col, float dot products)."""
+    lib = load(f"libvoc_ref_{build}.so")
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    c_out, c_in, kernel = w.shape
+    T = x.shape[-1]
+    pad = dilation * (kernel - 1)
+    scratch = np.empty(c_in * (T + pad) + c_in * kernel * T, np.float32)
+    out = np.empty((c_out, T), np.float32)
+    lib.voc_conv1d_causal(ptr(out), ptr(x), ptr(w),
+                          ptr(None if bias is None else np.ascontiguousarray(bias, np.float32)),
+                          c_in, c_out, T, kernel, dilation, 1, ptr(scratch))
+    return out
+
+
+def voc_resunit(x, p, dilation, lib=None):
+    """run_resunit on x [C, T] (or [B, C, T]); p: dict of ea1, ieb1, w1 [C,C,7], b1, ea2,
+    ieb2, w2 [C,C,1], b2 in the reference's layouts."""
+    lib = lib or load()
+    y = np.array(x, np.float32, copy=True, order="C")
+    C, T = y.shape[-2], y.shape[-1]
+    rows = y.reshape(-1, C, T)
+    scratch = np.empty(2 * C * T, np.float32)
+    q = {k: np.ascontiguousarray(v, np.float32) for k, v in p.items()}
+    for b in range(rows.shape[0]):
+        lib.oracle_voc_resunit(ptr(rows[b]), ptr(q["ea1"]), ptr(q["ieb1"]), ptr(q["w1"]),
+                               ptr(q["b1"]), ptr(q["ea2"]), ptr(q["ieb2"]), ptr(q["w2"]),
+                               ptr(q["b2"]), C, T, dilation, ptr(scratch))
+    return y
+
+
+def ref_voc_resunit(x, p, dilation, build: str = "scalar"):
+    """run_resunit's sequence (src/tts_vocoder.c:540-583) built from the reference's own
+    compiled voc_snake_beta and voc_conv1d_causal (the k = 1 conv through the same
+    function, which equals its naive pointwise loop term for term)."""
+    y = np.array(x, np.float32, copy=True, order="C")
+    C, T = y.shape[-2], y.shape[-1]
+    rows = y.reshape(-1, C, T)
+    for b in range(rows.shape[0]):
+        r = rows[b].copy()
+        s = ref_snake_beta(rows[b], p["ea1"], p["ieb1"], build)
+        h = ref_voc_conv1d_causal(s, p["w1"], p["b1"], dilation, build)
+        h = ref_snake_beta(h, p["ea2"], p["ieb2"], build)
+        rows[b] = ref_voc_conv1d_causal(h, p["w2"], p["b2"], 1, build) + r
+    return y

@@ -117,3 +117,38 @@ def test_fused_oracles_equal_reference_call_sequences():
     qo, _ = oracle.qk_norm_rope(q, None, wq, None, c, s, None, 4, 0, 128, 1e-6, bf16=False)
     ref = oracle.apply_rope_neox(oracle.rms_norm_per_head(q, wq, 4, 128, 1e-6), c, s, 4, 128)
     assert np.array_equal(qo, ref)
+
+
+@pytest.mark.skipif(not oracle.have_ref(), reason="oracle/_ref not built (reference absent)")
+@pytest.mark.parametrize("c_in,c_out,T,k,d", [(24, 16, 50, 7, 1), (16, 32, 40, 7, 3),
+                                               (8, 8, 30, 7, 9), (32, 24, 17, 1, 1)])
+def test_conv1d_restatement_against_reference_build(c_in, c_out, T, k, d):
+    # voc_conv1d_causal compiled from the reference source (no BLAS: pad, im2col, float
+    # dot products) against the restatement's double sums: F32 round-off only
+    rng = np.random.default_rng(c_in + T)
+    x = rng.standard_normal((c_in, T)).astype(np.float32)
+    w = (rng.standard_normal((c_out, c_in, k)) / np.sqrt(c_in * k)).astype(np.float32)
+    b = rng.normal(0, 0.1, c_out).astype(np.float32)
+    got = oracle.voc_conv1d_causal(x, w, b, d)
+    ref = oracle.ref_voc_conv1d_causal(x, w, b, d)
+    assert np.max(np.abs(got - ref)) / max(1.0, np.max(np.abs(ref))) <= 1e-5
+    # causality: output t never sees inputs after t
+    x2 = x.copy()
+    x2[:, T // 2:] += 1.0
+    got2 = oracle.voc_conv1d_causal(x2, w, b, d)
+    assert np.array_equal(got[:, : T // 2], got2[:, : T // 2])
+
+
+@pytest.mark.skipif(not oracle.have_ref(), reason="oracle/_ref not built (reference absent)")
+def test_resunit_restatement_against_reference_functions():
+    rng = np.random.default_rng(9)
+    C, T = 32, 90
+    p = {"ea1": np.exp(rng.normal(0, 0.1, C)), "ieb1": 1 / np.exp(rng.normal(0, 0.1, C)),
+         "w1": rng.standard_normal((C, C, 7)) / np.sqrt(7 * C), "b1": rng.normal(0, 0.1, C),
+         "ea2": np.exp(rng.normal(0, 0.1, C)), "ieb2": 1 / np.exp(rng.normal(0, 0.1, C)),
+         "w2": rng.standard_normal((C, C, 1)) / np.sqrt(C), "b2": rng.normal(0, 0.1, C)}
+    p = {k: v.astype(np.float32) for k, v in p.items()}
+    x = rng.standard_normal((2, C, T)).astype(np.float32)
+    for d in (1, 3, 9):
+        got, ref = oracle.voc_resunit(x, p, d), oracle.ref_voc_resunit(x, p, d)
+        assert np.max(np.abs(got - ref)) / max(1.0, np.max(np.abs(ref))) <= 1e-5
