@@ -2,7 +2,7 @@
 """Benchmark of the B200 per-layer kernels (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c1|c3|c4|c5] [--graph auto|on|off]
+                    [--config c2|c1|c3|c4|c5|g1|g2|v1] [--graph auto|on|off]
 
 A step is one decoder layer's elementwise chain over one batch (runner.LayerChain):
 fused residual-add+RMSNorm, fused q/k RMSNorm+RoPE, fused residual-add+RMSNorm,
@@ -12,6 +12,10 @@ FFN 6144), per GPU: N GPUs each run their own 65536-token batch, no collective
 ("scaling": "weak"). --config c5 runs the 2M-token chain split across the N GPUs
 instead ("strong"). `value` is tokens/s over all GPUs; the roofline object
 reports the dominant kernel's achieved HBM GB/s from live CUDA events.
+
+--config g1/g2 time the decode step's fused linear path (GEMVs with RMSNorm prologue
+and residual / SwiGLU epilogues) through 28 layers; --config v1 times the vocoder's
+12 BigVGAN ResUnits on tcgen05 tensor cores (roofline: TF32 tensor throughput).
 
 --impl reference times the reference's CPU implementation of the same chain
 (the oracle restatement of the absent qwen-asr C, built at the reference's
@@ -258,6 +262,268 @@ def cpu_snake_rate(stages, batch: int, min_seconds: float, steps: int | None = N
             "rows": rows}
 
 
+def cpu_resunit_rate(stages, batch: int, min_seconds: float, sample_t: int = 4000,
+                     steps: int | None = None, warmup: int = 1) -> dict:
+    """The reference's ResUnit (run_resunit, src/tts_vocoder.c:540-583) on host cores as
+    its USE_BLAS build runs it: voc_snake_beta from the reference's own AVX2 build
+    (oracle/_ref) over channel ranges on a thread pool, and voc_conv1d_causal's SGEMM
+    formulation (src/tts_vocoder_ops.c:83-125: left padding, then im2col + one SGEMM
+    when the column buffer holds <= 1e7 floats at the stage's FULL length, else one
+    SGEMM per tap) through numpy's OpenBLAS on all host cores. Each stage runs its three
+    units on `sample_t` time rows of one batch item; the measured per-row rate of each
+    stage is scaled to the whole step (batch x T rows per stage)."""
+    import concurrent.futures as cf
+
+    import numpy as np
+    from threadpoolctl import threadpool_limits
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle
+    import runner
+    snake = oracle.load("libvoc_ref_avx2.so").voc_snake_beta
+    F = ctypes.POINTER(ctypes.c_float)
+    nthreads = len(os.sched_getaffinity(0))
+    rng = np.random.default_rng(8)
+
+    def f32(a):
+        return np.ascontiguousarray(a, dtype=np.float32)
+
+    data = []
+    for c, t_full in stages:
+        units = []
+        for d in runner.RESUNIT_DILATIONS:
+            units.append({"ea1": f32(np.exp(rng.normal(0, 0.1, c))),
+                          "ieb1": f32(1 / np.exp(rng.normal(0, 0.1, c))),
+                          "w1": f32(rng.standard_normal((c, c * 7)) / np.sqrt(7 * c)),
+                          "b1": f32(rng.normal(0, 0.1, (c, 1))),
+                          "ea2": f32(np.exp(rng.normal(0, 0.1, c))),
+                          "ieb2": f32(1 / np.exp(rng.normal(0, 0.1, c))),
+                          "w2": f32(rng.standard_normal((c, c)) / np.sqrt(c)),
+                          "b2": f32(rng.normal(0, 0.1, (c, 1))), "d": d})
+        for u in units:  # per-tap weight slices, extracted once like the reference's w_slice
+            u["w1_taps"] = [f32(u["w1"].reshape(c, c, 7)[:, :, k]) for k in range(7)]
+        data.append((c, t_full, units, f32(rng.standard_normal((c, sample_t)))))
+
+    with cf.ThreadPoolExecutor(nthreads) as pool, threadpool_limits(nthreads):
+        def snake_mt(x, ea, ieb):
+            c, t = x.shape
+            per = max(1, -(-c // nthreads))
+            list(pool.map(lambda c0: snake(x[c0].ctypes.data_as(F), ea[c0:].ctypes.data_as(F),
+                                           ieb[c0:].ctypes.data_as(F), min(per, c - c0), t),
+                          range(0, c, per)))
+
+        def conv7(x, u, im2col):
+            c, t = x.shape
+            pad = 6 * u["d"]
+            padded = np.zeros((c, t + pad), np.float32)
+            padded[:, pad:] = x
+            if im2col:
+                cols = np.empty((c, 7, t), np.float32)
+                for k in range(7):
+                    cols[:, k, :] = padded[:, k * u["d"]:k * u["d"] + t]
+                out = u["w1"] @ cols.reshape(c * 7, t)
+            else:
+                out = u["w1_taps"][0] @ padded[:, :t]
+                for k in range(1, 7):
+                    out += u["w1_taps"][k] @ padded[:, k * u["d"]:k * u["d"] + t]
+            out += u["b1"]
+            return out
+
+        def stage_seconds(c, t_full, units, x0):
+            im2col = c * 7 * t_full <= 10_000_000
+            x = x0.copy()
+            t0 = time.perf_counter()
+            for u in units:
+                r = x.copy()
+                snake_mt(x, u["ea1"], u["ieb1"])
+                h = conv7(x, u, im2col)
+                snake_mt(h, u["ea2"], u["ieb2"])
+                x = u["w2"] @ h
+                x += u["b2"]
+                x += r
+            return time.perf_counter() - t0
+
+        for _ in range(warmup):
+            for st in data:
+                stage_seconds(*st)
+        n, secs = 0, [0.0] * len(data)
+        t_start = time.perf_counter()
+        while True:
+            for i, st in enumerate(data):
+                secs[i] += stage_seconds(*st)
+            n += 1
+            el = time.perf_counter() - t_start
+            if (steps is not None and n >= steps) or (steps is None and el >= min_seconds):
+                break
+    step_s = sum(batch * t_full * (secs[i] / n) / sample_t
+                 for i, (c, t_full, _, _) in enumerate(data))
+    rows = sum(batch * t for _, t in stages)
+    return {"rows_per_s": rows / step_s, "step_seconds": step_s, "threads": nthreads,
+            "passes": n, "seconds": el, "sample_t": sample_t,
+            "per_stage_rows_per_s": {f"{c}x{t}": round(sample_t * n / secs[i], 1)
+                                     for i, (c, t, _, _) in enumerate(data)}}
+
+
+def tf32_peak_tflops(n: int = 8192, reps: int = 10) -> float:
+    """cuBLAS FP32 GEMM with TF32 tensor cores (torch.matmul, allow_tf32), n^3, best of
+    `reps`: the live denominator for the tensor-bound ResUnit roofline."""
+    import torch
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        a = torch.randn(n, n, device="cuda")
+        b = torch.randn(n, n, device="cuda")
+        c = a @ b
+        best = float("inf")
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for _ in range(reps):
+            e0.record()
+            torch.matmul(a, b, out=c)
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        del a, b, c
+        torch.cuda.empty_cache()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    return 2.0 * n ** 3 / (best / 1000.0) / 1e12
+
+
+def run_resunits(args) -> None:
+    """--config v1: the vocoder's 12 BigVGAN ResUnits on tensor cores (runner.VocResUnits)."""
+    import torch
+    import torch.distributed as dist
+    import runner
+
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local = env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    tf32 = tf32_peak_tflops()
+    stages = [(c, t // args.t_div) for c, t in runner.RESUNIT_STAGES]
+    work = runner.VocResUnits(stages=stages, passes=args.passes, seed=args.seed + 1000 * rank)
+    launches = work.launches(None)
+    for _ in range(args.warmup):
+        for f in launches:
+            f()
+    torch.cuda.synchronize()
+    phys = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+    sampler = ClockSampler(phys[local] if local < len(phys) and phys[local] != "" else str(local))
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    total_ms, per = time_launches(launches, args.steps, False, work.kernel_names)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    t = torch.tensor([total_ms], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    assert int(work.err.item()) == 0, "a pipeline wait timed out in the ResUnit kernels"
+
+    hbm_peak, hbm_kind = measured_peaks()
+    rows_step = sum(work.rows_per_launch())
+    value = rows_step * world * args.steps / (max_ms / 1000.0)
+    per_kernel, dominant, dom_total = {}, None, -1.0
+    flops, nbytes, rows_pl = work.flops_per_launch(), work.bytes_per_launch(), work.rows_per_launch()
+    for j, name in enumerate(work.kernel_names):
+        avg_ms = statistics.mean(per[j])
+        tfs = flops[j] / (avg_ms / 1000.0) / 1e12
+        per_kernel[name] = {"avg_us": round(avg_ms * 1000, 1), "tflops": round(tfs, 1),
+                            "tensor_tflops_issued": round(tfs * args.passes, 1),
+                            "frac_of_tf32_peak": round(tfs / tf32, 4),
+                            "hbm_gbs": round(nbytes[j] / (avg_ms / 1000.0) / 1e9, 1),
+                            "rows_per_s": round(rows_pl[j] / (avg_ms / 1000.0), 1),
+                            "flops_per_launch": flops[j], "bytes_per_launch": nbytes[j]}
+        if sum(per[j]) > dom_total:
+            dominant, dom_total = name, sum(per[j])
+    d = per_kernel[dominant]
+    step_tflops = sum(flops) * args.steps / (total_ms / 1000.0) / 1e12
+    roofline = {"bound": "tensor", "kernel": dominant, "achieved": d["tflops"], "peak": round(tf32, 1),
+                "unit": "TFLOP/s", "frac": round(d["tflops"] / tf32, 4),
+                "peak_source": "cuBLAS FP32 GEMM on TF32 tensor cores (8192^3, best of 10), "
+                               "measured in this run",
+                "achieved_is": "FP32 convolution flops as the reference counts them; with "
+                               f"passes={args.passes} the tensor cores issue {args.passes}x that",
+                "traffic": load_traffic().get(f"{dominant}@v1"),
+                "algorithmic_bytes_per_launch": d["bytes_per_launch"],
+                "hbm_gbs": d["hbm_gbs"], "hbm_frac": round(d["hbm_gbs"] / hbm_peak, 4),
+                "step_tflops": round(step_tflops, 1), "step_frac": round(step_tflops / tf32, 4)}
+
+    e2e = None
+    if not args.no_e2e:
+        # the public device API around host data: per stage, pinned host x -> device,
+        # three ResUnits, device -> host, every step
+        hosts = [x.cpu().pin_memory() for x in work.x]
+        nb = sum(h.numel() * 4 for h in hosts)
+        stream = torch.cuda.current_stream()
+
+        def e2e_step():
+            for i, f in enumerate(launches):
+                work.x[i].copy_(hosts[i], non_blocking=True)
+                f()
+                hosts[i].copy_(work.x[i], non_blocking=True)
+        e2e_step()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        b.record(stream)
+        torch.cuda.synchronize()
+        et = torch.tensor([a.elapsed_time(b)], device="cuda", dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        e2e = {"value": round(rows_step * world * args.e2e_steps / (float(et.item()) / 1000.0), 1),
+               "unit": "rows/s", "h2d_bytes_per_step": nb, "d2h_bytes_per_step": nb,
+               "dtype": "f32", "api": "lai_voc_resunits_f32 per stage with x copied from and "
+                                       "back to pinned host memory inside the timed region"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        r = cpu_resunit_rate(stages, runner.RESUNIT_BATCH, args.cpu_seconds)
+        cpu = {"value": round(r["rows_per_s"], 1), "unit": "rows/s", "cores": r["threads"],
+               "kind": "port",
+               "sample": f"{r['passes']} sweeps of the 4 stages x 3 units on {r['sample_t']} "
+                         f"time rows of one item ({r['seconds']:.1f} s), scaled per stage to "
+                         f"batch {runner.RESUNIT_BATCH}: the reference's USE_BLAS ResUnit "
+                         "(its AVX2 voc_snake_beta + SGEMM convolutions through numpy's "
+                         f"OpenBLAS), host {cpu_model()}",
+               "per_stage_rows_per_s": r["per_stage_rows_per_s"]}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "rows/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded counter-based N(0,1) on device; conv weights N(0,1)/sqrt(fan_in))",
+        "config": {"workload": "vocoder BigVGAN ResUnits (snake1, dilated causal conv k=7, "
+                               "snake2, conv k=1, residual) x 3 per block, 4 blocks, FP32 "
+                               "channels-last on tcgen05 tensor cores",
+                   "config": "v1", "stages": stages, "batch": runner.RESUNIT_BATCH,
+                   "dilations": list(runner.RESUNIT_DILATIONS), "passes": args.passes,
+                   "precision": "3xTF32 split, F32 within 1e-5 per unit" if args.passes == 3
+                                else "TF32 (1e-2)",
+                   "rows": "time rows (batch x T) per stage through its 3 units",
+                   "parallelism": f"replicas x{world}, no collective",
+                   "l2": f"inputs larger than L2 ({sum(nbytes) / 1e9:.2f} GB moved per step)"},
+        "tflops": round(step_tflops, 1),
+        "per_kernel": per_kernel, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": args.steps * len(launches) * (1 + 2 * len(runner.RESUNIT_DILATIONS)),
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args) -> None:
     rank = env_int("RANK", 0)
     if rank != 0:
@@ -283,6 +549,34 @@ def run_reference(args) -> None:
                     ms_per_step=1000.0 * r["seconds"] / r["passes"], scaling="weak",
                     dtype="f32", config={"workload": "vocoder SnakeBeta stages", "config": "c4",
                                          "stages": runner.SNAKE_STAGES, "batch": batch})
+    elif args.config == "v1":
+        # all 4 stages x 3 units per step on sample_t time rows, sized to the budget
+        probe = cpu_resunit_rate(runner.RESUNIT_STAGES, runner.RESUNIT_BATCH, 0.0, sample_t=256,
+                                 steps=1, warmup=0)
+        sample_t = int(max(256, min(16000, 256 * per_step_s / max(probe["seconds"], 1e-3))))
+        r = cpu_resunit_rate(runner.RESUNIT_STAGES, runner.RESUNIT_BATCH, 0.0,
+                             sample_t=sample_t, steps=args.steps, warmup=args.warmup)
+        cb = {"value": r["rows_per_s"], "unit": "rows/s", "cores": r["threads"], "kind": "port",
+              "sample": f"{sample_t} time rows of one item per stage per step, scaled per stage "
+                        f"to batch {runner.RESUNIT_BATCH}; the reference's USE_BLAS ResUnit "
+                        "(AVX2 voc_snake_beta from its source + SGEMM convolutions through "
+                        f"numpy's OpenBLAS) on {r['threads']} threads, host {cpu_model()}"}
+        line = dict(common, value=r["rows_per_s"], unit="rows/s",
+                    ms_per_step=1000.0 * r["step_seconds"], scaling="weak", dtype="f32",
+                    config={"workload": "vocoder BigVGAN ResUnits", "config": "v1",
+                            "stages": runner.RESUNIT_STAGES, "batch": runner.RESUNIT_BATCH,
+                            "dilations": list(runner.RESUNIT_DILATIONS)})
+    elif args.config in runner.DECODE_CONFIGS:
+        cfg = runner.DECODE_CONFIGS[args.config]
+        r = cpu_decode_rate(cfg, per_step_s * args.steps)
+        cb = {"value": r["rows_per_s"], "unit": "rows/s", "cores": r["threads"], "kind": "port",
+              "sample": f"{r['passes']} single-layer linear paths, rate divided by "
+                        f"{cfg.layers} layers, FP32, host {cpu_model()}"}
+        line = dict(common, value=r["rows_per_s"], unit="rows/s",
+                    ms_per_step=1000.0 / r["rows_per_s"], scaling="weak",
+                    dtype="bf16 weights / f32 activations",
+                    config={"workload": f"{cfg.name} decode linear path", "config": args.config,
+                            "m": cfg.m, "dim": cfg.dim, "ffn": cfg.inter, "layers": cfg.layers})
     else:
         cfg = runner.CONFIGS[args.config]
         probe = cpu_chain_rate(cfg, min(cfg.tokens, 1024), 0.0, steps=2, warmup=1)
@@ -734,10 +1028,16 @@ def run_ours(args) -> None:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default 2000; 20 for v1, whose step is ~0.1 s)")
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "g1", "g2"], default="c2")
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "g1", "g2", "v1"],
+                    default="c2")
+    ap.add_argument("--t-div", type=int, default=1,
+                    help="v1: divide every stage's length (small profiling cases)")
+    ap.add_argument("--passes", type=int, choices=[1, 3], default=3,
+                    help="v1: 3 = F32-faithful 3xTF32 products, 1 = plain TF32")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--dtype", choices=["bf16", "f32"], default="bf16",
                     help="activation storage of the layer chain (f32: the drop-ins' type)")
@@ -760,8 +1060,12 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)  # timing rule: at least 3 untimed warm-up steps
+    if args.steps is None:
+        args.steps = 20 if args.config == "v1" else 2000
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == "v1":
+        run_resunits(args)
     else:
         run_ours(args)
 

@@ -93,6 +93,21 @@ DECODE_CONFIGS = {
 SNAKE_STAGES = [(1536, 2000), (768, 16000), (384, 48000), (192, 96000), (96, 192000)]
 SNAKE_BATCH = 8
 
+# Vocoder BigVGAN ResUnits: the four blocks' output widths at the SnakeBeta stages'
+# lengths, three units per block with dilations 1, 3, 9 (src/tts_vocoder.c:269, 725-728).
+RESUNIT_STAGES = [(768, 16000), (384, 48000), (192, 96000), (96, 192000)]
+RESUNIT_BATCH = 8
+RESUNIT_DILATIONS = (1, 3, 9)
+
+
+def resunit_hbm_bytes_per_element(n_units: int, passes: int) -> int:
+    """Algorithmic HBM bytes per activation element of lai_voc_resunits_f32: the first
+    snake1 reads x and writes s; per unit conv1 reads s and writes h, conv2 reads h and x
+    and writes x, and (all but the last unit) the next unit's s. s and h are hi/lo pairs
+    (8 bytes) with 3 passes, one TF32 plane (4 bytes) with 1."""
+    sp = 8 if passes == 3 else 4
+    return (4 + sp) + n_units * (2 * sp + sp + 8) + (n_units - 1) * sp
+
 
 def shard_range(n: int, world: int, rank: int) -> tuple[int, int]:
     """Contiguous balanced block [start, stop) of n rows for `rank` of `world`."""
@@ -204,6 +219,62 @@ class SnakeSweep:
 
     def rows_per_launch(self) -> list[int]:
         return [self.batch * c for c, _ in self.stages]
+
+
+class VocResUnits:
+    """The BigVGAN decoder's 12 ResUnits (config v1): per stage, x [batch, T, C] FP32
+    channels-last and three units (dilations 1, 3, 9) with their own weights, random
+    like a trained vocoder's scale (conv weights N(0,1)/sqrt(fan_in), biases N(0,0.1),
+    snake parameters pre-exponentiated from N(0,0.1)). One step = one
+    lai_voc_resunits_f32 call per stage (a snake1 kernel and two convolutions per unit)."""
+
+    def __init__(self, stages=RESUNIT_STAGES, batch=RESUNIT_BATCH, passes: int = 3,
+                 seed: int = 99, device="cuda"):
+        import torch
+        self.stages, self.batch, self.passes = list(stages), batch, passes
+        self.x, self.units, self._keep = [], [], []
+        k = 0
+
+        def normal(shape, std=1.0):
+            nonlocal k
+            t = torch.empty(shape, dtype=torch.float32, device=device)
+            lai.synth_normal(t, seed=seed + k, std=std)
+            k += 1
+            return t
+
+        for c, t in self.stages:
+            self.x.append(normal((batch, t, c)))
+            params = []
+            for d in RESUNIT_DILATIONS:
+                params.append({
+                    "ea1": torch.exp(normal(c, 0.1)), "ieb1": 1.0 / torch.exp(normal(c, 0.1)),
+                    "w1": normal((c, c, 7), (7 * c) ** -0.5), "b1": normal(c, 0.1),
+                    "ea2": torch.exp(normal(c, 0.1)), "ieb2": 1.0 / torch.exp(normal(c, 0.1)),
+                    "w2": normal((c, c, 1), c ** -0.5), "b2": normal(c, 0.1), "dilation": d})
+            arr, keep = lai.voc_units(params)
+            self.units.append(arr)
+            self._keep.append((params, keep))
+        n_max = max(batch * t * c for c, t in self.stages)
+        self.scratch = torch.empty(4 * n_max, dtype=torch.float32, device=device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.kernel_names = tuple(f"resunits_{c}x{t}" for c, t in self.stages)
+
+    def launches(self, stream=None):
+        return [(lambda i=i: lai.voc_resunits(self.x[i], self.units[i], self.scratch,
+                                              self.passes, self.err, stream))
+                for i in range(len(self.stages))]
+
+    def flops_per_launch(self) -> list[float]:
+        """FP32 convolution flops as the reference computes them: per unit and output
+        element 2 * 7C (conv1) + 2 * C (conv2) multiply-adds."""
+        return [16.0 * c * c * t * self.batch * len(RESUNIT_DILATIONS) for c, t in self.stages]
+
+    def bytes_per_launch(self) -> list[int]:
+        per = resunit_hbm_bytes_per_element(len(RESUNIT_DILATIONS), self.passes)
+        return [per * self.batch * t * c for c, t in self.stages]
+
+    def rows_per_launch(self) -> list[int]:
+        return [self.batch * t for _, t in self.stages]  # time rows through 3 units
 
 
 class DecodeLinear:
