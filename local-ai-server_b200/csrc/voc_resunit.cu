@@ -51,7 +51,9 @@ constexpr int kUmmaK = 8;       // K of one kind::tf32 MMA (32 bytes)
 constexpr int kEpiWarps = 8;    // two per TMEM lane quarter, each half of the columns
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA + TMEM, 2..9 drain
 constexpr int kChunkBlocks = 2; // K blocks per TMEM accumulation chunk (32 input channels)
-constexpr int kSmemTiles = 200 * 1024;
+constexpr int kSmemTiles = 192 * 1024;
+constexpr int kEpiPitch = 33;   // floats per row of a drain warp's 32 x 32 transpose buffer
+constexpr uint32_t kEpiBytes = kEpiWarps * 32 * kEpiPitch * 4;
 constexpr int kMaxStages = 8;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s: far beyond any healthy wait
 
@@ -73,7 +75,8 @@ struct Tile {
     static constexpr uint32_t kStage = (kA + kB) * (PASSES == 3 ? 2u : 1u);
     static constexpr int kStages =
         (int)(kSmemTiles / kStage) < kMaxStages ? (int)(kSmemTiles / kStage) : kMaxStages;
-    static constexpr uint32_t kSmem = 1024 + kStages * kStage + 256;  // align slack + barriers
+    // align slack + operand ring + the drain warps' transpose buffers + barriers
+    static constexpr uint32_t kSmem = 1024 + kStages * kStage + kEpiBytes + 256;
     // two accumulator buffers: the MMAs fill one chunk while the other is drained
     static constexpr uint32_t kBufCols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
     static constexpr uint32_t kTmemCols = 2 * kBufCols;
@@ -87,37 +90,29 @@ __device__ __forceinline__ void store4(float *p, float a, float b, float c, floa
     *reinterpret_cast<float4 *>(p) = make_float4(a, b, c, d);
 }
 
-// Epilogue for 16 finished sums, columns [n, n + 16) of output row `row` (global index).
+// Epilogue for 4 finished sums of output row `row` (global index), channels [c, c + 4):
+// bias, then either snake + hi/lo split (conv1) or residual in place and the next unit's
+// snake + split (conv2). `xr` holds x[row, c..c+3] for the residual, loaded earlier.
 template <int PASSES, int EPI>
-__device__ __forceinline__ void epilogue16(const ConvArgs &a, float (&v)[16], size_t row, int n) {
-    const size_t off = row * (size_t)a.c_out + n;
+__device__ __forceinline__ void epilogue4(const ConvArgs &a, float (&v)[4], const float4 &xr,
+                                          size_t row, int c) {
+    const size_t off = row * (size_t)a.c_out + c;
 #pragma unroll
-    for (int i = 0; i < 16; i++) v[i] += __ldg(a.bias + n + i);
+    for (int i = 0; i < 4; i++) v[i] += __ldg(a.bias + c + i);
     if (EPI == kEpiResidual) {
-        float *xr = a.x + off;
-#pragma unroll
-        for (int i = 0; i < 16; i += 4) {
-            const float4 r = *reinterpret_cast<const float4 *>(xr + i);
-            v[i] += r.x; v[i + 1] += r.y; v[i + 2] += r.z; v[i + 3] += r.w;
-            store4(xr + i, v[i], v[i + 1], v[i + 2], v[i + 3]);
-        }
+        v[0] += xr.x; v[1] += xr.y; v[2] += xr.z; v[3] += xr.w;
+        store4(a.x + off, v[0], v[1], v[2], v[3]);
         if (a.ea == nullptr) return;
     }
+    float hi[4];
 #pragma unroll
-    for (int i = 0; i < 16; i++) v[i] = snake1(v[i], __ldg(a.ea + n + i), __ldg(a.ieb + n + i));
-    float hi[16];
-#pragma unroll
-    for (int i = 0; i < 16; i++) hi[i] = umma::tf32_round(v[i]);
-    float *ph = a.out_hi + off;
-#pragma unroll
-    for (int i = 0; i < 16; i += 4) store4(ph + i, hi[i], hi[i + 1], hi[i + 2], hi[i + 3]);
-    if (PASSES == 3) {
-        float *pl = a.out_lo + off;
-#pragma unroll
-        for (int i = 0; i < 16; i += 4)
-            store4(pl + i, v[i] - hi[i], v[i + 1] - hi[i + 1], v[i + 2] - hi[i + 2],
-                   v[i + 3] - hi[i + 3]);
+    for (int i = 0; i < 4; i++) {
+        v[i] = snake1(v[i], __ldg(a.ea + c + i), __ldg(a.ieb + c + i));
+        hi[i] = umma::tf32_round(v[i]);
     }
+    store4(a.out_hi + off, hi[0], hi[1], hi[2], hi[3]);
+    if (PASSES == 3)
+        store4(a.out_lo + off, v[0] - hi[0], v[1] - hi[1], v[2] - hi[2], v[3] - hi[3]);
 }
 
 // Accumulation. The tensor core's F32 accumulation does not round to nearest: measured
@@ -139,7 +134,8 @@ conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
     extern __shared__ uint8_t smem_raw[];
     uint8_t *tiles = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t *full = reinterpret_cast<uint64_t *>(tiles + L::kStages * L::kStage);
+    float *epi_buf = reinterpret_cast<float *>(tiles + L::kStages * L::kStage);
+    uint64_t *full = reinterpret_cast<uint64_t *>(tiles + L::kStages * L::kStage + kEpiBytes);
     uint64_t *empty = full + L::kStages;
     uint64_t *acc_full = empty + L::kStages;  // [2]: chunk ready in buffer b
     uint64_t *acc_empty = acc_full + 2;       // [2]: buffer b drained
@@ -240,7 +236,6 @@ conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
     } else {  // drain / epilogue warps 2..9
         const int q = warp & 3;                 // the TMEM lane quarter this warp may read
         const int half = (warp - 2) >> 2;       // which half of the BN columns
-        const int t = t0 + q * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
         float sum[L::kHalf];
 #pragma unroll
@@ -265,14 +260,50 @@ conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
             __syncwarp();
             if (lane == 0) bulk::mbar_arrive(&acc_empty[j & 1]);
         }
-        if (ok && t < a.T) {
-            const size_t row = (size_t)b * a.T + t;
+        if (ok) {
+            // Coalesced epilogue: the warp's 32 rows x GW columns of sums go through a
+            // padded shared-memory buffer (row per lane in, conflict-free) and come back
+            // as GW/4 lanes per row, 4 consecutive channels each, so every global load and
+            // store covers whole 32-byte sectors (a 128-byte line per row when GW = 32).
+            constexpr int GW = L::kHalf % 32 == 0 ? 32 : 16;
+            constexpr int LPR = GW / 4;    // lanes per row
+            constexpr int RPP = 32 / LPR;  // rows per pass
+            constexpr int NP = 32 / RPP;   // passes over the 32 rows
+            float *buf = epi_buf + (warp - 2) * 32 * kEpiPitch;
+            const int r_off = lane / LPR, c4 = (lane % LPR) * 4;
+            const int row0 = t0 + q * 32;
 #pragma unroll
-            for (int g = 0; g < L::kHalf / 16; g++) {
-                float v[16];
+            for (int g = 0; g < L::kHalf / GW; g++) {
+                const int c = n0 + half * L::kHalf + g * GW + c4;
 #pragma unroll
-                for (int i = 0; i < 16; i++) v[i] = sum[g * 16 + i];
-                epilogue16<PASSES, EPI>(a, v, row, n0 + half * L::kHalf + g * 16);
+                for (int i = 0; i < GW; i++) buf[lane * kEpiPitch + i] = sum[g * GW + i];
+                __syncwarp();
+                constexpr int PB = NP < 4 ? NP : 4;  // passes whose residual loads fly together
+#pragma unroll
+                for (int p0 = 0; p0 < NP; p0 += PB) {
+                    float4 xr[PB];
+                    if (EPI == kEpiResidual) {
+#pragma unroll
+                        for (int p = 0; p < PB; p++) {
+                            const int t = row0 + (p0 + p) * RPP + r_off;
+                            xr[p] = t < a.T ? *reinterpret_cast<const float4 *>(
+                                                  a.x + ((size_t)b * a.T + t) * a.c_out + c)
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+                    }
+#pragma unroll
+                    for (int p = 0; p < PB; p++) {
+                        const int r = (p0 + p) * RPP + r_off;
+                        float v[4];
+#pragma unroll
+                        for (int i = 0; i < 4; i++) v[i] = buf[r * kEpiPitch + c4 + i];
+                        const int t = row0 + r;
+                        if (t < a.T)
+                            epilogue4<PASSES, EPI>(a, v, EPI == kEpiResidual ? xr[p] : xr[0],
+                                                   (size_t)b * a.T + t, c);
+                    }
+                }
+                __syncwarp();
             }
         }
     }
