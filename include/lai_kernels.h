@@ -22,6 +22,7 @@
 #ifndef LAI_KERNELS_H
 #define LAI_KERNELS_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifndef LAI_API
@@ -176,6 +177,27 @@ LAI_API int lai_gemv_residual_bf16w_f32(float *x_res, const float *a, const lai_
 LAI_API int lai_gemv_swiglu_bf16w_f32(float *out, const float *x, const float *norm_w, float eps,
                                       const lai_bf16 *W_gu, int64_t M, int K, int inter,
                                       lai_stream_t stream);
+
+/* ---- decode attention over the KV cache ----------------------------------------------------
+ * One query token per sequence: the decode step's cache append + qwen_causal_attention
+ * (src/tts_native.c:650-656: memcpy of k, v into kv_k_at / kv_v_at at pos, then
+ * attention over keys 0..pos with scale 1/sqrt(hd)), for n_seqs independent sequences.
+ *   q [n_seqs, n_heads*128] (RMSNorm'd + RoPE'd), k_new / v_new [n_seqs, n_kv*128]: this
+ *   token's k (RMSNorm'd + RoPE'd) and v; k_cache / v_cache [n_seqs, max_seq, n_kv*128]
+ *   (the reference's per-layer cache layout, one block per sequence); pos [n_seqs] device.
+ * Writes out [n_seqs, n_heads*128] and k_new / v_new into cache row pos (the same launch).
+ * Query head h reads kv head h / (n_heads / n_kv); n_heads / n_kv in {1, 2, 4, 8};
+ * head_dim must be 128. scratch: lai_decode_attention_scratch_bytes() bytes, zeroed once
+ * before first use (every call leaves it reusable). pos outside [0, max_seq) leaves that
+ * sequence's output untouched and sets LAI_DEVERR_POSITION in *err.
+ */
+LAI_API size_t lai_decode_attention_scratch_bytes(int n_seqs, int n_heads, int n_kv_heads,
+                                                  int max_seq);
+LAI_API int lai_decode_attention_f32(float *out, const float *q, const float *k_new,
+                                     const float *v_new, float *k_cache, float *v_cache,
+                                     const int32_t *pos, int n_seqs, int n_heads, int n_kv_heads,
+                                     int head_dim, int max_seq, float scale, void *scratch,
+                                     int *err, lai_stream_t stream);
 
 /* ---- vocoder BigVGAN ResUnits on tensor cores ------------------------------------------------
  * run_resunit(x, ru, C, T, scratch) (src/tts_vocoder.c:540-583) for n_units consecutive

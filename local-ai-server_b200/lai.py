@@ -17,7 +17,7 @@ LIB_PATH = os.path.join(HERE, "liblai_kernels.so")
 
 LAI_OK, LAI_ERR_INVALID, LAI_ERR_CUDA, LAI_ERR_RANGE, LAI_ERR_ALIAS, LAI_ERR_NOMEM, LAI_ERR_TOOBIG = \
     0, -1, -2, -3, -4, -5, -6
-LAI_DEVERR_TOKEN_ID, LAI_DEVERR_POSITION = 1, 2
+LAI_DEVERR_TOKEN_ID, LAI_DEVERR_POSITION, LAI_DEVERR_TIMEOUT = 1, 2, 4
 
 _vp, _i32, _i64, _f32, _u64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_uint64
 
@@ -46,6 +46,9 @@ SIGNATURES: dict[str, tuple] = {
     "lai_gemv_bf16w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
     "lai_gemv_residual_bf16w_f32": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _vp]),
     "lai_gemv_swiglu_bf16w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
+    "lai_decode_attention_scratch_bytes": (ctypes.c_size_t, [_i32, _i32, _i32, _i32]),
+    "lai_decode_attention_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32,
+                                        _i32, _i32, _f32, _vp, _vp, _vp]),
     "lai_voc_resunits_f32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
     "lai_voc_pack_conv_f32": (_i32, [_vp, _vp, _i32, _i32, _i32, _vp]),
     "lai_voc_transpose_f32": (_i32, [_vp, _vp, _i32, _i32, _i32, _vp]),
@@ -245,6 +248,29 @@ def gemv_swiglu(x, W_gu, norm_w=None, eps=1e-6, out=None, stream=None):
     out = torch.empty((M, inter), dtype=torch.float32, device=x.device) if out is None else out
     call("lai_gemv_swiglu_bf16w_f32", _p(out), _p(x), _p(norm_w), eps, _p(W_gu), M, K, inter,
          _s(stream))
+    return out
+
+
+def decode_attention_scratch(n_seqs, n_heads, n_kv_heads, max_seq, device="cuda"):
+    """Zeroed scratch for decode_attention (reusable across calls)."""
+    import torch
+    nb = load().lai_decode_attention_scratch_bytes(n_seqs, n_heads, n_kv_heads, max_seq)
+    return torch.zeros((nb + 15) // 16 * 4, dtype=torch.float32, device=device)
+
+
+def decode_attention(q, k_new, v_new, k_cache, v_cache, pos, n_heads, n_kv_heads, scratch=None,
+                     scale=None, out=None, err=None, stream=None):
+    """One token per sequence: append k_new/v_new at pos[s] and attend over keys 0..pos[s].
+    q [S, H*128]; k_new/v_new [S, Hkv*128]; caches [S, max_seq, Hkv*128]."""
+    import torch
+    S, max_seq = k_cache.shape[0], k_cache.shape[1]
+    hd = q.shape[1] // n_heads
+    if scratch is None:
+        scratch = decode_attention_scratch(S, n_heads, n_kv_heads, max_seq, q.device)
+    out = torch.empty_like(q) if out is None else out
+    call("lai_decode_attention_f32", _p(out), _p(q), _p(k_new), _p(v_new), _p(k_cache),
+         _p(v_cache), _p(pos), S, n_heads, n_kv_heads, hd, max_seq,
+         hd ** -0.5 if scale is None else scale, _p(scratch), _p(err), _s(stream))
     return out
 
 

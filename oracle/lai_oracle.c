@@ -403,6 +403,48 @@ void oracle_voc_resunit(float *x, const float *ea1, const float *ieb1, const flo
 }
 
 /* ---------------------------------------------------------------------------
+ * Decode attention: one query token per sequence (qwen_causal_attention with
+ * seq_q = 1 and q_offset = pos, src/tts_native.c:650-656; the math is the repo's numpy
+ * specification tools/verify_xfmr.py:57-77: scores = q.k * scale, max-subtracted
+ * softmax over keys 0..pos, weighted sum of v). GQA: query head h reads kv head
+ * h / (n_heads / n_kv_heads). In the checker build scores, the softmax and the
+ * weighted sum are accumulated in double.
+ * ------------------------------------------------------------------------- */
+void oracle_decode_attention(float *out, const float *q, const float *k_cache,
+                             const float *v_cache, const int32_t *pos, int n_seqs, int n_heads,
+                             int n_kv_heads, int head_dim, int max_seq, float scale) {
+    const int kv_dim = n_kv_heads * head_dim, group = n_heads / n_kv_heads;
+#pragma omp parallel for schedule(dynamic)
+    for (int sh = 0; sh < n_seqs * n_heads; sh++) {
+        const int s = sh / n_heads, h = sh % n_heads, kvh = h / group;
+        const int L = pos[s] + 1;
+        const float *qh = q + (size_t)s * n_heads * head_dim + (size_t)h * head_dim;
+        const float *kc = k_cache + (size_t)s * max_seq * kv_dim + (size_t)kvh * head_dim;
+        const float *vc = v_cache + (size_t)s * max_seq * kv_dim + (size_t)kvh * head_dim;
+        float *o = out + (size_t)s * n_heads * head_dim + (size_t)h * head_dim;
+        acc_t mx = -1e300;
+        for (int j = 0; j < L; j++) {
+            acc_t d = 0;
+            for (int e = 0; e < head_dim; e++) d += (acc_t)qh[e] * kc[(size_t)j * kv_dim + e];
+            d *= scale;
+            if (d > mx) mx = d;
+        }
+        acc_t sum = 0;
+        for (int e = 0; e < head_dim; e++) o[e] = 0.0f;
+        acc_t accv[512];
+        for (int e = 0; e < head_dim; e++) accv[e] = 0;
+        for (int j = 0; j < L; j++) {
+            acc_t d = 0;
+            for (int e = 0; e < head_dim; e++) d += (acc_t)qh[e] * kc[(size_t)j * kv_dim + e];
+            const acc_t p = exp((double)(d * scale - mx));
+            sum += p;
+            for (int e = 0; e < head_dim; e++) accv[e] += p * vc[(size_t)j * kv_dim + e];
+        }
+        for (int e = 0; e < head_dim; e++) o[e] = (float)(accv[e] / sum);
+    }
+}
+
+/* ---------------------------------------------------------------------------
  * Timed CPU reference: the elementwise ops of one decoder layer, FP32, in the
  * order talker_prefill calls them (src/tts_native.c:553-592), with the GEMM and
  * attention outputs supplied as inputs:

@@ -79,6 +79,15 @@ void oracle_voc_resunit(float *x, const float *ea1, const float *ieb1, const flo
                         const float *b1, const float *ea2, const float *ieb2, const float *w2,
                         const float *b2, int C, int T, int dilation, float *scratch);
 
+/* ---- decode attention, one query token per sequence (qwen_causal_attention with seq_q = 1,
+ * src/tts_native.c:650-656; math of tools/verify_xfmr.py:57-77). q [n_seqs, n_heads*hd];
+ * caches [n_seqs, max_seq, n_kv*hd]; keys 0..pos[s] (the reference appends the new k/v at
+ * pos before attending, src/tts_native.c:650-651). Query head h reads kv head
+ * h / (n_heads / n_kv). ---- */
+void oracle_decode_attention(float *out, const float *q, const float *k_cache,
+                             const float *v_cache, const int32_t *pos, int n_seqs, int n_heads,
+                             int n_kv_heads, int head_dim, int max_seq, float scale);
+
 /* ---- timed CPU reference: one decoder layer's elementwise chain, FP32, called in
  * the reference's own order (talker_prefill, src/tts_native.c:553-592) ---- */
 void oracle_layer_chain_f32(float *x, const float *delta_attn, const float *delta_ffn,

@@ -89,6 +89,8 @@ def _declare(lib: ctypes.CDLL) -> None:
         "oracle_layer_chain_f32": [_F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _F,
                                    _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float],
         "oracle_linear_bf16": [_F, _F, _U16, _c_int, _c_int, _c_int],
+        "oracle_decode_attention": [_F, _F, _F, _F, _I32, _c_int, _c_int, _c_int, _c_int,
+                                    _c_int, _c_float],
         "oracle_voc_conv1d_causal": [_F, _F, _F, _F, _c_int, _c_int, _c_int, _c_int, _c_int],
         "oracle_voc_resunit": [_F, _F, _F, _F, _F, _F, _F, _F, _F, _c_int, _c_int, _c_int, _F],
         "oracle_num_threads": [],
@@ -388,3 +390,19 @@ def ref_voc_resunit(x, p, dilation, build: str = "scalar"):
         h = ref_snake_beta(h, p["ea2"], p["ieb2"], build)
         rows[b] = ref_voc_conv1d_causal(h, p["w2"], p["b2"], 1, build) + r
     return y
+
+
+def decode_attention(q, k_cache, v_cache, pos, n_heads, n_kv_heads, head_dim, scale=None,
+                     lib=None):
+    """q [S, H*hd]; caches [S, max_seq, Hkv*hd]; attends keys 0..pos[s]. Returns [S, H*hd]."""
+    lib = lib or load()
+    q = np.ascontiguousarray(q, np.float32)
+    k_cache = np.ascontiguousarray(k_cache, np.float32)
+    v_cache = np.ascontiguousarray(v_cache, np.float32)
+    pos = np.ascontiguousarray(pos, np.int32)
+    S, max_seq = k_cache.shape[0], k_cache.shape[1]
+    out = np.empty((S, n_heads * head_dim), np.float32)
+    scale = head_dim ** -0.5 if scale is None else scale
+    lib.oracle_decode_attention(ptr(out), ptr(q), ptr(k_cache), ptr(v_cache), ptr(pos, _I32), S,
+                                n_heads, n_kv_heads, head_dim, max_seq, scale)
+    return out
