@@ -524,6 +524,144 @@ def run_resunits(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def cpu_attention_rate(seqs: int, n_heads: int, n_kv: int, max_seq: int, min_seconds: float,
+                       steps: int | None = None, warmup: int = 1) -> dict:
+    """Decode attention on host cores: the restated qwen_causal_attention for one query
+    token per sequence (oracle/_build/liblai_cpuref.so: float sums, the reference's
+    optimisation tier, OpenMP over (sequence, head)) on `seqs` sequences with positions
+    uniform in [0, max_seq). Returns sequences/s."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle
+    lib = oracle.load("liblai_cpuref.so")
+    lib.oracle_set_threads(len(os.sched_getaffinity(0)))
+    rng = np.random.default_rng(12)
+    kv_dim = n_kv * 128
+    q = rng.standard_normal((seqs, n_heads * 128), dtype=np.float32)
+    kc = rng.standard_normal((seqs, max_seq, kv_dim), dtype=np.float32)
+    vc = rng.standard_normal((seqs, max_seq, kv_dim), dtype=np.float32)
+    pos = rng.integers(0, max_seq, seqs).astype(np.int32)
+    for _ in range(warmup):
+        oracle.decode_attention(q, kc, vc, pos, n_heads, n_kv, 128, lib=lib)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        oracle.decode_attention(q, kc, vc, pos, n_heads, n_kv, 128, lib=lib)
+        n += 1
+        el = time.perf_counter() - t0
+        if (steps is not None and n >= steps) or (steps is None and el >= min_seconds):
+            break
+    return {"rows_per_s": seqs * n / el, "threads": lib.oracle_num_threads(), "passes": n,
+            "seconds": el, "seqs": seqs}
+
+
+def run_attention(args) -> None:
+    """--config a3: decode attention of the TTS talker decode config (runner.DecodeAttention)."""
+    import torch
+    import torch.distributed as dist
+    import runner
+
+    world, rank, local = env_int("WORLD_SIZE", 1), env_int("RANK", 0), env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    work = runner.DecodeAttention(seed=args.seed + 1000 * rank)
+    launches = work.launches(None)
+    for _ in range(args.warmup):
+        launches[0]()
+    torch.cuda.synchronize()
+    phys = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+    sampler = ClockSampler(phys[local] if local < len(phys) and phys[local] != "" else str(local))
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    total_ms, per = time_launches(launches, args.steps, False, work.kernel_names)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    t = torch.tensor([total_ms], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    assert int(work.err.item()) == 0, "a position was out of range"
+    peak, peak_kind = measured_peaks()
+    nbytes = work.bytes_per_launch()[0]
+    avg_ms = statistics.mean(per[0])
+    gbs = nbytes / (avg_ms / 1000.0) / 1e9
+    value = work.seqs * world * args.steps / (max_ms / 1000.0)
+    roofline = {"bound": "hbm", "kernel": "decode_attention", "achieved": round(gbs, 1),
+                "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                "traffic": load_traffic().get("decode_attention@a3"),
+                "algorithmic_bytes_per_launch": nbytes}
+    e2e = None
+    if not args.no_e2e:
+        # q, the new k/v and positions from pinned host memory, output back; the cache
+        # stays resident on the device as in a GPU decoder
+        hq, hk, hv, hp = (work.q.cpu().pin_memory(), work.k_new.cpu().pin_memory(),
+                          work.v_new.cpu().pin_memory(), work.pos.cpu().pin_memory())
+        ho = torch.empty_like(hq).pin_memory()
+        stream = torch.cuda.current_stream()
+
+        def e2e_step():
+            work.q.copy_(hq, non_blocking=True)
+            work.k_new.copy_(hk, non_blocking=True)
+            work.v_new.copy_(hv, non_blocking=True)
+            work.pos.copy_(hp, non_blocking=True)
+            launches[0]()
+            ho.copy_(work.out, non_blocking=True)
+        e2e_step()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        b.record(stream)
+        torch.cuda.synchronize()
+        h2d = (hq.numel() + hk.numel() + hv.numel() + hp.numel()) * 4
+        e2e = {"value": round(work.seqs * world * args.e2e_steps / (a.elapsed_time(b) / 1000.0), 1),
+               "unit": "rows/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": ho.numel() * 4,
+               "dtype": "f32", "api": "lai_decode_attention_f32 with q/k/v/pos copied from and "
+                                       "the output back to pinned host memory each step; cache "
+                                       "device-resident"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        r = cpu_attention_rate(16, work.n_heads, work.n_kv, work.max_seq, args.cpu_seconds)
+        cpu = {"value": round(r["rows_per_s"], 1), "unit": "rows/s", "cores": r["threads"],
+               "kind": "port",
+               "sample": f"{r['passes']} passes over {r['seqs']} sequences at uniform random "
+                         f"positions < {work.max_seq} ({r['seconds']:.1f} s): the restated "
+                         "qwen_causal_attention (seq_q = 1), float sums, OpenMP over "
+                         f"(sequence, head), host {cpu_model()}"}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "rows/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded counter-based N(0,1) cache, q, k, v; uniform positions)",
+        "config": {"workload": "TTS talker decode attention: cache append + attention over "
+                               "keys 0..pos, one token per sequence, F32 KV cache",
+                   "config": "a3", "sequences": work.seqs, "heads": [work.n_heads, work.n_kv, 128],
+                   "max_seq": work.max_seq, "keys_per_step": work.keys,
+                   "rows": "sequences (one token each)",
+                   "parallelism": f"replicas x{world}, no collective",
+                   "l2": f"inputs larger than L2 ({nbytes / 1e9:.2f} GB per step)"},
+        "per_kernel": {"decode_attention": {"avg_us": round(avg_ms * 1000, 2), "gbs": round(gbs, 1),
+                                            "frac_of_peak": round(gbs / peak, 4),
+                                            "bytes_per_launch": nbytes}},
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": args.steps, "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args) -> None:
     rank = env_int("RANK", 0)
     if rank != 0:
@@ -566,6 +704,15 @@ def run_reference(args) -> None:
                     config={"workload": "vocoder BigVGAN ResUnits", "config": "v1",
                             "stages": runner.RESUNIT_STAGES, "batch": runner.RESUNIT_BATCH,
                             "dilations": list(runner.RESUNIT_DILATIONS)})
+    elif args.config == "a3":
+        r = cpu_attention_rate(16, 16, 8, 4096, 0.0, steps=args.steps, warmup=args.warmup)
+        cb = {"value": r["rows_per_s"], "unit": "rows/s", "cores": r["threads"], "kind": "port",
+              "sample": f"16 sequences at uniform random positions < 4096 per step: the "
+                        f"restated qwen_causal_attention (seq_q = 1), OpenMP, host {cpu_model()}"}
+        line = dict(common, value=r["rows_per_s"], unit="rows/s",
+                    ms_per_step=1000.0 * r["seconds"] / r["passes"], scaling="weak", dtype="f32",
+                    config={"workload": "TTS talker decode attention", "config": "a3",
+                            "sequences": 16, "heads": [16, 8, 128], "max_seq": 4096})
     elif args.config in runner.DECODE_CONFIGS:
         cfg = runner.DECODE_CONFIGS[args.config]
         r = cpu_decode_rate(cfg, per_step_s * args.steps)
@@ -1032,7 +1179,7 @@ def main():
                     help="timed steps (default 2000; 20 for v1, whose step is ~0.1 s)")
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "g1", "g2", "v1"],
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "g1", "g2", "v1", "a3"],
                     default="c2")
     ap.add_argument("--t-div", type=int, default=1,
                     help="v1: divide every stage's length (small profiling cases)")
@@ -1066,6 +1213,8 @@ def main():
         run_reference(args)
     elif args.config == "v1":
         run_resunits(args)
+    elif args.config == "a3":
+        run_attention(args)
     else:
         run_ours(args)
 

@@ -223,9 +223,13 @@ class SnakeSweep:
 
 class VocResUnits:
     """The BigVGAN decoder's 12 ResUnits (config v1): per stage, x [batch, T, C] FP32
-    channels-last and three units (dilations 1, 3, 9) with their own weights, random
-    like a trained vocoder's scale (conv weights N(0,1)/sqrt(fan_in), biases N(0,0.1),
-    snake parameters pre-exponentiated from N(0,0.1)). One step = one
+    channels-last and three units (dilations 1, 3, 9) with their own random weights:
+    conv1 N(0,1)/sqrt(fan_in), conv2 0.1 N(0,1)/sqrt(fan_in), biases N(0,0.01), snake
+    parameters pre-exponentiated from N(0,0.1). The small residual branch keeps the
+    residual stream bounded, as a trained vocoder's is, although every timed step runs
+    the units in place on the same x again: with conv2 at full scale x grows by about 2x
+    per unit, passes 65536 within ~10 steps and moves SnakeBeta onto its full-range sinf
+    path (40% slower) - a state no real input reaches. One step = one
     lai_voc_resunits_f32 call per stage (a snake1 kernel and two convolutions per unit)."""
 
     def __init__(self, stages=RESUNIT_STAGES, batch=RESUNIT_BATCH, passes: int = 3,
@@ -248,9 +252,10 @@ class VocResUnits:
             for d in RESUNIT_DILATIONS:
                 params.append({
                     "ea1": torch.exp(normal(c, 0.1)), "ieb1": 1.0 / torch.exp(normal(c, 0.1)),
-                    "w1": normal((c, c, 7), (7 * c) ** -0.5), "b1": normal(c, 0.1),
+                    "w1": normal((c, c, 7), (7 * c) ** -0.5), "b1": normal(c, 0.01),
                     "ea2": torch.exp(normal(c, 0.1)), "ieb2": 1.0 / torch.exp(normal(c, 0.1)),
-                    "w2": normal((c, c, 1), c ** -0.5), "b2": normal(c, 0.1), "dilation": d})
+                    "w2": normal((c, c, 1), 0.1 * c ** -0.5), "b2": normal(c, 0.01),
+                    "dilation": d})
             arr, keep = lai.voc_units(params)
             self.units.append(arr)
             self._keep.append((params, keep))
@@ -275,6 +280,51 @@ class VocResUnits:
 
     def rows_per_launch(self) -> list[int]:
         return [self.batch * t for _, t in self.stages]  # time rows through 3 units
+
+
+class DecodeAttention:
+    """Decode attention of config a3: `seqs` sequences x 1 token at seeded random
+    positions 0..max_seq-1, GQA n_heads / n_kv_heads, head_dim 128, F32 KV cache
+    [seqs, max_seq, n_kv*128] filled with N(0,1). One step = lai_decode_attention_f32:
+    append each token's k/v at its position and attend over keys 0..pos."""
+
+    def __init__(self, seqs: int = 256, n_heads: int = 16, n_kv_heads: int = 8,
+                 max_seq: int = 4096, seed: int = 4242, device="cuda"):
+        import torch
+        self.seqs, self.n_heads, self.n_kv, self.max_seq = seqs, n_heads, n_kv_heads, max_seq
+        kv_dim = n_kv_heads * 128
+
+        def normal(shape, k):
+            t = torch.empty(shape, dtype=torch.float32, device=device)
+            lai.synth_normal(t, seed=seed + k)
+            return t
+
+        self.q = normal((seqs, n_heads * 128), 0)
+        self.k_new, self.v_new = normal((seqs, kv_dim), 1), normal((seqs, kv_dim), 2)
+        self.k_cache = normal((seqs, max_seq, kv_dim), 3)
+        self.v_cache = normal((seqs, max_seq, kv_dim), 4)
+        self.pos = torch.empty(seqs, dtype=torch.int32, device=device)
+        lai.synth_uniform_i32(self.pos, seed + 5, 0, max_seq)
+        self.out = torch.empty_like(self.q)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.scratch = lai.decode_attention_scratch(seqs, n_heads, n_kv_heads, max_seq, device)
+        self.keys = int((self.pos.to(torch.int64) + 1).sum().item())
+        self.kernel_names = ("decode_attention",)
+
+    def launches(self, stream=None):
+        return [lambda: lai.decode_attention(self.q, self.k_new, self.v_new, self.k_cache,
+                                             self.v_cache, self.pos, self.n_heads, self.n_kv,
+                                             self.scratch, out=self.out, err=self.err,
+                                             stream=stream)]
+
+    def bytes_per_launch(self) -> list[int]:
+        """K and V rows 0..pos read once per (sequence, kv head); q, the new k/v and the
+        output once; the appended cache rows written."""
+        kv_dim = self.n_kv * 128
+        return [self.keys * kv_dim * 4 * 2 + self.seqs * (2 * self.n_heads * 128 + 4 * kv_dim) * 4]
+
+    def rows_per_launch(self) -> list[int]:
+        return [self.seqs]
 
 
 class DecodeLinear:
