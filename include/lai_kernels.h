@@ -199,6 +199,22 @@ LAI_API int lai_decode_attention_f32(float *out, const float *q, const float *k_
                                      int head_dim, int max_seq, float scale, void *scratch,
                                      int *err, lai_stream_t stream);
 
+/* ---- token sampling on device logits ------------------------------------------------------
+ * Per row r of logits [rows, vocab]: tts_apply_repetition_penalty(logits, vocab, history,
+ * history_len, penalty) (src/tts_sampling.c:19-36; history [rows, history_stride] int32,
+ * history_len [rows], both device, both NULL or neither; penalty <= 1 skips it), then
+ * tts_sample_topk(logits, vocab, temperature, top_k) (:40-109) with its rand()/RAND_MAX
+ * draw supplied as u[r] (device floats in [0, 1]); out_tokens[r] receives the token.
+ * Same candidate order, softmax and cumulative walk as the reference, so the same u picks
+ * the same token (up to the last bit of expf at a cumulative boundary). The penalty is
+ * applied to logits in place, as the reference does. top_k <= 0 or > vocab means vocab.
+ * LAI_ERR_TOOBIG when top_k * 8 + vocab / 8 bytes exceed 200 KiB.
+ */
+LAI_API int lai_sample_topk_f32(int32_t *out_tokens, float *logits, int vocab, int rows,
+                                const int32_t *history, const int32_t *history_len,
+                                int history_stride, float penalty, float temperature, int top_k,
+                                const float *u, lai_stream_t stream);
+
 /* ---- vocoder BigVGAN ResUnits on tensor cores ------------------------------------------------
  * run_resunit(x, ru, C, T, scratch) (src/tts_vocoder.c:540-583) for n_units consecutive
  * units, as tts_vocoder_run calls them per block (src/tts_vocoder.c:725-728):

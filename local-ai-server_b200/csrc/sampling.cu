@@ -1,0 +1,157 @@
+// sampling.cu - repetition penalty + top-k token sampling on device logits, one CTA per row.
+//
+// Reference: tts_apply_repetition_penalty (src/tts_sampling.c:19-36) and tts_sample_topk
+// (:40-109), called once per decode step on the talker's codec logits
+// (src/tts_native.c:1096-1099) and per code-predictor group (:1132).
+//
+// The token the reference picks for a given random draw depends on the ORDER of its
+// candidate slots: the first top_k tokens fill the slots, then each later token strictly
+// above the current minimum replaces the slot that holds it (first such slot), and the
+// softmax / cumulative walk runs over the slots in that order. This kernel replays that
+// scan exactly: warp 0 tests 32 tokens per ballot against the current minimum, applies
+// the qualifying tokens one at a time in index order (the lowest set lane first, the
+// minimum re-found by a warp-wide first-argmin over the slots after each), and re-tests
+// the rest of the chunk against the new minimum. One thread then runs the softmax and the
+// cumulative walk sequentially so the float sums round in the reference's order. The
+// uniform draw the reference takes from libc rand() comes in as u[row].
+//
+// The penalty marks each history token's bit in a shared-memory bitmap with atomicOr; the
+// thread that sets the bit penalises the logit, so every distinct token is penalised once
+// whatever the order of the history, as in the reference.
+#include "lai_common.cuh"
+
+#include <float.h>
+#include <limits.h>
+
+namespace lai {
+namespace {
+
+constexpr int kThreads = 256;
+
+// first index of the minimum over v[0..n): lowest index among equal minima
+__device__ __forceinline__ void warp_argmin_first(const float *v, int n, float &mv, int &mi) {
+    const int lane = threadIdx.x & 31;
+    float bv = FLT_MAX;
+    int bi = INT_MAX;
+    for (int j = lane; j < n; j += 32) {
+        const float x = v[j];
+        if (bi == INT_MAX || x < bv) {  // strict: keeps this lane's first minimum
+            bv = x;
+            bi = j;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov < bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    mv = bv;
+    mi = bi;
+}
+
+__global__ void __launch_bounds__(kThreads)
+sample_topk_kernel(int32_t *out, float *logits, int vocab, int64_t ld, const int32_t *history,
+                   const int32_t *hist_len, int hist_stride, float penalty, float temperature,
+                   int k, const float *u) {
+    extern __shared__ uint8_t smem_raw[];
+    float *sv = reinterpret_cast<float *>(smem_raw);
+    int *si = reinterpret_cast<int *>(sv + k);
+    uint32_t *seen = reinterpret_cast<uint32_t *>(si + k);
+    const int row = blockIdx.x, tid = threadIdx.x;
+    float *lg = logits + (size_t)row * ld;
+
+    if (penalty > 1.0f && history && hist_len) {
+        const int words = (vocab + 31) / 32;
+        for (int w = tid; w < words; w += kThreads) seen[w] = 0u;
+        __syncthreads();
+        const int n = min(hist_len[row], hist_stride);  // never past this row's history
+        const int32_t *h = history + (size_t)row * hist_stride;
+        for (int i = tid; i < n; i += kThreads) {
+            const int tok = h[i];
+            if (tok < 0 || tok >= vocab) continue;
+            const uint32_t bit = 1u << (tok & 31);
+            if (atomicOr(&seen[tok >> 5], bit) & bit) continue;
+            const float v = lg[tok];
+            lg[tok] = v > 0.0f ? v / penalty : v * penalty;
+        }
+        __syncthreads();
+    }
+    for (int i = tid; i < k; i += kThreads) {
+        sv[i] = lg[i];
+        si[i] = i;
+    }
+    __syncthreads();
+    if (tid < 32) {
+        const int lane = tid;
+        float mv;
+        int mi;
+        warp_argmin_first(sv, k, mv, mi);
+        for (int i0 = k; i0 < vocab; i0 += 32) {
+            const int i = i0 + lane;
+            const bool valid = i < vocab;
+            const float v = valid ? lg[i] : 0.0f;
+            uint32_t mask = __ballot_sync(0xffffffffu, valid && v > mv);
+            while (mask) {
+                const int f = __ffs(mask) - 1;
+                const float vf = __shfl_sync(0xffffffffu, v, f);
+                if (lane == 0) {
+                    sv[mi] = vf;
+                    si[mi] = i0 + f;
+                }
+                __syncwarp();
+                warp_argmin_first(sv, k, mv, mi);
+                mask = __ballot_sync(0xffffffffu, valid && lane > f && v > mv);
+            }
+        }
+        if (lane == 0) {
+            float mx = sv[0];
+            for (int j = 1; j < k; j++)
+                if (sv[j] > mx) mx = sv[j];
+            float sum = 0.0f;
+            for (int j = 0; j < k; j++) {
+                sv[j] = expf((sv[j] - mx) / temperature);
+                sum += sv[j];
+            }
+            const float r = u[row] * sum;
+            float cum = 0.0f;
+            int sel = si[0];
+            for (int j = 0; j < k; j++) {
+                cum += sv[j];
+                if (cum >= r) {
+                    sel = si[j];
+                    break;
+                }
+            }
+            out[row] = sel;
+        }
+    }
+}
+
+}  // namespace
+}  // namespace lai
+
+extern "C" int lai_sample_topk_f32(int32_t *out_tokens, float *logits, int vocab, int rows,
+                                   const int32_t *history, const int32_t *history_len,
+                                   int history_stride, float penalty, float temperature,
+                                   int top_k, const float *u, lai_stream_t stream) {
+    using namespace lai;
+    if (!out_tokens || !logits || !u || vocab <= 0 || rows < 0 ||
+        ((history == nullptr) != (history_len == nullptr)) || history_stride < 0)
+        return LAI_ERR_INVALID;
+    if (rows == 0) return LAI_OK;
+    const int k = (top_k <= 0 || top_k > vocab) ? vocab : top_k;
+    const size_t smem = (size_t)k * 8 + (size_t)((vocab + 31) / 32) * 4;
+    if (smem > 200 * 1024) return LAI_ERR_TOOBIG;
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(sample_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+        return LAI_ERR_CUDA;
+    sample_topk_kernel<<<rows, kThreads, smem, as_stream(stream)>>>(
+        out_tokens, logits, vocab, (int64_t)vocab, history, history_len, history_stride, penalty,
+        temperature, k, u);
+    return launch_status();
+}

@@ -49,6 +49,8 @@ SIGNATURES: dict[str, tuple] = {
     "lai_decode_attention_scratch_bytes": (ctypes.c_size_t, [_i32, _i32, _i32, _i32]),
     "lai_decode_attention_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32,
                                         _i32, _i32, _f32, _vp, _vp, _vp]),
+    "lai_sample_topk_f32": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp, _i32, _f32, _f32, _i32, _vp,
+                                   _vp]),
     "lai_voc_resunits_f32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
     "lai_voc_pack_conv_f32": (_i32, [_vp, _vp, _i32, _i32, _i32, _vp]),
     "lai_voc_transpose_f32": (_i32, [_vp, _vp, _i32, _i32, _i32, _vp]),
@@ -271,6 +273,19 @@ def decode_attention(q, k_new, v_new, k_cache, v_cache, pos, n_heads, n_kv_heads
     call("lai_decode_attention_f32", _p(out), _p(q), _p(k_new), _p(v_new), _p(k_cache),
          _p(v_cache), _p(pos), S, n_heads, n_kv_heads, hd, max_seq,
          hd ** -0.5 if scale is None else scale, _p(scratch), _p(err), _s(stream))
+    return out
+
+
+def sample_topk(logits, u, temperature=1.0, top_k=50, history=None, history_len=None,
+                penalty=1.0, out=None, stream=None):
+    """Per row: repetition penalty (in place on logits) then top-k sampling with draw u[row].
+    logits [rows, vocab] F32; history [rows, stride] int32 + history_len [rows]; u [rows]."""
+    import torch
+    rows, vocab = logits.shape
+    out = torch.empty(rows, dtype=torch.int32, device=logits.device) if out is None else out
+    stride = history.shape[1] if history is not None else 0
+    call("lai_sample_topk_f32", _p(out), _p(logits), vocab, rows, _p(history), _p(history_len),
+         stride, penalty, temperature, top_k, _p(u), _s(stream))
     return out
 
 

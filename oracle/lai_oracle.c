@@ -30,6 +30,7 @@
 #include "lai_oracle.h"
 
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 #ifdef _OPENMP
 #include <omp.h>
@@ -442,6 +443,83 @@ void oracle_decode_attention(float *out, const float *q, const float *k_cache,
         }
         for (int e = 0; e < head_dim; e++) o[e] = (float)(accv[e] / sum);
     }
+}
+
+/* ---------------------------------------------------------------------------
+ * Repetition penalty (tts_apply_repetition_penalty, src/tts_sampling.c:19-36): every
+ * distinct history token in [0, vocab) is penalised once.
+ * ------------------------------------------------------------------------- */
+void oracle_repetition_penalty(float *logits, int vocab, const int32_t *history, int history_len,
+                               float penalty) {
+    if (penalty <= 1.0f) return;
+    for (int i = 0; i < history_len; i++) {
+        const int tok = history[i];
+        if (tok < 0 || tok >= vocab) continue;
+        int dup = 0;
+        for (int j = 0; j < i && !dup; j++) dup = history[j] == tok;
+        if (dup) continue;
+        logits[tok] = logits[tok] > 0.0f ? logits[tok] / penalty : logits[tok] * penalty;
+    }
+}
+
+/* ---------------------------------------------------------------------------
+ * Top-k sampling (tts_sample_topk, src/tts_sampling.c:40-109). The candidate list is
+ * built in the reference's order: the first top_k tokens fill slots 0..k-1, then each
+ * later token strictly above the current minimum replaces the slot holding it (the
+ * first such slot), after which the minimum is searched again over the slots. The
+ * softmax at the temperature and the cumulative walk run over the slots in that order
+ * with float sums, and the first slot whose running sum reaches r = u * sum is taken
+ * (slot 0 when none does). The order matters: it decides which token a given u picks.
+ * ------------------------------------------------------------------------- */
+int oracle_sample_topk(const float *logits, int vocab, float temperature, int top_k, float u,
+                       float *margin, float *sum_out) {
+    if (top_k <= 0 || top_k > vocab) top_k = vocab;
+    float *val = (float *)malloc((size_t)top_k * sizeof(float));
+    int *idx = (int *)malloc((size_t)top_k * sizeof(int));
+    if (!val || !idx) {
+        free(val);
+        free(idx);
+        return -1;
+    }
+    int slot_min = 0;
+    for (int i = 0; i < top_k; i++) {
+        val[i] = logits[i];
+        idx[i] = i;
+        if (logits[i] < val[slot_min]) slot_min = i;
+    }
+    for (int i = top_k; i < vocab; i++) {
+        if (!(logits[i] > val[slot_min])) continue;
+        val[slot_min] = logits[i];
+        idx[slot_min] = i;
+        slot_min = 0;
+        for (int j = 1; j < top_k; j++)
+            if (val[j] < val[slot_min]) slot_min = j;
+    }
+    float mx = val[0];
+    for (int i = 1; i < top_k; i++)
+        if (val[i] > mx) mx = val[i];
+    float sum = 0.0f;
+    for (int i = 0; i < top_k; i++) {
+        val[i] = expf((val[i] - mx) / temperature);
+        sum += val[i];
+    }
+    const float r = u * sum;
+    float cum = 0.0f, best = INFINITY;
+    int sel = idx[0], found = 0;
+    for (int i = 0; i < top_k; i++) {
+        cum += val[i];
+        const float d = fabsf(cum - r);
+        if (d < best) best = d;
+        if (!found && cum >= r) {
+            sel = idx[i];
+            found = 1;
+        }
+    }
+    if (margin) *margin = best;
+    if (sum_out) *sum_out = sum;
+    free(val);
+    free(idx);
+    return sel;
 }
 
 /* ---------------------------------------------------------------------------

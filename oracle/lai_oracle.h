@@ -88,6 +88,17 @@ void oracle_decode_attention(float *out, const float *q, const float *k_cache,
                              const float *v_cache, const int32_t *pos, int n_seqs, int n_heads,
                              int n_kv_heads, int head_dim, int max_seq, float scale);
 
+/* ---- token sampling (src/tts_sampling.c) ----
+ * tts_apply_repetition_penalty (:19-36): each distinct valid history token's logit is
+ * divided by penalty if positive, else multiplied; nothing when penalty <= 1. */
+void oracle_repetition_penalty(float *logits, int vocab, const int32_t *history, int history_len,
+                               float penalty);
+/* tts_sample_topk (:40-109) with the uniform draw u = rand()/RAND_MAX passed in instead of
+ * taken from libc. Returns the token; *margin (may be NULL) receives the distance between
+ * r = u * sum and the nearest cumulative boundary, *sum the softmax denominator. */
+int oracle_sample_topk(const float *logits, int vocab, float temperature, int top_k, float u,
+                       float *margin, float *sum);
+
 /* ---- timed CPU reference: one decoder layer's elementwise chain, FP32, called in
  * the reference's own order (talker_prefill, src/tts_native.c:553-592) ---- */
 void oracle_layer_chain_f32(float *x, const float *delta_attn, const float *delta_ffn,

@@ -32,7 +32,7 @@ def build() -> None:
 
 
 def _lib_path(name: str) -> str:
-    sub = "_ref" if name.startswith("libvoc_ref") else "_build"
+    sub = "_ref" if name.startswith(("libvoc_ref", "libtts_sampling_ref")) else "_build"
     return os.path.join(HERE, sub, name)
 
 
@@ -48,6 +48,11 @@ def load(name: str = "liblai_oracle.so") -> ctypes.CDLL:
     lib = ctypes.CDLL(path)
     if name.startswith("liblai_"):
         _declare(lib)
+    elif name.startswith("libtts_sampling"):
+        lib.tts_apply_repetition_penalty.argtypes = [_F, _c_int, _I32, _c_int, _c_float]
+        lib.tts_apply_repetition_penalty.restype = None
+        lib.tts_sample_topk.argtypes = [_F, _c_int, _c_float, _c_int]
+        lib.tts_sample_topk.restype = _c_int
     else:
         lib.voc_snake_beta.argtypes = [_F, _F, _F, _c_int, _c_int]
         lib.voc_snake_beta.restype = None
@@ -91,6 +96,8 @@ def _declare(lib: ctypes.CDLL) -> None:
         "oracle_linear_bf16": [_F, _F, _U16, _c_int, _c_int, _c_int],
         "oracle_decode_attention": [_F, _F, _F, _F, _I32, _c_int, _c_int, _c_int, _c_int,
                                     _c_int, _c_float],
+        "oracle_repetition_penalty": [_F, _c_int, _I32, _c_int, _c_float],
+        "oracle_sample_topk": [_F, _c_int, _c_float, _c_int, _c_float, _F, _F],
         "oracle_voc_conv1d_causal": [_F, _F, _F, _F, _c_int, _c_int, _c_int, _c_int, _c_int],
         "oracle_voc_resunit": [_F, _F, _F, _F, _F, _F, _F, _F, _F, _c_int, _c_int, _c_int, _F],
         "oracle_num_threads": [],
@@ -99,7 +106,7 @@ def _declare(lib: ctypes.CDLL) -> None:
     for name, args in sig.items():
         fn = getattr(lib, name)
         fn.argtypes = args
-        fn.restype = _c_int if name == "oracle_num_threads" else None
+        fn.restype = _c_int if name in ("oracle_num_threads", "oracle_sample_topk") else None
     lib.oracle_f32_to_bf16.argtypes = [_c_float]
     lib.oracle_f32_to_bf16.restype = ctypes.c_uint16
 
@@ -406,3 +413,55 @@ def decode_attention(q, k_cache, v_cache, pos, n_heads, n_kv_heads, head_dim, sc
     lib.oracle_decode_attention(ptr(out), ptr(q), ptr(k_cache), ptr(v_cache), ptr(pos, _I32), S,
                                 n_heads, n_kv_heads, head_dim, max_seq, scale)
     return out
+
+
+# ---- token sampling (src/tts_sampling.c) ----
+
+def repetition_penalty(logits, history, penalty, lib=None):
+    lib = lib or load()
+    y = np.array(logits, np.float32, copy=True, order="C")
+    h = np.ascontiguousarray(history, np.int32)
+    lib.oracle_repetition_penalty(ptr(y), y.size, ptr(h, _I32), h.size, penalty)
+    return y
+
+
+def sample_topk(logits, temperature, top_k, u, lib=None):
+    """(token, margin, sum): tts_sample_topk's choice for the uniform draw u, the distance of
+    r = u * sum from the nearest cumulative boundary, and the softmax denominator."""
+    lib = lib or load()
+    y = np.ascontiguousarray(logits, np.float32)
+    m, sm = ctypes.c_float(), ctypes.c_float()
+    tok = lib.oracle_sample_topk(ptr(y), y.size, temperature, top_k, np.float32(u),
+                                 ctypes.byref(m), ctypes.byref(sm))
+    return tok, m.value, sm.value
+
+
+def have_ref_sampling() -> bool:
+    return os.path.exists(_lib_path("libtts_sampling_ref.so"))
+
+
+def ref_rand_draw(seed: int) -> float:
+    """The u that tts_sample_topk computes from libc's first rand() after srand(seed):
+    (float)rand() / (float)RAND_MAX in float arithmetic (src/tts_sampling.c:92)."""
+    libc = ctypes.CDLL(None)
+    libc.srand(ctypes.c_uint(seed))
+    x = libc.rand()
+    return float(np.float32(x) / np.float32(2147483647))
+
+
+def ref_sample_topk(logits, temperature, top_k, seed: int):
+    """The reference's own tts_sample_topk (compiled from src/tts_sampling.c), its rand()
+    seeded with srand(seed) just before the call."""
+    lib = load("libtts_sampling_ref.so")
+    y = np.array(logits, np.float32, copy=True, order="C")
+    libc = ctypes.CDLL(None)
+    libc.srand(ctypes.c_uint(seed))
+    return lib.tts_sample_topk(ptr(y), y.size, temperature, top_k)
+
+
+def ref_repetition_penalty(logits, history, penalty):
+    lib = load("libtts_sampling_ref.so")
+    y = np.array(logits, np.float32, copy=True, order="C")
+    h = np.ascontiguousarray(history, np.int32)
+    lib.tts_apply_repetition_penalty(ptr(y), y.size, ptr(h, _I32), h.size, penalty)
+    return y

@@ -152,3 +152,30 @@ def test_resunit_restatement_against_reference_functions():
     for d in (1, 3, 9):
         got, ref = oracle.voc_resunit(x, p, d), oracle.ref_voc_resunit(x, p, d)
         assert np.max(np.abs(got - ref)) / max(1.0, np.max(np.abs(ref))) <= 1e-5
+
+
+@pytest.mark.skipif(not oracle.have_ref_sampling(), reason="oracle/_ref not built (reference absent)")
+@pytest.mark.parametrize("vocab,top_k,temp", [(3072, 50, 0.9), (2048, 50, 0.7), (3072, 1, 1.0),
+                                              (300, 0, 1.3), (3072, 3072, 0.8), (100, 7, 0.5)])
+def test_sampling_restatement_matches_reference_build(vocab, top_k, temp):
+    # the reference's own tts_sample_topk, its rand() driven by srand(seed), against the
+    # restatement given the same draw: identical tokens
+    rng = np.random.default_rng(vocab + top_k)
+    for trial in range(200):
+        logits = (rng.standard_normal(vocab) * (1 + trial % 5)).astype(np.float32)
+        if trial % 7 == 0:
+            logits[rng.integers(0, vocab, 20)] = logits.max()  # ties at the top
+        seed = 1000 + trial
+        want = oracle.ref_sample_topk(logits, temp, top_k, seed)
+        got, _, _ = oracle.sample_topk(logits, temp, top_k, oracle.ref_rand_draw(seed))
+        assert got == want, (trial, got, want)
+
+
+@pytest.mark.skipif(not oracle.have_ref_sampling(), reason="oracle/_ref not built (reference absent)")
+def test_repetition_penalty_matches_reference_build():
+    rng = np.random.default_rng(1)
+    logits = rng.standard_normal(3072).astype(np.float32)
+    hist = rng.integers(-5, 3100, 200).astype(np.int32)  # repeats and out-of-range ids
+    for pen in (1.0, 1.05, 1.3):
+        assert np.array_equal(oracle.repetition_penalty(logits, hist, pen),
+                              oracle.ref_repetition_penalty(logits, hist, pen))
