@@ -240,6 +240,27 @@ typedef struct {
 LAI_API int lai_voc_resunits_f32(float *x, float *scratch, const lai_voc_resunit_t *units,
                                  int n_units, int batch, int channels, int T, int passes,
                                  int *err, lai_stream_t stream);
+/* ---- vocoder ConvNeXt block (upsample stages) --------------------------------------------
+ * run_convnext(x, C, T, cn) (src/tts_vocoder.c:463-533): depthwise causal conv k=7 + bias,
+ * LayerNorm over channels (eps 1e-6), pointwise C -> 4C + bias, exact GELU, pointwise
+ * 4C -> C + bias, * gamma, + residual; in place on channels-last x [batch, T, C].
+ * C in {128, 256, 512, 1024, 2048} (the reference: 1024). scratch: 10 * batch * T * C
+ * floats. passes as for the ResUnits. dw_b, norm_w, norm_b 16-byte aligned.
+ */
+typedef struct {
+    const float *dw_w;             /* [C, 1, 7] depthwise weight, as loaded */
+    const float *dw_b;             /* [C] */
+    const float *norm_w, *norm_b;  /* [C] LayerNorm scale, shift */
+    const float *pw1_w;            /* lai_voc_pack_conv_f32 image of [4C, C, 1] */
+    const float *pw1_b;            /* [4C] */
+    const float *pw2_w;            /* lai_voc_pack_conv_f32 image of [C, 4C, 1] */
+    const float *pw2_b;            /* [C] */
+    const float *gamma;            /* [C] layer scale */
+} lai_voc_convnext_t;
+
+LAI_API int lai_voc_convnext_f32(float *x, float *scratch, const lai_voc_convnext_t *p, int batch,
+                                 int channels, int T, int passes, int *err, lai_stream_t stream);
+
 /* dst (2 * c_out * c_in * kernel floats) <- reference conv weight w [c_out, c_in, kernel]
  * regrouped per tap as [2][kernel][c_out][c_in]: TF32 high parts, then the remainders. */
 LAI_API int lai_voc_pack_conv_f32(float *dst, const float *w, int c_out, int c_in, int kernel,

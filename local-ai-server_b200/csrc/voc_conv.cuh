@@ -1,0 +1,411 @@
+// voc_conv.cuh - causal conv1d / pointwise conv as an implicit GEMM on tcgen05 tensor cores
+// (kind::tf32, F32 results), shared by the vocoder's ResUnit (voc_resunit.cu) and ConvNeXt
+// (voc_convnext.cu) blocks. Each including file instantiates the epilogues it uses.
+//
+// Layout. Activations are channels-last, [batch, T, C] F32, so that a convolution
+// tap is a shift along time = the OUTER coordinate of a TMA tile: tap k of output
+// rows [t0, t0 + 128) reads input rows starting at t0 - (taps-1-k) * d; a negative
+// start reads the tensor map's zero fill (the causal padding) and the inner (channel)
+// coordinate stays a multiple of 16 floats. A convolution is then the implicit GEMM
+// D[t, o] = sum_{k, c} S[t - (taps-1-k) d, c] * W_k[o, c] with M = time, N = output
+// channels, K = taps x input channels; no im2col buffer exists (the reference's
+// voc_conv1d_causal, src/tts_vocoder_ops.c:44-147, pads, builds im2col and calls SGEMM).
+//
+// Precision (3 passes, the default). kind::tf32 multiplies 10-bit-mantissa inputs,
+// so every operand is carried as a pair hi = tf32(v), lo = v - hi (both exact in
+// F32) and each product is hi*hi + hi*lo + lo*hi: the dropped lo*lo term and the
+// TF32 view of lo are ~2^-21 relative, below F32 round-off of the reference's own
+// sums. passes = 1 uses hi*hi alone (plain TF32). Activation planes are written in
+// this split form by the epilogue that produces them, weights by lai_voc_pack_conv_f32.
+//
+// Kernel: one CTA per 128-row x BN-channel output tile, 320 threads. Warp 0 issues
+// TMA loads into a STAGES-deep ring (64-byte-swizzled K-major tiles of 16 channels),
+// warp 1 owns TMEM and issues tcgen05.mma from one thread, warps 2-9 drain finished
+// K chunks from TMEM (lane quarter = warp % 4, half the columns each) into F32
+// registers and finally run the epilogue and store to HBM through a per-warp
+// shared-memory transpose (coalesced). Every mbarrier wait is bounded (globaltimer);
+// a timeout sets LAI_DEVERR_TIMEOUT in *err and the CTA still releases its TMEM.
+#pragma once
+
+#include <mutex>
+
+#include "lai_common.cuh"
+#include "snake_math.cuh"
+#include "umma.cuh"
+
+namespace lai {
+namespace {
+
+constexpr int kBM = 128;        // output time rows per tile = UMMA M = TMEM lanes
+constexpr int kBK = 16;         // input channels per K block: one 64-byte row of F32
+constexpr int kUmmaK = 8;       // K of one kind::tf32 MMA (32 bytes)
+constexpr int kEpiWarps = 8;    // two per TMEM lane quarter, each half of the columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA + TMEM, 2..9 drain
+constexpr int kChunkBlocks = 2; // K blocks per TMEM accumulation chunk (32 input channels)
+constexpr int kSmemTiles = 192 * 1024;
+constexpr int kEpiPitch = 33;   // floats per row of a drain warp's 32 x 32 transpose buffer
+constexpr uint32_t kEpiBytes = kEpiWarps * 32 * kEpiPitch * 4;
+constexpr int kMaxStages = 8;
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s: far beyond any healthy wait
+
+// Epilogues: conv1 of a ResUnit (bias, snake2, split store); conv2 of a ResUnit (bias,
+// residual in place, then the next unit's snake1 + split store when ea != null);
+// ConvNeXt pw1 (bias, exact GELU, split store); ConvNeXt pw2 (bias, * gamma, residual).
+enum Epi { kEpiSnakeSplit = 0, kEpiResidual = 1, kEpiGelu = 2, kEpiScaleResidual = 3 };
+
+struct ConvArgs {
+    float *out_hi, *out_lo;  // split output planes (kEpiResidual: next unit's input, or null)
+    float *x;                // kEpiResidual: residual stream, updated in place
+    const float *bias;       // [c_out]
+    const float *ea, *ieb;   // snake applied to the output (kEpiResidual: next snake1, or null)
+    const float *gamma;      // kEpiScaleResidual: per-channel layer scale
+    int T, c_in, c_out, taps, dilation;
+    int *err;
+};
+
+template <int BN, int PASSES>
+struct Tile {
+    static constexpr uint32_t kA = kBM * kBK * 4;  // 8 KiB
+    static constexpr uint32_t kB = BN * kBK * 4;
+    static constexpr uint32_t kStage = (kA + kB) * (PASSES == 3 ? 2u : 1u);
+    static constexpr int kStages =
+        (int)(kSmemTiles / kStage) < kMaxStages ? (int)(kSmemTiles / kStage) : kMaxStages;
+    // align slack + operand ring + the drain warps' transpose buffers + barriers
+    static constexpr uint32_t kSmem = 1024 + kStages * kStage + kEpiBytes + 256;
+    // two accumulator buffers: the MMAs fill one chunk while the other is drained
+    static constexpr uint32_t kBufCols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+    static constexpr uint32_t kTmemCols = 2 * kBufCols;
+    static constexpr int kHalf = BN / 2;  // columns per drain warp
+    static_assert(kA % 1024 == 0 && kB % 1024 == 0, "tiles must keep 1 KiB alignment");
+    static_assert(kStages >= 2, "pipeline needs two stages");
+    static_assert(kHalf % 16 == 0, "drain warps read 16-column groups");
+};
+
+__device__ __forceinline__ void store4(float *p, float a, float b, float c, float d) {
+    *reinterpret_cast<float4 *>(p) = make_float4(a, b, c, d);
+}
+
+// Epilogue for 4 finished sums of output row `row` (global index), channels [c, c + 4).
+// `xr` holds x[row, c..c+3] for the residual epilogues, loaded earlier.
+template <int PASSES, int EPI>
+__device__ __forceinline__ void epilogue4(const ConvArgs &a, float (&v)[4], const float4 &xr,
+                                          size_t row, int c) {
+    const size_t off = row * (size_t)a.c_out + c;
+#pragma unroll
+    for (int i = 0; i < 4; i++) v[i] += __ldg(a.bias + c + i);
+    if (EPI == kEpiScaleResidual) {  // x = (W h + b) * gamma + x  (run_convnext order)
+        const float r[4] = {xr.x, xr.y, xr.z, xr.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) v[i] = v[i] * __ldg(a.gamma + c + i) + r[i];
+        store4(a.x + off, v[0], v[1], v[2], v[3]);
+        return;
+    }
+    if (EPI == kEpiResidual) {
+        v[0] += xr.x; v[1] += xr.y; v[2] += xr.z; v[3] += xr.w;
+        store4(a.x + off, v[0], v[1], v[2], v[3]);
+        if (a.ea == nullptr) return;
+    }
+    float hi[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        if (EPI == kEpiGelu)
+            v[i] = 0.5f * v[i] * (1.0f + erff(v[i] * 0.7071067811865475f));  // voc_gelu
+        else
+            v[i] = snake1(v[i], __ldg(a.ea + c + i), __ldg(a.ieb + c + i));
+        hi[i] = umma::tf32_round(v[i]);
+    }
+    store4(a.out_hi + off, hi[0], hi[1], hi[2], hi[3]);
+    if (PASSES == 3)
+        store4(a.out_lo + off, v[0] - hi[0], v[1] - hi[1], v[2] - hi[2], v[3] - hi[3]);
+}
+
+// Accumulation. The tensor core's F32 accumulation does not round to nearest: measured
+// against double sums, its error grows linearly with the number of MMAs that update one
+// accumulator and leans toward zero (biased), reaching ~2e-4 relative for a 7 x 768
+// channel sum. Chunks of 2 blocks (6 MMAs per fresh accumulator with 3 passes) bring a
+// 768-channel unit to ~3e-6 of the double-precision oracle; 4 blocks gave ~5e-6. So K is cut into chunks of kChunkBlocks blocks; each chunk starts a fresh
+// TMEM accumulator (alternating between two buffers) and the drain warps add the
+// finished chunk into F32 registers with round-to-nearest adds while the MMAs fill the
+// other buffer. Chunk errors then carry each chunk's own sign and largely cancel.
+//
+// act_map: [2 planes][batch][T][c_in] (hi, lo); w_map: [2 * taps][c_out][c_in] (hi taps,
+// then lo taps). Grid: (ceil(T / 128), c_out / BN, batch).
+template <int BN, int PASSES, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
+                 const __grid_constant__ CUtensorMap w_map, const ConvArgs a) {
+    using L = Tile<BN, PASSES>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *tiles = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    float *epi_buf = reinterpret_cast<float *>(tiles + L::kStages * L::kStage);
+    uint64_t *full = reinterpret_cast<uint64_t *>(tiles + L::kStages * L::kStage + kEpiBytes);
+    uint64_t *empty = full + L::kStages;
+    uint64_t *acc_full = empty + L::kStages;  // [2]: chunk ready in buffer b
+    uint64_t *acc_empty = acc_full + 2;       // [2]: buffer b drained
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int t0 = blockIdx.x * kBM, n0 = blockIdx.y * BN, b = blockIdx.z;
+    const int kblocks = a.c_in / kBK;
+    const int n_iter = a.taps * kblocks;
+    const int n_chunks = (n_iter + kChunkBlocks - 1) / kChunkBlocks;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < L::kStages; s++) {
+            bulk::mbar_init(&full[s], 1);
+            bulk::mbar_init(&empty[s], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            bulk::mbar_init(&acc_full[i], 1);
+            bulk::mbar_init(&acc_empty[i], kEpiWarps);
+        }
+        bulk::fence_barrier_init();
+        umma::prefetch_tensormap(&act_map);
+        umma::prefetch_tensormap(&w_map);
+    }
+    if (warp == 1) {
+        umma::tmem_alloc(tmem_slot, L::kTmemCols);
+        umma::tmem_relinquish();
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    bool ok = true;
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer
+            for (int it = 0; it < n_iter; it++) {
+                const int s = it % L::kStages;
+                if (it >= L::kStages &&
+                    !bulk::mbar_wait_bounded(&empty[s], ((it / L::kStages) + 1) & 1, kWaitNs)) {
+                    ok = false;
+                    break;
+                }
+                const int tap = it / kblocks, kb = it - tap * kblocks;
+                const int c = kb * kBK;
+                const int row = t0 - (a.taps - 1 - tap) * a.dilation;
+                uint8_t *st = tiles + s * L::kStage;
+                bulk::mbar_arrive_expect_tx(&full[s], L::kStage);
+                umma::tma_load_4d(st, &act_map, c, row, b, 0, &full[s]);
+                umma::tma_load_3d(st + L::kA, &w_map, c, n0, tap, &full[s]);
+                if (PASSES == 3) {
+                    umma::tma_load_4d(st + L::kA + L::kB, &act_map, c, row, b, 1, &full[s]);
+                    umma::tma_load_3d(st + 2 * L::kA + L::kB, &w_map, c, n0, a.taps + tap,
+                                      &full[s]);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer
+            constexpr uint32_t idesc = umma::idesc_tf32<kBM, BN>();
+            for (int it = 0; it < n_iter; it++) {
+                const int s = it % L::kStages;
+                const int j = it / kChunkBlocks;
+                const bool first = it - j * kChunkBlocks == 0;
+                if (first && j >= 2 &&
+                    !bulk::mbar_wait_bounded(&acc_empty[j & 1], ((j >> 1) - 1) & 1, kWaitNs)) {
+                    ok = false;
+                    break;
+                }
+                if (!bulk::mbar_wait_bounded(&full[s], (it / L::kStages) & 1, kWaitNs)) {
+                    ok = false;
+                    break;
+                }
+                umma::fence_after_sync();
+                const uint32_t d = tmem + (uint32_t)(j & 1) * L::kBufCols;
+                const uint32_t st = umma::smem_addr(tiles + s * L::kStage);
+#pragma unroll
+                for (int k = 0; k < kBK / kUmmaK; k++) {
+                    const uint32_t kofs = k * kUmmaK * 4;
+                    const uint64_t ah = umma::desc_kmajor_sw64(st + kofs);
+                    const uint64_t bh = umma::desc_kmajor_sw64(st + L::kA + kofs);
+                    umma::mma_tf32(d, ah, bh, idesc, (first && k == 0) ? 0u : 1u);
+                    if (PASSES == 3) {
+                        const uint64_t al = umma::desc_kmajor_sw64(st + L::kA + L::kB + kofs);
+                        const uint64_t bl =
+                            umma::desc_kmajor_sw64(st + 2 * L::kA + L::kB + kofs);
+                        umma::mma_tf32(d, ah, bl, idesc, 1);
+                        umma::mma_tf32(d, al, bh, idesc, 1);
+                    }
+                }
+                umma::commit(&empty[s]);  // frees the stage once these MMAs have read it
+                if (it - j * kChunkBlocks == kChunkBlocks - 1 || it == n_iter - 1)
+                    umma::commit(&acc_full[j & 1]);
+            }
+        }
+        __syncwarp();
+    } else {  // drain / epilogue warps 2..9
+        const int q = warp & 3;                 // the TMEM lane quarter this warp may read
+        const int half = (warp - 2) >> 2;       // which half of the BN columns
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        float sum[L::kHalf];
+#pragma unroll
+        for (int i = 0; i < L::kHalf; i++) sum[i] = 0.0f;
+        for (int j = 0; j < n_chunks; j++) {
+            if (!bulk::mbar_wait_bounded(&acc_full[j & 1], (j >> 1) & 1, kWaitNs)) {
+                ok = false;
+                break;
+            }
+            umma::fence_after_sync();
+            const uint32_t base = tmem + lane_addr + (uint32_t)(j & 1) * L::kBufCols +
+                                  (uint32_t)(half * L::kHalf);
+#pragma unroll
+            for (int g = 0; g < L::kHalf / 16; g++) {
+                uint32_t r[16];
+                umma::tmem_ld_32x32b_x16(base + g * 16, r);
+                umma::tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 16; i++) sum[g * 16 + i] += __uint_as_float(r[i]);
+            }
+            umma::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) bulk::mbar_arrive(&acc_empty[j & 1]);
+        }
+        if (ok) {
+            // Coalesced epilogue: the warp's 32 rows x GW columns of sums go through a
+            // padded shared-memory buffer (row per lane in, conflict-free) and come back
+            // as GW/4 lanes per row, 4 consecutive channels each, so every global load and
+            // store covers whole 32-byte sectors (a 128-byte line per row when GW = 32).
+            constexpr int GW = L::kHalf % 32 == 0 ? 32 : 16;
+            constexpr int LPR = GW / 4;    // lanes per row
+            constexpr int RPP = 32 / LPR;  // rows per pass
+            constexpr int NP = 32 / RPP;   // passes over the 32 rows
+            float *buf = epi_buf + (warp - 2) * 32 * kEpiPitch;
+            const int r_off = lane / LPR, c4 = (lane % LPR) * 4;
+            const int row0 = t0 + q * 32;
+#pragma unroll
+            for (int g = 0; g < L::kHalf / GW; g++) {
+                const int c = n0 + half * L::kHalf + g * GW + c4;
+#pragma unroll
+                for (int i = 0; i < GW; i++) buf[lane * kEpiPitch + i] = sum[g * GW + i];
+                __syncwarp();
+                constexpr int PB = NP < 4 ? NP : 4;  // passes whose residual loads fly together
+#pragma unroll
+                for (int p0 = 0; p0 < NP; p0 += PB) {
+                    float4 xr[PB];
+                    if (EPI == kEpiResidual || EPI == kEpiScaleResidual) {
+#pragma unroll
+                        for (int p = 0; p < PB; p++) {
+                            const int t = row0 + (p0 + p) * RPP + r_off;
+                            xr[p] = t < a.T ? *reinterpret_cast<const float4 *>(
+                                                  a.x + ((size_t)b * a.T + t) * a.c_out + c)
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+                    }
+#pragma unroll
+                    for (int p = 0; p < PB; p++) {
+                        const int r = (p0 + p) * RPP + r_off;
+                        float v[4];
+#pragma unroll
+                        for (int i = 0; i < 4; i++) v[i] = buf[r * kEpiPitch + c4 + i];
+                        const int t = row0 + r;
+                        if (t < a.T)
+                            epilogue4<PASSES, EPI>(a, v, EPI == kEpiSnakeSplit || EPI == kEpiGelu ? xr[0] : xr[p],
+                                                   (size_t)b * a.T + t, c);
+                    }
+                }
+                __syncwarp();
+            }
+        }
+    }
+    if (!ok && a.err) atomicOr(a.err, LAI_DEVERR_TIMEOUT);
+    umma::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        umma::fence_after_sync();
+        umma::tmem_dealloc(tmem, L::kTmemCols);
+    }
+}
+
+// ---- host side: tensor maps and launches ------------------------------------------
+
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                 const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                 const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    return fn;
+}
+
+// [2][batch][T][C] split activation planes, box 16 channels x 128 rows.
+bool act_map(CUtensorMap *m, const float *planes, int batch, int T, int C) {
+    const cuuint64_t dims[4] = {(cuuint64_t)C, (cuuint64_t)T, (cuuint64_t)batch, 2};
+    const cuuint64_t strides[3] = {(cuuint64_t)C * 4, (cuuint64_t)T * C * 4,
+                                   (cuuint64_t)batch * T * C * 4};
+    const cuuint32_t box[4] = {kBK, kBM, 1, 1};
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float *>(planes), dims,
+                       strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                       CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// [2 * taps][c_out][c_in] packed weights, box 16 channels x bn rows.
+bool weight_map(CUtensorMap *m, const float *w, int taps, int c_out, int c_in, int bn) {
+    const cuuint64_t dims[3] = {(cuuint64_t)c_in, (cuuint64_t)c_out, (cuuint64_t)2 * taps};
+    const cuuint64_t strides[2] = {(cuuint64_t)c_in * 4, (cuuint64_t)c_out * c_in * 4};
+    const cuuint32_t box[3] = {kBK, (cuuint32_t)bn, 1};
+    const cuuint32_t es[3] = {1, 1, 1};
+    return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(w), dims,
+                       strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                       CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int pick_bn(int c_out) {
+    for (int bn : {256, 192, 128, 96, 64, 32})
+        if (c_out % bn == 0) return bn;
+    return 0;
+}
+
+template <int BN, int PASSES, int EPI>
+int launch_conv_t(const CUtensorMap &am, const CUtensorMap &wm, const ConvArgs &a, int batch,
+                  cudaStream_t st) {
+    using L = Tile<BN, PASSES>;
+    auto kern = conv_umma_kernel<BN, PASSES, EPI>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kSmem) !=
+        cudaSuccess)
+        return LAI_ERR_CUDA;
+    const dim3 grid((unsigned)((a.T + kBM - 1) / kBM), (unsigned)(a.c_out / BN), (unsigned)batch);
+    kern<<<grid, kThreads, L::kSmem, st>>>(am, wm, a);
+    return launch_status();
+}
+
+template <int PASSES, int EPI>
+int launch_conv_p(int bn, const CUtensorMap &am, const CUtensorMap &wm, const ConvArgs &a,
+                  int batch, cudaStream_t st) {
+    switch (bn) {
+        case 256: return launch_conv_t<256, PASSES, EPI>(am, wm, a, batch, st);
+        case 192: return launch_conv_t<192, PASSES, EPI>(am, wm, a, batch, st);
+        case 128: return launch_conv_t<128, PASSES, EPI>(am, wm, a, batch, st);
+        case 96: return launch_conv_t<96, PASSES, EPI>(am, wm, a, batch, st);
+        case 64: return launch_conv_t<64, PASSES, EPI>(am, wm, a, batch, st);
+        case 32: return launch_conv_t<32, PASSES, EPI>(am, wm, a, batch, st);
+        default: return LAI_ERR_INVALID;
+    }
+}
+
+template <int EPI>
+int launch_conv(int passes, const CUtensorMap &am, const CUtensorMap &wm, const ConvArgs &a,
+                int batch, cudaStream_t st) {
+    const int bn = pick_bn(a.c_out);
+    return passes == 3 ? launch_conv_p<3, EPI>(bn, am, wm, a, batch, st)
+                       : launch_conv_p<1, EPI>(bn, am, wm, a, batch, st);
+}
+
+}  // namespace
+}  // namespace lai

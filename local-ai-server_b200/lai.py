@@ -51,6 +51,7 @@ SIGNATURES: dict[str, tuple] = {
                                         _i32, _i32, _f32, _vp, _vp, _vp]),
     "lai_sample_topk_f32": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp, _i32, _f32, _f32, _i32, _vp,
                                    _vp]),
+    "lai_voc_convnext_f32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp]),
     "lai_voc_resunits_f32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
     "lai_voc_pack_conv_f32": (_i32, [_vp, _vp, _i32, _i32, _i32, _vp]),
     "lai_voc_transpose_f32": (_i32, [_vp, _vp, _i32, _i32, _i32, _vp]),
@@ -294,6 +295,34 @@ class VocResUnit(ctypes.Structure):
     _fields_ = [("snake1_ea", _vp), ("snake1_ieb", _vp), ("conv1_w", _vp), ("conv1_b", _vp),
                 ("snake2_ea", _vp), ("snake2_ieb", _vp), ("conv2_w", _vp), ("conv2_b", _vp),
                 ("dilation", _i32)]
+
+
+class VocConvNeXt(ctypes.Structure):
+    """lai_voc_convnext_t: device pointers of one ConvNeXt block's parameters."""
+    _fields_ = [("dw_w", _vp), ("dw_b", _vp), ("norm_w", _vp), ("norm_b", _vp),
+                ("pw1_w", _vp), ("pw1_b", _vp), ("pw2_w", _vp), ("pw2_b", _vp), ("gamma", _vp)]
+
+
+def voc_convnext_params(p):
+    """p: dict of CUDA tensors in the reference's layouts (dw_w [C,1,7], pw1_w [4C,C,1],
+    pw2_w [C,4C,1], ...). Returns (lai_voc_convnext_t, tensors kept alive)."""
+    w1, w2 = voc_pack_conv(p["pw1_w"]), voc_pack_conv(p["pw2_w"])
+    st = VocConvNeXt(p["dw_w"].data_ptr(), p["dw_b"].data_ptr(), p["norm_w"].data_ptr(),
+                     p["norm_b"].data_ptr(), w1.data_ptr(), p["pw1_b"].data_ptr(), w2.data_ptr(),
+                     p["pw2_b"].data_ptr(), p["gamma"].data_ptr())
+    return st, [w1, w2, p]
+
+
+def voc_convnext(x, params, scratch=None, passes=3, err=None, stream=None):
+    """In place on x [batch, T, C]; params from voc_convnext_params()."""
+    import torch
+    b, t, c = (1, *x.shape) if x.dim() == 2 else x.shape
+    if scratch is None:
+        scratch = torch.empty(10 * b * t * c, dtype=torch.float32, device=x.device)
+    st = params[0] if isinstance(params, tuple) else params
+    call("lai_voc_convnext_f32", _p(x), _p(scratch), ctypes.byref(st), b, c, t, passes, _p(err),
+         _s(stream))
+    return x
 
 
 def voc_pack_conv(w, stream=None):

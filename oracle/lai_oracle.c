@@ -404,6 +404,81 @@ void oracle_voc_resunit(float *x, const float *ea1, const float *ieb1, const flo
 }
 
 /* ---------------------------------------------------------------------------
+ * ConvNeXt pieces. Depthwise causal conv: voc_conv1d_causal with groups == c_in ==
+ * c_out (src/tts_vocoder_ops.c:52-73), out[c,t] = b[c] + sum_k w[c,k] x[c, t-(K-1)+k]
+ * (zero before t = 0), summed in acc_t in tap order. out may equal in (the reference
+ * pads into scratch first); here a row copy keeps that safe.
+ * ------------------------------------------------------------------------- */
+void oracle_voc_conv1d_depthwise(float *out, const float *in, const float *w, const float *bias,
+                                 int channels, int T, int kernel) {
+#pragma omp parallel for schedule(static)
+    for (int c = 0; c < channels; c++) {
+        float *row = (float *)malloc((size_t)T * sizeof(float));
+        if (!row) continue;
+        memcpy(row, in + (size_t)c * T, (size_t)T * sizeof(float));
+        for (int t = 0; t < T; t++) {
+            acc_t s = 0;
+            for (int k = 0; k < kernel; k++) {
+                const int src = t - (kernel - 1) + k;
+                if (src >= 0) s += (acc_t)w[(size_t)c * kernel + k] * row[src];
+            }
+            out[(size_t)c * T + t] = (float)s + (bias ? bias[c] : 0.0f);
+        }
+        free(row);
+    }
+}
+
+/* LayerNorm over channels at each time step of x [C, T] (voc_layer_norm_channels,
+ * src/tts_vocoder_ops.c:311-336): mean, then the mean of squared deviations, then
+ * (x - mean) / sqrt(var + eps) * w + b; sums in acc_t. */
+void oracle_voc_layer_norm_channels(float *x, const float *w, const float *b, int channels, int T,
+                                    float eps) {
+#pragma omp parallel for schedule(static)
+    for (int t = 0; t < T; t++) {
+        acc_t mean = 0, var = 0;
+        for (int c = 0; c < channels; c++) mean += x[(size_t)c * T + t];
+        mean /= channels;
+        for (int c = 0; c < channels; c++) {
+            const acc_t d = x[(size_t)c * T + t] - mean;
+            var += d * d;
+        }
+        var /= channels;
+        const float inv_std = 1.0f / sqrtf((float)var + eps);
+        for (int c = 0; c < channels; c++) {
+            const float v = (x[(size_t)c * T + t] - (float)mean) * inv_std;
+            x[(size_t)c * T + t] = v * w[c] + b[c];
+        }
+    }
+}
+
+/* Exact GELU: 0.5 x (1 + erf(x / sqrt 2)) (voc_gelu, src/tts_vocoder_ops.c:344-349). */
+void oracle_voc_gelu(float *x, int64_t n) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; i++) x[i] = 0.5f * x[i] * (1.0f + erff(x[i] * 0.7071067811865475f));
+}
+
+/* run_convnext (src/tts_vocoder.c:463-533) in place on x [C, T]:
+ *   r = x; x = dwconv(x) + dw_b; x = LN_c(x); h = gelu(W1 x + b1) (W1 [4C, C]);
+ *   x = W2 h + b2 (W2 [C, 4C]); x = x * gamma; x = x + r
+ * scratch: 5 * C * T floats (the residual copy and h). */
+void oracle_voc_convnext(float *x, const float *dw_w, const float *dw_b, const float *norm_w,
+                         const float *norm_b, const float *pw1_w, const float *pw1_b,
+                         const float *pw2_w, const float *pw2_b, const float *gamma, int C, int T,
+                         float *scratch) {
+    const size_t cT = (size_t)C * T;
+    float *res = scratch, *h = scratch + cT;
+    memcpy(res, x, cT * sizeof(float));
+    oracle_voc_conv1d_depthwise(x, x, dw_w, dw_b, C, T, 7);
+    oracle_voc_layer_norm_channels(x, norm_w, norm_b, C, T, 1e-6f);
+    oracle_voc_conv1d_causal(h, x, pw1_w, pw1_b, C, 4 * C, T, 1, 1);
+    oracle_voc_gelu(h, (int64_t)4 * cT);
+    oracle_voc_conv1d_causal(x, h, pw2_w, pw2_b, 4 * C, C, T, 1, 1);
+    for (int c = 0; c < C; c++)
+        for (int t = 0; t < T; t++) x[(size_t)c * T + t] *= gamma[c];
+    for (size_t i = 0; i < cT; i++) x[i] += res[i];
+}
+
+/* ---------------------------------------------------------------------------
  * Decode attention: one query token per sequence (qwen_causal_attention with
  * seq_q = 1 and q_offset = pos, src/tts_native.c:650-656; the math is the repo's numpy
  * specification tools/verify_xfmr.py:57-77: scores = q.k * scale, max-subtracted

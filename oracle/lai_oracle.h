@@ -79,6 +79,20 @@ void oracle_voc_resunit(float *x, const float *ea1, const float *ieb1, const flo
                         const float *b1, const float *ea2, const float *ieb2, const float *w2,
                         const float *b2, int C, int T, int dilation, float *scratch);
 
+/* ConvNeXt pieces (src/tts_vocoder_ops.c): depthwise causal conv (voc_conv1d_causal with
+ * groups == channels, :52-73; w [C, 1, kernel]), LayerNorm over channels per time step
+ * (voc_layer_norm_channels, :311-336), exact GELU (voc_gelu, :344-349); and the block
+ * run_convnext (src/tts_vocoder.c:463-533) in place on x [C, T]; scratch 5 * C * T floats */
+void oracle_voc_conv1d_depthwise(float *out, const float *in, const float *w, const float *bias,
+                                 int channels, int T, int kernel);
+void oracle_voc_layer_norm_channels(float *x, const float *w, const float *b, int channels, int T,
+                                    float eps);
+void oracle_voc_gelu(float *x, int64_t n);
+void oracle_voc_convnext(float *x, const float *dw_w, const float *dw_b, const float *norm_w,
+                         const float *norm_b, const float *pw1_w, const float *pw1_b,
+                         const float *pw2_w, const float *pw2_b, const float *gamma, int C, int T,
+                         float *scratch);
+
 /* ---- decode attention, one query token per sequence (qwen_causal_attention with seq_q = 1,
  * src/tts_native.c:650-656; math of tools/verify_xfmr.py:57-77). q [n_seqs, n_heads*hd];
  * caches [n_seqs, max_seq, n_kv*hd]; keys 0..pos[s] (the reference appends the new k/v at

@@ -56,6 +56,10 @@ def load(name: str = "liblai_oracle.so") -> ctypes.CDLL:
     else:
         lib.voc_snake_beta.argtypes = [_F, _F, _F, _c_int, _c_int]
         lib.voc_snake_beta.restype = None
+        lib.voc_layer_norm_channels.argtypes = [_F, _F, _F, _c_int, _c_int, _c_float]
+        lib.voc_layer_norm_channels.restype = None
+        lib.voc_gelu.argtypes = [_F, _c_int]
+        lib.voc_gelu.restype = None
         lib.voc_conv1d_causal.argtypes = [_F, _F, _F, _F, _c_int, _c_int, _c_int, _c_int,
                                           _c_int, _c_int, _F]
         lib.voc_conv1d_causal.restype = None
@@ -98,6 +102,10 @@ def _declare(lib: ctypes.CDLL) -> None:
                                     _c_int, _c_float],
         "oracle_repetition_penalty": [_F, _c_int, _I32, _c_int, _c_float],
         "oracle_sample_topk": [_F, _c_int, _c_float, _c_int, _c_float, _F, _F],
+        "oracle_voc_conv1d_depthwise": [_F, _F, _F, _F, _c_int, _c_int, _c_int],
+        "oracle_voc_layer_norm_channels": [_F, _F, _F, _c_int, _c_int, _c_float],
+        "oracle_voc_gelu": [_F, _c_i64],
+        "oracle_voc_convnext": [_F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _c_int, _c_int, _F],
         "oracle_voc_conv1d_causal": [_F, _F, _F, _F, _c_int, _c_int, _c_int, _c_int, _c_int],
         "oracle_voc_resunit": [_F, _F, _F, _F, _F, _F, _F, _F, _F, _c_int, _c_int, _c_int, _F],
         "oracle_num_threads": [],
@@ -464,4 +472,46 @@ def ref_repetition_penalty(logits, history, penalty):
     y = np.array(logits, np.float32, copy=True, order="C")
     h = np.ascontiguousarray(history, np.int32)
     lib.tts_apply_repetition_penalty(ptr(y), y.size, ptr(h, _I32), h.size, penalty)
+    return y
+
+
+# ---- ConvNeXt block (channels-first [C, T] per batch item) ----
+CONVNEXT_KEYS = ("dw_w", "dw_b", "norm_w", "norm_b", "pw1_w", "pw1_b", "pw2_w", "pw2_b", "gamma")
+
+
+def voc_convnext(x, p, lib=None):
+    """run_convnext on x [C, T] or [B, C, T]; p: dw_w [C,1,7], dw_b, norm_w, norm_b,
+    pw1_w [4C,C,1], pw1_b, pw2_w [C,4C,1], pw2_b, gamma."""
+    lib = lib or load()
+    y = np.array(x, np.float32, copy=True, order="C")
+    C, T = y.shape[-2], y.shape[-1]
+    rows = y.reshape(-1, C, T)
+    q = [np.ascontiguousarray(p[k], np.float32) for k in CONVNEXT_KEYS]
+    scratch = np.empty(5 * C * T, np.float32)
+    for b in range(rows.shape[0]):
+        lib.oracle_voc_convnext(ptr(rows[b]), *[ptr(a) for a in q], C, T, ptr(scratch))
+    return y
+
+
+def ref_voc_convnext(x, p, build: str = "scalar"):
+    """run_convnext's sequence (src/tts_vocoder.c:463-533) composed from the reference's own
+    compiled voc_conv1d_causal (depthwise branch, and k = 1 for the pointwise convs),
+    voc_layer_norm_channels and voc_gelu."""
+    lib = load(f"libvoc_ref_{build}.so")
+    y = np.array(x, np.float32, copy=True, order="C")
+    C, T = y.shape[-2], y.shape[-1]
+    rows = y.reshape(-1, C, T)
+    f = lambda a: np.ascontiguousarray(a, np.float32)  # noqa: E731
+    for b in range(rows.shape[0]):
+        r = rows[b].copy()
+        xin = rows[b].copy()
+        dw = np.empty((C, T), np.float32)
+        scratch = np.empty(C * (T + 6) + 16, np.float32)
+        lib.voc_conv1d_causal(ptr(dw), ptr(xin), ptr(f(p["dw_w"])), ptr(f(p["dw_b"])), C, C, T, 7,
+                              1, C, ptr(scratch))
+        lib.voc_layer_norm_channels(ptr(dw), ptr(f(p["norm_w"])), ptr(f(p["norm_b"])), C, T, 1e-6)
+        h = ref_voc_conv1d_causal(dw, p["pw1_w"], p["pw1_b"], 1, build)
+        lib.voc_gelu(ptr(h), h.size)
+        out = ref_voc_conv1d_causal(h, p["pw2_w"], p["pw2_b"], 1, build)
+        rows[b] = out * f(p["gamma"])[:, None] + r
     return y
