@@ -554,8 +554,126 @@ def cpu_attention_rate(seqs: int, n_heads: int, n_kv: int, max_seq: int, min_sec
             "seconds": el, "seqs": seqs}
 
 
-def run_attention(args) -> None:
-    """--config a3: decode attention of the TTS talker decode config (runner.DecodeAttention)."""
+def cpu_convnext_rate(stages, batch: int, min_seconds: float, sample_t: int = 500,
+                      steps: int | None = None, warmup: int = 1) -> dict:
+    """The reference's ConvNeXt block (run_convnext, src/tts_vocoder.c:463-533) on host cores
+    as its USE_BLAS build runs it: its own compiled voc_conv1d_causal (depthwise branch),
+    voc_layer_norm_channels and voc_gelu (oracle/_ref, single-threaded C as in the
+    reference) and the two pointwise convolutions as SGEMMs through numpy's OpenBLAS on
+    all host cores. `sample_t` time rows of one item per stage, scaled to the step."""
+    import numpy as np
+    from threadpoolctl import threadpool_limits
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle
+    lib = oracle.load("libvoc_ref_avx2.so")
+    P = oracle.ptr
+    nthreads = len(os.sched_getaffinity(0))
+    rng = np.random.default_rng(4)
+    f = lambda a: np.ascontiguousarray(a, np.float32)  # noqa: E731
+    data = []
+    for c, t_full in stages:
+        prm = {"dw_w": f(rng.standard_normal((c, 1, 7)) / np.sqrt(7)), "dw_b": f(rng.normal(0, .01, c)),
+               "nw": f(1 + rng.normal(0, .1, c)), "nb": f(rng.normal(0, .1, c)),
+               "w1": f(rng.standard_normal((4 * c, c)) / np.sqrt(c)), "b1": f(rng.normal(0, .01, (4 * c, 1))),
+               "w2": f(rng.standard_normal((c, 4 * c)) / np.sqrt(4 * c)), "b2": f(rng.normal(0, .01, (c, 1))),
+               "g": f(rng.normal(0, .1, (c, 1)))}
+        data.append((c, t_full, prm, f(rng.standard_normal((c, sample_t)))))
+
+    def stage_seconds(c, t_full, p, x0):
+        t = x0.shape[1]
+        x = x0.copy()
+        dw = np.empty_like(x)
+        scratch = np.empty(c * (t + 6) + 16, np.float32)
+        t0 = time.perf_counter()
+        lib.voc_conv1d_causal(P(dw), P(x), P(p["dw_w"]), P(p["dw_b"]), c, c, t, 7, 1, c, P(scratch))
+        lib.voc_layer_norm_channels(P(dw), P(p["nw"]), P(p["nb"]), c, t, 1e-6)
+        h = p["w1"] @ dw
+        h += p["b1"]
+        lib.voc_gelu(P(h), h.size)
+        y = p["w2"] @ h
+        y += p["b2"]
+        y *= p["g"]
+        x += y
+        return time.perf_counter() - t0
+
+    with threadpool_limits(nthreads):
+        for _ in range(warmup):
+            for st in data:
+                stage_seconds(*st)
+        n, secs = 0, [0.0] * len(data)
+        t_start = time.perf_counter()
+        while True:
+            for i, st in enumerate(data):
+                secs[i] += stage_seconds(*st)
+            n += 1
+            el = time.perf_counter() - t_start
+            if (steps is not None and n >= steps) or (steps is None and el >= min_seconds):
+                break
+    step_s = sum(batch * t_full * (secs[i] / n) / sample_t for i, (c, t_full, _, _) in enumerate(data))
+    return {"rows_per_s": sum(batch * t for _, t in stages) / step_s, "step_seconds": step_s,
+            "threads": nthreads, "passes": n, "seconds": el, "sample_t": sample_t}
+
+
+def cpu_sampling_rate(rows: int, vocab: int, top_k: int, temperature: float, penalty: float,
+                      hist: int, min_seconds: float, steps: int | None = None) -> dict:
+    """The reference's own tts_apply_repetition_penalty + tts_sample_topk (oracle/_ref, built
+    from src/tts_sampling.c at its server tier) over `rows` rows, one thread as the
+    reference calls them. Returns rows/s."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle
+    lib = oracle.load("libtts_sampling_ref.so")
+    rng = np.random.default_rng(3)
+    logits = (2 * rng.standard_normal((rows, vocab))).astype(np.float32)
+    history = rng.integers(0, vocab, (rows, hist)).astype(np.int32)
+    P = oracle.ptr
+    n, t0 = 0, time.perf_counter()
+    while True:
+        for r in range(rows):
+            lib.tts_apply_repetition_penalty(P(logits[r]), vocab, P(history[r], oracle._I32), hist,
+                                             penalty)
+            lib.tts_sample_topk(P(logits[r]), vocab, temperature, top_k)
+        n += 1
+        el = time.perf_counter() - t0
+        if (steps is not None and n >= steps) or (steps is None and el >= min_seconds):
+            break
+    return {"rows_per_s": rows * n / el, "threads": 1, "passes": n, "seconds": el}
+
+
+def _e2e_copy_loop(work, launches, steps, pairs, world, dist):
+    """Time `steps` steps of: copy every (device, pinned host) input in, the step's launches,
+    copy outputs back. pairs: (inputs [(dev, host)], outputs [(host, dev)])."""
+    import torch
+    ins, outs = pairs
+    stream = torch.cuda.current_stream()
+
+    def step():
+        for dev, host in ins:
+            dev.copy_(host, non_blocking=True)
+        for f in launches:
+            f()
+        for host, dev in outs:
+            host.copy_(dev, non_blocking=True)
+    step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    et = torch.tensor([a.elapsed_time(b)], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(et, op=dist.ReduceOp.MAX)
+    h2d = sum(h.numel() * h.element_size() for _, h in ins)
+    d2h = sum(h.numel() * h.element_size() for h, _ in outs)
+    return float(et.item()), h2d, d2h
+
+
+def run_single(args) -> None:
+    """--config a3 / n1 / s3: one workload object (runner.DecodeAttention, VocConvNeXt,
+    SampleBatch), per-launch CUDA events, roofline against HBM (a3, s3) or the live
+    cuBLAS TF32 GEMM (n1), e2e through the same entry with host copies, CPU baseline."""
     import torch
     import torch.distributed as dist
     import runner
@@ -565,10 +683,19 @@ def run_attention(args) -> None:
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-    work = runner.DecodeAttention(seed=args.seed + 1000 * rank)
+    seed = args.seed + 1000 * rank
+    tensor = args.config == "n1"
+    tf32 = tf32_peak_tflops() if tensor else None
+    if args.config == "a3":
+        work = runner.DecodeAttention(seed=seed)
+    elif args.config == "n1":
+        work = runner.VocConvNeXt(passes=args.passes, seed=seed)
+    else:
+        work = runner.SampleBatch(seed=seed)
     launches = work.launches(None)
     for _ in range(args.warmup):
-        launches[0]()
+        for f in launches:
+            f()
     torch.cuda.synchronize()
     phys = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
     sampler = ClockSampler(phys[local] if local < len(phys) and phys[local] != "" else str(local))
@@ -586,78 +713,124 @@ def run_attention(args) -> None:
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     max_ms = float(t.item())
-    assert int(work.err.item()) == 0, "a position was out of range"
+    if hasattr(work, "err"):
+        assert int(work.err.item()) == 0, "a device error flag was set"
     peak, peak_kind = measured_peaks()
-    nbytes = work.bytes_per_launch()[0]
-    avg_ms = statistics.mean(per[0])
-    gbs = nbytes / (avg_ms / 1000.0) / 1e9
-    value = work.seqs * world * args.steps / (max_ms / 1000.0)
-    roofline = {"bound": "hbm", "kernel": "decode_attention", "achieved": round(gbs, 1),
-                "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
-                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                "traffic": load_traffic().get("decode_attention@a3"),
-                "algorithmic_bytes_per_launch": nbytes}
+    nbytes, rows_pl = work.bytes_per_launch(), work.rows_per_launch()
+    flops = work.flops_per_launch() if tensor else [0.0] * len(launches)
+    per_kernel, dominant, dom_total = {}, None, -1.0
+    for j, name in enumerate(work.kernel_names):
+        avg_ms = statistics.mean(per[j])
+        k = {"avg_us": round(avg_ms * 1000, 2),
+             "gbs": round(nbytes[j] / (avg_ms / 1000.0) / 1e9, 1),
+             "frac_of_hbm_peak": round(nbytes[j] / (avg_ms / 1000.0) / 1e9 / peak, 4),
+             "rows_per_s": round(rows_pl[j] / (avg_ms / 1000.0), 1), "bytes_per_launch": nbytes[j]}
+        if tensor:
+            k["tflops"] = round(flops[j] / (avg_ms / 1000.0) / 1e12, 1)
+            k["tensor_tflops_issued"] = round(k["tflops"] * args.passes, 1)
+            k["frac_of_tf32_peak"] = round(k["tflops"] / tf32, 4)
+            k["flops_per_launch"] = flops[j]
+        per_kernel[name] = k
+        if sum(per[j]) > dom_total:
+            dominant, dom_total = name, sum(per[j])
+    d = per_kernel[dominant]
+    if tensor:
+        roofline = {"bound": "tensor", "kernel": dominant, "achieved": d["tflops"],
+                    "peak": round(tf32, 1), "unit": "TFLOP/s", "frac": d["frac_of_tf32_peak"],
+                    "peak_source": "cuBLAS FP32 GEMM on TF32 tensor cores (8192^3, best of 10), "
+                                   "measured in this run",
+                    "achieved_is": "F32 pointwise-convolution flops; with passes=3 the tensor "
+                                   "cores issue 3x that"}
+    else:
+        roofline = {"bound": "hbm", "kernel": dominant, "achieved": d["gbs"], "peak": peak,
+                    "unit": "GB/s", "frac": d["frac_of_hbm_peak"],
+                    "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"}
+    roofline.update({"traffic": load_traffic().get(f"{dominant}@{args.config}"),
+                     "algorithmic_bytes_per_launch": d["bytes_per_launch"]})
+    rows_step = sum(rows_pl)
+    value = rows_step * world * args.steps / (max_ms / 1000.0)
+
     e2e = None
     if not args.no_e2e:
-        # q, the new k/v and positions from pinned host memory, output back; the cache
-        # stays resident on the device as in a GPU decoder
-        hq, hk, hv, hp = (work.q.cpu().pin_memory(), work.k_new.cpu().pin_memory(),
-                          work.v_new.cpu().pin_memory(), work.pos.cpu().pin_memory())
-        ho = torch.empty_like(hq).pin_memory()
-        stream = torch.cuda.current_stream()
+        pin = lambda t: t.cpu().pin_memory()  # noqa: E731
+        if args.config == "a3":
+            ins = [(work.q, pin(work.q)), (work.k_new, pin(work.k_new)),
+                   (work.v_new, pin(work.v_new)), (work.pos, pin(work.pos))]
+            outs = [(pin(work.out), work.out)]
+            api = ("lai_decode_attention_f32 with q/k/v/pos copied in from pinned host memory and "
+                   "the output back each step; the cache stays on the device")
+        elif args.config == "n1":
+            ins = [(x, pin(x)) for x in work.x]
+            outs = [(pin(x), x) for x in work.x]
+            api = "lai_voc_convnext_f32 per stage with x copied in from and back to pinned host memory"
+        else:
+            ins = [(work.logits, pin(work.logits))]
+            outs = [(pin(work.out), work.out)]
+            api = "lai_sample_topk_f32 with logits copied in from pinned host memory, tokens back"
+        ms, h2d, d2h = _e2e_copy_loop(work, launches, args.e2e_steps, (ins, outs), world, dist)
+        e2e = {"value": round(rows_step * world * args.e2e_steps / (ms / 1000.0), 1),
+               "unit": "rows/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "dtype": "f32", "api": api}
 
-        def e2e_step():
-            work.q.copy_(hq, non_blocking=True)
-            work.k_new.copy_(hk, non_blocking=True)
-            work.v_new.copy_(hv, non_blocking=True)
-            work.pos.copy_(hp, non_blocking=True)
-            launches[0]()
-            ho.copy_(work.out, non_blocking=True)
-        e2e_step()
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        for _ in range(args.e2e_steps):
-            e2e_step()
-        b.record(stream)
-        torch.cuda.synchronize()
-        h2d = (hq.numel() + hk.numel() + hv.numel() + hp.numel()) * 4
-        e2e = {"value": round(work.seqs * world * args.e2e_steps / (a.elapsed_time(b) / 1000.0), 1),
-               "unit": "rows/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": ho.numel() * 4,
-               "dtype": "f32", "api": "lai_decode_attention_f32 with q/k/v/pos copied from and "
-                                       "the output back to pinned host memory each step; cache "
-                                       "device-resident"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        r = cpu_attention_rate(16, work.n_heads, work.n_kv, work.max_seq, args.cpu_seconds)
-        cpu = {"value": round(r["rows_per_s"], 1), "unit": "rows/s", "cores": r["threads"],
-               "kind": "port",
-               "sample": f"{r['passes']} passes over {r['seqs']} sequences at uniform random "
-                         f"positions < {work.max_seq} ({r['seconds']:.1f} s): the restated "
-                         "qwen_causal_attention (seq_q = 1), float sums, OpenMP over "
-                         f"(sequence, head), host {cpu_model()}"}
+        if args.config == "a3":
+            r = cpu_attention_rate(16, work.n_heads, work.n_kv, work.max_seq, args.cpu_seconds)
+            cpu = {"value": round(r["rows_per_s"], 1), "unit": "rows/s", "cores": r["threads"],
+                   "kind": "port",
+                   "sample": f"{r['passes']} passes over {r['seqs']} sequences at uniform random "
+                             f"positions < {work.max_seq} ({r['seconds']:.1f} s): the restated "
+                             "qwen_causal_attention (seq_q = 1), float sums, OpenMP over "
+                             f"(sequence, head), host {cpu_model()}"}
+        elif args.config == "n1":
+            r = cpu_convnext_rate(work.stages, work.batch, args.cpu_seconds)
+            cpu = {"value": round(r["rows_per_s"], 1), "unit": "rows/s", "cores": r["threads"],
+                   "kind": "port",
+                   "sample": f"{r['passes']} sweeps of both stages on {r['sample_t']} time rows of "
+                             f"one item ({r['seconds']:.1f} s), scaled per stage to batch "
+                             f"{work.batch}: the reference's compiled depthwise conv, channel "
+                             "LayerNorm and GELU + OpenBLAS SGEMM pointwise convs, host "
+                             f"{cpu_model()}"}
+        else:
+            r = cpu_sampling_rate(work.rows, work.vocab, work.top_k, work.temperature,
+                                  work.penalty, work.history.shape[1], args.cpu_seconds)
+            cpu = {"value": round(r["rows_per_s"], 1), "unit": "rows/s", "cores": 1,
+                   "kind": "reference",
+                   "sample": f"{r['passes']} passes over {work.rows} rows ({r['seconds']:.1f} s) of "
+                             "the reference's own tts_apply_repetition_penalty + "
+                             "tts_sample_topk (built from src/tts_sampling.c), one thread as "
+                             f"the reference calls them, host {cpu_model()}"}
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
+    desc = {
+        "a3": {"workload": "TTS talker decode attention: cache append + attention over keys "
+                           "0..pos, one token per sequence, F32 KV cache",
+               "sequences": getattr(work, "seqs", None), "heads": [16, 8, 128], "max_seq": 4096,
+               "keys_per_step": getattr(work, "keys", None), "rows": "sequences (one token each)"},
+        "n1": {"workload": "vocoder ConvNeXt upsample blocks (depthwise conv k=7 + channel "
+                           "LayerNorm, pointwise 4x MLP with GELU on tcgen05, layer scale, "
+                           "residual), FP32 channels-last",
+               "stages": getattr(work, "stages", None), "batch": getattr(work, "batch", None),
+               "passes": args.passes, "rows": "time rows (batch x T) per stage"},
+        "s3": {"workload": "talker token sampling: repetition penalty + top-k 50 at temperature "
+                           "0.9 over codec logits (vocab 3072), 64-token histories",
+               "rows": "decode rows (one token drawn each)", "batch": getattr(work, "rows", None)},
+    }[args.config]
+    desc.update({"config": args.config, "parallelism": f"replicas x{world}, no collective",
+                 "l2": (f"inputs larger than L2 ({sum(nbytes) / 1e9:.2f} GB per step)"
+                        if sum(nbytes) > 126e6 else
+                        f"L2-resident working set ({sum(nbytes) / 1e6:.1f} MB per step)")})
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "rows/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded counter-based N(0,1) cache, q, k, v; uniform positions)",
-        "config": {"workload": "TTS talker decode attention: cache append + attention over "
-                               "keys 0..pos, one token per sequence, F32 KV cache",
-                   "config": "a3", "sequences": work.seqs, "heads": [work.n_heads, work.n_kv, 128],
-                   "max_seq": work.max_seq, "keys_per_step": work.keys,
-                   "rows": "sequences (one token each)",
-                   "parallelism": f"replicas x{world}, no collective",
-                   "l2": f"inputs larger than L2 ({nbytes / 1e9:.2f} GB per step)"},
-        "per_kernel": {"decode_attention": {"avg_us": round(avg_ms * 1000, 2), "gbs": round(gbs, 1),
-                                            "frac_of_peak": round(gbs / peak, 4),
-                                            "bytes_per_launch": nbytes}},
-        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-        "gpu_launches": args.steps, "clocks": clocks,
+        "data": "synthetic (seeded counter-based N(0,1) on device)", "config": desc,
+        "per_kernel": per_kernel, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": args.steps * len(launches) * (3 if args.config == "n1" else 1),
+        "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
 
@@ -713,6 +886,26 @@ def run_reference(args) -> None:
                     ms_per_step=1000.0 * r["seconds"] / r["passes"], scaling="weak", dtype="f32",
                     config={"workload": "TTS talker decode attention", "config": "a3",
                             "sequences": 16, "heads": [16, 8, 128], "max_seq": 4096})
+    elif args.config == "n1":
+        stages = [(1024, 1000), (1024, 2000)]
+        r = cpu_convnext_rate(stages, 8, 0.0, sample_t=500, steps=args.steps, warmup=args.warmup)
+        cb = {"value": r["rows_per_s"], "unit": "rows/s", "cores": r["threads"], "kind": "port",
+              "sample": f"500 time rows of one item per stage per step, scaled to batch 8: the "
+                        "reference's compiled depthwise conv, LayerNorm, GELU + OpenBLAS "
+                        f"SGEMMs, host {cpu_model()}"}
+        line = dict(common, value=r["rows_per_s"], unit="rows/s",
+                    ms_per_step=1000.0 * r["step_seconds"], scaling="weak", dtype="f32",
+                    config={"workload": "vocoder ConvNeXt blocks", "config": "n1",
+                            "stages": stages, "batch": 8})
+    elif args.config == "s3":
+        r = cpu_sampling_rate(256, 3072, 50, 0.9, 1.05, 64, 0.0, steps=args.steps)
+        cb = {"value": r["rows_per_s"], "unit": "rows/s", "cores": 1, "kind": "reference",
+              "sample": "256 rows per step through the reference's own tts_sample_topk + "
+                        f"repetition penalty, one thread, host {cpu_model()}"}
+        line = dict(common, value=r["rows_per_s"], unit="rows/s",
+                    ms_per_step=1000.0 * r["seconds"] / r["passes"], scaling="weak", dtype="f32",
+                    config={"workload": "talker token sampling", "config": "s3", "rows": 256,
+                            "vocab": 3072, "top_k": 50})
     elif args.config in runner.DECODE_CONFIGS:
         cfg = runner.DECODE_CONFIGS[args.config]
         r = cpu_decode_rate(cfg, per_step_s * args.steps)
@@ -1179,7 +1372,8 @@ def main():
                     help="timed steps (default 2000; 20 for v1, whose step is ~0.1 s)")
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "g1", "g2", "v1", "a3"],
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "g1", "g2", "v1", "a3", "n1",
+                                         "s3"],
                     default="c2")
     ap.add_argument("--t-div", type=int, default=1,
                     help="v1: divide every stage's length (small profiling cases)")
@@ -1208,13 +1402,13 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)  # timing rule: at least 3 untimed warm-up steps
     if args.steps is None:
-        args.steps = 20 if args.config == "v1" else 2000
+        args.steps = {"v1": 20, "n1": 50, "a3": 200}.get(args.config, 2000)
     if args.impl == "reference":
         run_reference(args)
     elif args.config == "v1":
         run_resunits(args)
-    elif args.config == "a3":
-        run_attention(args)
+    elif args.config in ("a3", "n1", "s3"):
+        run_single(args)
     else:
         run_ours(args)
 

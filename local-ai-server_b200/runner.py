@@ -282,6 +282,93 @@ class VocResUnits:
         return [self.batch * t for _, t in self.stages]  # time rows through 3 units
 
 
+class VocConvNeXt:
+    """The vocoder's two ConvNeXt upsample blocks (config n1): C = 1024 at 2 T0 and 4 T0
+    time rows (T0 = 500 codec frames, src/tts_vocoder.c:658-670), batch 8, FP32
+    channels-last; weights random at trained-model scale (depthwise N(0,1)/sqrt 7,
+    pointwise N(0,1)/sqrt(fan_in), LayerNorm 1+N(0,0.1) / N(0,0.1), biases N(0,0.01),
+    layer scale N(0,0.1): the block adds a small update, so repeated in-place steps keep
+    x bounded). One step = one lai_voc_convnext_f32 call per stage (3 launches each)."""
+
+    def __init__(self, stages=((1024, 1000), (1024, 2000)), batch=8, passes: int = 3,
+                 seed: int = 555, device="cuda"):
+        import torch
+        self.stages, self.batch, self.passes = list(stages), batch, passes
+        k = 0
+
+        def normal(shape, std=1.0, mean=0.0):
+            nonlocal k
+            t = torch.empty(shape, dtype=torch.float32, device=device)
+            lai.synth_normal(t, seed=seed + k, mean=mean, std=std)
+            k += 1
+            return t
+
+        self.x, self.params = [], []
+        for c, t in self.stages:
+            self.x.append(normal((batch, t, c)))
+            self.params.append(lai.voc_convnext_params({
+                "dw_w": normal((c, 1, 7), 7 ** -0.5), "dw_b": normal(c, 0.01),
+                "norm_w": normal(c, 0.1, 1.0), "norm_b": normal(c, 0.1),
+                "pw1_w": normal((4 * c, c, 1), c ** -0.5), "pw1_b": normal(4 * c, 0.01),
+                "pw2_w": normal((c, 4 * c, 1), (4 * c) ** -0.5), "pw2_b": normal(c, 0.01),
+                "gamma": normal(c, 0.1)}))
+        n_max = max(batch * t * c for c, t in self.stages)
+        self.scratch = torch.empty(10 * n_max, dtype=torch.float32, device=device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.kernel_names = tuple(f"convnext_{c}x{t}" for c, t in self.stages)
+
+    def launches(self, stream=None):
+        return [(lambda i=i: lai.voc_convnext(self.x[i], self.params[i], self.scratch,
+                                              self.passes, self.err, stream))
+                for i in range(len(self.stages))]
+
+    def flops_per_launch(self) -> list[float]:
+        """The two pointwise convolutions: 2 * (C * 4C + 4C * C) flops per time row."""
+        return [16.0 * c * c * t * self.batch for c, t in self.stages]
+
+    def bytes_per_launch(self) -> list[int]:
+        """Per element of x: depthwise+LayerNorm reads 4 and writes the 8-byte operand;
+        pw1 reads 8 and writes 32 (h is 4C wide, hi/lo); pw2 reads 32 and x, writes x."""
+        per = 92 if self.passes == 3 else 48
+        return [per * self.batch * t * c for c, t in self.stages]
+
+    def rows_per_launch(self) -> list[int]:
+        return [self.batch * t for _, t in self.stages]
+
+
+class SampleBatch:
+    """Token sampling of config s3: `rows` decode rows of codec logits (vocab 3072,
+    src/tts_native.c:1096-1099) with repetition penalty over 64-token histories, top-k 50,
+    temperature 0.9. One step = one lai_sample_topk_f32 launch."""
+
+    def __init__(self, rows: int = 256, vocab: int = 3072, top_k: int = 50, temperature=0.9,
+                 penalty=1.05, hist: int = 64, seed: int = 31, device="cuda"):
+        import torch
+        self.rows, self.vocab, self.top_k = rows, vocab, top_k
+        self.temperature, self.penalty = temperature, penalty
+        self.logits = torch.empty((rows, vocab), dtype=torch.float32, device=device)
+        lai.synth_normal(self.logits, seed=seed, std=2.0)
+        self.history = torch.empty((rows, hist), dtype=torch.int32, device=device)
+        lai.synth_uniform_i32(self.history, seed + 1, 0, vocab)
+        self.hist_len = torch.full((rows,), hist, dtype=torch.int32, device=device)
+        self.u = torch.empty(rows, dtype=torch.float32, device=device)
+        lai.synth_normal(self.u, seed=seed + 2, std=0.25, mean=0.5)
+        self.u.clamp_(0.0, 1.0)
+        self.out = torch.empty(rows, dtype=torch.int32, device=device)
+        self.kernel_names = ("sample_topk",)
+
+    def launches(self, stream=None):
+        return [lambda: lai.sample_topk(self.logits, self.u, self.temperature, self.top_k,
+                                        self.history, self.hist_len, self.penalty,
+                                        out=self.out, stream=stream)]
+
+    def bytes_per_launch(self) -> list[int]:
+        return [self.rows * (self.vocab * 4 + self.history.shape[1] * 4 + 8)]
+
+    def rows_per_launch(self) -> list[int]:
+        return [self.rows]
+
+
 class DecodeAttention:
     """Decode attention of config a3: `seqs` sequences x 1 token at seeded random
     positions 0..max_seq-1, GQA n_heads / n_kv_heads, head_dim 128, F32 KV cache

@@ -179,3 +179,20 @@ def test_repetition_penalty_matches_reference_build():
     for pen in (1.0, 1.05, 1.3):
         assert np.array_equal(oracle.repetition_penalty(logits, hist, pen),
                               oracle.ref_repetition_penalty(logits, hist, pen))
+
+
+@pytest.mark.skipif(not oracle.have_ref(), reason="oracle/_ref not built (reference absent)")
+def test_convnext_restatement_against_reference_functions():
+    # run_convnext's sequence composed from the reference's compiled voc_conv1d_causal
+    # (depthwise branch and k = 1), voc_layer_norm_channels and voc_gelu
+    rng = np.random.default_rng(5)
+    C, T = 32, 30
+    f = lambda a: np.asarray(a, np.float32)  # noqa: E731
+    p = {"dw_w": f(rng.standard_normal((C, 1, 7)) / np.sqrt(7)), "dw_b": f(rng.normal(0, .1, C)),
+         "norm_w": f(1 + rng.normal(0, .1, C)), "norm_b": f(rng.normal(0, .1, C)),
+         "pw1_w": f(rng.standard_normal((4 * C, C, 1)) / np.sqrt(C)), "pw1_b": f(rng.normal(0, .1, 4 * C)),
+         "pw2_w": f(rng.standard_normal((C, 4 * C, 1)) / np.sqrt(4 * C)), "pw2_b": f(rng.normal(0, .1, C)),
+         "gamma": f(rng.normal(0, .3, C))}
+    x = rng.standard_normal((2, C, T)).astype(np.float32)
+    got, ref = oracle.voc_convnext(x, p), oracle.ref_voc_convnext(x, p)
+    assert np.max(np.abs(got - ref)) / max(1.0, np.max(np.abs(ref))) <= 1e-5
