@@ -240,6 +240,33 @@ typedef struct {
 LAI_API int lai_voc_resunits_f32(float *x, float *scratch, const lai_voc_resunit_t *units,
                                  int n_units, int batch, int channels, int T, int passes,
                                  int *err, lai_stream_t stream);
+/* ---- vocoder BigVGAN block: SnakeBeta -> ConvTranspose1d (kernel 2r, stride r) -> ResUnits --
+ * One block of tts_vocoder_run (src/tts_vocoder.c:709-728): voc_snake_beta(x, snake) then
+ * voc_conv_transpose1d (src/tts_vocoder_ops.c:153-221; T_out = (T - 1) r) then n_units
+ * run_resunit calls. x [batch, T, c_in] -> out [batch, (T - 1) r, c_out], channels-last.
+ * The transposed conv runs as r interleaved 2-tap convs on the tensor cores (output row
+ * q r + f = W[.., f]^T x[q + 1] + W[.., r + f]^T x[q]); its epilogue also writes the first
+ * unit's snake1 input. tconv_w: lai_voc_pack_tconv_f32 image of the reference weight
+ * [c_in, c_out, 2r]. scratch: 2 batch T c_in + 4 batch T_out c_out floats. c_in, c_out
+ * multiples of 32; T >= 2.
+ */
+typedef struct {
+    const float *snake_ea, *snake_ieb; /* [c_in] the block's SnakeBeta, pre-exponentiated */
+    const float *tconv_w;              /* packed, 4 * rate * c_out * c_in floats */
+    const float *tconv_b;              /* [c_out] */
+    int rate;                          /* 8, 5, 4, 3 in the reference (src/tts_vocoder.c:247) */
+    int n_units;                       /* ResUnits that follow (3) */
+    const lai_voc_resunit_t *units;    /* host array of n_units */
+} lai_voc_bigvgan_block_t;
+
+LAI_API int lai_voc_bigvgan_block_f32(float *out, const float *x, float *scratch,
+                                      const lai_voc_bigvgan_block_t *blk, int batch, int c_in,
+                                      int c_out, int T, int passes, int *err, lai_stream_t stream);
+/* dst (4 * rate * c_out * c_in floats) <- reference weight w [c_in, c_out, 2 * rate], split
+ * per phase into the two taps of the interleaved convs, TF32 high parts then remainders. */
+LAI_API int lai_voc_pack_tconv_f32(float *dst, const float *w, int c_in, int c_out, int rate,
+                                   lai_stream_t stream);
+
 /* ---- vocoder ConvNeXt block (upsample stages) --------------------------------------------
  * run_convnext(x, C, T, cn) (src/tts_vocoder.c:463-533): depthwise causal conv k=7 + bias,
  * LayerNorm over channels (eps 1e-6), pointwise C -> 4C + bias, exact GELU, pointwise

@@ -50,8 +50,11 @@ constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s: far beyond any healthy wait
 
 // Epilogues: conv1 of a ResUnit (bias, snake2, split store); conv2 of a ResUnit (bias,
 // residual in place, then the next unit's snake1 + split store when ea != null);
-// ConvNeXt pw1 (bias, exact GELU, split store); ConvNeXt pw2 (bias, * gamma, residual).
-enum Epi { kEpiSnakeSplit = 0, kEpiResidual = 1, kEpiGelu = 2, kEpiScaleResidual = 3 };
+// ConvNeXt pw1 (bias, exact GELU, split store); ConvNeXt pw2 (bias, * gamma, residual);
+// transposed conv of a BigVGAN block (bias, store x, then the first ResUnit's snake1 +
+// split store when ea != null).
+enum Epi { kEpiSnakeSplit = 0, kEpiResidual = 1, kEpiGelu = 2, kEpiScaleResidual = 3,
+           kEpiStoreSnake = 4 };
 
 struct ConvArgs {
     float *out_hi, *out_lo;  // split output planes (kEpiResidual: next unit's input, or null)
@@ -61,6 +64,10 @@ struct ConvArgs {
     const float *gamma;      // kEpiScaleResidual: per-channel layer scale
     int T, c_in, c_out, taps, dilation;
     int *err;
+    // Phased output (a transposed conv as `phases` interleaved 2-tap convs): GEMM row t >= 1
+    // of phase f goes to output row (t - 1) * phases + f of a T_out-row sequence. 0 or 1: an
+    // ordinary conv, row t to row t.
+    int phases, T_out;
 };
 
 template <int BN, int PASSES>
@@ -105,6 +112,10 @@ __device__ __forceinline__ void epilogue4(const ConvArgs &a, float (&v)[4], cons
         store4(a.x + off, v[0], v[1], v[2], v[3]);
         if (a.ea == nullptr) return;
     }
+    if (EPI == kEpiStoreSnake) {
+        store4(a.x + off, v[0], v[1], v[2], v[3]);
+        if (a.ea == nullptr) return;
+    }
     float hi[4];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
@@ -146,7 +157,16 @@ conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int t0 = blockIdx.x * kBM, n0 = blockIdx.y * BN, b = blockIdx.z;
+    const int P = a.phases > 1 ? a.phases : 1;
+    const int t0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
+    const int b = blockIdx.z / P, phase = blockIdx.z - (blockIdx.z / P) * P;
+    // global output row of GEMM row t, or -1 when it has none
+    auto out_row = [&](int t) -> int64_t {
+        if (t >= a.T) return -1;
+        if (P == 1) return (int64_t)b * a.T + t;
+        if (t == 0) return -1;
+        return (int64_t)b * a.T_out + (int64_t)(t - 1) * P + phase;
+    };
     const int kblocks = a.c_in / kBK;
     const int n_iter = a.taps * kblocks;
     const int n_chunks = (n_iter + kChunkBlocks - 1) / kChunkBlocks;
@@ -189,10 +209,11 @@ conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
                 uint8_t *st = tiles + s * L::kStage;
                 bulk::mbar_arrive_expect_tx(&full[s], L::kStage);
                 umma::tma_load_4d(st, &act_map, c, row, b, 0, &full[s]);
-                umma::tma_load_3d(st + L::kA, &w_map, c, n0, tap, &full[s]);
+                umma::tma_load_3d(st + L::kA, &w_map, c, n0, phase * a.taps + tap, &full[s]);
                 if (PASSES == 3) {
                     umma::tma_load_4d(st + L::kA + L::kB, &act_map, c, row, b, 1, &full[s]);
-                    umma::tma_load_3d(st + 2 * L::kA + L::kB, &w_map, c, n0, a.taps + tap,
+                    umma::tma_load_3d(st + 2 * L::kA + L::kB, &w_map, c, n0,
+                                      (P + phase) * a.taps + tap,
                                       &full[s]);
                 }
             }
@@ -289,10 +310,10 @@ conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
                     if (EPI == kEpiResidual || EPI == kEpiScaleResidual) {
 #pragma unroll
                         for (int p = 0; p < PB; p++) {
-                            const int t = row0 + (p0 + p) * RPP + r_off;
-                            xr[p] = t < a.T ? *reinterpret_cast<const float4 *>(
-                                                  a.x + ((size_t)b * a.T + t) * a.c_out + c)
-                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+                            const int64_t orow = out_row(row0 + (p0 + p) * RPP + r_off);
+                            xr[p] = orow >= 0 ? *reinterpret_cast<const float4 *>(
+                                                    a.x + (size_t)orow * a.c_out + c)
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
                         }
                     }
 #pragma unroll
@@ -301,10 +322,12 @@ conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
                         float v[4];
 #pragma unroll
                         for (int i = 0; i < 4; i++) v[i] = buf[r * kEpiPitch + c4 + i];
-                        const int t = row0 + r;
-                        if (t < a.T)
-                            epilogue4<PASSES, EPI>(a, v, EPI == kEpiSnakeSplit || EPI == kEpiGelu ? xr[0] : xr[p],
-                                                   (size_t)b * a.T + t, c);
+                        const int64_t orow = out_row(row0 + r);
+                        if (orow >= 0)
+                            epilogue4<PASSES, EPI>(
+                                a, v,
+                                EPI == kEpiResidual || EPI == kEpiScaleResidual ? xr[p] : xr[0],
+                                (size_t)orow, c);
                     }
                 }
                 __syncwarp();
@@ -380,7 +403,9 @@ int launch_conv_t(const CUtensorMap &am, const CUtensorMap &wm, const ConvArgs &
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kSmem) !=
         cudaSuccess)
         return LAI_ERR_CUDA;
-    const dim3 grid((unsigned)((a.T + kBM - 1) / kBM), (unsigned)(a.c_out / BN), (unsigned)batch);
+    const unsigned phases = a.phases > 1 ? (unsigned)a.phases : 1u;
+    const dim3 grid((unsigned)((a.T + kBM - 1) / kBM), (unsigned)(a.c_out / BN),
+                    (unsigned)batch * phases);
     kern<<<grid, kThreads, L::kSmem, st>>>(am, wm, a);
     return launch_status();
 }

@@ -101,6 +101,92 @@ extern "C" int lai_voc_transpose_f32(float *dst, const float *src, int batch, in
     return lai::launch_status();
 }
 
+namespace lai {
+namespace {
+
+bool units_valid(const lai_voc_resunit_t *units, int n_units) {
+    for (int u = 0; u < n_units; u++) {
+        const lai_voc_resunit_t &p = units[u];
+        if (!p.snake1_ea || !p.snake1_ieb || !p.conv1_w || !p.conv1_b || !p.snake2_ea ||
+            !p.snake2_ieb || !p.conv2_w || !p.conv2_b || p.dilation <= 0 ||
+            (int64_t)p.dilation * 6 > (int64_t)1 << 30 || !aligned16(p.conv1_w) ||
+            !aligned16(p.conv2_w))
+            return false;
+    }
+    return true;
+}
+
+// s = snake(x) split into scratch planes hi / lo ([rows, C] channels-last)
+void launch_snake_split(const float *x, const float *ea, const float *ieb, float *hi, float *lo,
+                        size_t n, int C, int passes, cudaStream_t st) {
+    const int64_t n4 = (int64_t)n / 4;
+    const unsigned g = grid_for(n4, 256) < 148u * 16 ? grid_for(n4, 256) : 148u * 16;
+    if (passes == 3)
+        snake_split_kernel<3><<<g, 256, 0, st>>>(x, ea, ieb, hi, lo, n4, C);
+    else
+        snake_split_kernel<1><<<g, 256, 0, st>>>(x, ea, ieb, hi, lo, n4, C);
+}
+
+// The ResUnit chain on x [batch, T, C]; scratch = [s hi, s lo, h hi, h lo] planes. With
+// s_ready the first unit's split input is already in the s planes (written by the
+// transposed conv's epilogue).
+int run_resunits(float *x, float *scratch, const lai_voc_resunit_t *units, int n_units, int batch,
+                 int channels, int T, int passes, int *err, cudaStream_t st, bool s_ready) {
+    const size_t plane = (size_t)batch * T * channels;
+    float *s_hi = scratch, *s_lo = scratch + plane, *h_hi = scratch + 2 * plane,
+          *h_lo = scratch + 3 * plane;
+    CUtensorMap s_map, h_map;
+    if (!act_map(&s_map, s_hi, batch, T, channels) || !act_map(&h_map, h_hi, batch, T, channels))
+        return LAI_ERR_INVALID;
+    const int bn = pick_bn(channels);
+    int rc = LAI_OK;
+    if (!s_ready) {
+        launch_snake_split(x, units[0].snake1_ea, units[0].snake1_ieb, s_hi, s_lo, plane, channels,
+                           passes, st);
+        rc = launch_status();
+    }
+    for (int u = 0; u < n_units && rc == LAI_OK; u++) {
+        const lai_voc_resunit_t &p = units[u];
+        CUtensorMap w1, w2;
+        if (!weight_map(&w1, p.conv1_w, 7, channels, channels, bn) ||
+            !weight_map(&w2, p.conv2_w, 1, channels, channels, bn))
+            return LAI_ERR_INVALID;
+        ConvArgs c1{h_hi, h_lo, nullptr, p.conv1_b, p.snake2_ea, p.snake2_ieb, nullptr,
+                    T, channels, channels, 7, p.dilation, err, 1, T};
+        rc = launch_conv<kEpiSnakeSplit>(passes, s_map, w1, c1, batch, st);
+        if (rc != LAI_OK) break;
+        const bool last = u + 1 == n_units;
+        ConvArgs c2{last ? nullptr : s_hi, last ? nullptr : s_lo, x, p.conv2_b,
+                    last ? nullptr : units[u + 1].snake1_ea,
+                    last ? nullptr : units[u + 1].snake1_ieb, nullptr, T, channels, channels, 1,
+                    1, err, 1, T};
+        rc = launch_conv<kEpiResidual>(passes, h_map, w2, c2, batch, st);
+    }
+    return rc;
+}
+
+// Reference transposed-conv weight [c_in, c_out, 2r] -> [2][r][2][c_out][c_in]: part (hi,
+// lo), phase f, tap (0: W[.., r + f] applied to x[t - 1]; 1: W[.., f] applied to x[t]).
+__global__ void pack_tconv_kernel(float *dst, const float *__restrict__ w, int c_in, int c_out,
+                                  int rate) {
+    const int64_t per_part = (int64_t)rate * 2 * c_out * c_in;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < per_part;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t oc = i % ((int64_t)c_out * c_in);  // o * c_in + c
+        const int64_t pk = i / ((int64_t)c_out * c_in);  // phase * 2 + tap
+        const int f = (int)(pk / 2), tap = (int)(pk % 2);
+        const int64_t o = oc / c_in, c = oc % c_in;
+        const int ki = tap == 0 ? rate + f : f;
+        const float v = w[(c * c_out + o) * 2 * rate + ki];
+        const float h = umma::tf32_round(v);
+        dst[i] = h;
+        dst[per_part + i] = v - h;
+    }
+}
+
+}  // namespace
+}  // namespace lai
+
 extern "C" int lai_voc_resunits_f32(float *x, float *scratch, const lai_voc_resunit_t *units,
                                     int n_units, int batch, int channels, int T, int passes,
                                     int *err, lai_stream_t stream) {
@@ -111,50 +197,67 @@ extern "C" int lai_voc_resunits_f32(float *x, float *scratch, const lai_voc_resu
     if (n_units == 0 || batch == 0 || T == 0) return LAI_OK;
     if (channels % 32 != 0 || !aligned16(x) || !aligned16(scratch)) return LAI_ERR_INVALID;
     if (batch > 65535) return LAI_ERR_RANGE;
-    for (int u = 0; u < n_units; u++) {
-        const lai_voc_resunit_t &p = units[u];
-        if (!p.snake1_ea || !p.snake1_ieb || !p.conv1_w || !p.conv1_b || !p.snake2_ea ||
-            !p.snake2_ieb || !p.conv2_w || !p.conv2_b || p.dilation <= 0 ||
-            (int64_t)p.dilation * 6 > (int64_t)1 << 30 || !aligned16(p.conv1_w) ||
-            !aligned16(p.conv2_w))
-            return LAI_ERR_INVALID;
-    }
+    if (!units_valid(units, n_units)) return LAI_ERR_INVALID;
     const size_t plane = (size_t)batch * T * channels;
     if (overlaps(x, plane * 4, scratch, 4 * plane * 4)) return LAI_ERR_ALIAS;
     if (!encode_fn()) return LAI_ERR_CUDA;
-    float *s_hi = scratch, *s_lo = scratch + plane, *h_hi = scratch + 2 * plane,
-          *h_lo = scratch + 3 * plane;
-    CUtensorMap s_map, h_map;
-    if (!act_map(&s_map, s_hi, batch, T, channels) || !act_map(&h_map, h_hi, batch, T, channels))
-        return LAI_ERR_INVALID;
-    const cudaStream_t st = as_stream(stream);
-    const int bn = pick_bn(channels);
+    return run_resunits(x, scratch, units, n_units, batch, channels, T, passes, err,
+                        as_stream(stream), false);
+}
 
-    const int64_t n4 = (int64_t)plane / 4;
-    const unsigned g = grid_for(n4, 256) < 148u * 16 ? grid_for(n4, 256) : 148u * 16;
-    if (passes == 3)
-        snake_split_kernel<3><<<g, 256, 0, st>>>(x, units[0].snake1_ea, units[0].snake1_ieb, s_hi,
-                                                s_lo, n4, channels);
-    else
-        snake_split_kernel<1><<<g, 256, 0, st>>>(x, units[0].snake1_ea, units[0].snake1_ieb, s_hi,
-                                                s_lo, n4, channels);
+extern "C" int lai_voc_pack_tconv_f32(float *dst, const float *w, int c_in, int c_out, int rate,
+                                      lai_stream_t stream) {
+    if (!dst || !w || c_in <= 0 || c_out <= 0 || rate <= 0) return LAI_ERR_INVALID;
+    const size_t n = (size_t)c_in * c_out * 2 * rate;
+    if (lai::overlaps(dst, 2 * n * sizeof(float), w, n * sizeof(float))) return LAI_ERR_ALIAS;
+    const unsigned grid = lai::grid_for((int64_t)n, 256) < 148u * 8 ? lai::grid_for((int64_t)n, 256)
+                                                                   : 148u * 8;
+    lai::pack_tconv_kernel<<<grid, 256, 0, lai::as_stream(stream)>>>(dst, w, c_in, c_out, rate);
+    return lai::launch_status();
+}
+
+extern "C" int lai_voc_bigvgan_block_f32(float *out, const float *x, float *scratch,
+                                         const lai_voc_bigvgan_block_t *blk, int batch, int c_in,
+                                         int c_out, int T, int passes, int *err,
+                                         lai_stream_t stream) {
+    using namespace lai;
+    if (!out || !x || !scratch || !blk || batch < 0 || T < 0 || (passes != 1 && passes != 3))
+        return LAI_ERR_INVALID;
+    if (!blk->snake_ea || !blk->snake_ieb || !blk->tconv_w || !blk->tconv_b || blk->rate <= 0 ||
+        blk->n_units < 0 || (blk->n_units > 0 && !blk->units))
+        return LAI_ERR_INVALID;
+    if (batch == 0 || T < 2) return batch == 0 ? LAI_OK : LAI_ERR_INVALID;
+    if (c_in % 32 != 0 || c_out % 32 != 0 || !aligned16(out) || !aligned16(x) ||
+        !aligned16(scratch) || !aligned16(blk->tconv_w))
+        return LAI_ERR_INVALID;
+    if ((int64_t)batch * blk->rate > 65535) return LAI_ERR_RANGE;
+    if (!units_valid(blk->units, blk->n_units)) return LAI_ERR_INVALID;
+    const int r = blk->rate;
+    const int T_out = (T - 1) * r;  // (T + 1) r - 2r
+    const size_t in_plane = (size_t)batch * T * c_in, out_plane = (size_t)batch * T_out * c_out;
+    if (overlaps(out, out_plane * 4, x, in_plane * 4) ||
+        overlaps(out, out_plane * 4, scratch, (2 * in_plane + 4 * out_plane) * 4) ||
+        overlaps(x, in_plane * 4, scratch, (2 * in_plane + 4 * out_plane) * 4))
+        return LAI_ERR_ALIAS;
+    if (!encode_fn()) return LAI_ERR_CUDA;
+    const cudaStream_t st = as_stream(stream);
+    float *in_hi = scratch, *in_lo = scratch + in_plane;
+    float *rs = scratch + 2 * in_plane;  // the ResUnits' scratch; its s planes come first
+    // block snake -> split planes of the transposed conv's input
+    launch_snake_split(x, blk->snake_ea, blk->snake_ieb, in_hi, in_lo, in_plane, c_in, passes, st);
     int rc = launch_status();
-    for (int u = 0; u < n_units && rc == LAI_OK; u++) {
-        const lai_voc_resunit_t &p = units[u];
-        CUtensorMap w1, w2;
-        if (!weight_map(&w1, p.conv1_w, 7, channels, channels, bn) ||
-            !weight_map(&w2, p.conv2_w, 1, channels, channels, bn))
-            return LAI_ERR_INVALID;
-        ConvArgs c1{h_hi, h_lo, nullptr, p.conv1_b, p.snake2_ea, p.snake2_ieb, nullptr,
-                    T, channels, channels, 7, p.dilation, err};
-        rc = launch_conv<kEpiSnakeSplit>(passes, s_map, w1, c1, batch, st);
-        if (rc != LAI_OK) break;
-        const bool last = u + 1 == n_units;
-        ConvArgs c2{last ? nullptr : s_hi, last ? nullptr : s_lo, x, p.conv2_b,
-                    last ? nullptr : units[u + 1].snake1_ea,
-                    last ? nullptr : units[u + 1].snake1_ieb, nullptr, T, channels, channels, 1,
-                    1, err};
-        rc = launch_conv<kEpiResidual>(passes, h_map, w2, c2, batch, st);
-    }
-    return rc;
+    if (rc != LAI_OK) return rc;
+    CUtensorMap in_map, w_map;
+    if (!act_map(&in_map, in_hi, batch, T, c_in) ||
+        !weight_map(&w_map, blk->tconv_w, 2 * r, c_out, c_in, pick_bn(c_out)))
+        return LAI_ERR_INVALID;
+    const bool fuse = blk->n_units > 0;  // epilogue also writes the first unit's snake1 input
+    const ConvArgs a{fuse ? rs : nullptr, fuse ? rs + out_plane : nullptr, out, blk->tconv_b,
+                     fuse ? blk->units[0].snake1_ea : nullptr,
+                     fuse ? blk->units[0].snake1_ieb : nullptr, nullptr, T, c_in, c_out, 2, 1,
+                     err, r, T_out};
+    rc = launch_conv<kEpiStoreSnake>(passes, in_map, w_map, a, batch, st);
+    if (rc != LAI_OK || !fuse) return rc;
+    return run_resunits(out, rs, blk->units, blk->n_units, batch, c_out, T_out, passes, err, st,
+                        true);
 }

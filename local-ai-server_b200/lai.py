@@ -51,6 +51,9 @@ SIGNATURES: dict[str, tuple] = {
                                         _i32, _i32, _f32, _vp, _vp, _vp]),
     "lai_sample_topk_f32": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp, _i32, _f32, _f32, _i32, _vp,
                                    _vp]),
+    "lai_voc_bigvgan_block_f32": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp,
+                                         _vp]),
+    "lai_voc_pack_tconv_f32": (_i32, [_vp, _vp, _i32, _i32, _i32, _vp]),
     "lai_voc_convnext_f32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp]),
     "lai_voc_resunits_f32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
     "lai_voc_pack_conv_f32": (_i32, [_vp, _vp, _i32, _i32, _i32, _vp]),
@@ -295,6 +298,47 @@ class VocResUnit(ctypes.Structure):
     _fields_ = [("snake1_ea", _vp), ("snake1_ieb", _vp), ("conv1_w", _vp), ("conv1_b", _vp),
                 ("snake2_ea", _vp), ("snake2_ieb", _vp), ("conv2_w", _vp), ("conv2_b", _vp),
                 ("dilation", _i32)]
+
+
+class VocBigVGANBlock(ctypes.Structure):
+    """lai_voc_bigvgan_block_t."""
+    _fields_ = [("snake_ea", _vp), ("snake_ieb", _vp), ("tconv_w", _vp), ("tconv_b", _vp),
+                ("rate", _i32), ("n_units", _i32), ("units", _vp)]
+
+
+def voc_pack_tconv(w, rate, stream=None):
+    """Reference transposed-conv weight [c_in, c_out, 2 rate] -> packed [2, rate, 2, c_out, c_in]."""
+    import torch
+    c_in, c_out, _ = w.shape
+    dst = torch.empty((2, rate, 2, c_out, c_in), dtype=torch.float32, device=w.device)
+    call("lai_voc_pack_tconv_f32", _p(dst), _p(w), c_in, c_out, rate, _s(stream))
+    return dst
+
+
+def voc_block_params(blk):
+    """blk: dict with ea, ieb [c_in], w [c_in, c_out, 2r], b [c_out], rate, units (list of
+    ResUnit dicts as voc_units takes). Returns (lai_voc_bigvgan_block_t, tensors kept alive)."""
+    wp = voc_pack_tconv(blk["w"], blk["rate"])
+    arr, keep = voc_units(blk["units"]) if blk["units"] else (None, [])
+    st = VocBigVGANBlock(blk["ea"].data_ptr(), blk["ieb"].data_ptr(), wp.data_ptr(),
+                         blk["b"].data_ptr(), int(blk["rate"]), len(blk["units"]),
+                         ctypes.cast(arr, _vp).value if arr is not None else None)
+    return st, [wp, arr, keep, blk]
+
+
+def voc_bigvgan_block(x, params, c_out, scratch=None, passes=3, err=None, stream=None):
+    """x [batch, T, c_in] -> new tensor [batch, (T - 1) rate, c_out]."""
+    import torch
+    b, t, c_in = (1, *x.shape) if x.dim() == 2 else x.shape
+    st = params[0] if isinstance(params, tuple) else params
+    t_out = (t - 1) * st.rate
+    out = torch.empty((b, t_out, c_out), dtype=torch.float32, device=x.device)
+    if scratch is None:
+        scratch = torch.empty(2 * b * t * c_in + 4 * b * t_out * c_out, dtype=torch.float32,
+                              device=x.device)
+    call("lai_voc_bigvgan_block_f32", _p(out), _p(x), _p(scratch), ctypes.byref(st), b, c_in,
+         c_out, t, passes, _p(err), _s(stream))
+    return out
 
 
 class VocConvNeXt(ctypes.Structure):

@@ -404,6 +404,31 @@ void oracle_voc_resunit(float *x, const float *ea1, const float *ieb1, const flo
 }
 
 /* ---------------------------------------------------------------------------
+ * Transposed conv1d (voc_conv_transpose1d, src/tts_vocoder_ops.c:153-221, its scatter
+ * formulation): out[oc, t*stride + ki - trim] += x[ic, t] * w[ic, oc, ki] over all ic, t,
+ * ki with 0 <= index < T_out, trim = kernel - stride, T_out = (T + 1) * stride - kernel;
+ * then + bias. Summed per output in acc_t (gathered instead of scattered).
+ * ------------------------------------------------------------------------- */
+void oracle_voc_conv_transpose1d(float *out, const float *in, const float *w, const float *bias,
+                                 int c_in, int c_out, int T, int kernel, int stride) {
+    const int trim = kernel - stride, T_out = (T + 1) * stride - kernel;
+#pragma omp parallel for schedule(static)
+    for (int oc = 0; oc < c_out; oc++)
+        for (int oi = 0; oi < T_out; oi++) {
+            acc_t s = 0;
+            for (int ki = 0; ki < kernel; ki++) {
+                const int num = oi + trim - ki;  /* = t * stride */
+                if (num < 0 || num % stride) continue;
+                const int t = num / stride;
+                if (t >= T) continue;
+                for (int ic = 0; ic < c_in; ic++)
+                    s += (acc_t)in[(size_t)ic * T + t] * w[((size_t)ic * c_out + oc) * kernel + ki];
+            }
+            out[(size_t)oc * T_out + oi] = (float)s + (bias ? bias[oc] : 0.0f);
+        }
+}
+
+/* ---------------------------------------------------------------------------
  * ConvNeXt pieces. Depthwise causal conv: voc_conv1d_causal with groups == c_in ==
  * c_out (src/tts_vocoder_ops.c:52-73), out[c,t] = b[c] + sum_k w[c,k] x[c, t-(K-1)+k]
  * (zero before t = 0), summed in acc_t in tap order. out may equal in (the reference

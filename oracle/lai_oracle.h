@@ -79,6 +79,11 @@ void oracle_voc_resunit(float *x, const float *ea1, const float *ieb1, const flo
                         const float *b1, const float *ea2, const float *ieb2, const float *w2,
                         const float *b2, int C, int T, int dilation, float *scratch);
 
+/* voc_conv_transpose1d (src/tts_vocoder_ops.c:153-221): w [c_in, c_out, kernel]; output
+ * length (T + 1) * stride - kernel, trimming kernel - stride from each side */
+void oracle_voc_conv_transpose1d(float *out, const float *in, const float *w, const float *bias,
+                                 int c_in, int c_out, int T, int kernel, int stride);
+
 /* ConvNeXt pieces (src/tts_vocoder_ops.c): depthwise causal conv (voc_conv1d_causal with
  * groups == channels, :52-73; w [C, 1, kernel]), LayerNorm over channels per time step
  * (voc_layer_norm_channels, :311-336), exact GELU (voc_gelu, :344-349); and the block

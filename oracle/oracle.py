@@ -63,6 +63,9 @@ def load(name: str = "liblai_oracle.so") -> ctypes.CDLL:
         lib.voc_conv1d_causal.argtypes = [_F, _F, _F, _F, _c_int, _c_int, _c_int, _c_int,
                                           _c_int, _c_int, _F]
         lib.voc_conv1d_causal.restype = None
+        lib.voc_conv_transpose1d.argtypes = [_F, _F, _F, _F, _c_int, _c_int, _c_int, _c_int,
+                                             _c_int, _F]
+        lib.voc_conv_transpose1d.restype = None
     _LIBS[name] = lib
     return lib
 
@@ -102,6 +105,7 @@ def _declare(lib: ctypes.CDLL) -> None:
                                     _c_int, _c_float],
         "oracle_repetition_penalty": [_F, _c_int, _I32, _c_int, _c_float],
         "oracle_sample_topk": [_F, _c_int, _c_float, _c_int, _c_float, _F, _F],
+        "oracle_voc_conv_transpose1d": [_F, _F, _F, _F, _c_int, _c_int, _c_int, _c_int, _c_int],
         "oracle_voc_conv1d_depthwise": [_F, _F, _F, _F, _c_int, _c_int, _c_int],
         "oracle_voc_layer_norm_channels": [_F, _F, _F, _c_int, _c_int, _c_float],
         "oracle_voc_gelu": [_F, _c_i64],
@@ -515,3 +519,48 @@ def ref_voc_convnext(x, p, build: str = "scalar"):
         out = ref_voc_conv1d_causal(h, p["pw2_w"], p["pw2_b"], 1, build)
         rows[b] = out * f(p["gamma"])[:, None] + r
     return y
+
+
+# ---- BigVGAN block: SnakeBeta -> ConvTranspose1d (k = 2r, stride r) -> 3 ResUnits ----
+
+def voc_conv_transpose1d(x, w, bias, stride, lib=None):
+    """x [c_in, T], w [c_in, c_out, kernel] -> [c_out, (T + 1) * stride - kernel]."""
+    lib = lib or load()
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    c_in, c_out, kernel = w.shape
+    T = x.shape[-1]
+    out = np.empty((c_out, (T + 1) * stride - kernel), np.float32)
+    lib.oracle_voc_conv_transpose1d(ptr(out), ptr(x), ptr(w), ptr(np.ascontiguousarray(bias, np.float32)),
+                                    c_in, c_out, T, kernel, stride)
+    return out
+
+
+def ref_voc_conv_transpose1d(x, w, bias, stride, build: str = "scalar"):
+    """The reference's own voc_conv_transpose1d (compiled, no BLAS: scatter-add loop)."""
+    lib = load(f"libvoc_ref_{build}.so")
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    c_in, c_out, kernel = w.shape
+    T = x.shape[-1]
+    out = np.empty((c_out, (T + 1) * stride - kernel), np.float32)
+    lib.voc_conv_transpose1d(ptr(out), ptr(x), ptr(w), ptr(np.ascontiguousarray(bias, np.float32)),
+                             c_in, c_out, T, kernel, stride, None)
+    return out
+
+
+def voc_bigvgan_block(x, blk, lib=None):
+    """One block of tts_vocoder_run (src/tts_vocoder.c:709-728) on x [c_in, T] or [B, c_in, T]:
+    snake (blk["ea"], blk["ieb"]), transposed conv (blk["w"] [c_in, c_out, 2r], blk["b"],
+    stride blk["rate"]), then the ResUnits blk["units"] (dicts as voc_resunit's, with
+    "dilation")."""
+    y = np.asarray(x, np.float32)
+    batch = y.reshape(-1, y.shape[-2], y.shape[-1])
+    outs = []
+    for b in range(batch.shape[0]):
+        s = snake_beta(batch[b], blk["ea"], blk["ieb"], lib)
+        h = voc_conv_transpose1d(s, blk["w"], blk["b"], blk["rate"], lib)
+        for u in blk["units"]:
+            h = voc_resunit(h, {k: v for k, v in u.items() if k != "dilation"}, u["dilation"], lib)
+        outs.append(h)
+    return np.stack(outs)
