@@ -614,6 +614,98 @@ def cpu_convnext_rate(stages, batch: int, min_seconds: float, sample_t: int = 50
             "threads": nthreads, "passes": n, "seconds": el, "sample_t": sample_t}
 
 
+def cpu_decoder_rate(t0: int, batch: int, min_seconds: float, t0_sample: int = 40,
+                     steps: int | None = None, warmup: int = 1) -> dict:
+    """The BigVGAN decoder's 4 blocks on host cores as the reference's USE_BLAS build runs
+    them (src/tts_vocoder.c:709-728): its own compiled AVX2 voc_snake_beta over channel
+    ranges on a thread pool; voc_conv_transpose1d as its SGEMM + col2im formulation
+    (src/tts_vocoder_ops.c:169-194) and the ResUnits as in cpu_resunit_rate, the SGEMMs
+    through numpy's OpenBLAS on all host cores. Runs from t0_sample input rows; every op is
+    linear in T, so the step time is scaled by t0 / t0_sample. Returns audio samples/s."""
+    import concurrent.futures as cf
+
+    import numpy as np
+    from threadpoolctl import threadpool_limits
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle
+    import runner
+    snake = oracle.load("libvoc_ref_avx2.so").voc_snake_beta
+    F = ctypes.POINTER(ctypes.c_float)
+    nthreads = len(os.sched_getaffinity(0))
+    rng = np.random.default_rng(10)
+    f = lambda a: np.ascontiguousarray(a, dtype=np.float32)  # noqa: E731
+    blocks = []
+    for b, r in enumerate(runner.BIGVGAN_RATES):
+        c_in, c_out = runner.BIGVGAN_CHANNELS[b], runner.BIGVGAN_CHANNELS[b + 1]
+        units = []
+        for d in runner.RESUNIT_DILATIONS:
+            units.append({"ea1": f(np.exp(rng.normal(0, .1, c_out))), "ieb1": f(np.exp(-rng.normal(0, .1, c_out))),
+                          "w1t": [f(rng.standard_normal((c_out, c_out)) / np.sqrt(7 * c_out)) for _ in range(7)],
+                          "b1": f(rng.normal(0, .01, (c_out, 1))),
+                          "ea2": f(np.exp(rng.normal(0, .1, c_out))), "ieb2": f(np.exp(-rng.normal(0, .1, c_out))),
+                          "w2": f(0.1 * rng.standard_normal((c_out, c_out)) / np.sqrt(c_out)),
+                          "b2": f(rng.normal(0, .01, (c_out, 1))), "d": d})
+        blocks.append({"ea": f(np.exp(rng.normal(0, .1, c_in))), "ieb": f(np.exp(-rng.normal(0, .1, c_in))),
+                       "wt": f((rng.standard_normal((c_in, c_out * 2 * r)) / np.sqrt(2 * c_in)).T),
+                       "b": f(rng.normal(0, .01, (c_out, 1))), "r": r, "c_out": c_out,
+                       "units": units})
+    x0 = f(rng.standard_normal((runner.BIGVGAN_CHANNELS[0], t0_sample)))
+
+    with cf.ThreadPoolExecutor(nthreads) as pool, threadpool_limits(nthreads):
+        def snake_mt(x, ea, ieb):
+            c, t = x.shape
+            per = max(1, -(-c // nthreads))
+            list(pool.map(lambda c0: snake(x[c0].ctypes.data_as(F), ea[c0:].ctypes.data_as(F),
+                                           ieb[c0:].ctypes.data_as(F), min(per, c - c0), t),
+                          range(0, c, per)))
+
+        def decoder():
+            x = x0.copy()
+            for blk in blocks:
+                snake_mt(x, blk["ea"], blk["ieb"])
+                r, c_out, t = blk["r"], blk["c_out"], x.shape[1]
+                cols = (blk["wt"] @ x).reshape(c_out, 2 * r, t)  # W^T X, then col2im
+                y = np.zeros((c_out, (t - 1) * r), np.float32)
+                for ki in range(2 * r):
+                    if ki < r:
+                        y[:, ki::r] += cols[:, ki, 1:]
+                    else:
+                        y[:, ki - r::r] += cols[:, ki, :t - 1]
+                y += blk["b"]
+                x = y
+                for u in blk["units"]:
+                    res = x.copy()
+                    snake_mt(x, u["ea1"], u["ieb1"])
+                    pad = np.zeros((c_out, x.shape[1] + 6 * u["d"]), np.float32)
+                    pad[:, 6 * u["d"]:] = x
+                    tt = x.shape[1]
+                    h = u["w1t"][0] @ pad[:, :tt]
+                    for k in range(1, 7):
+                        h += u["w1t"][k] @ pad[:, k * u["d"]:k * u["d"] + tt]
+                    h += u["b1"]
+                    snake_mt(h, u["ea2"], u["ieb2"])
+                    x = u["w2"] @ h
+                    x += u["b2"]
+                    x += res
+            return x
+
+        for _ in range(warmup):
+            decoder()
+        n, t_start = 0, time.perf_counter()
+        while True:
+            out = decoder()
+            n += 1
+            el = time.perf_counter() - t_start
+            if (steps is not None and n >= steps) or (steps is None and el >= min_seconds):
+                break
+    step_s = (el / n) * (t0 / t0_sample) * batch
+    t_final = t0
+    for r in runner.BIGVGAN_RATES:
+        t_final = (t_final - 1) * r
+    return {"rows_per_s": batch * t_final / step_s, "step_seconds": step_s, "threads": nthreads,
+            "passes": n, "seconds": el, "t0_sample": t0_sample, "samples_sample": out.shape[1]}
+
+
 def cpu_sampling_rate(rows: int, vocab: int, top_k: int, temperature: float, penalty: float,
                       hist: int, min_seconds: float, steps: int | None = None) -> dict:
     """The reference's own tts_apply_repetition_penalty + tts_sample_topk (oracle/_ref, built
@@ -684,12 +776,15 @@ def run_single(args) -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     seed = args.seed + 1000 * rank
-    tensor = args.config == "n1"
+    tensor = args.config in ("n1", "v2")
     tf32 = tf32_peak_tflops() if tensor else None
     if args.config == "a3":
-        work = runner.DecodeAttention(seed=seed)
+        work = runner.DecodeAttention(seqs=args.rows or 256, seed=seed)
     elif args.config == "n1":
-        work = runner.VocConvNeXt(passes=args.passes, seed=seed)
+        work = runner.VocConvNeXt(stages=[(1024, 1000 // args.t_div), (1024, 2000 // args.t_div)],
+                                  passes=args.passes, seed=seed)
+    elif args.config == "v2":
+        work = runner.VocDecoder(t0=2000 // args.t_div, passes=args.passes, seed=seed)
     else:
         work = runner.SampleBatch(seed=seed)
     launches = work.launches(None)
@@ -747,7 +842,7 @@ def run_single(args) -> None:
                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"}
     roofline.update({"traffic": load_traffic().get(f"{dominant}@{args.config}"),
                      "algorithmic_bytes_per_launch": d["bytes_per_launch"]})
-    rows_step = sum(rows_pl)
+    rows_step = getattr(work, "rows_step", sum(rows_pl))
     value = rows_step * world * args.steps / (max_ms / 1000.0)
 
     e2e = None
@@ -759,6 +854,11 @@ def run_single(args) -> None:
             outs = [(pin(work.out), work.out)]
             api = ("lai_decode_attention_f32 with q/k/v/pos copied in from pinned host memory and "
                    "the output back each step; the cache stays on the device")
+        elif args.config == "v2":
+            ins = [(work.x0, pin(work.x0))]
+            outs = [(pin(work.outs[-1]), work.outs[-1])]
+            api = ("lai_voc_bigvgan_block_f32 x 4 with the decoder input copied in from and the "
+                   "audio-rate output back to pinned host memory each step")
         elif args.config == "n1":
             ins = [(x, pin(x)) for x in work.x]
             outs = [(pin(x), x) for x in work.x]
@@ -782,6 +882,15 @@ def run_single(args) -> None:
                              f"positions < {work.max_seq} ({r['seconds']:.1f} s): the restated "
                              "qwen_causal_attention (seq_q = 1), float sums, OpenMP over "
                              f"(sequence, head), host {cpu_model()}"}
+        elif args.config == "v2":
+            r = cpu_decoder_rate(work.t0, work.batch, args.cpu_seconds)
+            cpu = {"value": round(r["rows_per_s"], 1), "unit": "rows/s", "cores": r["threads"],
+                   "kind": "port",
+                   "sample": f"{r['passes']} runs of the whole decoder from {r['t0_sample']} input "
+                             f"rows ({r['samples_sample']} output samples, {r['seconds']:.1f} s), "
+                             f"scaled to t0 = {work.t0}: the reference's USE_BLAS path (its AVX2 "
+                             "voc_snake_beta, transposed conv as SGEMM + col2im, ResUnits as "
+                             f"SGEMMs through numpy's OpenBLAS), host {cpu_model()}"}
         elif args.config == "n1":
             r = cpu_convnext_rate(work.stages, work.batch, args.cpu_seconds)
             cpu = {"value": round(r["rows_per_s"], 1), "unit": "rows/s", "cores": r["threads"],
@@ -815,6 +924,12 @@ def run_single(args) -> None:
                            "residual), FP32 channels-last",
                "stages": getattr(work, "stages", None), "batch": getattr(work, "batch", None),
                "passes": args.passes, "rows": "time rows (batch x T) per stage"},
+        "v2": {"workload": "vocoder BigVGAN decoder after its init conv: 4 blocks of SnakeBeta, "
+                           "transposed conv (2r, stride r) and 3 ResUnits on tcgen05, FP32 "
+                           "channels-last, at the reference's length progression",
+               "t0": getattr(work, "t0", None), "batch": getattr(work, "batch", None),
+               "stages": getattr(work, "shapes", None), "passes": args.passes,
+               "rows": "audio samples (24 kHz) out of the last block per step"},
         "s3": {"workload": "talker token sampling: repetition penalty + top-k 50 at temperature "
                            "0.9 over codec logits (vocab 3072), 64-token histories",
                "rows": "decode rows (one token drawn each)", "batch": getattr(work, "rows", None)},
@@ -829,7 +944,7 @@ def run_single(args) -> None:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded counter-based N(0,1) on device)", "config": desc,
         "per_kernel": per_kernel, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-        "gpu_launches": args.steps * len(launches) * (3 if args.config == "n1" else 1),
+        "gpu_launches": args.steps * len(launches) * {"n1": 3, "v2": 8}.get(args.config, 1),
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
@@ -886,6 +1001,16 @@ def run_reference(args) -> None:
                     ms_per_step=1000.0 * r["seconds"] / r["passes"], scaling="weak", dtype="f32",
                     config={"workload": "TTS talker decode attention", "config": "a3",
                             "sequences": 16, "heads": [16, 8, 128], "max_seq": 4096})
+    elif args.config == "v2":
+        r = cpu_decoder_rate(2000, 1, 0.0, t0_sample=40, steps=args.steps, warmup=args.warmup)
+        cb = {"value": r["rows_per_s"], "unit": "rows/s", "cores": r["threads"], "kind": "port",
+              "sample": f"the whole decoder from 40 input rows per step ({r['samples_sample']} "
+                        "output samples), scaled to t0 = 2000; the reference's USE_BLAS path "
+                        f"(AVX2 voc_snake_beta + OpenBLAS SGEMMs), host {cpu_model()}"}
+        line = dict(common, value=r["rows_per_s"], unit="rows/s",
+                    ms_per_step=1000.0 * r["step_seconds"], scaling="weak", dtype="f32",
+                    config={"workload": "vocoder BigVGAN decoder (4 blocks)", "config": "v2",
+                            "t0": 2000, "batch": 1})
     elif args.config == "n1":
         stages = [(1024, 1000), (1024, 2000)]
         r = cpu_convnext_rate(stages, 8, 0.0, sample_t=500, steps=args.steps, warmup=args.warmup)
@@ -1372,8 +1497,8 @@ def main():
                     help="timed steps (default 2000; 20 for v1, whose step is ~0.1 s)")
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "g1", "g2", "v1", "a3", "n1",
-                                         "s3"],
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "g1", "g2", "v1", "v2", "a3",
+                                         "n1", "s3"],
                     default="c2")
     ap.add_argument("--t-div", type=int, default=1,
                     help="v1: divide every stage's length (small profiling cases)")
@@ -1402,12 +1527,12 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)  # timing rule: at least 3 untimed warm-up steps
     if args.steps is None:
-        args.steps = {"v1": 20, "n1": 50, "a3": 200}.get(args.config, 2000)
+        args.steps = {"v1": 20, "v2": 20, "n1": 50, "a3": 200}.get(args.config, 2000)
     if args.impl == "reference":
         run_reference(args)
     elif args.config == "v1":
         run_resunits(args)
-    elif args.config in ("a3", "n1", "s3"):
+    elif args.config in ("a3", "n1", "s3", "v2"):
         run_single(args)
     else:
         run_ours(args)

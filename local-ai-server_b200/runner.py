@@ -282,6 +282,87 @@ class VocResUnits:
         return [self.batch * t for _, t in self.stages]  # time rows through 3 units
 
 
+BIGVGAN_CHANNELS = (1536, 768, 384, 192, 96)  # src/tts_vocoder.c:245
+BIGVGAN_RATES = (8, 5, 4, 3)                   # src/tts_vocoder.c:244
+
+
+class VocDecoder:
+    """The BigVGAN decoder after its init conv (config v2): 4 blocks, each SnakeBeta ->
+    transposed conv (kernel 2r, stride r) -> 3 ResUnits, at the reference's own length
+    progression T -> (T - 1) r (src/tts_vocoder.c:709-728): for t0 = 2000 (500 codec frames,
+    40 s of audio) 1536 x 2000 -> 768 x 15992 -> 384 x 79955 -> 192 x 319816 -> 96 x 959445.
+    Every step recomputes the decoder from the same input (no state carries over). Weights:
+    transposed convs N(0,1)/sqrt(2 c_in), ResUnits as VocResUnits."""
+
+    def __init__(self, t0: int = 2000, batch: int = 1, passes: int = 3, seed: int = 77,
+                 device="cuda"):
+        import torch
+        self.t0, self.batch, self.passes = t0, batch, passes
+        k = 0
+
+        def normal(shape, std=1.0):
+            nonlocal k
+            t = torch.empty(shape, dtype=torch.float32, device=device)
+            lai.synth_normal(t, seed=seed + k, std=std)
+            k += 1
+            return t
+
+        self.x0 = normal((batch, t0, BIGVGAN_CHANNELS[0]))
+        self.blocks, self.outs, self.shapes = [], [], []
+        t = t0
+        scratch = 0
+        for b, r in enumerate(BIGVGAN_RATES):
+            c_in, c_out = BIGVGAN_CHANNELS[b], BIGVGAN_CHANNELS[b + 1]
+            t_out = (t - 1) * r
+            units = []
+            for d in RESUNIT_DILATIONS:
+                units.append({
+                    "ea1": torch.exp(normal(c_out, 0.1)), "ieb1": 1.0 / torch.exp(normal(c_out, 0.1)),
+                    "w1": normal((c_out, c_out, 7), (7 * c_out) ** -0.5), "b1": normal(c_out, 0.01),
+                    "ea2": torch.exp(normal(c_out, 0.1)), "ieb2": 1.0 / torch.exp(normal(c_out, 0.1)),
+                    "w2": normal((c_out, c_out, 1), 0.1 * c_out ** -0.5), "b2": normal(c_out, 0.01),
+                    "dilation": d})
+            self.blocks.append(lai.voc_block_params({
+                "ea": torch.exp(normal(c_in, 0.1)), "ieb": 1.0 / torch.exp(normal(c_in, 0.1)),
+                "w": normal((c_in, c_out, 2 * r), (2 * c_in) ** -0.5), "b": normal(c_out, 0.01),
+                "rate": r, "units": units}))
+            self.outs.append(torch.empty((batch, t_out, c_out), dtype=torch.float32, device=device))
+            self.shapes.append((c_in, c_out, t, t_out, r))
+            scratch = max(scratch, 2 * batch * t * c_in + 4 * batch * t_out * c_out)
+            t = t_out
+        self.scratch = torch.empty(scratch, dtype=torch.float32, device=device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.kernel_names = tuple(f"block{b}_{c_in}to{c_out}x{t_out}"
+                                  for b, (c_in, c_out, _, t_out, _) in enumerate(self.shapes))
+        self.rows_step = batch * self.shapes[-1][3]  # audio samples (24 kHz) per step
+
+    def launches(self, stream=None):
+        def block(i):
+            src = self.x0 if i == 0 else self.outs[i - 1]
+            c_in, c_out, t, t_out, r = self.shapes[i]
+            st = self.blocks[i][0]
+            lai.call("lai_voc_bigvgan_block_f32", lai._p(self.outs[i]), lai._p(src),
+                     lai._p(self.scratch), lai.ctypes.byref(st), self.batch, c_in, c_out, t,
+                     self.passes, lai._p(self.err), lai._s(stream))
+        return [(lambda i=i: block(i)) for i in range(len(self.shapes))]
+
+    def flops_per_launch(self) -> list[float]:
+        """F32 convolution flops: the transposed conv 2 * c_in * c_out * 2 per output row (two
+        taps reach each output), the ResUnits 16 * c_out^2 per output row and unit."""
+        return [self.batch * t_out * (4.0 * c_in * c_out + 16.0 * c_out * c_out * 3)
+                for c_in, c_out, _, t_out, _ in self.shapes]
+
+    def bytes_per_launch(self) -> list[int]:
+        """Snake split of the input (read 4, write 8 per element); the transposed conv reads
+        the 8-byte operand and writes x and the first unit's split input (12 per output
+        element); the 3 ResUnits then move 112 per element (124 less the first split)."""
+        return [self.batch * (20 * t * c_in + 124 * t_out * c_out)
+                for c_in, c_out, t, t_out, _ in self.shapes]
+
+    def rows_per_launch(self) -> list[int]:
+        return [self.batch * t_out for _, _, _, t_out, _ in self.shapes]
+
+
 class VocConvNeXt:
     """The vocoder's two ConvNeXt upsample blocks (config n1): C = 1024 at 2 T0 and 4 T0
     time rows (T0 = 500 codec frames, src/tts_vocoder.c:658-670), batch 8, FP32
