@@ -66,6 +66,35 @@ P = V(16)  # a non-NULL dummy pointer: never dereferenced, the checks fail first
     (lambda l: l.lai_snake_beta_f32(P, P, None, 1, 4, 16, None), lai.LAI_ERR_INVALID),
     (lambda l: l.lai_rope_table_f32(P, P, None, 4, 1024, 1e6, None), lai.LAI_ERR_INVALID),
     (lambda l: l.lai_synth_uniform_i32(P, 4, 1, 0, 5, 5, None), lai.LAI_ERR_INVALID),
+    # decode attention: head_dim other than 128, heads not a multiple of kv heads, group of 3
+    (lambda l: l.lai_decode_attention_f32(P, P, P, P, P, P, P, 1, 16, 8, 64, 100, 0.1, P, None,
+                                          None), lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_decode_attention_f32(P, P, P, P, P, P, P, 1, 12, 4, 128, 100, 0.1, P, None,
+                                          None), lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_decode_attention_f32(V(4096), P, P, P, V(4096), P, P, 1, 16, 8, 128, 100,
+                                          0.1, P, None, None), lai.LAI_ERR_ALIAS),
+    # sampling: empty vocab; history without lengths; shared memory beyond 200 KiB
+    (lambda l: l.lai_sample_topk_f32(P, P, 0, 1, None, None, 0, 1.0, 1.0, 5, P, None),
+     lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_sample_topk_f32(P, P, 100, 1, P, None, 4, 1.0, 1.0, 5, P, None),
+     lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_sample_topk_f32(P, P, 1 << 22, 1, None, None, 0, 1.0, 1.0, 1 << 20, P, None),
+     lai.LAI_ERR_TOOBIG),
+    # vocoder: passes other than 1 / 3; channels not a multiple of 32; unsupported ConvNeXt
+    # width; a BigVGAN block needs T >= 2; packers need their weights
+    (lambda l: l.lai_voc_resunits_f32(P, P, P, 1, 1, 96, 128, 2, None, None), lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_voc_resunits_f32(P, P, P, 1, 1, 80, 128, 3, None, None), lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_voc_convnext_f32(P, P, P, 1, 300, 64, 3, None, None), lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_voc_bigvgan_block_f32(P, P, P, None, 1, 64, 32, 10, 3, None, None),
+     lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_voc_pack_conv_f32(P, None, 8, 8, 7, None), lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_voc_pack_tconv_f32(P, P, 8, 8, 0, None), lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_voc_transpose_f32(V(4096), V(4096 + 8), 1, 4, 4, None), lai.LAI_ERR_ALIAS),
+    # decode GEMVs: output overlapping input; K beyond the staged maximum
+    (lambda l: l.lai_gemv_bf16w_f32(V(256), V(256), None, 1e-6, P, 1, 64, 8, None),
+     lai.LAI_ERR_ALIAS),
+    (lambda l: l.lai_gemv_bf16w_f32(V(256), V(1 << 30), None, 1e-6, P, 1, 60000, 8, None),
+     lai.LAI_ERR_TOOBIG),
 ])
 def test_argument_checks(call, want):
     assert call(lai.load()) == want
