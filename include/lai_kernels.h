@@ -252,7 +252,7 @@ LAI_API int lai_voc_resunits_f32(float *x, float *scratch, const lai_voc_resunit
  */
 typedef struct {
     const float *snake_ea, *snake_ieb; /* [c_in] the block's SnakeBeta, pre-exponentiated */
-    const float *tconv_w;              /* packed, 4 * rate * c_out * c_in floats */
+    const float *tconv_w;              /* lai_voc_pack_tconv_f32 image, kernel 2 * rate */
     const float *tconv_b;              /* [c_out] */
     int rate;                          /* 8, 5, 4, 3 in the reference (src/tts_vocoder.c:247) */
     int n_units;                       /* ResUnits that follow (3) */
@@ -262,10 +262,37 @@ typedef struct {
 LAI_API int lai_voc_bigvgan_block_f32(float *out, const float *x, float *scratch,
                                       const lai_voc_bigvgan_block_t *blk, int batch, int c_in,
                                       int c_out, int T, int passes, int *err, lai_stream_t stream);
-/* dst (4 * rate * c_out * c_in floats) <- reference weight w [c_in, c_out, 2 * rate], split
- * per phase into the two taps of the interleaved convs, TF32 high parts then remainders. */
-LAI_API int lai_voc_pack_tconv_f32(float *dst, const float *w, int c_in, int c_out, int rate,
-                                   lai_stream_t stream);
+/* dst (2 * kernel * c_out * c_in floats) <- reference transposed-conv weight
+ * w [c_in, c_out, kernel], kernel = stride or 2 * stride, regrouped per output phase into the
+ * taps of the interleaved convs, TF32 high parts then remainders. */
+LAI_API int lai_voc_pack_tconv_f32(float *dst, const float *w, int c_in, int c_out, int kernel,
+                                   int stride, lai_stream_t stream);
+
+/* ---- the vocoder decoder's other convolutions (channels-last [batch, T, C] F32) ------------
+ * lai_voc_conv1d_f32: voc_conv1d_causal (src/tts_vocoder_ops.c:44-147, groups 1) with w the
+ *   lai_voc_pack_conv_f32 image of [c_out, c_in, kernel]: out [batch, T, c_out] = conv(x) + bias
+ *   (the BigVGAN init conv 1024 -> 1536, k=7, src/tts_vocoder.c:694-697). scratch:
+ *   2 * batch * T * c_in floats.
+ * lai_voc_conv_transpose1d_f32: voc_conv_transpose1d (:153-221) for kernel = stride (the
+ *   ConvNeXt upsample stages, src/tts_vocoder.c:658-667) or 2 * stride, w the
+ *   lai_voc_pack_tconv_f32 image; out [batch, (T + 1) stride - kernel, c_out]. scratch:
+ *   2 * batch * T * c_in floats.
+ * lai_voc_final_f32: the decoder's last step (src/tts_vocoder.c:748-758): voc_snake_beta over
+ *   x [batch, T, channels], conv1d channels -> 1 (k = 7, w [1, channels, 7] as loaded, bias [1]),
+ *   clamp to [-1, 1]; audio [batch, T]. channels <= ~190 (shared-memory window).
+ * c_in, c_out multiples of 32; passes as for the ResUnits.
+ */
+LAI_API int lai_voc_conv1d_f32(float *out, const float *x, float *scratch, const float *w,
+                               const float *bias, int batch, int c_in, int c_out, int T,
+                               int kernel, int dilation, int passes, int *err,
+                               lai_stream_t stream);
+LAI_API int lai_voc_conv_transpose1d_f32(float *out, const float *x, float *scratch,
+                                         const float *w, const float *bias, int batch, int c_in,
+                                         int c_out, int T, int kernel, int stride, int passes,
+                                         int *err, lai_stream_t stream);
+LAI_API int lai_voc_final_f32(float *audio, const float *x, const float *exp_alpha,
+                              const float *inv_exp_beta, const float *w, const float *bias,
+                              int batch, int channels, int T, lai_stream_t stream);
 
 /* ---- vocoder ConvNeXt block (upsample stages) --------------------------------------------
  * run_convnext(x, C, T, cn) (src/tts_vocoder.c:463-533): depthwise causal conv k=7 + bias,

@@ -65,10 +65,11 @@ struct ConvArgs {
     const float *gamma;      // kEpiScaleResidual: per-channel layer scale
     int T, c_in, c_out, taps, dilation;
     int *err;
-    // Phased output (a transposed conv as `phases` interleaved 2-tap convs): GEMM row t >= 1
-    // of phase f goes to output row (t - 1) * phases + f of a T_out-row sequence. 0 or 1: an
-    // ordinary conv, row t to row t.
-    int phases, T_out;
+    // Phased output (a transposed conv as `phases` interleaved convs of taps taps): GEMM row
+    // t >= row_trim of phase f goes to output row (t - row_trim) * phases + f of a T_out-row
+    // sequence (kernel 2r: 2 taps, row_trim 1; kernel r: 1 tap, row_trim 0). phases 0 or 1:
+    // an ordinary conv, row t to row t.
+    int phases, T_out, row_trim;
 };
 
 template <int BN, int PASSES>
@@ -170,8 +171,8 @@ conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
     auto out_row = [&](int t) -> int64_t {
         if (t >= a.T) return -1;
         if (P == 1) return (int64_t)b * a.T + t;
-        if (t == 0) return -1;
-        return (int64_t)b * a.T_out + (int64_t)(t - 1) * P + phase;
+        if (t < a.row_trim) return -1;
+        return (int64_t)b * a.T_out + (int64_t)(t - a.row_trim) * P + phase;
     };
     const int kblocks = a.c_in / kBK;
     const int n_iter = a.taps * kblocks;

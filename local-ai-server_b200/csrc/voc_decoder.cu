@@ -1,0 +1,172 @@
+// voc_decoder.cu - the vocoder decoder's remaining convolutions, channels-last F32:
+//   lai_voc_conv1d_f32           causal conv1d (the BigVGAN init conv 1024 -> 1536, k=7,
+//                                src/tts_vocoder.c:694-697) on the tensor-core GEMM
+//   lai_voc_conv_transpose1d_f32 transposed conv with kernel = stride (the ConvNeXt upsample
+//                                stages, :658-667) or kernel = 2 stride (BigVGAN blocks)
+//   lai_voc_final_f32            SnakeBeta -> conv1d C -> 1 (k=7) -> clamp(-1, 1), the decoder's
+//                                last step (:748-758), fused into one HBM pass
+// The GEMM forms (voc_conv.cuh) read their input in the 3xTF32 hi/lo split, made here by a
+// plain split kernel; the transposed conv runs `stride` interleaved convs of kernel / stride
+// taps, output row (t - trim) * stride + f for phase f (trim 1 for kernel 2 stride, else 0).
+#include "voc_conv.cuh"
+
+namespace lai {
+namespace {
+
+// hi = tf32(x), lo = x - hi over n elements (n % 4 == 0)
+template <int PASSES>
+__global__ void __launch_bounds__(256)
+split_kernel(const float *__restrict__ x, float *hi, float *lo, int64_t n4) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const float4 v = reinterpret_cast<const float4 *>(x)[i];
+        const float4 h = make_float4(umma::tf32_round(v.x), umma::tf32_round(v.y),
+                                     umma::tf32_round(v.z), umma::tf32_round(v.w));
+        reinterpret_cast<float4 *>(hi)[i] = h;
+        if (PASSES == 3)
+            reinterpret_cast<float4 *>(lo)[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z,
+                                                            v.w - h.w);
+    }
+}
+
+int launch_split(const float *x, float *hi, float *lo, size_t n, int passes, cudaStream_t st) {
+    const int64_t n4 = (int64_t)n / 4;
+    const unsigned g = grid_for(n4, 256) < 148u * 16 ? grid_for(n4, 256) : 148u * 16;
+    if (passes == 3)
+        split_kernel<3><<<g, 256, 0, st>>>(x, hi, lo, n4);
+    else
+        split_kernel<1><<<g, 256, 0, st>>>(x, hi, lo, n4);
+    return launch_status();
+}
+
+// Final step: one CTA writes kFinalRows consecutive samples of one item. It stages input rows
+// [t0 - 6, t0 + kFinalRows) of x [T, C] through SnakeBeta into shared memory (zero before
+// t = 0; rows padded to C + 1 floats so the per-thread row reads hit distinct banks), then
+// each thread sums its sample's 7 x C window and clamps.
+constexpr int kFinalRows = 256;
+
+__global__ void __launch_bounds__(kFinalRows)
+final_kernel(float *audio, const float *__restrict__ x, const float *__restrict__ ea,
+             const float *__restrict__ ieb, const float *__restrict__ w,
+             const float *__restrict__ bias, int T, int C) {
+    extern __shared__ float sm[];
+    const int pitch = C + 1;
+    float *s = sm;                                   // [kFinalRows + 6][C + 1]
+    float *wt = sm + (size_t)(kFinalRows + 6) * pitch;  // [7][C]: tap-major weights
+    const int b = blockIdx.y, t0 = blockIdx.x * kFinalRows;
+    const float *xb = x + (size_t)b * T * C;
+    for (int i = threadIdx.x; i < 7 * C; i += kFinalRows) {
+        const int c = i / 7, k = i - c * 7;
+        wt[k * C + c] = w[i];  // w [1, C, 7] as loaded
+    }
+    const int n = (kFinalRows + 6) * C;
+    for (int i = threadIdx.x; i < n; i += kFinalRows) {
+        const int r = i / C, c = i - r * C;
+        const int t = t0 - 6 + r;
+        s[r * pitch + c] = (t >= 0 && t < T) ? snake1(xb[(size_t)t * C + c], __ldg(ea + c),
+                                                      __ldg(ieb + c))
+                                             : 0.0f;
+    }
+    __syncthreads();
+    const int t = t0 + threadIdx.x;
+    if (t >= T) return;
+    float acc = 0.0f;
+    for (int k = 0; k < 7; k++) {
+        const float *row = s + (threadIdx.x + k) * pitch;
+        const float *wk = wt + k * C;
+        for (int c = 0; c < C; c++) acc = fmaf(wk[c], row[c], acc);
+    }
+    acc += __ldg(bias);
+    audio[(size_t)b * T + t] = fminf(fmaxf(acc, -1.0f), 1.0f);
+}
+
+}  // namespace
+}  // namespace lai
+
+extern "C" int lai_voc_conv1d_f32(float *out, const float *x, float *scratch, const float *w,
+                                  const float *bias, int batch, int c_in, int c_out, int T,
+                                  int kernel, int dilation, int passes, int *err,
+                                  lai_stream_t stream) {
+    using namespace lai;
+    if (!out || !x || !scratch || !w || !bias || batch < 0 || T < 0 || kernel <= 0 ||
+        dilation <= 0 || (passes != 1 && passes != 3))
+        return LAI_ERR_INVALID;
+    if (batch == 0 || T == 0) return LAI_OK;
+    if (c_in % 32 != 0 || c_out % 32 != 0 || !aligned16(out) || !aligned16(x) ||
+        !aligned16(scratch) || !aligned16(w) || (int64_t)(kernel - 1) * dilation > (1 << 30))
+        return LAI_ERR_INVALID;
+    if (batch > 65535) return LAI_ERR_RANGE;
+    const size_t in_plane = (size_t)batch * T * c_in, out_plane = (size_t)batch * T * c_out;
+    if (overlaps(out, out_plane * 4, x, in_plane * 4) ||
+        overlaps(out, out_plane * 4, scratch, 2 * in_plane * 4) ||
+        overlaps(x, in_plane * 4, scratch, 2 * in_plane * 4))
+        return LAI_ERR_ALIAS;
+    if (!encode_fn()) return LAI_ERR_CUDA;
+    const cudaStream_t st = as_stream(stream);
+    int rc = launch_split(x, scratch, scratch + in_plane, in_plane, passes, st);
+    if (rc != LAI_OK) return rc;
+    CUtensorMap am, wm;
+    if (!act_map(&am, scratch, batch, T, c_in) ||
+        !weight_map(&wm, w, kernel, c_out, c_in, pick_bn(c_out)))
+        return LAI_ERR_INVALID;
+    const ConvArgs a{nullptr, nullptr, out, bias, nullptr, nullptr, nullptr,
+                     T, c_in, c_out, kernel, dilation, err, 1, T, 0};
+    return launch_conv<kEpiStoreSnake>(passes, am, wm, a, batch, st);
+}
+
+extern "C" int lai_voc_conv_transpose1d_f32(float *out, const float *x, float *scratch,
+                                            const float *w, const float *bias, int batch,
+                                            int c_in, int c_out, int T, int kernel, int stride,
+                                            int passes, int *err, lai_stream_t stream) {
+    using namespace lai;
+    if (!out || !x || !scratch || !w || !bias || batch < 0 || T < 0 || stride <= 0 ||
+        (kernel != stride && kernel != 2 * stride) || (passes != 1 && passes != 3))
+        return LAI_ERR_INVALID;
+    if (batch == 0 || T == 0) return LAI_OK;
+    const int taps = kernel / stride, trim = taps - 1;
+    const int T_out = (T + 1) * stride - kernel;
+    if (T_out <= 0) return LAI_ERR_INVALID;
+    if (c_in % 32 != 0 || c_out % 32 != 0 || !aligned16(out) || !aligned16(x) ||
+        !aligned16(scratch) || !aligned16(w))
+        return LAI_ERR_INVALID;
+    if ((int64_t)batch * stride > 65535) return LAI_ERR_RANGE;
+    const size_t in_plane = (size_t)batch * T * c_in, out_plane = (size_t)batch * T_out * c_out;
+    if (overlaps(out, out_plane * 4, x, in_plane * 4) ||
+        overlaps(out, out_plane * 4, scratch, 2 * in_plane * 4) ||
+        overlaps(x, in_plane * 4, scratch, 2 * in_plane * 4))
+        return LAI_ERR_ALIAS;
+    if (!encode_fn()) return LAI_ERR_CUDA;
+    const cudaStream_t st = as_stream(stream);
+    int rc = launch_split(x, scratch, scratch + in_plane, in_plane, passes, st);
+    if (rc != LAI_OK) return rc;
+    CUtensorMap am, wm;
+    if (!act_map(&am, scratch, batch, T, c_in) ||
+        !weight_map(&wm, w, kernel, c_out, c_in, pick_bn(c_out)))
+        return LAI_ERR_INVALID;
+    const ConvArgs a{nullptr, nullptr, out, bias, nullptr, nullptr, nullptr,
+                     T, c_in, c_out, taps, 1, err, stride, T_out, trim};
+    return launch_conv<kEpiStoreSnake>(passes, am, wm, a, batch, st);
+}
+
+extern "C" int lai_voc_final_f32(float *audio, const float *x, const float *exp_alpha,
+                                 const float *inv_exp_beta, const float *w, const float *bias,
+                                 int batch, int channels, int T, lai_stream_t stream) {
+    using namespace lai;
+    if (!audio || !x || !exp_alpha || !inv_exp_beta || !w || !bias || batch < 0 || T < 0 ||
+        channels <= 0 || channels > 1024)
+        return LAI_ERR_INVALID;
+    if (batch == 0 || T == 0) return LAI_OK;
+    if (batch > 65535) return LAI_ERR_RANGE;
+    if (overlaps(audio, (size_t)batch * T * 4, x, (size_t)batch * T * channels * 4))
+        return LAI_ERR_ALIAS;
+    const size_t smem = ((size_t)(kFinalRows + 6) * (channels + 1) + 7 * channels) * sizeof(float);
+    if (smem > 200 * 1024) return LAI_ERR_TOOBIG;
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(final_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+        return LAI_ERR_CUDA;
+    const dim3 grid((unsigned)((T + kFinalRows - 1) / kFinalRows), (unsigned)batch);
+    final_kernel<<<grid, kFinalRows, smem, as_stream(stream)>>>(audio, x, exp_alpha, inv_exp_beta,
+                                                                 w, bias, T, channels);
+    return launch_status();
+}

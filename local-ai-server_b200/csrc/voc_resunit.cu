@@ -165,19 +165,21 @@ int run_resunits(float *x, float *scratch, const lai_voc_resunit_t *units, int n
     return rc;
 }
 
-// Reference transposed-conv weight [c_in, c_out, 2r] -> [2][r][2][c_out][c_in]: part (hi,
-// lo), phase f, tap (0: W[.., r + f] applied to x[t - 1]; 1: W[.., f] applied to x[t]).
+// Reference transposed-conv weight [c_in, c_out, kernel] -> [2][stride][taps][c_out][c_in],
+// taps = kernel / stride: part (hi, lo), phase f, tap. kernel 2r: tap 0 = W[.., r + f]
+// (applied to x[t - 1]), tap 1 = W[.., f] (applied to x[t]); kernel r: tap 0 = W[.., f].
 __global__ void pack_tconv_kernel(float *dst, const float *__restrict__ w, int c_in, int c_out,
-                                  int rate) {
-    const int64_t per_part = (int64_t)rate * 2 * c_out * c_in;
+                                  int kernel, int stride) {
+    const int taps = kernel / stride;
+    const int64_t per_part = (int64_t)kernel * c_out * c_in;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < per_part;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t oc = i % ((int64_t)c_out * c_in);  // o * c_in + c
-        const int64_t pk = i / ((int64_t)c_out * c_in);  // phase * 2 + tap
-        const int f = (int)(pk / 2), tap = (int)(pk % 2);
+        const int64_t pk = i / ((int64_t)c_out * c_in);  // phase * taps + tap
+        const int f = (int)(pk / taps), tap = (int)(pk % taps);
         const int64_t o = oc / c_in, c = oc % c_in;
-        const int ki = tap == 0 ? rate + f : f;
-        const float v = w[(c * c_out + o) * 2 * rate + ki];
+        const int ki = taps == 2 && tap == 0 ? stride + f : f;
+        const float v = w[(c * c_out + o) * kernel + ki];
         const float h = umma::tf32_round(v);
         dst[i] = h;
         dst[per_part + i] = v - h;
@@ -205,14 +207,17 @@ extern "C" int lai_voc_resunits_f32(float *x, float *scratch, const lai_voc_resu
                         as_stream(stream), false);
 }
 
-extern "C" int lai_voc_pack_tconv_f32(float *dst, const float *w, int c_in, int c_out, int rate,
-                                      lai_stream_t stream) {
-    if (!dst || !w || c_in <= 0 || c_out <= 0 || rate <= 0) return LAI_ERR_INVALID;
-    const size_t n = (size_t)c_in * c_out * 2 * rate;
+extern "C" int lai_voc_pack_tconv_f32(float *dst, const float *w, int c_in, int c_out, int kernel,
+                                      int stride, lai_stream_t stream) {
+    if (!dst || !w || c_in <= 0 || c_out <= 0 || stride <= 0 ||
+        (kernel != stride && kernel != 2 * stride))
+        return LAI_ERR_INVALID;
+    const size_t n = (size_t)c_in * c_out * kernel;
     if (lai::overlaps(dst, 2 * n * sizeof(float), w, n * sizeof(float))) return LAI_ERR_ALIAS;
     const unsigned grid = lai::grid_for((int64_t)n, 256) < 148u * 8 ? lai::grid_for((int64_t)n, 256)
                                                                    : 148u * 8;
-    lai::pack_tconv_kernel<<<grid, 256, 0, lai::as_stream(stream)>>>(dst, w, c_in, c_out, rate);
+    lai::pack_tconv_kernel<<<grid, 256, 0, lai::as_stream(stream)>>>(dst, w, c_in, c_out, kernel,
+                                                                     stride);
     return lai::launch_status();
 }
 
@@ -255,7 +260,7 @@ extern "C" int lai_voc_bigvgan_block_f32(float *out, const float *x, float *scra
     const ConvArgs a{fuse ? rs : nullptr, fuse ? rs + out_plane : nullptr, out, blk->tconv_b,
                      fuse ? blk->units[0].snake1_ea : nullptr,
                      fuse ? blk->units[0].snake1_ieb : nullptr, nullptr, T, c_in, c_out, 2, 1,
-                     err, r, T_out};
+                     err, r, T_out, 1};
     rc = launch_conv<kEpiStoreSnake>(passes, in_map, w_map, a, batch, st);
     if (rc != LAI_OK || !fuse) return rc;
     return run_resunits(out, rs, blk->units, blk->n_units, batch, c_out, T_out, passes, err, st,

@@ -53,7 +53,12 @@ SIGNATURES: dict[str, tuple] = {
                                    _vp]),
     "lai_voc_bigvgan_block_f32": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp,
                                          _vp]),
-    "lai_voc_pack_tconv_f32": (_i32, [_vp, _vp, _i32, _i32, _i32, _vp]),
+    "lai_voc_pack_tconv_f32": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp]),
+    "lai_voc_conv1d_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32,
+                                  _i32, _vp, _vp]),
+    "lai_voc_conv_transpose1d_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32,
+                                            _i32, _i32, _i32, _vp, _vp]),
+    "lai_voc_final_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     "lai_voc_convnext_f32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp]),
     "lai_voc_resunits_f32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
     "lai_voc_pack_conv_f32": (_i32, [_vp, _vp, _i32, _i32, _i32, _vp]),
@@ -306,12 +311,14 @@ class VocBigVGANBlock(ctypes.Structure):
                 ("rate", _i32), ("n_units", _i32), ("units", _vp)]
 
 
-def voc_pack_tconv(w, rate, stream=None):
-    """Reference transposed-conv weight [c_in, c_out, 2 rate] -> packed [2, rate, 2, c_out, c_in]."""
+def voc_pack_tconv(w, stride, stream=None):
+    """Reference transposed-conv weight [c_in, c_out, kernel] (kernel = stride or 2 stride) ->
+    packed [2, stride, kernel / stride, c_out, c_in]."""
     import torch
-    c_in, c_out, _ = w.shape
-    dst = torch.empty((2, rate, 2, c_out, c_in), dtype=torch.float32, device=w.device)
-    call("lai_voc_pack_tconv_f32", _p(dst), _p(w), c_in, c_out, rate, _s(stream))
+    c_in, c_out, kernel = w.shape
+    dst = torch.empty((2, stride, kernel // stride, c_out, c_in), dtype=torch.float32,
+                      device=w.device)
+    call("lai_voc_pack_tconv_f32", _p(dst), _p(w), c_in, c_out, kernel, stride, _s(stream))
     return dst
 
 
@@ -338,6 +345,41 @@ def voc_bigvgan_block(x, params, c_out, scratch=None, passes=3, err=None, stream
                               device=x.device)
     call("lai_voc_bigvgan_block_f32", _p(out), _p(x), _p(scratch), ctypes.byref(st), b, c_in,
          c_out, t, passes, _p(err), _s(stream))
+    return out
+
+
+def voc_conv1d(x, w_packed, bias, c_out, kernel, dilation=1, scratch=None, passes=3, err=None,
+               stream=None):
+    """Causal conv on x [batch, T, c_in] -> new [batch, T, c_out]; w_packed from voc_pack_conv."""
+    import torch
+    b, t, c_in = x.shape
+    out = torch.empty((b, t, c_out), dtype=torch.float32, device=x.device)
+    if scratch is None:
+        scratch = torch.empty(2 * b * t * c_in, dtype=torch.float32, device=x.device)
+    call("lai_voc_conv1d_f32", _p(out), _p(x), _p(scratch), _p(w_packed), _p(bias), b, c_in, c_out,
+         t, kernel, dilation, passes, _p(err), _s(stream))
+    return out
+
+
+def voc_conv_transpose1d(x, w_packed, bias, c_out, kernel, stride, scratch=None, passes=3,
+                         err=None, stream=None):
+    """Transposed conv on x [batch, T, c_in] -> new [batch, (T + 1) stride - kernel, c_out]."""
+    import torch
+    b, t, c_in = x.shape
+    out = torch.empty((b, (t + 1) * stride - kernel, c_out), dtype=torch.float32, device=x.device)
+    if scratch is None:
+        scratch = torch.empty(2 * b * t * c_in, dtype=torch.float32, device=x.device)
+    call("lai_voc_conv_transpose1d_f32", _p(out), _p(x), _p(scratch), _p(w_packed), _p(bias), b,
+         c_in, c_out, t, kernel, stride, passes, _p(err), _s(stream))
+    return out
+
+
+def voc_final(x, ea, ieb, w, bias, out=None, stream=None):
+    """SnakeBeta -> conv C -> 1 (k = 7) -> clamp on x [batch, T, C]; returns audio [batch, T]."""
+    import torch
+    b, t, c = x.shape
+    out = torch.empty((b, t), dtype=torch.float32, device=x.device) if out is None else out
+    call("lai_voc_final_f32", _p(out), _p(x), _p(ea), _p(ieb), _p(w), _p(bias), b, c, t, _s(stream))
     return out
 
 

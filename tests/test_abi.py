@@ -88,7 +88,12 @@ P = V(16)  # a non-NULL dummy pointer: never dereferenced, the checks fail first
     (lambda l: l.lai_voc_bigvgan_block_f32(P, P, P, None, 1, 64, 32, 10, 3, None, None),
      lai.LAI_ERR_INVALID),
     (lambda l: l.lai_voc_pack_conv_f32(P, None, 8, 8, 7, None), lai.LAI_ERR_INVALID),
-    (lambda l: l.lai_voc_pack_tconv_f32(P, P, 8, 8, 0, None), lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_voc_pack_tconv_f32(P, P, 8, 8, 3, 2, None), lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_voc_conv1d_f32(P, P, P, P, P, 1, 48, 64, 10, 7, 1, 3, None, None),
+     lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_voc_conv_transpose1d_f32(P, P, P, P, P, 1, 64, 64, 10, 3, 2, 3, None, None),
+     lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_voc_final_f32(P, P, P, P, P, None, 1, 96, 100, None), lai.LAI_ERR_INVALID),
     (lambda l: l.lai_voc_transpose_f32(V(4096), V(4096 + 8), 1, 4, 4, None), lai.LAI_ERR_ALIAS),
     # decode GEMVs: output overlapping input; K beyond the staged maximum
     (lambda l: l.lai_gemv_bf16w_f32(V(256), V(256), None, 1e-6, P, 1, 64, 8, None),
