@@ -615,13 +615,17 @@ def cpu_convnext_rate(stages, batch: int, min_seconds: float, sample_t: int = 50
 
 
 def cpu_decoder_rate(t0: int, batch: int, min_seconds: float, t0_sample: int = 40,
-                     steps: int | None = None, warmup: int = 1) -> dict:
+                     steps: int | None = None, warmup: int = 1, full: bool = False) -> dict:
     """The BigVGAN decoder's 4 blocks on host cores as the reference's USE_BLAS build runs
     them (src/tts_vocoder.c:709-728): its own compiled AVX2 voc_snake_beta over channel
     ranges on a thread pool; voc_conv_transpose1d as its SGEMM + col2im formulation
     (src/tts_vocoder_ops.c:169-194) and the ResUnits as in cpu_resunit_rate, the SGEMMs
     through numpy's OpenBLAS on all host cores. Runs from t0_sample input rows; every op is
-    linear in T, so the step time is scaled by t0 / t0_sample. Returns audio samples/s."""
+    linear in T, so the step time is scaled by t0 / t0_sample. Returns audio samples/s.
+    full: start from the pre-transformer's output [1024, t0 / 4] instead - 2 upsample stages
+    (transposed conv k = s = 2 as SGEMM + col2im, ConvNeXt as cpu_convnext_rate runs it),
+    the init conv 1024 -> 1536 (per-tap SGEMMs), then the blocks, then the final SnakeBeta ->
+    conv 96 -> 1 -> clamp (the reference's compiled voc_snake_beta and voc_conv1d_causal)."""
     import concurrent.futures as cf
 
     import numpy as np
@@ -650,6 +654,21 @@ def cpu_decoder_rate(t0: int, batch: int, min_seconds: float, t0_sample: int = 4
                        "b": f(rng.normal(0, .01, (c_out, 1))), "r": r, "c_out": c_out,
                        "units": units})
     x0 = f(rng.standard_normal((runner.BIGVGAN_CHANNELS[0], t0_sample)))
+    ref = oracle.load("libvoc_ref_avx2.so")
+    Pt = oracle.ptr
+    if full:
+        C = 1024
+        x0 = f(rng.standard_normal((C, t0_sample // 4)))
+        ups = [{"wt": f((rng.standard_normal((C, C * 2)) / np.sqrt(C)).T), "b": f(rng.normal(0, .01, (C, 1))),
+                "dw_w": f(rng.standard_normal((C, 1, 7)) / np.sqrt(7)), "dw_b": f(rng.normal(0, .01, C)),
+                "nw": f(1 + rng.normal(0, .1, C)), "nb": f(rng.normal(0, .1, C)),
+                "w1": f(rng.standard_normal((4 * C, C)) / np.sqrt(C)), "b1": f(rng.normal(0, .01, (4 * C, 1))),
+                "w2": f(rng.standard_normal((C, 4 * C)) / np.sqrt(4 * C)), "b2": f(rng.normal(0, .01, (C, 1))),
+                "g": f(rng.normal(0, .1, (C, 1)))} for _ in range(2)]
+        init_taps = [f(rng.standard_normal((1536, C)) / np.sqrt(7 * C)) for _ in range(7)]
+        init_b = f(rng.normal(0, .01, (1536, 1)))
+        fin = {"ea": f(np.exp(rng.normal(0, .1, 96))), "ieb": f(np.exp(-rng.normal(0, .1, 96))),
+               "w": f(rng.standard_normal((1, 96, 7)) / np.sqrt(672)), "b": f(rng.normal(0, .01, 1))}
 
     with cf.ThreadPoolExecutor(nthreads) as pool, threadpool_limits(nthreads):
         def snake_mt(x, ea, ieb):
@@ -659,8 +678,46 @@ def cpu_decoder_rate(t0: int, batch: int, min_seconds: float, t0_sample: int = 4
                                            ieb[c0:].ctypes.data_as(F), min(per, c - c0), t),
                           range(0, c, per)))
 
+        def front(x):
+            for u in ups:  # transposed conv k = s = 2 (no overlap), then ConvNeXt
+                t = x.shape[1]
+                cols = (u["wt"] @ x).reshape(1024, 2, t)
+                y = np.empty((1024, 2 * t), np.float32)
+                y[:, 0::2], y[:, 1::2] = cols[:, 0, :], cols[:, 1, :]
+                y += u["b"]
+                dw = np.empty_like(y)
+                scr = np.empty(1024 * (2 * t + 6) + 16, np.float32)
+                ref.voc_conv1d_causal(Pt(dw), Pt(y), Pt(u["dw_w"]), Pt(u["dw_b"]), 1024, 1024, 2 * t,
+                                      7, 1, 1024, Pt(scr))
+                ref.voc_layer_norm_channels(Pt(dw), Pt(u["nw"]), Pt(u["nb"]), 1024, 2 * t, 1e-6)
+                h = u["w1"] @ dw
+                h += u["b1"]
+                ref.voc_gelu(Pt(h), h.size)
+                z = u["w2"] @ h
+                z += u["b2"]
+                z *= u["g"]
+                x = y + z
+            t = x.shape[1]
+            pad = np.zeros((1024, t + 6), np.float32)
+            pad[:, 6:] = x
+            out = init_taps[0] @ pad[:, :t]
+            for k in range(1, 7):
+                out += init_taps[k] @ pad[:, k:k + t]
+            out += init_b
+            return out
+
+        def final(x):
+            snake_mt(x, fin["ea"], fin["ieb"])
+            t = x.shape[1]
+            y = np.empty((1, t), np.float32)
+            scr = np.empty(96 * (t + 6) + 96 * 7 * t, np.float32)
+            ref.voc_conv1d_causal(Pt(y), Pt(x), Pt(fin["w"]), Pt(fin["b"]), 96, 1, t, 7, 1, 1,
+                                  Pt(scr))
+            np.clip(y, -1.0, 1.0, out=y)
+            return y
+
         def decoder():
-            x = x0.copy()
+            x = front(x0.copy()) if full else x0.copy()
             for blk in blocks:
                 snake_mt(x, blk["ea"], blk["ieb"])
                 r, c_out, t = blk["r"], blk["c_out"], x.shape[1]
@@ -687,7 +744,7 @@ def cpu_decoder_rate(t0: int, batch: int, min_seconds: float, t0_sample: int = 4
                     x = u["w2"] @ h
                     x += u["b2"]
                     x += res
-            return x
+            return final(x) if full else x
 
         for _ in range(warmup):
             decoder()
@@ -776,7 +833,7 @@ def run_single(args) -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     seed = args.seed + 1000 * rank
-    tensor = args.config in ("n1", "v2")
+    tensor = args.config in ("n1", "v2", "v3")
     tf32 = tf32_peak_tflops() if tensor else None
     if args.config == "a3":
         work = runner.DecodeAttention(seqs=args.rows or 256, seed=seed)
@@ -785,6 +842,8 @@ def run_single(args) -> None:
                                   passes=args.passes, seed=seed)
     elif args.config == "v2":
         work = runner.VocDecoder(t0=2000 // args.t_div, passes=args.passes, seed=seed)
+    elif args.config == "v3":
+        work = runner.VocFullDecoder(t_frames=500 // args.t_div, passes=args.passes, seed=seed)
     else:
         work = runner.SampleBatch(seed=seed)
     launches = work.launches(None)
@@ -859,6 +918,11 @@ def run_single(args) -> None:
             outs = [(pin(work.outs[-1]), work.outs[-1])]
             api = ("lai_voc_bigvgan_block_f32 x 4 with the decoder input copied in from and the "
                    "audio-rate output back to pinned host memory each step")
+        elif args.config == "v3":
+            ins = [(work.x_in, pin(work.x_in))]
+            outs = [(pin(work.audio), work.audio)]
+            api = ("the 10 vocoder-decoder calls with the pre-transformer output copied in from and "
+                   "the audio copied back to pinned host memory each step")
         elif args.config == "n1":
             ins = [(x, pin(x)) for x in work.x]
             outs = [(pin(x), x) for x in work.x]
@@ -891,6 +955,15 @@ def run_single(args) -> None:
                              f"scaled to t0 = {work.t0}: the reference's USE_BLAS path (its AVX2 "
                              "voc_snake_beta, transposed conv as SGEMM + col2im, ResUnits as "
                              f"SGEMMs through numpy's OpenBLAS), host {cpu_model()}"}
+        elif args.config == "v3":
+            r = cpu_decoder_rate(work.t_dec, work.batch, args.cpu_seconds, full=True)
+            cpu = {"value": round(r["rows_per_s"], 1), "unit": "rows/s", "cores": r["threads"],
+                   "kind": "port",
+                   "sample": f"{r['passes']} runs of the whole path from {r['t0_sample'] // 4} "
+                             f"frames ({r['samples_sample']} samples, {r['seconds']:.1f} s), "
+                             f"scaled to {work.t_frames} frames: the reference's USE_BLAS path "
+                             "(its compiled SnakeBeta, depthwise conv, LayerNorm, GELU and final "
+                             f"conv + OpenBLAS SGEMMs), host {cpu_model()}"}
         elif args.config == "n1":
             r = cpu_convnext_rate(work.stages, work.batch, args.cpu_seconds)
             cpu = {"value": round(r["rows_per_s"], 1), "unit": "rows/s", "cores": r["threads"],
@@ -930,6 +1003,12 @@ def run_single(args) -> None:
                "t0": getattr(work, "t0", None), "batch": getattr(work, "batch", None),
                "stages": getattr(work, "shapes", None), "passes": args.passes,
                "rows": "audio samples (24 kHz) out of the last block per step"},
+        "v3": {"workload": "tts_vocoder_run from the pre-transformer output to audio: 2 x "
+                           "(transposed conv + ConvNeXt), init conv, 4 BigVGAN blocks, final "
+                           "SnakeBeta + conv + clamp; FP32 channels-last on tcgen05",
+               "frames": getattr(work, "t_frames", None), "batch": getattr(work, "batch", None),
+               "audio_samples": getattr(work, "t_final", None), "passes": args.passes,
+               "rows": "audio samples (24 kHz) per step"},
         "s3": {"workload": "talker token sampling: repetition penalty + top-k 50 at temperature "
                            "0.9 over codec logits (vocab 3072), 64-token histories",
                "rows": "decode rows (one token drawn each)", "batch": getattr(work, "rows", None)},
@@ -944,7 +1023,8 @@ def run_single(args) -> None:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded counter-based N(0,1) on device)", "config": desc,
         "per_kernel": per_kernel, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-        "gpu_launches": args.steps * len(launches) * {"n1": 3, "v2": 8}.get(args.config, 1),
+        "gpu_launches": args.steps * {"n1": 3 * len(launches), "v2": 8 * len(launches),
+                                      "v3": 2 + 2 * 3 + 2 + 4 * 8 + 1}.get(args.config, len(launches)),
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
@@ -1497,8 +1577,8 @@ def main():
                     help="timed steps (default 2000; 20 for v1, whose step is ~0.1 s)")
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "g1", "g2", "v1", "v2", "a3",
-                                         "n1", "s3"],
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "g1", "g2", "v1", "v2", "v3",
+                                         "a3", "n1", "s3"],
                     default="c2")
     ap.add_argument("--t-div", type=int, default=1,
                     help="v1: divide every stage's length (small profiling cases)")
@@ -1527,12 +1607,12 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)  # timing rule: at least 3 untimed warm-up steps
     if args.steps is None:
-        args.steps = {"v1": 20, "v2": 20, "n1": 50, "a3": 200}.get(args.config, 2000)
+        args.steps = {"v1": 20, "v2": 20, "v3": 20, "n1": 50, "a3": 200}.get(args.config, 2000)
     if args.impl == "reference":
         run_reference(args)
     elif args.config == "v1":
         run_resunits(args)
-    elif args.config in ("a3", "n1", "s3", "v2"):
+    elif args.config in ("a3", "n1", "s3", "v2", "v3"):
         run_single(args)
     else:
         run_ours(args)

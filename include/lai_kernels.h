@@ -279,7 +279,7 @@ LAI_API int lai_voc_pack_tconv_f32(float *dst, const float *w, int c_in, int c_o
  *   2 * batch * T * c_in floats.
  * lai_voc_final_f32: the decoder's last step (src/tts_vocoder.c:748-758): voc_snake_beta over
  *   x [batch, T, channels], conv1d channels -> 1 (k = 7, w [1, channels, 7] as loaded, bias [1]),
- *   clamp to [-1, 1]; audio [batch, T]. channels <= ~190 (shared-memory window).
+ *   clamp to [-1, 1]; audio [batch, T]. channels in {32, 64, 96, 128} (the reference: 96).
  * c_in, c_out multiples of 32; passes as for the ResUnits.
  */
 LAI_API int lai_voc_conv1d_f32(float *out, const float *x, float *scratch, const float *w,

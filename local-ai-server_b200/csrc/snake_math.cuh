@@ -42,15 +42,20 @@ __device__ __forceinline__ float sin2_fast(float y) {
     return fmaf(-0.5f, c, 0.5f);                // (1 - cos 2y) / 2
 }
 
+// Huge or non-finite arguments: CUDA's full-range sinf. Kept out of line so the kernels that
+// apply SnakeBeta many times per thread do not inline its long, never-taken reduction path.
+static __device__ __noinline__ float sin2_full_range(float y) {
+    const float s = sinf(y);
+    return s * s;
+}
+
 __device__ __forceinline__ float snake1(float x, float ea, float ieb) {
     const float y = __fmul_rn(ea, x);
     float s2;
-    if (fabsf(y) <= 65536.0f) {
+    if (fabsf(y) <= 65536.0f)
         s2 = sin2_fast(y);
-    } else {  // huge or non-finite argument: full-range sinf
-        const float s = sinf(y);
-        s2 = s * s;
-    }
+    else
+        s2 = sin2_full_range(y);
     return fmaf(ieb, s2, x);  // x + ieb * sin^2(ea * x)
 }
 

@@ -41,43 +41,86 @@ int launch_split(const float *x, float *hi, float *lo, size_t n, int passes, cud
 
 // Final step: one CTA writes kFinalRows consecutive samples of one item. It stages input rows
 // [t0 - 6, t0 + kFinalRows) of x [T, C] through SnakeBeta into shared memory (zero before
-// t = 0; rows padded to C + 1 floats so the per-thread row reads hit distinct banks), then
-// each thread sums its sample's 7 x C window and clamps.
+// t = 0; rows padded to C + 1 floats so the per-thread row reads hit distinct banks), loading
+// float4 vectors eight per thread at a time so enough bytes are in flight to cover HBM
+// latency, then each thread sums its sample's 7 x C window and clamps.
 constexpr int kFinalRows = 256;
+constexpr int kFinalBatch = 8;  // float4 loads in flight per thread while staging
 
+template <int C>
 __global__ void __launch_bounds__(kFinalRows)
 final_kernel(float *audio, const float *__restrict__ x, const float *__restrict__ ea,
              const float *__restrict__ ieb, const float *__restrict__ w,
-             const float *__restrict__ bias, int T, int C) {
+             const float *__restrict__ bias, int T) {
+    constexpr int pitch = C + 1;
+    constexpr int V = C / 4;                       // float4 vectors per row
+    constexpr int NV = (kFinalRows + 6) * V;
     extern __shared__ float sm[];
-    const int pitch = C + 1;
-    float *s = sm;                                   // [kFinalRows + 6][C + 1]
-    float *wt = sm + (size_t)(kFinalRows + 6) * pitch;  // [7][C]: tap-major weights
+    float *s = sm;                                 // [kFinalRows + 6][C + 1]
+    float *wt = s + (kFinalRows + 6) * pitch;      // [7][C]: tap-major weights
+    float *sa = wt + 7 * C, *sb = sa + C;          // snake parameters
     const int b = blockIdx.y, t0 = blockIdx.x * kFinalRows;
     const float *xb = x + (size_t)b * T * C;
     for (int i = threadIdx.x; i < 7 * C; i += kFinalRows) {
         const int c = i / 7, k = i - c * 7;
         wt[k * C + c] = w[i];  // w [1, C, 7] as loaded
     }
-    const int n = (kFinalRows + 6) * C;
-    for (int i = threadIdx.x; i < n; i += kFinalRows) {
-        const int r = i / C, c = i - r * C;
-        const int t = t0 - 6 + r;
-        s[r * pitch + c] = (t >= 0 && t < T) ? snake1(xb[(size_t)t * C + c], __ldg(ea + c),
-                                                      __ldg(ieb + c))
-                                             : 0.0f;
+    for (int i = threadIdx.x; i < C; i += kFinalRows) {
+        sa[i] = ea[i];
+        sb[i] = ieb[i];
+    }
+    __syncthreads();
+    for (int base = threadIdx.x; base < NV; base += kFinalRows * kFinalBatch) {
+        float4 v[kFinalBatch];
+#pragma unroll
+        for (int u = 0; u < kFinalBatch; u++) {
+            const int i = base + u * kFinalRows;
+            const int r = i / V, c4 = i - r * V, t = t0 - 6 + r;
+            v[u] = (i < NV && t >= 0 && t < T)
+                       ? *reinterpret_cast<const float4 *>(xb + (size_t)t * C + 4 * c4)
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < kFinalBatch; u++) {
+            const int i = base + u * kFinalRows;
+            if (i < NV) {
+                const int r = i / V, c = 4 * (i - r * V), t = t0 - 6 + r;
+                const bool in = t >= 0 && t < T;
+                float *dst = s + r * pitch + c;
+                dst[0] = in ? snake1(v[u].x, sa[c], sb[c]) : 0.f;
+                dst[1] = in ? snake1(v[u].y, sa[c + 1], sb[c + 1]) : 0.f;
+                dst[2] = in ? snake1(v[u].z, sa[c + 2], sb[c + 2]) : 0.f;
+                dst[3] = in ? snake1(v[u].w, sa[c + 3], sb[c + 3]) : 0.f;
+            }
+        }
     }
     __syncthreads();
     const int t = t0 + threadIdx.x;
     if (t >= T) return;
     float acc = 0.0f;
+#pragma unroll
     for (int k = 0; k < 7; k++) {
         const float *row = s + (threadIdx.x + k) * pitch;
         const float *wk = wt + k * C;
+#pragma unroll 8
         for (int c = 0; c < C; c++) acc = fmaf(wk[c], row[c], acc);
     }
     acc += __ldg(bias);
     audio[(size_t)b * T + t] = fminf(fmaxf(acc, -1.0f), 1.0f);
+}
+
+template <int C>
+int launch_final(float *audio, const float *x, const float *ea, const float *ieb, const float *w,
+                 const float *bias, int batch, int T, cudaStream_t st) {
+    const size_t smem = ((size_t)(kFinalRows + 6) * (C + 1) + 9 * C) * sizeof(float);
+    auto kern = final_kernel<C>;
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+        return LAI_ERR_CUDA;
+    const dim3 grid((unsigned)((T + kFinalRows - 1) / kFinalRows), (unsigned)batch);
+    kern<<<grid, kFinalRows, smem, st>>>(audio, x, ea, ieb, w, bias, T);
+    return launch_status();
 }
 
 }  // namespace
@@ -153,20 +196,19 @@ extern "C" int lai_voc_final_f32(float *audio, const float *x, const float *exp_
                                  int batch, int channels, int T, lai_stream_t stream) {
     using namespace lai;
     if (!audio || !x || !exp_alpha || !inv_exp_beta || !w || !bias || batch < 0 || T < 0 ||
-        channels <= 0 || channels > 1024)
+        channels <= 0)
         return LAI_ERR_INVALID;
     if (batch == 0 || T == 0) return LAI_OK;
     if (batch > 65535) return LAI_ERR_RANGE;
     if (overlaps(audio, (size_t)batch * T * 4, x, (size_t)batch * T * channels * 4))
         return LAI_ERR_ALIAS;
-    const size_t smem = ((size_t)(kFinalRows + 6) * (channels + 1) + 7 * channels) * sizeof(float);
-    if (smem > 200 * 1024) return LAI_ERR_TOOBIG;
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(final_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) != cudaSuccess)
-        return LAI_ERR_CUDA;
-    const dim3 grid((unsigned)((T + kFinalRows - 1) / kFinalRows), (unsigned)batch);
-    final_kernel<<<grid, kFinalRows, smem, as_stream(stream)>>>(audio, x, exp_alpha, inv_exp_beta,
-                                                                 w, bias, T, channels);
-    return launch_status();
+    if (!aligned16(x)) return LAI_ERR_INVALID;
+    const cudaStream_t st = as_stream(stream);
+    switch (channels) {
+        case 32: return launch_final<32>(audio, x, exp_alpha, inv_exp_beta, w, bias, batch, T, st);
+        case 64: return launch_final<64>(audio, x, exp_alpha, inv_exp_beta, w, bias, batch, T, st);
+        case 96: return launch_final<96>(audio, x, exp_alpha, inv_exp_beta, w, bias, batch, T, st);
+        case 128: return launch_final<128>(audio, x, exp_alpha, inv_exp_beta, w, bias, batch, T, st);
+        default: return LAI_ERR_INVALID;
+    }
 }

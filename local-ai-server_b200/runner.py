@@ -295,7 +295,7 @@ class VocDecoder:
     transposed convs N(0,1)/sqrt(2 c_in), ResUnits as VocResUnits."""
 
     def __init__(self, t0: int = 2000, batch: int = 1, passes: int = 3, seed: int = 77,
-                 device="cuda"):
+                 device="cuda", x0=None):
         import torch
         self.t0, self.batch, self.passes = t0, batch, passes
         k = 0
@@ -307,7 +307,7 @@ class VocDecoder:
             k += 1
             return t
 
-        self.x0 = normal((batch, t0, BIGVGAN_CHANNELS[0]))
+        self.x0 = normal((batch, t0, BIGVGAN_CHANNELS[0])) if x0 is None else x0
         self.blocks, self.outs, self.shapes = [], [], []
         t = t0
         scratch = 0
@@ -361,6 +361,114 @@ class VocDecoder:
 
     def rows_per_launch(self) -> list[int]:
         return [self.batch * t_out for _, _, _, t_out, _ in self.shapes]
+
+
+class VocFullDecoder:
+    """tts_vocoder_run from the pre-transformer's output to audio (config v3,
+    src/tts_vocoder.c:658-758): 2 ConvNeXt upsample stages (transposed conv 1024 -> 1024,
+    kernel = stride = 2, then the ConvNeXt block), the BigVGAN init conv 1024 -> 1536 (k=7),
+    the 4 BigVGAN blocks (VocDecoder) and the final SnakeBeta -> conv 96 -> 1 -> clamp, for
+    t_frames = 500 codec frames (40 s of audio): 1024 x 500 in, 959445 samples out, batch 1.
+    Every step recomputes from the same input."""
+
+    def __init__(self, t_frames: int = 500, batch: int = 1, passes: int = 3, seed: int = 88,
+                 device="cuda"):
+        import torch
+        self.batch, self.passes, self.t_frames = batch, passes, t_frames
+        k = 0
+
+        def normal(shape, std=1.0, mean=0.0):
+            nonlocal k
+            t = torch.empty(shape, dtype=torch.float32, device=device)
+            lai.synth_normal(t, seed=seed + k, mean=mean, std=std)
+            k += 1
+            return t
+
+        C = 1024
+        self.x_in = normal((batch, t_frames, C))
+        self.ups = []
+        t = t_frames
+        for _ in range(2):
+            self.ups.append({"w": lai.voc_pack_tconv(normal((C, C, 2), C ** -0.5), 2),
+                             "b": normal(C, 0.01),
+                             "cn": lai.voc_convnext_params({
+                                 "dw_w": normal((C, 1, 7), 7 ** -0.5), "dw_b": normal(C, 0.01),
+                                 "norm_w": normal(C, 0.1, 1.0), "norm_b": normal(C, 0.1),
+                                 "pw1_w": normal((4 * C, C, 1), C ** -0.5),
+                                 "pw1_b": normal(4 * C, 0.01),
+                                 "pw2_w": normal((C, 4 * C, 1), (4 * C) ** -0.5),
+                                 "pw2_b": normal(C, 0.01), "gamma": normal(C, 0.1)}),
+                             "out": torch.empty((batch, 2 * t, C), dtype=torch.float32,
+                                                device=device), "t": t})
+            t *= 2
+        self.t_dec = t
+        self.init_w = lai.voc_pack_conv(normal((1536, C, 7), (7 * C) ** -0.5))
+        self.init_b = normal(1536, 0.01)
+        self.init_out = torch.empty((batch, t, 1536), dtype=torch.float32, device=device)
+        self.dec = VocDecoder(t0=t, batch=batch, passes=passes, seed=seed + 1000, device=device,
+                              x0=self.init_out)
+        self.fin = {"ea": torch.exp(normal(96, 0.1)), "ieb": 1.0 / torch.exp(normal(96, 0.1)),
+                    "w": normal((1, 96, 7), (96 * 7) ** -0.5), "b": normal(1, 0.01)}
+        self.t_final = self.dec.shapes[-1][3]
+        self.audio = torch.empty((batch, self.t_final), dtype=torch.float32, device=device)
+        self.scratch = self.dec.scratch  # the largest need (the last block's) covers every stage
+        self.err = self.dec.err
+        self.kernel_names = ("upsample0_tconv", "upsample0_convnext", "upsample1_tconv",
+                             "upsample1_convnext", "init_conv") + self.dec.kernel_names + ("final",)
+        self.rows_step = batch * self.t_final
+
+    def launches(self, stream=None):
+        L = []
+        src = self.x_in
+        for u in self.ups:
+            def tconv(u=u, src=src):
+                lai.call("lai_voc_conv_transpose1d_f32", lai._p(u["out"]), lai._p(src),
+                         lai._p(self.scratch), lai._p(u["w"]), lai._p(u["b"]), self.batch, 1024,
+                         1024, u["t"], 2, 2, self.passes, lai._p(self.err), lai._s(stream))
+            L.append(tconv)
+            L.append(lambda u=u: lai.voc_convnext(u["out"], u["cn"], self.scratch, self.passes,
+                                                  self.err, stream))
+            src = u["out"]
+
+        def init(src=src):
+            lai.call("lai_voc_conv1d_f32", lai._p(self.init_out), lai._p(src), lai._p(self.scratch),
+                     lai._p(self.init_w), lai._p(self.init_b), self.batch, 1024, 1536, self.t_dec,
+                     7, 1, self.passes, lai._p(self.err), lai._s(stream))
+        L.append(init)
+        L += self.dec.launches(stream)
+        L.append(lambda: lai.voc_final(self.dec.outs[-1], self.fin["ea"], self.fin["ieb"],
+                                       self.fin["w"], self.fin["b"], out=self.audio, stream=stream))
+        return L
+
+    def flops_per_launch(self) -> list[float]:
+        C, B = 1024, self.batch
+        f = []
+        for u in self.ups:
+            f += [2.0 * C * C * 2 * u["t"] * B, 16.0 * C * C * 2 * u["t"] * B]
+        f.append(2.0 * C * 1536 * 7 * self.t_dec * B)
+        f += self.dec.flops_per_launch()
+        f.append(2.0 * 96 * 7 * self.t_final * B)
+        return f
+
+    def bytes_per_launch(self) -> list[int]:
+        C, B = 1024, self.batch
+        b = []
+        for u in self.ups:
+            b += [B * (12 * u["t"] * C + 4 * 2 * u["t"] * C), 92 * B * 2 * u["t"] * C]
+        b.append(B * self.t_dec * (12 * C + 4 * 1536))
+        b += self.dec.bytes_per_launch()
+        b.append(B * self.t_final * (4 * 96 + 4))
+        return b
+
+    def rows_per_launch(self) -> list[int]:
+        B = self.batch
+        r = []
+        for u in self.ups:
+            r += [B * 2 * u["t"], B * 2 * u["t"]]
+        r.append(B * self.t_dec)
+        r += self.dec.rows_per_launch()
+        r.append(B * self.t_final)
+        return r
 
 
 class VocConvNeXt:
