@@ -1091,6 +1091,18 @@ def run_reference(args) -> None:
                     ms_per_step=1000.0 * r["step_seconds"], scaling="weak", dtype="f32",
                     config={"workload": "vocoder BigVGAN decoder (4 blocks)", "config": "v2",
                             "t0": 2000, "batch": 1})
+    elif args.config == "v3":
+        r = cpu_decoder_rate(2000, 1, 0.0, t0_sample=40, steps=args.steps, warmup=args.warmup,
+                             full=True)
+        cb = {"value": r["rows_per_s"], "unit": "rows/s", "cores": r["threads"], "kind": "port",
+              "sample": f"the whole path from 10 frames per step ({r['samples_sample']} output "
+                        "samples), scaled to 500 frames; the reference's USE_BLAS path (its "
+                        "compiled SnakeBeta, depthwise conv, LayerNorm, GELU and final conv + "
+                        f"OpenBLAS SGEMMs), host {cpu_model()}"}
+        line = dict(common, value=r["rows_per_s"], unit="rows/s",
+                    ms_per_step=1000.0 * r["step_seconds"], scaling="weak", dtype="f32",
+                    config={"workload": "tts_vocoder_run from the pre-transformer output to audio",
+                            "config": "v3", "frames": 500, "batch": 1})
     elif args.config == "n1":
         stages = [(1024, 1000), (1024, 2000)]
         r = cpu_convnext_rate(stages, 8, 0.0, sample_t=500, steps=args.steps, warmup=args.warmup)
