@@ -52,8 +52,11 @@ enum {
 
 /* Bits ORed into the caller's device error word. LAI_DEVERR_TIMEOUT: a kernel's
  * bounded wait on its own asynchronous copies ran out (never expected; the kernel
- * drains what it issued and returns instead of hanging). */
-enum { LAI_DEVERR_TOKEN_ID = 1, LAI_DEVERR_POSITION = 2, LAI_DEVERR_TIMEOUT = 4 };
+ * drains what it issued and returns instead of hanging). LAI_DEVERR_SMEM_ALIGN: a
+ * tensor-core kernel found its dynamic shared memory less than 1 KiB aligned and
+ * computed nothing (never expected). */
+enum { LAI_DEVERR_TOKEN_ID = 1, LAI_DEVERR_POSITION = 2, LAI_DEVERR_TIMEOUT = 4,
+       LAI_DEVERR_SMEM_ALIGN = 8 };
 
 LAI_API const char *lai_status_string(int status);
 LAI_API int lai_version(void); /* major*10000 + minor*100 + patch */

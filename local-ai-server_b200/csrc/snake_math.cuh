@@ -6,16 +6,16 @@ namespace lai {
 
 // sin^2(y) without a full sin, from textbook pieces:
 //  * Cody-Waite reduction (W. J. Cody, W. Waite, "Software Manual for the Elementary
-//    Functions", 1980): m = rint(y * 2/pi), r = y - m*pi/2 with pi/2 split into three
+//    Functions", 1980): m = nearest integer to y * 2/pi, r = y - m*pi/2 with pi/2 split into three
 //    floats so that r keeps ~full precision for |m| < 2^16;
 //  * sin^2 y = (1 - cos 2y) / 2 and cos 2y = cos(m*pi + 2r) = (-1)^m cos t, t = 2r,
 //    |t| <= pi/2;
 //  * cos t by its Taylor series through t^12 (coefficients 1/(2k)!): the remainder is
 //    below (pi/2)^14 / 14! < 6.4e-9 on |t| <= pi/2, under float resolution.
-// About 14 FP instructions instead of a full-range sinf plus a square. Arguments
-// beyond 65536 in magnitude (and inf/NaN) take CUDA's sinf. The absolute error of
-// sin^2 stays within a few 1e-8 (tests/test_gpu_parity.py bounds it against the
-// reference's own compiled voc_snake_beta).
+// About 14 FP instructions, none on the XU pipe, instead of a full-range sinf plus a
+// square. Arguments beyond 65536 in magnitude (and inf/NaN) take CUDA's sinf. The
+// absolute error of sin^2 stays within a few 1e-8 (tests/test_gpu_parity.py bounds it
+// against the reference's own compiled voc_snake_beta).
 // pi/2 = hi + mid + lo, each the float nearest to what remains (computed in 80-digit
 // decimal arithmetic); 2/pi rounded to float.
 constexpr float kTwoOverPi = 0.6366197466850281f;
@@ -23,8 +23,16 @@ constexpr float kPiO2Hi = 1.5707963705062866f;
 constexpr float kPiO2Mid = -4.371138828673793e-08f;
 constexpr float kPiO2Lo = -1.7151245100058819e-15f;
 
+// 1.5 * 2^23: a float in [2^23, 2^24) has unit spacing, so adding this shift to a value of
+// magnitude below 2^22 rounds it to the nearest integer (ties to even) and leaves that
+// integer's parity in the lowest mantissa bit. Rounding and parity then cost an FMA, an add
+// and an AND instead of a round and a float-to-int conversion on the narrow XU pipe.
+constexpr float kRoundShift = 12582912.0f;
+
 __device__ __forceinline__ float sin2_fast(float y) {
-    const float m = rintf(y * kTwoOverPi);
+    // |y| <= 65536 here, so |y * 2/pi| < 41723, well inside the shift's exact range
+    const float shifted = fmaf(y, kTwoOverPi, kRoundShift);
+    const float m = shifted - kRoundShift;
     float r = fmaf(-m, kPiO2Hi, y);
     r = fmaf(-m, kPiO2Mid, r);
     r = fmaf(-m, kPiO2Lo, r);
@@ -37,7 +45,7 @@ __device__ __forceinline__ float sin2_fast(float y) {
     c = fmaf(c, u, 1.0f / 24.0f);               // 1/4!
     c = fmaf(c, u, -0.5f);                      // 1/2!
     c = fmaf(c, u, 1.0f);
-    const int odd = static_cast<int>(m) & 1;
+    const int odd = __float_as_int(shifted) & 1;
     c = odd ? -c : c;                           // cos 2y
     return fmaf(-0.5f, c, 0.5f);                // (1 - cos 2y) / 2
 }

@@ -139,11 +139,17 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// FP32 -> nearest TF32 value (low 13 mantissa bits zero), ties away from zero.
+// FP32 -> nearest TF32 value (low 13 mantissa bits zero), ties away from zero, on the
+// integer pipe (the conversion instruction runs on the narrow XU pipe, which limited the
+// epilogues that split every output): IEEE bit patterns order magnitudes, so adding half a
+// TF32 unit (bit 12) to the bits and clearing the low 13 rounds the magnitude to nearest
+// with ties up; a carry out of the mantissa steps into the next binade, and past FLT_MAX
+// to inf, as the rounding does. NaN is returned unchanged (the add could carry a NaN with
+// a full mantissa into the sign bit).
 __device__ __forceinline__ float tf32_round(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return __uint_as_float(r);
+    const uint32_t u = __float_as_uint(x);
+    const uint32_t r = (u + 0x1000u) & 0xffffe000u;
+    return (u & 0x7fffffffu) > 0x7f800000u ? x : __uint_as_float(r);
 }
 
 }  // namespace umma

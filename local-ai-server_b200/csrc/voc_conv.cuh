@@ -43,7 +43,8 @@ constexpr int kUmmaK = 8;       // K of one kind::tf32 MMA (32 bytes)
 constexpr int kEpiWarps = 8;    // two per TMEM lane quarter, each half of the columns
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA + TMEM, 2..9 drain
 constexpr int kChunkBlocks = 2; // K blocks per TMEM accumulation chunk (32 input channels)
-constexpr int kSmemTiles = 192 * 1024;
+constexpr int kSmemTiles = 227 * 1024;  // the per-CTA maximum when one CTA runs per SM
+constexpr int kBarBytes = 256;          // mbarriers + the TMEM address slot
 constexpr int kEpiPitch = 33;   // floats per row of a drain warp's 32 x 32 transpose buffer
 constexpr uint32_t kEpiBytes = kEpiWarps * 32 * kEpiPitch * 4;
 constexpr int kMaxStages = 8;
@@ -81,17 +82,27 @@ struct Tile {
     // the shared memory each, so one CTA's fill, drain and epilogue overlap the other's MMAs
     // (measured: the 96/192/384-channel vocoder stages 24-30% faster than one CTA per SM).
     static constexpr int kMinBlocks = BN <= 128 ? 2 : 1;
-    static constexpr int kBudget = kMinBlocks == 2 ? 76 * 1024 : kSmemTiles;
+    // An SM has 228 KiB of shared memory and reserves 1 KiB per resident CTA; the ring
+    // takes what is left after the barriers. The drain warps' transpose buffers reuse the
+    // ring once the last MMA has completed, so they cost no pipeline depth: the operand
+    // bytes in flight per CTA (all stages but the one the MMAs read) set the rate at
+    // which L2 can feed the tensor core.
+    static constexpr int kBudget = (kMinBlocks == 2 ? 113 * 1024 : kSmemTiles) - kBarBytes;
     static constexpr int kStages =
         (int)(kBudget / kStage) < kMaxStages ? (int)(kBudget / kStage) : kMaxStages;
-    // align slack + operand ring + the drain warps' transpose buffers + barriers
-    static constexpr uint32_t kSmem = 1024 + kStages * kStage + kEpiBytes + 256;
+    static constexpr uint32_t kRing = kStages * kStage > kEpiBytes ? kStages * kStage : kEpiBytes;
+    // operand ring (1 KiB-aligned dynamic shared memory) + barriers
+    static constexpr uint32_t kSmem = kRing + kBarBytes;
     // two accumulator buffers: the MMAs fill one chunk while the other is drained
     static constexpr uint32_t kBufCols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
     static constexpr uint32_t kTmemCols = 2 * kBufCols;
     static constexpr int kHalf = BN / 2;  // columns per drain warp
+    static constexpr int kChunk = kChunkBlocks;
     static_assert(kA % 1024 == 0 && kB % 1024 == 0, "tiles must keep 1 KiB alignment");
     static_assert(kStages >= 2, "pipeline needs two stages");
+    static_assert(kMinBlocks == 1 ? kSmem <= 227 * 1024 : 2 * (kSmem + 1024) <= 228 * 1024,
+                  "shared memory beyond the SM's capacity for kMinBlocks CTAs");
+    static_assert(2 * kStages + 4 <= kBarBytes / 8 - 1, "barrier area too small");
     static_assert(kHalf % 16 == 0, "drain warps read 16-column groups");
 };
 
@@ -147,26 +158,41 @@ __device__ __forceinline__ void epilogue4(const ConvArgs &a, float (&v)[4], cons
 // other buffer. Chunk errors then carry each chunk's own sign and largely cancel.
 //
 // act_map: [2 planes][batch][T][c_in] (hi, lo); w_map: [2 * taps][c_out][c_in] (hi taps,
-// then lo taps). Grid: (ceil(T / 128), c_out / BN, batch).
+// then lo taps). Grid: ceil(T / 128) x (c_out / BN) x phases x batch tiles, one dimension.
 template <int BN, int PASSES, int EPI>
 __global__ void __launch_bounds__(kThreads, (BN <= 128 ? 2 : 1))
 conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
                  const __grid_constant__ CUtensorMap w_map, const ConvArgs a) {
     using L = Tile<BN, PASSES>;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *tiles = reinterpret_cast<uint8_t *>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    float *epi_buf = reinterpret_cast<float *>(tiles + L::kStages * L::kStage);
-    uint64_t *full = reinterpret_cast<uint64_t *>(tiles + L::kStages * L::kStage + kEpiBytes);
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // 64-byte swizzled tiles need 512-byte alignment; the declaration asks for 1 KiB. A base
+    // that is not aligned makes the CTA report LAI_DEVERR_SMEM_ALIGN and do nothing.
+    if (reinterpret_cast<uintptr_t>(smem_raw) & 1023) {
+        if (threadIdx.x == 0 && a.err) atomicOr(a.err, LAI_DEVERR_SMEM_ALIGN);
+        return;
+    }
+    uint8_t *tiles = smem_raw;
+    float *epi_buf = reinterpret_cast<float *>(tiles);  // reused after the last MMA
+    uint64_t *full = reinterpret_cast<uint64_t *>(tiles + L::kRing);
     uint64_t *empty = full + L::kStages;
     uint64_t *acc_full = empty + L::kStages;  // [2]: chunk ready in buffer b
     uint64_t *acc_empty = acc_full + 2;       // [2]: buffer b drained
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    // Tile order (fastest first): output-channel tile, phase, time tile, batch. The CTAs
+    // that read the same input rows (every channel tile and phase of one time tile) run
+    // side by side, so an input larger than L2 comes from HBM once, not once per channel
+    // tile or phase.
     const int P = a.phases > 1 ? a.phases : 1;
-    const int t0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
-    const int b = blockIdx.z / P, phase = blockIdx.z - (blockIdx.z / P) * P;
+    const int n_nt = a.c_out / BN, n_tt = (a.T + kBM - 1) / kBM;
+    int rest = (int)blockIdx.x;
+    const int nt = rest % n_nt;
+    rest /= n_nt;
+    const int phase = rest % P;
+    rest /= P;
+    const int t0 = (rest % n_tt) * kBM, n0 = nt * BN;
+    const int b = rest / n_tt;
     // global output row of GEMM row t, or -1 when it has none
     auto out_row = [&](int t) -> int64_t {
         if (t >= a.T) return -1;
@@ -176,7 +202,7 @@ conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
     };
     const int kblocks = a.c_in / kBK;
     const int n_iter = a.taps * kblocks;
-    const int n_chunks = (n_iter + kChunkBlocks - 1) / kChunkBlocks;
+    const int n_chunks = (n_iter + L::kChunk - 1) / L::kChunk;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < L::kStages; s++) {
@@ -231,8 +257,8 @@ conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
             constexpr uint32_t idesc = umma::idesc_tf32<kBM, BN>();
             for (int it = 0; it < n_iter; it++) {
                 const int s = it % L::kStages;
-                const int j = it / kChunkBlocks;
-                const bool first = it - j * kChunkBlocks == 0;
+                const int j = it / L::kChunk;
+                const bool first = it - j * L::kChunk == 0;
                 if (first && j >= 2 &&
                     !bulk::mbar_wait_bounded(&acc_empty[j & 1], ((j >> 1) - 1) & 1, kWaitNs)) {
                     ok = false;
@@ -260,7 +286,7 @@ conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
                     }
                 }
                 umma::commit(&empty[s]);  // frees the stage once these MMAs have read it
-                if (it - j * kChunkBlocks == kChunkBlocks - 1 || it == n_iter - 1)
+                if (it - j * L::kChunk == L::kChunk - 1 || it == n_iter - 1)
                     umma::commit(&acc_full[j & 1]);
             }
         }
@@ -415,9 +441,9 @@ int launch_conv_t(const CUtensorMap &am, const CUtensorMap &wm, const ConvArgs &
         cudaSuccess)
         return LAI_ERR_CUDA;
     const unsigned phases = a.phases > 1 ? (unsigned)a.phases : 1u;
-    const dim3 grid((unsigned)((a.T + kBM - 1) / kBM), (unsigned)(a.c_out / BN),
-                    (unsigned)batch * phases);
-    kern<<<grid, kThreads, L::kSmem, st>>>(am, wm, a);
+    const long long tiles = (long long)((a.T + kBM - 1) / kBM) * (a.c_out / BN) * phases * batch;
+    if (tiles > 0x7fffffffLL) return LAI_ERR_TOOBIG;
+    kern<<<(unsigned)tiles, kThreads, L::kSmem, st>>>(am, wm, a);
     return launch_status();
 }
 

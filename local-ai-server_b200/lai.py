@@ -17,7 +17,7 @@ LIB_PATH = os.path.join(HERE, "liblai_kernels.so")
 
 LAI_OK, LAI_ERR_INVALID, LAI_ERR_CUDA, LAI_ERR_RANGE, LAI_ERR_ALIAS, LAI_ERR_NOMEM, LAI_ERR_TOOBIG = \
     0, -1, -2, -3, -4, -5, -6
-LAI_DEVERR_TOKEN_ID, LAI_DEVERR_POSITION, LAI_DEVERR_TIMEOUT = 1, 2, 4
+LAI_DEVERR_TOKEN_ID, LAI_DEVERR_POSITION, LAI_DEVERR_TIMEOUT, LAI_DEVERR_SMEM_ALIGN = 1, 2, 4, 8
 
 _vp, _i32, _i64, _f32, _u64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_uint64
 

@@ -126,6 +126,16 @@ def test_pack_conv_bit_exact():
     want = np.stack([hi.transpose(2, 0, 1), lo.transpose(2, 0, 1)])  # [2, k, c_out, c_in]
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
     assert np.array_equal((got[0] + got[1]), w.transpose(2, 0, 1))
+    # specials: NaN with a full mantissa (CUDA's canonical 0x7fffffff) stays NaN, inf stays
+    # inf, a tie rounds away from zero
+    sp = np.array([0x7FFFFFFF, 0xFFFFFFFF, 0x7F800000, 0xFF800000, 0x3F801000, 0xBF801000,
+                   0x3F800FFF, 0x00000000], np.uint32).view(np.float32)
+    w2 = np.zeros((32, 32, 1), np.float32)
+    w2[0, :8, 0] = sp
+    hi2 = lai.voc_pack_conv(torch.from_numpy(w2).to(DEV)).cpu().numpy()[0, 0, 0, :8]
+    assert np.isnan(hi2[:2]).all()
+    assert hi2[2] == np.inf and hi2[3] == -np.inf
+    assert hi2[4:].view(np.uint32).tolist() == [0x3F802000, 0xBF802000, 0x3F800000, 0]
 
 
 def test_transpose_round_trip():
