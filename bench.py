@@ -1386,7 +1386,7 @@ def run_ours(args) -> None:
         cfg = None
     elif decode:
         cfg = runner.DECODE_CONFIGS[args.config]
-        work = runner.DecodeLinear(cfg, seed=args.seed + 1000 * rank)
+        work = runner.DecodeLinear(cfg, seed=args.seed + 1000 * rank, wfmt=args.wfmt)
         rows = cfg.m
     else:
         cfg = runner.CONFIGS[args.config]
@@ -1400,8 +1400,8 @@ def run_ours(args) -> None:
     launches = work.launches(None)  # each launch goes to the current stream when called
     graph = args.graph == "on" or (args.graph == "auto" and not snake and rows <= 4096)
     unfused_us = None
-    if decode:  # the same step as separate kernels around cuBLAS GEMMs, for comparison
-        ul = work.unfused_library_launches()
+    ul = work.unfused_library_launches() if decode else None
+    if ul:  # the same step as separate kernels around cuBLAS GEMMs, for comparison
         for _ in range(args.warmup):
             for f in ul:
                 f()
@@ -1542,7 +1542,7 @@ def run_ours(args) -> None:
                               f"{cfg.layers} layers (per layer RMSNorm+QKV GEMV, O GEMV+residual, "
                               "RMSNorm+gate/up GEMV+SwiGLU, down GEMV+residual)",
                   "config": args.config, "m": cfg.m, "dim": cfg.dim, "ffn": cfg.inter,
-                  "layers": cfg.layers, "bytes_per_step": step_bytes,
+                  "layers": cfg.layers, "weights": args.wfmt, "bytes_per_step": step_bytes,
                   "timing": "CUDA graph replay" if graph else "direct launches",
                   "unfused_library_us_per_step": unfused_us,
                   "l2": f"weights larger than L2 ({step_bytes / 1e9:.2f} GB per step)"}
@@ -1570,7 +1570,8 @@ def run_ours(args) -> None:
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(max_ms / args.steps, 4), "higher_is_better": True,
         "scaling": "strong" if strong else "weak", "vs_baseline": None,
-        "dtype": "f32" if snake else ("bf16 weights / f32 activations" if decode else args.dtype),
+        "dtype": "f32" if snake else (f"{args.wfmt} weights / f32 activations" if decode
+                                      else args.dtype),
         "data": "synthetic (seeded counter-based N(0,1) on device; norm weights 1+N(0,0.02))",
         "config": config,
         "hbm_gbs": round(step_gbs * (1 if strong else world), 1),
@@ -1597,6 +1598,9 @@ def main():
     ap.add_argument("--passes", type=int, choices=[1, 3], default=3,
                     help="v1: 3 = F32-faithful 3xTF32 products, 1 = plain TF32")
     ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--wfmt", choices=["bf16", "f16", "i8", "f32"], default="bf16",
+                    help="g1/g2: decode weight format (the reference's GPU modes: BF16 as stored, "
+                         "FP16, INT8 + per-row scale, F32)")
     ap.add_argument("--dtype", choices=["bf16", "f32"], default="bf16",
                     help="activation storage of the layer chain (f32: the drop-ins' type)")
     ap.add_argument("--rows", type=int, default=0,

@@ -38,6 +38,7 @@ extern "C" {
 #endif
 
 typedef uint16_t lai_bf16;
+typedef uint16_t lai_f16;   /* IEEE binary16 bit patterns */
 typedef void *lai_stream_t; /* a cudaStream_t */
 
 enum {
@@ -180,6 +181,51 @@ LAI_API int lai_gemv_residual_bf16w_f32(float *x_res, const float *a, const lai_
 LAI_API int lai_gemv_swiglu_bf16w_f32(float *out, const float *x, const float *norm_w, float eps,
                                       const lai_bf16 *W_gu, int64_t M, int K, int inter,
                                       lai_stream_t stream);
+
+/* The same three decode linears over the reference's other GPU weight formats
+ * (tts_pipeline_init's fp16 / int8 flags, src/tts_pipeline.h:37-40; upload_gpu_weights,
+ * src/tts_native.c:1185-1240):
+ *   _f16w: FP16 weights (its fp16 mode, and the codec head in int8 mode);
+ *   _i8w:  INT8 weights with one F32 scale per output row, y = (q_row . x) * scale[row]
+ *          (its int8 mode, tools/asr_benchmarks.md:342-352; make them with
+ *          lai_quantize_rows_i8_bf16);
+ *   _f32w: F32 weights (its default GPU mode).
+ * Arguments, fusions and limits as for the BF16 entries above; the INT8 vector path
+ * needs K % 16 == 0 (others fall back to scalar weight reads). */
+LAI_API int lai_gemv_f16w_f32(float *y, const float *x, const float *norm_w, float eps,
+                              const lai_f16 *W, int64_t M, int K, int N, lai_stream_t stream);
+LAI_API int lai_gemv_residual_f16w_f32(float *x_res, const float *a, const lai_f16 *W, int64_t M,
+                                       int K, int N, lai_stream_t stream);
+LAI_API int lai_gemv_swiglu_f16w_f32(float *out, const float *x, const float *norm_w, float eps,
+                                     const lai_f16 *W_gu, int64_t M, int K, int inter,
+                                     lai_stream_t stream);
+LAI_API int lai_gemv_i8w_f32(float *y, const float *x, const float *norm_w, float eps,
+                             const int8_t *W, const float *scales, int64_t M, int K, int N,
+                             lai_stream_t stream);
+LAI_API int lai_gemv_residual_i8w_f32(float *x_res, const float *a, const int8_t *W,
+                                      const float *scales, int64_t M, int K, int N,
+                                      lai_stream_t stream);
+LAI_API int lai_gemv_swiglu_i8w_f32(float *out, const float *x, const float *norm_w, float eps,
+                                    const int8_t *W_gu, const float *scales, int64_t M, int K,
+                                    int inter, lai_stream_t stream);
+LAI_API int lai_gemv_f32w_f32(float *y, const float *x, const float *norm_w, float eps,
+                              const float *W, int64_t M, int K, int N, lai_stream_t stream);
+LAI_API int lai_gemv_residual_f32w_f32(float *x_res, const float *a, const float *W, int64_t M,
+                                       int K, int N, lai_stream_t stream);
+LAI_API int lai_gemv_swiglu_f32w_f32(float *out, const float *x, const float *norm_w, float eps,
+                                     const float *W_gu, int64_t M, int K, int inter,
+                                     lai_stream_t stream);
+
+/* Load-time weight preparation (the reference converts BF16 safetensors when it uploads
+ * weights, src/tts_native.c:1185-1240):
+ *   lai_quantize_rows_i8_bf16: W [N, K] BF16 -> q [N, K] INT8 and scales [N] F32 with
+ *     scale = max|row| / 127, q = round(w / scale) (halves away from zero), clamped to
+ *     +-127; an all-zero row gets scale 0.
+ *   lai_convert_bf16_to_f16: n values, round to nearest even (beyond FP16 range: +-inf). */
+LAI_API int lai_quantize_rows_i8_bf16(int8_t *q, float *scales, const lai_bf16 *W, int N, int K,
+                                      lai_stream_t stream);
+LAI_API int lai_convert_bf16_to_f16(lai_f16 *dst, const lai_bf16 *src, int64_t n,
+                                    lai_stream_t stream);
 
 /* ---- decode attention over the KV cache ----------------------------------------------------
  * One query token per sequence: the decode step's cache append + qwen_causal_attention

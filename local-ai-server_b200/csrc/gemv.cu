@@ -20,6 +20,16 @@
 // kernel start launching once its own weight stream has been read, so one layer's
 // weight stream overlaps the previous kernel's tail.
 //
+// Weight formats (the reference's GPU decode modes, src/tts_pipeline.h:37-40 and
+// src/tts_native.c:1185-1240): BF16 as stored in the safetensors (linear_bf16), FP16
+// (its fp16 mode; also the codec head in int8 mode), INT8 with one F32 scale per row
+// (its int8 mode: scale = max|row| / 127, q = round(w / scale), the scale applied after
+// the row's reduction, tools/asr_benchmarks.md:342-352) and F32. One kernel template
+// serves them all; a format only changes how a 16-byte weight vector becomes floats
+// (8 BF16 or FP16, 16 INT8, 4 F32 elements), and INT8 multiplies each row's total by
+// its scale. The conversions avoid the narrow XU pipe: BF16 is a shift, INT8 a byte
+// permute into a float's mantissa and one subtraction.
+//
 // Layout: each CTA first stages the M input rows in shared memory (normalising
 // them when a norm weight is given: every CTA recomputes the norm of the <= 8 short
 // rows, cheaper than a separate launch and its HBM round trip). Each warp then owns
@@ -28,6 +38,7 @@
 // flight, against the staged inputs; a warp-shuffle tree reduces each dot product.
 #include "lai_common.cuh"
 
+#include <cuda_fp16.h>
 #include <math.h>
 
 namespace lai {
@@ -40,6 +51,65 @@ constexpr int kUnrollK = 8;  // 16-byte weight vectors in flight per lane per ro
 constexpr size_t kMaxSmem = 200 * 1024;
 
 enum Epi { kStore = 0, kResidual = 1, kSwiglu = 2 };
+
+// ---- weight formats: storage type, elements per 16-byte vector, conversions ----------
+struct WBf16 {
+    using T = uint16_t;
+    static constexpr int kEpv = 8;
+    static constexpr bool kScaled = false;
+    static __device__ __forceinline__ void unpack(const uint4 &v, float (&f)[kEpv]) {
+        lai::unpack<uint16_t>(v, f);
+    }
+    static __device__ __forceinline__ float to_f(T w) { return lai::to_f(w); }
+};
+struct WF16 {
+    using T = uint16_t;  // IEEE binary16 bit patterns
+    static constexpr int kEpv = 8;
+    static constexpr bool kScaled = false;
+    static __device__ __forceinline__ float2 pair(uint32_t u) {
+        return __half22float2(*reinterpret_cast<const __half2 *>(&u));
+    }
+    static __device__ __forceinline__ void unpack(const uint4 &v, float (&f)[kEpv]) {
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float2 p = pair(w[i]);
+            f[2 * i] = p.x;
+            f[2 * i + 1] = p.y;
+        }
+    }
+    static __device__ __forceinline__ float to_f(T w) { return __half2float(__ushort_as_half(w)); }
+};
+struct WI8 {
+    using T = int8_t;
+    static constexpr int kEpv = 16;
+    static constexpr bool kScaled = true;
+    // A signed byte b becomes b + 128 when its top bit flips; placed as the low mantissa
+    // byte of 2^23 (exponent byte 0x4B) it reads as the float 2^23 + b + 128, and one
+    // exact subtraction leaves b.
+    static __device__ __forceinline__ void four(uint32_t u, float *f) {
+        const uint32_t b = u ^ 0x80808080u;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            f[i] = __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7440u + i)) - 8388736.0f;
+    }
+    static __device__ __forceinline__ void unpack(const uint4 &v, float (&f)[kEpv]) {
+        four(v.x, f);
+        four(v.y, f + 4);
+        four(v.z, f + 8);
+        four(v.w, f + 12);
+    }
+    static __device__ __forceinline__ float to_f(T w) { return (float)w; }
+};
+struct WF32 {
+    using T = float;
+    static constexpr int kEpv = 4;
+    static constexpr bool kScaled = false;
+    static __device__ __forceinline__ void unpack(const uint4 &v, float (&f)[kEpv]) {
+        lai::unpack<float>(v, f);
+    }
+    static __device__ __forceinline__ float to_f(T w) { return w; }
+};
 
 // Programmatic dependent launch: let the next kernel on the stream start launching
 // now, and wait for the previous kernel's results only where they are first read.
@@ -95,17 +165,21 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
     return __fmul_rn(__fmul_rn(g, sig), u);
 }
 
-// K % 8 == 0 and W 16-byte aligned: 16-byte weight vectors.
-template <int M, int EPI>
+// K % (elements per vector) == 0 and W 16-byte aligned: 16-byte weight vectors.
+template <typename WF, int M, int EPI>
 __global__ void __launch_bounds__(kThreads)
 gemv_vec_kernel(float *y, const float *x, const float *norm_w, float eps,
-                const uint16_t *__restrict__ W, int K, int N, int ldy) {
+                const typename WF::T *__restrict__ W, const float *__restrict__ scales, int K,
+                int N, int ldy) {
+    using T = typename WF::T;
     constexpr int RPW = EPI == kSwiglu ? 2 : 1;
+    constexpr int E = WF::kEpv;   // weight elements per 16-byte vector
+    constexpr int S = 32 * E;     // elements one warp covers per vector step
     extern __shared__ __align__(16) float xs[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int row0 = (blockIdx.x * kWarps + warp) * RPW;
     const bool active = row0 < N;
-    const uint16_t *wr[RPW];
+    const T *wr[RPW];
 #pragma unroll
     for (int r = 0; r < RPW; r++) wr[r] = W + (size_t)(active ? row0 + r : 0) * K;
     // the weights depend on nothing earlier on the stream: their first chunk is in
@@ -113,12 +187,20 @@ gemv_vec_kernel(float *y, const float *x, const float *norm_w, float eps,
     uint4 wv[kUnrollK][RPW];
 #pragma unroll
     for (int u = 0; u < kUnrollK; u++) {
-        const int k0 = u * 256 + lane * 8;
+        const int k0 = u * S + lane * E;
 #pragma unroll
         for (int r = 0; r < RPW; r++)
             if (active && k0 < K) wv[u][r] = ld_stream(wr[r] + k0);
     }
+    // the row scales are weights too (no dependency): in flight with them
+    float sc[RPW];
+#pragma unroll
+    for (int r = 0; r < RPW; r++) sc[r] = WF::kScaled && active ? __ldg(scales + row0 + r) : 1.0f;
     pdl_wait_prior();
+    // the residual this lane adds into (written by the previous kernel): read now, so the
+    // epilogue does not wait on a load after the reduction
+    float res = 0.0f;
+    if (EPI == kResidual && active && lane < M) res = y[(size_t)lane * ldy + row0];
     stage_inputs<M>(xs, x, norm_w, eps, K);
     if (!active) {
         pdl_launch_dependents();
@@ -130,11 +212,11 @@ gemv_vec_kernel(float *y, const float *x, const float *norm_w, float eps,
 #pragma unroll
         for (int m = 0; m < M; m++) acc[r][m] = 0.f;
 
-    for (int kb = 0; kb < K; kb += 256 * kUnrollK) {
+    for (int kb = 0; kb < K; kb += S * kUnrollK) {
         if (kb > 0) {
 #pragma unroll
             for (int u = 0; u < kUnrollK; u++) {
-                const int k0 = kb + u * 256 + lane * 8;
+                const int k0 = kb + u * S + lane * E;
 #pragma unroll
                 for (int r = 0; r < RPW; r++)
                     if (k0 < K) wv[u][r] = ld_stream(wr[r] + k0);
@@ -142,19 +224,22 @@ gemv_vec_kernel(float *y, const float *x, const float *norm_w, float eps,
         }
 #pragma unroll
         for (int u = 0; u < kUnrollK; u++) {
-            const int k0 = kb + u * 256 + lane * 8;
+            const int k0 = kb + u * S + lane * E;
             if (k0 >= K) break;
+            float wf[RPW][E];
+#pragma unroll
+            for (int r = 0; r < RPW; r++) WF::unpack(wv[u][r], wf[r]);
 #pragma unroll
             for (int m = 0; m < M; m++) {
-                const float4 a = *reinterpret_cast<const float4 *>(xs + m * K + k0);
-                const float4 b = *reinterpret_cast<const float4 *>(xs + m * K + k0 + 4);
-                const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-                for (int r = 0; r < RPW; r++) {
-                    float wf[8];
-                    unpack<uint16_t>(wv[u][r], wf);
+                for (int q = 0; q < E / 4; q++) {
+                    const float4 a = *reinterpret_cast<const float4 *>(xs + m * K + k0 + 4 * q);
+                    const float xv[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
-                    for (int e = 0; e < 8; e++) acc[r][m] = fmaf(wf[e], xv[e], acc[r][m]);
+                    for (int r = 0; r < RPW; r++)
+#pragma unroll
+                        for (int e = 0; e < 4; e++)
+                            acc[r][m] = fmaf(wf[r][4 * q + e], xv[e], acc[r][m]);
                 }
             }
         }
@@ -163,24 +248,28 @@ gemv_vec_kernel(float *y, const float *x, const float *norm_w, float eps,
     // stream their own weights, then wait for this grid before reading activations)
     pdl_launch_dependents();
 #pragma unroll
-    for (int r = 0; r < RPW; r++)
+    for (int r = 0; r < RPW; r++) {
 #pragma unroll
-        for (int m = 0; m < M; m++) acc[r][m] = group_sum<32>(acc[r][m]);
+        for (int m = 0; m < M; m++) {
+            acc[r][m] = group_sum<32>(acc[r][m]);
+            if (WF::kScaled) acc[r][m] *= sc[r];
+        }
+    }
     // lane m writes input m's result (all lanes hold every total after the tree)
 #pragma unroll
     for (int m = 0; m < M; m++) {
         if (lane != m) continue;
         if constexpr (EPI == kStore) y[(size_t)m * ldy + row0] = acc[0][m];
-        if constexpr (EPI == kResidual) y[(size_t)m * ldy + row0] += acc[0][m];
+        if constexpr (EPI == kResidual) y[(size_t)m * ldy + row0] = res + acc[0][m];
         if constexpr (EPI == kSwiglu) y[(size_t)m * ldy + row0 / 2] = silu_mul(acc[0][m], acc[1][m]);
     }
 }
 
 // Any K / alignment: scalar weight reads, same structure.
-template <int M, int EPI>
+template <typename WF, int M, int EPI>
 __global__ void __launch_bounds__(kThreads)
-gemv_scalar_kernel(float *y, const float *x, const float *norm_w, float eps, const uint16_t *W,
-                   int K, int N, int ldy) {
+gemv_scalar_kernel(float *y, const float *x, const float *norm_w, float eps,
+                   const typename WF::T *W, const float *scales, int K, int N, int ldy) {
     constexpr int RPW = EPI == kSwiglu ? 2 : 1;
     extern __shared__ __align__(16) float xs[];
     pdl_launch_dependents();
@@ -193,14 +282,19 @@ gemv_scalar_kernel(float *y, const float *x, const float *norm_w, float eps, con
     for (int k = lane; k < K; k += 32)
 #pragma unroll
         for (int r = 0; r < RPW; r++) {
-            const float wf = to_f(W[(size_t)(row0 + r) * K + k]);
+            const float wf = WF::to_f(W[(size_t)(row0 + r) * K + k]);
 #pragma unroll
             for (int m = 0; m < M; m++) acc[r][m] = fmaf(wf, xs[m * K + k], acc[r][m]);
         }
 #pragma unroll
-    for (int r = 0; r < RPW; r++)
+    for (int r = 0; r < RPW; r++) {
+        const float sc = WF::kScaled ? scales[row0 + r] : 1.0f;
 #pragma unroll
-        for (int m = 0; m < M; m++) acc[r][m] = group_sum<32>(acc[r][m]);
+        for (int m = 0; m < M; m++) {
+            acc[r][m] = group_sum<32>(acc[r][m]);
+            if (WF::kScaled) acc[r][m] *= sc;
+        }
+    }
 #pragma unroll
     for (int m = 0; m < M; m++) {
         if (lane != m) continue;
@@ -210,12 +304,12 @@ gemv_scalar_kernel(float *y, const float *x, const float *norm_w, float eps, con
     }
 }
 
-template <int M, int EPI>
-int launch(float *y, const float *x, const float *norm_w, float eps, const uint16_t *W, int K, int N,
-           int ldy, bool vec, cudaStream_t s) {
+template <typename WF, int M, int EPI>
+int launch(float *y, const float *x, const float *norm_w, float eps, const typename WF::T *W,
+           const float *scales, int K, int N, int ldy, bool vec, cudaStream_t s) {
     constexpr int RPW = EPI == kSwiglu ? 2 : 1;
     const size_t smem = (size_t)M * K * sizeof(float);
-    auto kern = vec ? gemv_vec_kernel<M, EPI> : gemv_scalar_kernel<M, EPI>;
+    auto kern = vec ? gemv_vec_kernel<WF, M, EPI> : gemv_scalar_kernel<WF, M, EPI>;
     // opt in above 47 KiB: the default 48 KiB limit also covers the kernel's small static array
     if (smem > 47 * 1024 &&
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
@@ -232,17 +326,18 @@ int launch(float *y, const float *x, const float *norm_w, float eps, const uint1
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, kern, y, x, norm_w, eps, W, K, N, ldy) != cudaSuccess) {
+    if (cudaLaunchKernelEx(&cfg, kern, y, x, norm_w, eps, W, scales, K, N, ldy) != cudaSuccess) {
         cudaGetLastError();
         return LAI_ERR_CUDA;
     }
     return launch_status();
 }
 
-template <int EPI>
-int run(float *y, const float *x, const float *norm_w, float eps, const uint16_t *W, int64_t M,
-        int K, int N, lai_stream_t stream) {
-    if (!y || !x || !W || M < 0 || K <= 0 || N <= 0 || (EPI == kSwiglu && (N & 1)))
+template <typename WF, int EPI>
+int run(float *y, const float *x, const float *norm_w, float eps, const typename WF::T *W,
+        const float *scales, int64_t M, int K, int N, lai_stream_t stream) {
+    if (!y || !x || !W || M < 0 || K <= 0 || N <= 0 || (EPI == kSwiglu && (N & 1)) ||
+        (WF::kScaled && !scales))
         return LAI_ERR_INVALID;
     if (M == 0) return LAI_OK;
     const int ny = EPI == kSwiglu ? N / 2 : N;  // output row length
@@ -251,7 +346,7 @@ int run(float *y, const float *x, const float *norm_w, float eps, const uint16_t
     int64_t per = kMaxM;
     while (per > 1 && (size_t)per * K * 4 > kMaxSmem) per /= 2;
     if ((size_t)K * 4 > kMaxSmem) return LAI_ERR_TOOBIG;
-    const bool vec = K % 8 == 0 && aligned16(W);
+    const bool vec = K % WF::kEpv == 0 && aligned16(W);
     cudaStream_t s = as_stream(stream);
     for (int64_t m0 = 0; m0 < M;) {
         const int64_t cap = M - m0 < per ? M - m0 : per;
@@ -260,10 +355,10 @@ int run(float *y, const float *x, const float *norm_w, float eps, const uint16_t
         const float *xp = x + m0 * K;
         int st;
         switch (take) {
-            case 8: st = launch<8, EPI>(yp, xp, norm_w, eps, W, K, N, ny, vec, s); break;
-            case 4: st = launch<4, EPI>(yp, xp, norm_w, eps, W, K, N, ny, vec, s); break;
-            case 2: st = launch<2, EPI>(yp, xp, norm_w, eps, W, K, N, ny, vec, s); break;
-            default: st = launch<1, EPI>(yp, xp, norm_w, eps, W, K, N, ny, vec, s); break;
+            case 8: st = launch<WF, 8, EPI>(yp, xp, norm_w, eps, W, scales, K, N, ny, vec, s); break;
+            case 4: st = launch<WF, 4, EPI>(yp, xp, norm_w, eps, W, scales, K, N, ny, vec, s); break;
+            case 2: st = launch<WF, 2, EPI>(yp, xp, norm_w, eps, W, scales, K, N, ny, vec, s); break;
+            default: st = launch<WF, 1, EPI>(yp, xp, norm_w, eps, W, scales, K, N, ny, vec, s); break;
         }
         if (st != LAI_OK) return st;
         m0 += take;
@@ -278,19 +373,74 @@ extern "C" {
 
 int lai_gemv_bf16w_f32(float *y, const float *x, const float *norm_w, float eps, const lai_bf16 *W,
                        int64_t M, int K, int N, lai_stream_t stream) {
-    return lai::run<lai::kStore>(y, x, norm_w, eps, W, M, K, N, stream);
+    return lai::run<lai::WBf16, lai::kStore>(y, x, norm_w, eps, W, nullptr, M, K, N, stream);
 }
 
 int lai_gemv_residual_bf16w_f32(float *x_res, const float *a, const lai_bf16 *W, int64_t M, int K,
                                 int N, lai_stream_t stream) {
-    return lai::run<lai::kResidual>(x_res, a, nullptr, 0.f, W, M, K, N, stream);
+    return lai::run<lai::WBf16, lai::kResidual>(x_res, a, nullptr, 0.f, W, nullptr, M, K, N, stream);
 }
 
 int lai_gemv_swiglu_bf16w_f32(float *out, const float *x, const float *norm_w, float eps,
                               const lai_bf16 *W_gu, int64_t M, int K, int inter,
                               lai_stream_t stream) {
     if (inter <= 0 || inter > (1 << 29)) return LAI_ERR_INVALID;
-    return lai::run<lai::kSwiglu>(out, x, norm_w, eps, W_gu, M, K, 2 * inter, stream);
+    return lai::run<lai::WBf16, lai::kSwiglu>(out, x, norm_w, eps, W_gu, nullptr, M, K, 2 * inter,
+                                              stream);
+}
+
+int lai_gemv_f16w_f32(float *y, const float *x, const float *norm_w, float eps, const lai_f16 *W,
+                      int64_t M, int K, int N, lai_stream_t stream) {
+    return lai::run<lai::WF16, lai::kStore>(y, x, norm_w, eps, W, nullptr, M, K, N, stream);
+}
+
+int lai_gemv_residual_f16w_f32(float *x_res, const float *a, const lai_f16 *W, int64_t M, int K,
+                               int N, lai_stream_t stream) {
+    return lai::run<lai::WF16, lai::kResidual>(x_res, a, nullptr, 0.f, W, nullptr, M, K, N, stream);
+}
+
+int lai_gemv_swiglu_f16w_f32(float *out, const float *x, const float *norm_w, float eps,
+                             const lai_f16 *W_gu, int64_t M, int K, int inter,
+                             lai_stream_t stream) {
+    if (inter <= 0 || inter > (1 << 29)) return LAI_ERR_INVALID;
+    return lai::run<lai::WF16, lai::kSwiglu>(out, x, norm_w, eps, W_gu, nullptr, M, K, 2 * inter,
+                                             stream);
+}
+
+int lai_gemv_i8w_f32(float *y, const float *x, const float *norm_w, float eps, const int8_t *W,
+                     const float *scales, int64_t M, int K, int N, lai_stream_t stream) {
+    return lai::run<lai::WI8, lai::kStore>(y, x, norm_w, eps, W, scales, M, K, N, stream);
+}
+
+int lai_gemv_residual_i8w_f32(float *x_res, const float *a, const int8_t *W, const float *scales,
+                              int64_t M, int K, int N, lai_stream_t stream) {
+    return lai::run<lai::WI8, lai::kResidual>(x_res, a, nullptr, 0.f, W, scales, M, K, N, stream);
+}
+
+int lai_gemv_swiglu_i8w_f32(float *out, const float *x, const float *norm_w, float eps,
+                            const int8_t *W_gu, const float *scales, int64_t M, int K, int inter,
+                            lai_stream_t stream) {
+    if (inter <= 0 || inter > (1 << 29)) return LAI_ERR_INVALID;
+    return lai::run<lai::WI8, lai::kSwiglu>(out, x, norm_w, eps, W_gu, scales, M, K, 2 * inter,
+                                            stream);
+}
+
+int lai_gemv_f32w_f32(float *y, const float *x, const float *norm_w, float eps, const float *W,
+                      int64_t M, int K, int N, lai_stream_t stream) {
+    return lai::run<lai::WF32, lai::kStore>(y, x, norm_w, eps, W, nullptr, M, K, N, stream);
+}
+
+int lai_gemv_residual_f32w_f32(float *x_res, const float *a, const float *W, int64_t M, int K,
+                               int N, lai_stream_t stream) {
+    return lai::run<lai::WF32, lai::kResidual>(x_res, a, nullptr, 0.f, W, nullptr, M, K, N, stream);
+}
+
+int lai_gemv_swiglu_f32w_f32(float *out, const float *x, const float *norm_w, float eps,
+                             const float *W_gu, int64_t M, int K, int inter,
+                             lai_stream_t stream) {
+    if (inter <= 0 || inter > (1 << 29)) return LAI_ERR_INVALID;
+    return lai::run<lai::WF32, lai::kSwiglu>(out, x, norm_w, eps, W_gu, nullptr, M, K, 2 * inter,
+                                             stream);
 }
 
 }  // extern "C"

@@ -46,6 +46,17 @@ SIGNATURES: dict[str, tuple] = {
     "lai_gemv_bf16w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
     "lai_gemv_residual_bf16w_f32": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _vp]),
     "lai_gemv_swiglu_bf16w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
+    "lai_gemv_f16w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
+    "lai_gemv_residual_f16w_f32": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _vp]),
+    "lai_gemv_swiglu_f16w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
+    "lai_gemv_i8w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _vp, _i64, _i32, _i32, _vp]),
+    "lai_gemv_residual_i8w_f32": (_i32, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _vp]),
+    "lai_gemv_swiglu_i8w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _vp, _i64, _i32, _i32, _vp]),
+    "lai_gemv_f32w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
+    "lai_gemv_residual_f32w_f32": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _vp]),
+    "lai_gemv_swiglu_f32w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
+    "lai_quantize_rows_i8_bf16": (_i32, [_vp, _vp, _vp, _i32, _i32, _vp]),
+    "lai_convert_bf16_to_f16": (_i32, [_vp, _vp, _i64, _vp]),
     "lai_decode_attention_scratch_bytes": (ctypes.c_size_t, [_i32, _i32, _i32, _i32]),
     "lai_decode_attention_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32,
                                         _i32, _i32, _f32, _vp, _vp, _vp]),
@@ -234,31 +245,70 @@ def snake_beta(x, ea, ieb, stream=None):
     return x
 
 
-def gemv(x, W, norm_w=None, eps=1e-6, y=None, stream=None):
-    """y[M,N] = W[N,K] @ (RMSNorm(x) if norm_w is given else x), x [M,K] FP32, W BF16."""
+def _wfmt(W, scales):
+    """The entry-point suffix for a weight tensor's format: torch.bfloat16 -> bf16w,
+    float16 -> f16w, int8 (needs per-row scales) -> i8w, float32 -> f32w."""
+    import torch
+    fmt = {torch.bfloat16: "bf16w", torch.float16: "f16w", torch.int8: "i8w",
+           torch.float32: "f32w"}.get(W.dtype)
+    if fmt is None:
+        raise TypeError(f"unsupported weight dtype {W.dtype}")
+    if (fmt == "i8w") != (scales is not None):
+        raise ValueError("INT8 weights need per-row scales (and only they take them)")
+    return fmt
+
+
+def gemv(x, W, norm_w=None, eps=1e-6, y=None, stream=None, scales=None):
+    """y[M,N] = W[N,K] @ (RMSNorm(x) if norm_w is given else x), x [M,K] FP32; W BF16, FP16,
+    F32, or INT8 with scales [N] (y = (q . x) * scale)."""
     import torch
     M, K = x.shape
     N = W.shape[0]
     y = torch.empty((M, N), dtype=torch.float32, device=x.device) if y is None else y
-    call("lai_gemv_bf16w_f32", _p(y), _p(x), _p(norm_w), eps, _p(W), M, K, N, _s(stream))
+    fmt = _wfmt(W, scales)
+    sc = (_p(scales),) if fmt == "i8w" else ()
+    call(f"lai_gemv_{fmt}_f32", _p(y), _p(x), _p(norm_w), eps, _p(W), *sc, M, K, N, _s(stream))
     return y
 
 
-def gemv_residual(x_res, a, W, stream=None):
+def gemv_residual(x_res, a, W, stream=None, scales=None):
     """x_res[M,N] += W[N,K] @ a[M,K]."""
-    call("lai_gemv_residual_bf16w_f32", _p(x_res), _p(a), _p(W), a.shape[0], a.shape[1],
+    fmt = _wfmt(W, scales)
+    sc = (_p(scales),) if fmt == "i8w" else ()
+    call(f"lai_gemv_residual_{fmt}_f32", _p(x_res), _p(a), _p(W), *sc, a.shape[0], a.shape[1],
          W.shape[0], _s(stream))
     return x_res
 
 
-def gemv_swiglu(x, W_gu, norm_w=None, eps=1e-6, out=None, stream=None):
+def gemv_swiglu(x, W_gu, norm_w=None, eps=1e-6, out=None, stream=None, scales=None):
     """out[M,I] = silu(W_gu[2j].xn) * W_gu[2j+1].xn, W_gu [2I, K] rows interleaved."""
     import torch
     M, K = x.shape
     inter = W_gu.shape[0] // 2
     out = torch.empty((M, inter), dtype=torch.float32, device=x.device) if out is None else out
-    call("lai_gemv_swiglu_bf16w_f32", _p(out), _p(x), _p(norm_w), eps, _p(W_gu), M, K, inter,
-         _s(stream))
+    fmt = _wfmt(W_gu, scales)
+    sc = (_p(scales),) if fmt == "i8w" else ()
+    call(f"lai_gemv_swiglu_{fmt}_f32", _p(out), _p(x), _p(norm_w), eps, _p(W_gu), *sc, M, K,
+         inter, _s(stream))
+    return out
+
+
+def quantize_rows_i8(W, stream=None):
+    """BF16 W [N, K] -> (INT8 q [N, K], F32 scales [N]): scale = max|row| / 127,
+    q = round(w / scale)."""
+    import torch
+    N, K = W.shape
+    q = torch.empty((N, K), dtype=torch.int8, device=W.device)
+    scales = torch.empty((N,), dtype=torch.float32, device=W.device)
+    call("lai_quantize_rows_i8_bf16", _p(q), _p(scales), _p(W), N, K, _s(stream))
+    return q, scales
+
+
+def convert_bf16_to_f16(W, stream=None):
+    """BF16 tensor -> FP16 tensor of the same shape (round to nearest even)."""
+    import torch
+    out = torch.empty(W.shape, dtype=torch.float16, device=W.device)
+    call("lai_convert_bf16_to_f16", _p(out), _p(W), W.numel(), _s(stream))
     return out
 
 

@@ -612,16 +612,31 @@ class DecodeLinear:
     them all from HBM. The attention output is a fixed stand-in (attention is not part
     of this path)."""
 
-    def __init__(self, cfg: DecodeConfig, seed: int = 4321, device: str = "cuda"):
+    # weight bytes per element and the entry points' format names (the reference's GPU modes)
+    WEIGHT_BYTES = {"bf16": 2, "f16": 2, "i8": 1, "f32": 4}
+
+    def __init__(self, cfg: DecodeConfig, seed: int = 4321, device: str = "cuda",
+                 wfmt: str = "bf16"):
         import torch
-        self.cfg, self.rows = cfg, cfg.m
+        self.cfg, self.rows, self.wfmt = cfg, cfg.m, wfmt
+        self.wbytes = self.WEIGHT_BYTES[wfmt]
         D, I, M = cfg.dim, cfg.inter, cfg.m
         self.qkv_n = cfg.q_dim + 2 * cfg.kv_dim
         f32, bf = torch.float32, torch.bfloat16
+        self.scales = {}  # id(weight) -> per-row scales (INT8)
 
         def w(n, k, s):
             t = torch.empty((n, k), dtype=bf, device=device)
-            return lai.synth_normal(t, seed=seed + s, std=float(k) ** -0.5)
+            t = lai.synth_normal(t, seed=seed + s, std=float(k) ** -0.5)
+            if wfmt == "f16":
+                return lai.convert_bf16_to_f16(t)
+            if wfmt == "f32":
+                return t.float()
+            if wfmt == "i8":
+                q, sc = lai.quantize_rows_i8(t)
+                self.scales[id(q)] = sc
+                return q
+            return t
 
         L = cfg.layers
         self.Wqkv = [w(self.qkv_n, D, 10 * l + 1) for l in range(L)]
@@ -642,49 +657,57 @@ class DecodeLinear:
 
     def launches(self, stream=None):
         c = self.cfg
+        sc = lambda W: self.scales.get(id(W))  # noqa: E731
         out = []
         for l in range(c.layers):
             out += [
-                lambda l=l: lai.gemv(self.x, self.Wqkv[l], self.w_in, c.eps, y=self.qkv, stream=stream),
-                lambda l=l: lai.gemv_residual(self.x, self.attn, self.Wo[l], stream=stream),
+                lambda l=l: lai.gemv(self.x, self.Wqkv[l], self.w_in, c.eps, y=self.qkv,
+                                     stream=stream, scales=sc(self.Wqkv[l])),
+                lambda l=l: lai.gemv_residual(self.x, self.attn, self.Wo[l], stream=stream,
+                                              scales=sc(self.Wo[l])),
                 lambda l=l: lai.gemv_swiglu(self.x, self.Wgu[l], self.w_post, c.eps, out=self.act,
-                                            stream=stream),
-                lambda l=l: lai.gemv_residual(self.x, self.act, self.Wd[l], stream=stream),
+                                            stream=stream, scales=sc(self.Wgu[l])),
+                lambda l=l: lai.gemv_residual(self.x, self.act, self.Wd[l], stream=stream,
+                                              scales=sc(self.Wd[l])),
             ]
         return out
 
     def unfused_library_launches(self):
-        """The same step as separate kernels around cuBLAS BF16 GEMMs (torch), every
-        intermediate through HBM: the library baseline the fusion is measured against."""
-        import torch
+        """The same step as separate kernels around cuBLAS GEMMs in the weights' own type
+        (torch), every intermediate through HBM: the library baseline the fusion is measured
+        against. None for INT8 weights, which cuBLAS does not take as they are stored."""
         import torch.nn.functional as F
         c = self.cfg
+        if self.wfmt == "i8":
+            return None
+        wt = self.Wqkv[0].dtype
 
         def layer(l):
             def qkv():
                 xn = lai.rmsnorm(self.x, self.w_in, c.eps)
-                self.qkv.copy_(F.linear(xn.to(torch.bfloat16), self.Wqkv[l]))
+                self.qkv.copy_(F.linear(xn.to(wt), self.Wqkv[l]))
 
             def o():
-                lai.add(self.x, F.linear(self.attn.to(torch.bfloat16), self.Wo[l]).float())
+                lai.add(self.x, F.linear(self.attn.to(wt), self.Wo[l]).float())
 
             def gu():
                 xn = lai.rmsnorm(self.x, self.w_post, c.eps)
-                lai.swiglu(F.linear(xn.to(torch.bfloat16), self.Wgu[l]).float(), c.inter,
-                           out=self.act)
+                lai.swiglu(F.linear(xn.to(wt), self.Wgu[l]).float(), c.inter, out=self.act)
 
             def down():
-                lai.add(self.x, F.linear(self.act.to(torch.bfloat16), self.Wd[l]).float())
+                lai.add(self.x, F.linear(self.act.to(wt), self.Wd[l]).float())
             return [qkv, o, gu, down]
         return [f for l in range(c.layers) for f in layer(l)]
 
     def bytes_per_launch(self) -> list[int]:
-        c, M = self.cfg, self.cfg.m
+        """Weights (wbytes per element, plus 4 bytes of scale per row for INT8) + activations."""
+        c, M, e = self.cfg, self.cfg.m, self.wbytes
         D, I = c.dim, c.inter
-        return [self.qkv_n * D * 2 + M * D * 4 + M * self.qkv_n * 4 + D * 4,
-                D * c.q_dim * 2 + M * c.q_dim * 4 + 2 * M * D * 4,
-                2 * I * D * 2 + M * D * 4 + M * I * 4 + D * 4,
-                D * I * 2 + M * I * 4 + 2 * M * D * 4] * c.layers
+        s = 4 if self.wfmt == "i8" else 0
+        return [self.qkv_n * (D * e + s) + M * D * 4 + M * self.qkv_n * 4 + D * 4,
+                D * (c.q_dim * e + s) + M * c.q_dim * 4 + 2 * M * D * 4,
+                2 * I * (D * e + s) + M * D * 4 + M * I * 4 + D * 4,
+                D * (I * e + s) + M * I * 4 + 2 * M * D * 4] * c.layers
 
     def rows_per_launch(self) -> list[int]:
         return [self.cfg.m] * 4 * self.cfg.layers

@@ -357,6 +357,110 @@ void oracle_linear_bf16(float *out, const float *in, const uint16_t *W, int M, i
 }
 
 /* ---------------------------------------------------------------------------
+ * The reference's other GPU weight formats for the same linears: FP16 (its fp16 mode),
+ * INT8 with a per-row scale (its int8 mode) and F32 (src/tts_pipeline.h:37-40,
+ * src/tts_native.c:1185-1240). The INT8 recipe is tools/asr_benchmarks.md:342-352:
+ * scale = max(abs(row)) / 127, int8[j] = round(row[j] / scale), the scale applied after
+ * the row's reduction. The conversion code sits in the un-vendored qwen-asr GPU sources,
+ * so "round" is taken as C roundf (halves away from zero) on the F32 quotient.
+ * ------------------------------------------------------------------------- */
+float oracle_f16_to_f32(uint16_t h) {
+    /* binary16: sign, 5-bit exponent (bias 15), 10-bit fraction; exponent 0 is
+     * subnormal (f * 2^-24), 31 is inf / NaN; normal = (1024 + f) * 2^(e - 25) */
+    const int s = h >> 15, e = (h >> 10) & 31, f = h & 1023;
+    float v;
+    if (e == 0)
+        v = ldexpf((float)f, -24);
+    else if (e == 31)
+        v = f ? NAN : INFINITY;
+    else
+        v = ldexpf((float)(f | 1024), e - 25);
+    return s ? -v : v;
+}
+
+uint16_t oracle_f32_to_f16(float x) {
+    const uint16_t sign = signbit(x) ? 0x8000 : 0;
+    const float a = fabsf(x);
+    if (isnan(x)) return sign | 0x7e00;
+    if (isinf(x)) return sign | 0x7c00;
+    if (a < 0x1p-14f) /* subnormal range: k * 2^-24 with k rounded to nearest even */
+        return sign | (uint16_t)nearbyintf(a * 0x1p24f); /* k = 1024 is the least normal */
+    int e;
+    frexpf(a, &e); /* a in [2^(e-1), 2^e) */
+    float q = nearbyintf(ldexpf(a, 11 - e)); /* 11 significant bits, in [1024, 2048] */
+    int E = e - 1 + 15;
+    if (q >= 2048.0f) {
+        q = 1024.0f;
+        E++;
+    }
+    if (E >= 31) return sign | 0x7c00;
+    return sign | (uint16_t)(E << 10) | (uint16_t)((int)q - 1024);
+}
+
+void oracle_f32_to_f16_array(uint16_t *dst, const float *src, int64_t n) {
+    for (int64_t i = 0; i < n; i++) dst[i] = oracle_f32_to_f16(src[i]);
+}
+
+void oracle_linear_f16(float *out, const float *in, const uint16_t *W, int M, int K, int N) {
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; n++) {
+        const uint16_t *wr = W + (size_t)n * K;
+        for (int m = 0; m < M; m++) {
+            const float *xr = in + (size_t)m * K;
+            acc_t s = 0;
+            for (int k = 0; k < K; k++) s += (acc_t)oracle_f16_to_f32(wr[k]) * (acc_t)xr[k];
+            out[(size_t)m * N + n] = (float)s;
+        }
+    }
+}
+
+void oracle_linear_i8(float *out, const float *in, const int8_t *W, const float *scales, int M,
+                      int K, int N) {
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; n++) {
+        const int8_t *wr = W + (size_t)n * K;
+        for (int m = 0; m < M; m++) {
+            const float *xr = in + (size_t)m * K;
+            acc_t s = 0;
+            for (int k = 0; k < K; k++) s += (acc_t)wr[k] * (acc_t)xr[k];
+            out[(size_t)m * N + n] = (float)(s * (acc_t)scales[n]);
+        }
+    }
+}
+
+void oracle_linear_f32(float *out, const float *in, const float *W, int M, int K, int N) {
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; n++) {
+        const float *wr = W + (size_t)n * K;
+        for (int m = 0; m < M; m++) {
+            const float *xr = in + (size_t)m * K;
+            acc_t s = 0;
+            for (int k = 0; k < K; k++) s += (acc_t)wr[k] * (acc_t)xr[k];
+            out[(size_t)m * N + n] = (float)s;
+        }
+    }
+}
+
+void oracle_quantize_rows_i8_bf16(int8_t *q, float *scales, const uint16_t *W, int N, int K) {
+    for (int n = 0; n < N; n++) {
+        const uint16_t *wr = W + (size_t)n * K;
+        float amax = 0.0f;
+        for (int k = 0; k < K; k++) {
+            const float a = fabsf(oracle_bf16_to_f32(wr[k]));
+            if (a > amax) amax = a;
+        }
+        const float scale = amax / 127.0f;
+        scales[n] = scale;
+        for (int k = 0; k < K; k++) {
+            float v = scale > 0.0f ? roundf(oracle_bf16_to_f32(wr[k]) / scale) : 0.0f;
+            if (v > 127.0f) v = 127.0f;
+            if (v < -127.0f) v = -127.0f;
+            q[(size_t)n * K + k] = (int8_t)(int)v;
+        }
+    }
+}
+
+/* ---------------------------------------------------------------------------
  * Causal dilated conv1d, channels-first, groups == 1 (voc_conv1d_causal,
  * src/tts_vocoder_ops.c:44-147): the input is left-padded with
  * dilation * (kernel - 1) zeros, so tap k of output t reads

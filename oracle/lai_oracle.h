@@ -70,6 +70,21 @@ void oracle_add_bf16(uint16_t *x, const uint16_t *y, int64_t n);
 /* ---- linear_bf16 (src/tts_native.c:66-79): out[M,N] = in[M,K] @ W[N,K]^T, W BF16 ---- */
 void oracle_linear_bf16(float *out, const float *in, const uint16_t *W, int M, int K, int N);
 
+/* ---- the reference's other GPU weight formats (src/tts_pipeline.h:37-40,
+ * src/tts_native.c:1185-1240; INT8 recipe tools/asr_benchmarks.md:342-352) ----
+ * FP16 weights; INT8 weights with per-row scales, out = (sum_k q[n,k] x[m,k]) * scale[n];
+ * F32 weights. oracle_quantize_rows_i8_bf16: scale = max|row| / 127 (F32),
+ * q = roundf(w / scale) clamped to +-127, an all-zero row scale 0. IEEE binary16 <-> F32
+ * conversions (exact decode; round-to-nearest-even encode, overflow to inf). */
+float oracle_f16_to_f32(uint16_t h);
+uint16_t oracle_f32_to_f16(float f);
+void oracle_f32_to_f16_array(uint16_t *dst, const float *src, int64_t n);
+void oracle_linear_f16(float *out, const float *in, const uint16_t *W, int M, int K, int N);
+void oracle_linear_i8(float *out, const float *in, const int8_t *W, const float *scales, int M,
+                      int K, int N);
+void oracle_linear_f32(float *out, const float *in, const float *W, int M, int K, int N);
+void oracle_quantize_rows_i8_bf16(int8_t *q, float *scales, const uint16_t *W, int N, int K);
+
 /* ---- vocoder ResUnit, channels-first [C, T] F32 as the reference stores it ----
  * voc_conv1d_causal (src/tts_vocoder_ops.c:44-147, groups == 1): w [c_out, c_in, kernel] */
 void oracle_voc_conv1d_causal(float *out, const float *in, const float *w, const float *bias,

@@ -23,6 +23,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 _F = ctypes.POINTER(ctypes.c_float)
 _U16 = ctypes.POINTER(ctypes.c_uint16)
 _I32 = ctypes.POINTER(ctypes.c_int32)
+_I8 = ctypes.POINTER(ctypes.c_int8)
 _c_int, _c_float, _c_i64 = ctypes.c_int, ctypes.c_float, ctypes.c_int64
 
 
@@ -101,6 +102,11 @@ def _declare(lib: ctypes.CDLL) -> None:
         "oracle_layer_chain_f32": [_F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _F, _F,
                                    _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float],
         "oracle_linear_bf16": [_F, _F, _U16, _c_int, _c_int, _c_int],
+        "oracle_linear_f16": [_F, _F, _U16, _c_int, _c_int, _c_int],
+        "oracle_linear_i8": [_F, _F, _I8, _F, _c_int, _c_int, _c_int],
+        "oracle_linear_f32": [_F, _F, _F, _c_int, _c_int, _c_int],
+        "oracle_quantize_rows_i8_bf16": [_I8, _F, _U16, _c_int, _c_int],
+        "oracle_f32_to_f16_array": [_U16, _F, _c_i64],
         "oracle_decode_attention": [_F, _F, _F, _F, _I32, _c_int, _c_int, _c_int, _c_int,
                                     _c_int, _c_float],
         "oracle_repetition_penalty": [_F, _c_int, _I32, _c_int, _c_float],
@@ -336,6 +342,60 @@ def linear_bf16(x, W, lib=None):
     N = W.shape[0]
     out = np.empty((M, N), np.float32)
     lib.oracle_linear_bf16(ptr(out), ptr(x), ptr(W, _U16), M, K, N)
+    return out
+
+
+def linear_f16(x, W, lib=None):
+    """out[M,N] = x[M,K] @ W[N,K]^T with W as IEEE binary16 bit patterns."""
+    lib = lib or load()
+    x = np.ascontiguousarray(x, np.float32)
+    W = np.ascontiguousarray(W, np.uint16)
+    M, K = x.shape
+    out = np.empty((M, W.shape[0]), np.float32)
+    lib.oracle_linear_f16(ptr(out), ptr(x), ptr(W, _U16), M, K, W.shape[0])
+    return out
+
+
+def linear_i8(x, q, scales, lib=None):
+    """out[M,N] = (x[M,K] @ q[N,K]^T) * scales[N] with INT8 q."""
+    lib = lib or load()
+    x = np.ascontiguousarray(x, np.float32)
+    q = np.ascontiguousarray(q, np.int8)
+    scales = np.ascontiguousarray(scales, np.float32)
+    M, K = x.shape
+    out = np.empty((M, q.shape[0]), np.float32)
+    lib.oracle_linear_i8(ptr(out), ptr(x), ptr(q, _I8), ptr(scales), M, K, q.shape[0])
+    return out
+
+
+def linear_f32(x, W, lib=None):
+    """out[M,N] = x[M,K] @ W[N,K]^T with F32 W."""
+    lib = lib or load()
+    x = np.ascontiguousarray(x, np.float32)
+    W = np.ascontiguousarray(W, np.float32)
+    M, K = x.shape
+    out = np.empty((M, W.shape[0]), np.float32)
+    lib.oracle_linear_f32(ptr(out), ptr(x), ptr(W), M, K, W.shape[0])
+    return out
+
+
+def quantize_rows_i8_bf16(W, lib=None):
+    """BF16 bit patterns W [N, K] -> (INT8 q [N, K], F32 scales [N])."""
+    lib = lib or load()
+    W = np.ascontiguousarray(W, np.uint16)
+    N, K = W.shape
+    q = np.empty((N, K), np.int8)
+    scales = np.empty(N, np.float32)
+    lib.oracle_quantize_rows_i8_bf16(ptr(q, _I8), ptr(scales), ptr(W, _U16), N, K)
+    return q, scales
+
+
+def f32_to_f16_bits(x, lib=None):
+    """F32 values -> IEEE binary16 bit patterns, round to nearest even."""
+    lib = lib or load()
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty(x.shape, np.uint16)
+    lib.oracle_f32_to_f16_array(ptr(out, _U16), ptr(x), x.size)
     return out
 
 

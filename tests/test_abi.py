@@ -100,6 +100,16 @@ P = V(16)  # a non-NULL dummy pointer: never dereferenced, the checks fail first
      lai.LAI_ERR_ALIAS),
     (lambda l: l.lai_gemv_bf16w_f32(V(256), V(1 << 30), None, 1e-6, P, 1, 60000, 8, None),
      lai.LAI_ERR_TOOBIG),
+    # other weight formats: INT8 needs its scales; odd SwiGLU width; quantizer / converter
+    (lambda l: l.lai_gemv_i8w_f32(P, V(1 << 20), None, 1e-6, P, None, 1, 64, 8, None),
+     lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_gemv_swiglu_f16w_f32(P, V(1 << 20), None, 1e-6, P, 1, 64, 0, None),
+     lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_gemv_residual_f32w_f32(V(256), V(256), P, 1, 64, 8, None), lai.LAI_ERR_ALIAS),
+    (lambda l: l.lai_quantize_rows_i8_bf16(P, P, P, 4, 0, None), lai.LAI_ERR_INVALID),
+    (lambda l: l.lai_quantize_rows_i8_bf16(V(4096), V(1 << 20), V(4096 + 16), 4, 64, None),
+     lai.LAI_ERR_ALIAS),
+    (lambda l: l.lai_convert_bf16_to_f16(V(4096), V(4096 + 2), 64, None), lai.LAI_ERR_ALIAS),
 ])
 def test_argument_checks(call, want):
     assert call(lai.load()) == want

@@ -106,3 +106,93 @@ def test_gemv_argument_checks():
                                        None) == lai.LAI_ERR_INVALID
     assert L.lai_gemv_bf16w_f32(P, ctypes.c_void_p(1 << 30), None, 1e-6, P, 1, 60000, 8,
                                 None) == lai.LAI_ERR_TOOBIG
+
+
+# ---- the reference's other GPU weight formats: FP16, INT8 + per-row scale, F32 ----------
+def make_fmt(fmt, N, K, seed):
+    """Weights in format fmt on the device + their oracle product function."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    Wf = torch.randn(N, K, generator=g) / np.sqrt(K)
+    if fmt == "f16":
+        W = Wf.to(torch.float16)
+        return W.to(DEV), None, lambda xn: oracle.linear_f16(xn, W.view(torch.int16).numpy().view(np.uint16))
+    if fmt == "f32":
+        return Wf.to(DEV), None, lambda xn: oracle.linear_f32(xn, Wf.numpy())
+    Wb = Wf.to(torch.bfloat16)
+    q, s = oracle.quantize_rows_i8_bf16(wbits(Wb))
+    return (torch.from_numpy(q).to(DEV), torch.from_numpy(s).to(DEV),
+            lambda xn: oracle.linear_i8(xn, q, s))
+
+
+FMT_SHAPES = [(1, 1024, 2048), (1, 2048, 1024), (4, 1024, 512), (8, 2048, 64), (3, 100, 37),
+              (1, 40, 24)]
+
+
+@pytest.mark.parametrize("fmt", ["f16", "i8", "f32"])
+@pytest.mark.parametrize("M,K,N", FMT_SHAPES)
+@pytest.mark.parametrize("norm", [False, True])
+def test_gemv_formats(fmt, M, K, N, norm):
+    W, sc, ref = make_fmt(fmt, N, K, M + K)
+    x, _, w = make(M, K, N, 7)
+    y = lai.gemv(x.to(DEV), W, w.to(DEV) if norm else None, 1e-6, scales=sc)
+    torch.cuda.synchronize()
+    xn = oracle.rms_norm(x.numpy(), w.numpy(), 1e-6) if norm else x.numpy()
+    assert max_rel_err(y.cpu().numpy(), ref(xn)) <= TOL_F32
+
+
+@pytest.mark.parametrize("fmt", ["f16", "i8", "f32"])
+@pytest.mark.parametrize("M,K,N", [(1, 3072, 1024), (5, 512, 96), (2, 48, 17)])
+def test_gemv_residual_formats(fmt, M, K, N):
+    W, sc, ref = make_fmt(fmt, N, K, 11)
+    a, _, _ = make(M, K, N, 12)
+    x = torch.randn(M, N)
+    xd = x.to(DEV)
+    lai.gemv_residual(xd, a.to(DEV), W, scales=sc)
+    torch.cuda.synchronize()
+    assert max_rel_err(xd.cpu().numpy(), oracle.add_inplace(x.numpy(), ref(a.numpy()))) <= TOL_F32
+
+
+@pytest.mark.parametrize("fmt", ["f16", "i8", "f32"])
+@pytest.mark.parametrize("M,K,inter", [(1, 1024, 3072), (3, 512, 96), (1, 40, 7)])
+def test_gemv_swiglu_formats(fmt, M, K, inter):
+    W, sc, ref = make_fmt(fmt, 2 * inter, K, 13)
+    x, _, w = make(M, K, 2 * inter, 14)
+    out = lai.gemv_swiglu(x.to(DEV), W, w.to(DEV), 1e-6, scales=sc)
+    torch.cuda.synchronize()
+    gate_up = ref(oracle.rms_norm(x.numpy(), w.numpy(), 1e-6))
+    assert max_rel_err(out.cpu().numpy(), oracle.swiglu_multiply(gate_up, inter)) <= TOL_F32
+
+
+@pytest.mark.parametrize("N,K", [(2048, 1024), (37, 100), (5, 1)])
+def test_quantize_rows_i8_bit_exact(N, K):
+    g = torch.Generator(device="cpu").manual_seed(N)
+    Wb = (torch.randn(N, K, generator=g) * 0.05).to(torch.bfloat16)
+    Wb[0] = 0  # all-zero row: scale 0
+    q, s = lai.quantize_rows_i8(Wb.to(DEV))
+    qo, so = oracle.quantize_rows_i8_bf16(wbits(Wb))
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), so.view(np.uint32))
+    assert np.array_equal(q.cpu().numpy(), qo)
+
+
+def test_convert_bf16_to_f16_bit_exact():
+    g = torch.Generator(device="cpu").manual_seed(3)
+    x = torch.randn(1 << 16, generator=g) * torch.pow(10.0, torch.randint(-8, 6, (1 << 16,),
+                                                                        generator=g).float())
+    x[:6] = torch.tensor([0.0, -0.0, 65504.0, 70000.0, float("inf"), 2.0 ** -24])
+    xb = x.to(torch.bfloat16)
+    got = lai.convert_bf16_to_f16(xb.to(DEV)).cpu().view(torch.int16).numpy().view(np.uint16)
+    want = oracle.f32_to_f16_bits(xb.float().numpy())
+    assert np.array_equal(got, want)
+
+
+def test_i8_decode_layer_tracks_bf16():
+    # quantising a layer's weights changes its outputs by the quantisation error only
+    # (scale / 2 per weight), the reference's int8 trade-off
+    M, K, N = 1, 2048, 2048
+    x, W, _ = make(M, K, N, 21)
+    q, s = lai.quantize_rows_i8(W.to(DEV))
+    y8 = lai.gemv(x.to(DEV), q, scales=s)
+    y16 = lai.gemv(x.to(DEV), W.to(DEV))
+    torch.cuda.synchronize()
+    bound = (s.cpu() / 2)[None, :] * x.abs().sum(1, keepdim=True)  # |sum (w - q s) x| bound
+    assert ((y8 - y16).abs().cpu() <= bound + 1e-5).all()
