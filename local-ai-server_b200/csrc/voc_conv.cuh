@@ -110,18 +110,42 @@ __device__ __forceinline__ void store4(float *p, float a, float b, float c, floa
     *reinterpret_cast<float4 *>(p) = make_float4(a, b, c, d);
 }
 
+// Per-channel epilogue parameters of channels [c, c + 4), loaded once per channel group and
+// reused for every row the lane finishes (scalar loads: the caller's arrays need only
+// 4-byte alignment).
+struct EpiParams {
+    float bias[4], p1[4], p2[4];  // p1, p2: snake ea, ieb; or gamma (kEpiScaleResidual) in p1
+};
+
+template <int EPI>
+__device__ __forceinline__ EpiParams epi_params(const ConvArgs &a, int c) {
+    EpiParams q;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        q.bias[i] = __ldg(a.bias + c + i);
+        q.p1[i] = q.p2[i] = 0.0f;
+        if (EPI == kEpiScaleResidual) {
+            q.p1[i] = __ldg(a.gamma + c + i);
+        } else if (EPI != kEpiGelu && a.ea != nullptr) {
+            q.p1[i] = __ldg(a.ea + c + i);
+            q.p2[i] = __ldg(a.ieb + c + i);
+        }
+    }
+    return q;
+}
+
 // Epilogue for 4 finished sums of output row `row` (global index), channels [c, c + 4).
 // `xr` holds x[row, c..c+3] for the residual epilogues, loaded earlier.
 template <int PASSES, int EPI>
-__device__ __forceinline__ void epilogue4(const ConvArgs &a, float (&v)[4], const float4 &xr,
-                                          size_t row, int c) {
+__device__ __forceinline__ void epilogue4(const ConvArgs &a, const EpiParams &q, float (&v)[4],
+                                          const float4 &xr, size_t row, int c) {
     const size_t off = row * (size_t)a.c_out + c;
 #pragma unroll
-    for (int i = 0; i < 4; i++) v[i] += __ldg(a.bias + c + i);
+    for (int i = 0; i < 4; i++) v[i] += q.bias[i];
     if (EPI == kEpiScaleResidual) {  // x = (W h + b) * gamma + x  (run_convnext order)
         const float r[4] = {xr.x, xr.y, xr.z, xr.w};
 #pragma unroll
-        for (int i = 0; i < 4; i++) v[i] = v[i] * __ldg(a.gamma + c + i) + r[i];
+        for (int i = 0; i < 4; i++) v[i] = v[i] * q.p1[i] + r[i];
         store4(a.x + off, v[0], v[1], v[2], v[3]);
         return;
     }
@@ -140,7 +164,7 @@ __device__ __forceinline__ void epilogue4(const ConvArgs &a, float (&v)[4], cons
         if (EPI == kEpiGelu)
             v[i] = 0.5f * v[i] * (1.0f + erff(v[i] * 0.7071067811865475f));  // voc_gelu
         else
-            v[i] = snake1(v[i], __ldg(a.ea + c + i), __ldg(a.ieb + c + i));
+            v[i] = snake1(v[i], q.p1[i], q.p2[i]);
         hi[i] = umma::tf32_round(v[i]);
     }
     store4(a.out_hi + off, hi[0], hi[1], hi[2], hi[3]);
@@ -333,6 +357,7 @@ conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
 #pragma unroll
             for (int g = 0; g < L::kHalf / GW; g++) {
                 const int c = n0 + half * L::kHalf + g * GW + c4;
+                const EpiParams prm = epi_params<EPI>(a, c);
 #pragma unroll
                 for (int i = 0; i < GW; i++) buf[lane * kEpiPitch + i] = sum[g * GW + i];
                 __syncwarp();
@@ -358,7 +383,7 @@ conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
                         const int64_t orow = out_row(row0 + r);
                         if (orow >= 0)
                             epilogue4<PASSES, EPI>(
-                                a, v,
+                                a, prm, v,
                                 EPI == kEpiResidual || EPI == kEpiScaleResidual ? xr[p] : xr[0],
                                 (size_t)orow, c);
                     }
