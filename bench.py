@@ -789,6 +789,96 @@ def cpu_sampling_rate(rows: int, vocab: int, top_k: int, temperature: float, pen
     return {"rows_per_s": rows * n / el, "threads": 1, "passes": n, "seconds": el}
 
 
+def cpu_tts_frame_rate(min_seconds: float, frames: int | None = None) -> dict:
+    """run_decode_loop's frame (config d1) on the host cores: the same steps as runner.TtsFrame
+    restated with the oracle's C functions in their timed build (liblai_cpuref.so: -O2 -mavx2
+    -ffast-math, OpenMP over output rows, float sums) -- RMSNorm, the BF16 linear, per-head
+    q/k norm + RoPE, cache attention, SwiGLU, repetition penalty, top-k -- with distinct
+    synthetic weights per layer, so the host streams the same 1.7 GB of BF16 weights per frame
+    as the device. The code predictor runs each row once against a 16-row cache, as on the
+    device (the reference's recompute of all rows per sub-code does more work). Returns
+    frames/s."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle
+    import runner
+    lib = oracle.load("liblai_cpuref.so")
+    c = runner.TtsConfig()
+    H, qd, kvd, hd = c.hidden, c.n_q * c.head_dim, c.n_kv * c.head_dim, c.head_dim
+    rng = np.random.default_rng(3)
+    pool = rng.standard_normal(1 << 22, dtype=np.float32)
+    offs = iter(rng.integers(0, 1 << 21, 4096))
+
+    def w(n, k, scale=None):  # distinct arrays (same bytes streamed), values tiled from a pool
+        x = np.resize(pool[next(offs):], (n, k)) * np.float32(scale or k ** -0.5)
+        return (x.view(np.uint32) >> 16).astype(np.uint16)
+
+    def nrm(n):
+        return (1 + 0.02 * rng.standard_normal(n)).astype(np.float32)
+
+    def layer(inter):
+        return {"wqkv": w(qd + 2 * kvd, H), "wo": w(H, qd), "wgu": w(2 * inter, H),
+                "wd": w(H, inter), "in": nrm(H), "post": nrm(H), "qn": nrm(hd), "kn": nrm(hd)}
+
+    talker = [layer(c.inter) for _ in range(c.layers)]
+    cp = [layer(c.cp_inter) for _ in range(c.cp_layers)]
+    head, embed = w(c.talker_vocab, H), w(c.talker_vocab, H, 0.5)
+    cp_heads = [w(c.codec_vocab, H) for _ in range(c.groups - 1)]
+    cp_embed = [w(c.codec_vocab, H, 0.5) for _ in range(c.groups - 1)]
+    fnorm, cnorm = nrm(H), nrm(H)
+    max_seq = 256
+    ang = np.arange(max_seq)[:, None] * (1.0 / c.theta ** (np.arange(0, hd, 2) / hd))[None]
+    cos_t = np.concatenate([np.cos(ang), np.cos(ang)], 1).astype(np.float32)
+    sin_t = np.concatenate([np.sin(ang), np.sin(ang)], 1).astype(np.float32)
+    kc = np.zeros((c.layers, 1, max_seq, kvd), np.float32)
+    vc = np.zeros_like(kc)
+    ckc = np.zeros((c.cp_layers, 1, c.groups, kvd), np.float32)
+    cvc = np.zeros_like(ckc)
+
+    def run_layers(x, layers, kcs, vcs, pos, inter):
+        p = np.array([pos], np.int32)
+        for i, L in enumerate(layers):
+            qkv = oracle.linear_bf16(oracle.rms_norm(x, L["in"], c.eps, lib), L["wqkv"], lib)
+            q, k = oracle.qk_norm_rope(qkv[:, :qd], qkv[:, qd:qd + kvd], L["qn"], L["kn"], cos_t,
+                                       sin_t, p, c.n_q, c.n_kv, hd, c.eps, bf16=False, lib=lib)
+            kcs[i, 0, pos], vcs[i, 0, pos] = k[0], qkv[0, qd + kvd:]
+            a = oracle.decode_attention(q, kcs[i], vcs[i], p, c.n_q, c.n_kv, hd, lib=lib)
+            x = oracle.add_inplace(x, oracle.linear_bf16(a, L["wo"], lib), lib)
+            gu = oracle.linear_bf16(oracle.rms_norm(x, L["post"], c.eps, lib), L["wgu"], lib)
+            x = oracle.add_inplace(
+                x, oracle.linear_bf16(oracle.swiglu_multiply(gu, inter, lib), L["wd"], lib), lib)
+        return x
+
+    codec_sum = (0.5 * rng.standard_normal((1, H))).astype(np.float32)
+    hist = []
+    n, pos, t0 = 0, 0, time.perf_counter()
+    while True:
+        x = run_layers(codec_sum, talker, kc, vc, pos, c.inter)
+        hidden = oracle.rms_norm(x, fnorm, c.eps, lib)
+        lg = oracle.linear_bf16(hidden, head, lib)
+        keep = lg[0, c.eos]
+        lg[0, c.suppress_start:] = -1.0e9
+        lg[0, c.eos] = keep
+        lg = oracle.repetition_penalty(lg, np.array(hist, np.int32), c.penalty, lib)
+        cb0 = oracle.sample_topk(lg, c.temperature, c.top_k, rng.random(), lib)[0]
+        hist.append(cb0)
+        run_layers(hidden, cp, ckc, cvc, 0, c.cp_inter)
+        e = oracle.gather_bf16_to_f32(embed, np.array([cb0], np.int32), lib)
+        codec_sum = e.copy()
+        for j in range(c.groups - 1):
+            y = run_layers(e, cp, ckc, cvc, j + 1, c.cp_inter)
+            lgj = oracle.linear_bf16(oracle.rms_norm(y, cnorm, c.eps, lib), cp_heads[j], lib)
+            sub = oracle.sample_topk(lgj, c.temperature, c.top_k, rng.random(), lib)[0]
+            e = oracle.gather_bf16_to_f32(cp_embed[j], np.array([sub], np.int32), lib)
+            codec_sum = oracle.add_inplace(codec_sum, e, lib)
+        n, pos = n + 1, pos + 1
+        el = time.perf_counter() - t0
+        if (frames is not None and n >= frames) or (frames is None and el >= min_seconds):
+            break
+    return {"rows_per_s": n / el, "frames": n, "seconds": el,
+            "threads": len(os.sched_getaffinity(0))}
+
+
 def _e2e_copy_loop(work, launches, steps, pairs, world, dist):
     """Time `steps` steps of: copy every (device, pinned host) input in, the step's launches,
     copy outputs back. pairs: (inputs [(dev, host)], outputs [(host, dev)])."""
@@ -844,6 +934,8 @@ def run_single(args) -> None:
         work = runner.VocDecoder(t0=2000 // args.t_div, passes=args.passes, seed=seed)
     elif args.config == "v3":
         work = runner.VocFullDecoder(t_frames=500 // args.t_div, passes=args.passes, seed=seed)
+    elif args.config == "d1":
+        work = runner.TtsDecode(frames=args.warmup + args.steps + args.e2e_steps + 2, seed=seed)
     else:
         work = runner.SampleBatch(seed=seed)
     launches = work.launches(None)
@@ -923,6 +1015,14 @@ def run_single(args) -> None:
             outs = [(pin(work.audio), work.audio)]
             api = ("the 10 vocoder-decoder calls with the pre-transformer output copied in from and "
                    "the audio copied back to pinned host memory each step")
+        elif args.config == "d1":
+            tf = work.tf
+            ins = [(tf.u_frame, pin(tf.draws[:1])), (tf.trail_frame, pin(tf.trailing[:1]))]
+            outs = [(pin(tf.codes_frame), tf.codes_frame)]
+            launches = [lambda: tf.frame(graph=True, staged=True)]
+            api = ("one frame per step with its 16 sampling draws and trailing text embedding "
+                   "copied in from pinned host memory and its 16 codes copied back (the host "
+                   "needs cb0 every frame for the EOS check, src/tts_native.c:1100-1103)")
         elif args.config == "n1":
             ins = [(x, pin(x)) for x in work.x]
             outs = [(pin(x), x) for x in work.x]
@@ -964,6 +1064,14 @@ def run_single(args) -> None:
                              f"scaled to {work.t_frames} frames: the reference's USE_BLAS path "
                              "(its compiled SnakeBeta, depthwise conv, LayerNorm, GELU and final "
                              f"conv + OpenBLAS SGEMMs), host {cpu_model()}"}
+        elif args.config == "d1":
+            r = cpu_tts_frame_rate(args.cpu_seconds)
+            cpu = {"value": round(r["rows_per_s"], 3), "unit": "rows/s", "cores": r["threads"],
+                   "kind": "port",
+                   "sample": f"{r['frames']} frames ({r['seconds']:.1f} s) of the same frame "
+                             "restated with the oracle's timed C build (BF16 linears, norms, "
+                             "RoPE, cache attention, SwiGLU, penalty, top-k; OpenMP over output "
+                             f"rows), distinct weights per layer, host {cpu_model()}"}
         elif args.config == "n1":
             r = cpu_convnext_rate(work.stages, work.batch, args.cpu_seconds)
             cpu = {"value": round(r["rows_per_s"], 1), "unit": "rows/s", "cores": r["threads"],
@@ -1009,6 +1117,15 @@ def run_single(args) -> None:
                "frames": getattr(work, "t_frames", None), "batch": getattr(work, "batch", None),
                "audio_samples": getattr(work, "t_final", None), "passes": args.passes,
                "rows": "audio samples (24 kHz) per step"},
+        "d1": {"workload": "run_decode_loop frames of Qwen3-TTS 0.6B: talker step (28 layers, "
+                           "fused GEMVs, q/k norm + RoPE, KV-cache attention, codec head), "
+                           "cb0 suppression + penalty + top-k, 15 code-predictor sub-codes (5 "
+                           "layers, 16-row cache, lm_head, top-k, embedding feedback); BF16 "
+                           "weights, F32 activations; one CUDA graph per frame",
+               "layers": [28, 5], "hidden": 1024, "ffn": 3072, "codes_per_frame": 16,
+               "weight_bytes_per_frame": work.tf.weight_bytes_per_frame()
+               if args.config == "d1" else None,
+               "rows": "frames (16 codec codes = 80 ms of audio each)"},
         "s3": {"workload": "talker token sampling: repetition penalty + top-k 50 at temperature "
                            "0.9 over codec logits (vocab 3072), 64-token histories",
                "rows": "decode rows (one token drawn each)", "batch": getattr(work, "rows", None)},
@@ -1024,7 +1141,10 @@ def run_single(args) -> None:
         "data": "synthetic (seeded counter-based N(0,1) on device)", "config": desc,
         "per_kernel": per_kernel, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
         "gpu_launches": args.steps * {"n1": 3 * len(launches), "v2": 8 * len(launches),
-                                      "v3": 2 + 2 * 3 + 2 + 4 * 8 + 1}.get(args.config, len(launches)),
+                                      "v3": 2 + 2 * 3 + 2 + 4 * 8 + 1,
+                                      "d1": work.tf.launches_per_frame()
+                                      if args.config == "d1" else 0}.get(args.config,
+                                                                         len(launches)),
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
@@ -1103,6 +1223,15 @@ def run_reference(args) -> None:
                     ms_per_step=1000.0 * r["step_seconds"], scaling="weak", dtype="f32",
                     config={"workload": "tts_vocoder_run from the pre-transformer output to audio",
                             "config": "v3", "frames": 500, "batch": 1})
+    elif args.config == "d1":
+        r = cpu_tts_frame_rate(0.0, frames=max(1, min(args.steps, int(args.ref_budget / 2))))
+        cb = {"value": r["rows_per_s"], "unit": "rows/s", "cores": r["threads"], "kind": "port",
+              "sample": f"{r['frames']} frames of the run_decode_loop frame restated with the "
+                        "oracle's timed C build (the reference's qwen_* sources are not "
+                        f"vendored), host {cpu_model()}"}
+        line = dict(common, value=r["rows_per_s"], unit="rows/s",
+                    ms_per_step=1000.0 / r["rows_per_s"], scaling="weak", dtype="bf16 weights",
+                    config={"workload": "run_decode_loop frames, Qwen3-TTS 0.6B", "config": "d1"})
     elif args.config == "n1":
         stages = [(1024, 1000), (1024, 2000)]
         r = cpu_convnext_rate(stages, 8, 0.0, sample_t=500, steps=args.steps, warmup=args.warmup)
@@ -1590,7 +1719,7 @@ def main():
                     help="timed steps (default 2000; 20 for v1, whose step is ~0.1 s)")
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "g1", "g2", "v1", "v2", "v3",
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "d1", "g1", "g2", "v1", "v2", "v3",
                                          "a3", "n1", "s3"],
                     default="c2")
     ap.add_argument("--t-div", type=int, default=1,
@@ -1623,12 +1752,13 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)  # timing rule: at least 3 untimed warm-up steps
     if args.steps is None:
-        args.steps = {"v1": 20, "v2": 20, "v3": 20, "n1": 50, "a3": 200}.get(args.config, 2000)
+        args.steps = {"v1": 20, "v2": 20, "v3": 20, "n1": 50, "a3": 200, "d1": 50}.get(
+            args.config, 2000)
     if args.impl == "reference":
         run_reference(args)
     elif args.config == "v1":
         run_resunits(args)
-    elif args.config in ("a3", "n1", "s3", "v2", "v3"):
+    elif args.config in ("a3", "d1", "n1", "s3", "v2", "v3"):
         run_single(args)
     else:
         run_ours(args)

@@ -264,6 +264,17 @@ LAI_API int lai_sample_topk_f32(int32_t *out_tokens, float *logits, int vocab, i
                                 int history_stride, float penalty, float temperature, int top_k,
                                 const float *u, lai_stream_t stream);
 
+/* run_decode_loop's bookkeeping around the sampler, on the device so a decode frame needs no
+ * host round trip between its samples (src/tts_native.c:1092-1105):
+ *   lai_logits_mask_range_f32: logits[r, c] = value for lo <= c < hi, c != keep (the
+ *     suppression of [2048, 3072) except EOS with value -1e9);
+ *   lai_history_append_i32: history[r, history_len[r]++] = tokens[r]; a full row
+ *     (history_len[r] >= history_stride) is left as it is and sets LAI_DEVERR_POSITION. */
+LAI_API int lai_logits_mask_range_f32(float *logits, int vocab, int rows, int lo, int hi,
+                                      int keep, float value, lai_stream_t stream);
+LAI_API int lai_history_append_i32(int32_t *history, int32_t *history_len, const int32_t *tokens,
+                                   int rows, int history_stride, int *err, lai_stream_t stream);
+
 /* ---- vocoder BigVGAN ResUnits on tensor cores ------------------------------------------------
  * run_resunit(x, ru, C, T, scratch) (src/tts_vocoder.c:540-583) for n_units consecutive
  * units, as tts_vocoder_run calls them per block (src/tts_vocoder.c:725-728):

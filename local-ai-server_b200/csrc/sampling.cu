@@ -155,3 +155,60 @@ extern "C" int lai_sample_topk_f32(int32_t *out_tokens, float *logits, int vocab
         temperature, k, u);
     return launch_status();
 }
+
+namespace lai {
+namespace {
+
+__global__ void mask_range_kernel(float *logits, int64_t vocab, int rows, int lo, int hi,
+                                  int keep, float value) {
+    const int64_t n = (int64_t)rows * (hi - lo);
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / (hi - lo);
+        const int c = lo + (int)(i - r * (hi - lo));
+        if (c != keep) logits[r * vocab + c] = value;
+    }
+}
+
+__global__ void history_append_kernel(int32_t *history, int32_t *len, const int32_t *tokens,
+                                      int rows, int stride, int *err) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    const int n = len[r];
+    if (n < 0 || n >= stride) {  // full: the token is not recorded
+        if (err) atomicOr(err, LAI_DEVERR_POSITION);
+        return;
+    }
+    history[(int64_t)r * stride + n] = tokens[r];
+    len[r] = n + 1;
+}
+
+}  // namespace
+}  // namespace lai
+
+// Suppression before sampling (run_decode_loop, src/tts_native.c:1092-1095: logits
+// [suppress_start, vocab) set to -1e9 except EOS).
+extern "C" int lai_logits_mask_range_f32(float *logits, int vocab, int rows, int lo, int hi,
+                                         int keep, float value, lai_stream_t stream) {
+    using namespace lai;
+    if (!logits || vocab <= 0 || rows < 0 || lo < 0 || hi > vocab || lo > hi)
+        return LAI_ERR_INVALID;
+    if (rows == 0 || lo == hi) return LAI_OK;
+    const int64_t n = (int64_t)rows * (hi - lo);
+    mask_range_kernel<<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(logits, vocab, rows, lo,
+                                                                        hi, keep, value);
+    return launch_status();
+}
+
+// cb0_history[history_len++] = cb0 (src/tts_native.c:1105) for each row, on the device.
+extern "C" int lai_history_append_i32(int32_t *history, int32_t *history_len,
+                                      const int32_t *tokens, int rows, int history_stride,
+                                      int *err, lai_stream_t stream) {
+    using namespace lai;
+    if (!history || !history_len || !tokens || rows < 0 || history_stride <= 0)
+        return LAI_ERR_INVALID;
+    if (rows == 0) return LAI_OK;
+    history_append_kernel<<<(rows + 127) / 128, 128, 0, as_stream(stream)>>>(
+        history, history_len, tokens, rows, history_stride, err);
+    return launch_status();
+}

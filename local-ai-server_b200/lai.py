@@ -56,6 +56,8 @@ SIGNATURES: dict[str, tuple] = {
     "lai_gemv_residual_f32w_f32": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _vp]),
     "lai_gemv_swiglu_f32w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
     "lai_quantize_rows_i8_bf16": (_i32, [_vp, _vp, _vp, _i32, _i32, _vp]),
+    "lai_logits_mask_range_f32": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _f32, _vp]),
+    "lai_history_append_i32": (_i32, [_vp, _vp, _vp, _i32, _i32, _vp, _vp]),
     "lai_convert_bf16_to_f16": (_i32, [_vp, _vp, _i64, _vp]),
     "lai_decode_attention_scratch_bytes": (ctypes.c_size_t, [_i32, _i32, _i32, _i32]),
     "lai_decode_attention_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32,
@@ -310,6 +312,20 @@ def convert_bf16_to_f16(W, stream=None):
     out = torch.empty(W.shape, dtype=torch.float16, device=W.device)
     call("lai_convert_bf16_to_f16", _p(out), _p(W), W.numel(), _s(stream))
     return out
+
+
+def logits_mask_range(logits, lo, hi, keep=-1, value=-1.0e9, stream=None):
+    """logits [rows, vocab]: [lo, hi) set to value except column keep (in place)."""
+    rows, vocab = (1, logits.shape[0]) if logits.dim() == 1 else logits.shape
+    call("lai_logits_mask_range_f32", _p(logits), vocab, rows, lo, hi, keep, value, _s(stream))
+    return logits
+
+
+def history_append(history, history_len, tokens, err=None, stream=None):
+    """history [rows, stride] int32, history_len [rows] int32, tokens [rows] int32 (device)."""
+    rows, stride = (1, history.shape[0]) if history.dim() == 1 else history.shape
+    call("lai_history_append_i32", _p(history), _p(history_len), _p(tokens), rows, stride,
+         _p(err), _s(stream))
 
 
 def decode_attention_scratch(n_seqs, n_heads, n_kv_heads, max_seq, device="cuda"):

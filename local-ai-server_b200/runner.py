@@ -711,3 +711,249 @@ class DecodeLinear:
 
     def rows_per_launch(self) -> list[int]:
         return [self.cfg.m] * 4 * self.cfg.layers
+
+
+@dataclasses.dataclass(frozen=True)
+class TtsConfig:
+    """Shapes of run_decode_loop's per-frame work (src/tts_native.h:29-56). Defaults: the
+    Qwen3-TTS 0.6B talker (hidden 1024, FFN 3072, 28 layers) and its 5-layer code predictor
+    of the same width (mtp_project is then a copy, src/tts_native.c:88-99)."""
+    name: str = "qwen3-tts-0.6b"
+    hidden: int = 1024
+    inter: int = 3072
+    layers: int = 28
+    cp_inter: int = 3072
+    cp_layers: int = 5
+    n_q: int = 16
+    n_kv: int = 8
+    head_dim: int = 128
+    talker_vocab: int = 3072
+    codec_vocab: int = 2048
+    groups: int = 16
+    suppress_start: int = 2048
+    eos: int = 2150
+    max_seq: int = 4096
+    eps: float = 1e-6
+    theta: float = 1e6
+    temperature: float = 0.9
+    top_k: int = 50
+    penalty: float = 1.05
+
+
+class TtsFrame:
+    """One frame of run_decode_loop (src/tts_native.c:1042-1165) on the device, every step a
+    library call on one stream and every sampled token kept in device memory:
+
+      talker_forward(codec_sum) (:608-686): per layer RMSNorm + fused q|k|v GEMV, per-head
+        q/k RMSNorm + RoPE at the cache position, cache append + attention, o GEMV + residual,
+        RMSNorm + gate/up GEMV + SwiGLU, down GEMV + residual; final RMSNorm (the hidden state
+        the code predictor starts from) and the codec head GEMV -> 3072 logits;
+      logits [2048, 3072) except EOS -> -1e9, repetition penalty over the cb0 history, top-k
+        sampling -> cb0, appended to the history (:1092-1105);
+      the code predictor (:1110-1149): its input rows are the talker hidden state, cb0's codec
+        embedding, then each sub-code's embedding; for j = 0..14 the 5-layer transformer's last
+        row -> RMSNorm -> lm_head[j] -> top-k -> sub-code j + 1 -> embedding (talker space)
+        added into codec_sum;
+      codec_sum += the trailing text embedding (:1152-1156), the next frame's input.
+
+    The reference re-runs the code predictor over all rows for every sub-code
+    (code_predictor_forward, :689-760, no cache). Attention is causal, so the last row's
+    output depends only on the rows before it: this runs each row once against a 16-row KV
+    cache and gets the same result for the row that feeds lm_head[j] (15 + 1 row-steps per
+    frame instead of 2 + 3 + ... + 16 = 135).
+
+    Weights are synthetic BF16 (q, k, v rows concatenated; gate/up rows interleaved as the
+    reference's fused weight), norms ~1 + N(0, 0.02). The uniform draws are taken in order
+    from `draws` (16 per frame: cb0, then sub-codes 1..15), as rand() would be.
+    """
+
+    def __init__(self, cfg: TtsConfig, frames: int, seed: int = 77, device: str = "cuda"):
+        import torch
+        self.cfg, self.frames, self.device = cfg, frames, device
+        c = cfg
+        H, qd, kvd = c.hidden, c.n_q * c.head_dim, c.n_kv * c.head_dim
+        self.qd, self.kvd = qd, kvd
+        bf, f32 = torch.bfloat16, torch.float32
+        g = torch.Generator(device=device).manual_seed(seed)
+
+        def w(n, k, scale=None):
+            t = torch.randn((n, k), generator=g, device=device) * (scale or k ** -0.5)
+            return t.to(bf)
+
+        def nrm(n):
+            return (1.0 + 0.02 * torch.randn(n, generator=g, device=device)).to(f32)
+
+        def layer(inter):
+            return {"wqkv": w(qd + 2 * kvd, H), "wo": w(H, qd), "wgu": w(2 * inter, H),
+                    "wd": w(H, inter), "in_norm": nrm(H), "post_norm": nrm(H),
+                    "q_norm": nrm(c.head_dim), "k_norm": nrm(c.head_dim)}
+
+        self.talker = [layer(c.inter) for _ in range(c.layers)]
+        self.final_norm = nrm(H)
+        self.codec_head = w(c.talker_vocab, H)
+        self.codec_embed = w(c.talker_vocab, H, 0.5)
+        self.cp = [layer(c.cp_inter) for _ in range(c.cp_layers)]
+        self.cp_norm = nrm(H)
+        self.cp_heads = [w(c.codec_vocab, H) for _ in range(c.groups - 1)]
+        self.cp_embed = [w(c.codec_vocab, H, 0.5) for _ in range(c.groups - 1)]
+        self.trailing = (0.5 * torch.randn((frames, H), generator=g, device=device)).to(f32)
+        self.draws = torch.rand((frames, c.groups), generator=g, device=device)
+        # caches, tables, buffers
+        self.kc = [torch.zeros((1, c.max_seq, kvd), dtype=f32, device=device)
+                   for _ in range(c.layers)]
+        self.vc = [torch.zeros_like(k) for k in self.kc]
+        self.cp_kc = [torch.zeros((1, c.groups, kvd), dtype=f32, device=device)
+                      for _ in range(c.cp_layers)]
+        self.cp_vc = [torch.zeros_like(k) for k in self.cp_kc]
+        pos_all = torch.arange(c.max_seq, dtype=torch.int32, device=device)
+        self.cos, self.sin = lai.rope_table(pos_all, c.max_seq, c.head_dim, c.theta,
+                                            device=device)
+        self.cp_pos = torch.arange(c.groups, dtype=torch.int32, device=device)
+        self.scr = lai.decode_attention_scratch(1, c.n_q, c.n_kv, c.max_seq, device)
+        self.cp_scr = lai.decode_attention_scratch(1, c.n_q, c.n_kv, c.groups, device)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=device)
+        self.x = torch.zeros((1, H), dtype=f32, device=device)
+        self.qkv = torch.empty((1, qd + 2 * kvd), dtype=f32, device=device)
+        self.attn = torch.empty((1, qd), dtype=f32, device=device)
+        self.act = torch.empty((1, max(c.inter, c.cp_inter)), dtype=f32, device=device)
+        self.hidden = torch.empty((1, H), dtype=f32, device=device)
+        self.logits = torch.empty((1, c.talker_vocab), dtype=f32, device=device)
+        self.cp_logits = torch.empty((1, c.codec_vocab), dtype=f32, device=device)
+        self.emb = torch.empty((1, H), dtype=f32, device=device)
+        self.codec_sum = (0.5 * torch.randn((1, H), generator=g, device=device)).to(f32)
+        self.codes = torch.zeros((frames, c.groups), dtype=torch.int32, device=device)
+        self.history = torch.zeros((1, frames), dtype=torch.int32, device=device)
+        self.hist_len = torch.zeros(1, dtype=torch.int32, device=device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        # the frame body reads and writes only these fixed buffers, so it can be captured
+        # once as a CUDA graph and replayed for every frame
+        self.u_frame = torch.zeros((1, c.groups), dtype=f32, device=device)
+        self.trail_frame = torch.zeros((1, H), dtype=f32, device=device)
+        self.codes_frame = torch.zeros((1, c.groups), dtype=torch.int32, device=device)
+        self.frame_idx = 0
+        self.record = None  # list: logits before each sampling (tests)
+        self.graph = None
+
+    def _layers(self, layers, kc, vc, pos, scr, inter, stream):
+        c = self.cfg
+        q = self.qkv[:, :self.qd]
+        k = self.qkv[:, self.qd:self.qd + self.kvd]
+        v = self.qkv[:, self.qd + self.kvd:]
+        act = self.act[:, :inter]
+        for i, L in enumerate(layers):
+            lai.gemv(self.x, L["wqkv"], L["in_norm"], c.eps, y=self.qkv, stream=stream)
+            lai.qk_norm_rope(q, k, L["q_norm"], L["k_norm"], self.cos, self.sin, pos, c.n_q,
+                             c.n_kv, c.head_dim, c.eps, err=self.err, stream=stream)
+            lai.decode_attention(q, k, v, kc[i], vc[i], pos, c.n_q, c.n_kv, scratch=scr,
+                                 out=self.attn, err=self.err, stream=stream)
+            lai.gemv_residual(self.x, self.attn, L["wo"], stream=stream)
+            lai.gemv_swiglu(self.x, L["wgu"], L["post_norm"], c.eps, out=act, stream=stream)
+            lai.gemv_residual(self.x, act, L["wd"], stream=stream)
+
+    def _sample(self, logits, j, history, stream):
+        c = self.cfg
+        if self.record is not None:
+            self.record.append(logits.clone())
+        out = self.codes_frame[:, j]
+        u = self.u_frame[:, j]
+        if history:
+            lai.sample_topk(logits, u, c.temperature, c.top_k, self.history, self.hist_len,
+                            c.penalty, out=out, stream=stream)
+        else:
+            lai.sample_topk(logits, u, c.temperature, c.top_k, out=out, stream=stream)
+        return out
+
+    def _gather(self, table, ids, stream):
+        lai.call("lai_embed_gather_bf16_to_f32", lai._p(self.emb), lai._p(table), lai._p(ids),
+                 1, self.cfg.hidden, table.shape[0], lai._p(self.err), lai._s(stream))
+
+    def frame(self, graph: bool = False, staged: bool = False):
+        """Run one frame; its 16 codes land in codes[frame] (and codes_frame). graph: replay
+        the frame body as one CUDA graph (captured on first use) instead of launching its ~750
+        kernels. staged: the caller has already put this frame's 16 draws and trailing
+        embedding into u_frame and trail_frame."""
+        import torch
+        f = self.frame_idx
+        if f >= self.frames:
+            raise RuntimeError("frame capacity reached")
+        if not staged:
+            self.u_frame.copy_(self.draws[f:f + 1])
+            self.trail_frame.copy_(self.trailing[f:f + 1])
+        if not graph:
+            self._body(None)
+        else:
+            if self.graph is None:
+                self.graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(self.graph):
+                    self._body(None)
+                # capture records without running: replay for this frame
+            self.graph.replay()
+        self.codes[f:f + 1].copy_(self.codes_frame)
+        self.frame_idx += 1
+
+    def _body(self, stream):
+        c = self.cfg
+        # talker step on codec_sum at the cache position
+        self.x.copy_(self.codec_sum)
+        self._layers(self.talker, self.kc, self.vc, self.pos, self.scr, c.inter, stream)
+        lai.rmsnorm(self.x, self.final_norm, c.eps, y=self.hidden, stream=stream)
+        lai.gemv(self.hidden, self.codec_head, y=self.logits, stream=stream)
+        lai.logits_mask_range(self.logits, c.suppress_start, c.talker_vocab, keep=c.eos,
+                              stream=stream)
+        cb0 = self._sample(self.logits, 0, True, stream)
+        lai.history_append(self.history, self.hist_len, cb0, err=self.err, stream=stream)
+        # code predictor: row 0 = hidden state, row 1 = cb0's embedding, then sub-codes
+        self.x.copy_(self.hidden)
+        self._layers(self.cp, self.cp_kc, self.cp_vc, self.cp_pos[0:1], self.cp_scr,
+                     c.cp_inter, stream)
+        self._gather(self.codec_embed, cb0, stream)
+        self.codec_sum.copy_(self.emb)
+        for j in range(c.groups - 1):
+            self.x.copy_(self.emb)
+            self._layers(self.cp, self.cp_kc, self.cp_vc, self.cp_pos[j + 1:j + 2], self.cp_scr,
+                         c.cp_inter, stream)
+            lai.rmsnorm(self.x, self.cp_norm, c.eps, y=self.hidden, stream=stream)
+            lai.gemv(self.hidden, self.cp_heads[j], y=self.cp_logits, stream=stream)
+            sub = self._sample(self.cp_logits, j + 1, False, stream)
+            self._gather(self.cp_embed[j], sub, stream)
+            lai.add(self.codec_sum, self.emb, stream=stream)
+        lai.add(self.codec_sum, self.trail_frame, stream=stream)
+        self.pos.add_(1)
+
+    def launches_per_frame(self) -> int:
+        c = self.cfg
+        per_layer = 6
+        return (c.layers * per_layer + 5 + (c.groups) * c.cp_layers * per_layer
+                + (c.groups - 1) * 5 + 1 + 1)
+
+    def weight_bytes_per_frame(self) -> int:
+        """Weights streamed from HBM per frame: every talker layer once, every code-predictor
+        layer once per row (16 rows), the codec head once, the 15 lm_heads once each."""
+        c = self.cfg
+        H, qd, kvd = c.hidden, self.qd, self.kvd
+
+        def layer(inter):
+            return 2 * ((qd + 2 * kvd) * H + H * qd + 2 * inter * H + H * inter)
+        return (c.layers * layer(c.inter) + c.groups * c.cp_layers * layer(c.cp_inter)
+                + 2 * c.talker_vocab * H + (c.groups - 1) * 2 * c.codec_vocab * H)
+
+
+class TtsDecode:
+    """Config d1: run_decode_loop frames of the Qwen3-TTS 0.6B talker + code predictor
+    (TtsFrame with TtsConfig defaults), one frame per step, each replayed as one CUDA graph.
+    Rows are frames (16 codec codes each, 80 ms of 24 kHz audio at 12.5 frames/s)."""
+
+    def __init__(self, frames: int, seed: int = 77, device: str = "cuda"):
+        self.cfg = TtsConfig()
+        self.tf = TtsFrame(self.cfg, frames, seed=seed, device=device)
+        self.kernel_names = ("tts_frame",)
+        self.err = self.tf.err
+
+    def launches(self, stream=None):
+        return [lambda: self.tf.frame(graph=True)]
+
+    def bytes_per_launch(self) -> list[int]:
+        return [self.tf.weight_bytes_per_frame()]
+
+    def rows_per_launch(self) -> list[int]:
+        return [1]
