@@ -816,10 +816,8 @@ class TtsFrame:
         self.qkv = torch.empty((1, qd + 2 * kvd), dtype=f32, device=device)
         self.attn = torch.empty((1, qd), dtype=f32, device=device)
         self.act = torch.empty((1, max(c.inter, c.cp_inter)), dtype=f32, device=device)
-        self.hidden = torch.empty((1, H), dtype=f32, device=device)
         self.logits = torch.empty((1, c.talker_vocab), dtype=f32, device=device)
         self.cp_logits = torch.empty((1, c.codec_vocab), dtype=f32, device=device)
-        self.emb = torch.empty((1, H), dtype=f32, device=device)
         self.codec_sum = (0.5 * torch.randn((1, H), generator=g, device=device)).to(f32)
         self.codes = torch.zeros((frames, c.groups), dtype=torch.int32, device=device)
         self.history = torch.zeros((1, frames), dtype=torch.int32, device=device)
@@ -863,8 +861,8 @@ class TtsFrame:
             lai.sample_topk(logits, u, c.temperature, c.top_k, out=out, stream=stream)
         return out
 
-    def _gather(self, table, ids, stream):
-        lai.call("lai_embed_gather_bf16_to_f32", lai._p(self.emb), lai._p(table), lai._p(ids),
+    def _gather(self, table, ids, stream):  # one embedding row into x
+        lai.call("lai_embed_gather_bf16_to_f32", lai._p(self.x), lai._p(table), lai._p(ids),
                  1, self.cfg.hidden, table.shape[0], lai._p(self.err), lai._s(stream))
 
     def frame(self, graph: bool = False, staged: bool = False):
@@ -896,35 +894,36 @@ class TtsFrame:
         # talker step on codec_sum at the cache position
         self.x.copy_(self.codec_sum)
         self._layers(self.talker, self.kc, self.vc, self.pos, self.scr, c.inter, stream)
-        lai.rmsnorm(self.x, self.final_norm, c.eps, y=self.hidden, stream=stream)
-        lai.gemv(self.hidden, self.codec_head, y=self.logits, stream=stream)
+        lai.rmsnorm(self.x, self.final_norm, c.eps, y=self.x, stream=stream)  # hidden state
+        lai.gemv(self.x, self.codec_head, y=self.logits, stream=stream)
         lai.logits_mask_range(self.logits, c.suppress_start, c.talker_vocab, keep=c.eos,
                               stream=stream)
         cb0 = self._sample(self.logits, 0, True, stream)
         lai.history_append(self.history, self.hist_len, cb0, err=self.err, stream=stream)
-        # code predictor: row 0 = hidden state, row 1 = cb0's embedding, then sub-codes
-        self.x.copy_(self.hidden)
+        # code predictor: row 0 = the hidden state (already in x), row 1 = cb0's embedding,
+        # then each sub-code's; an embedding is gathered straight into x, the row's input
         self._layers(self.cp, self.cp_kc, self.cp_vc, self.cp_pos[0:1], self.cp_scr,
                      c.cp_inter, stream)
         self._gather(self.codec_embed, cb0, stream)
-        self.codec_sum.copy_(self.emb)
+        self.codec_sum.copy_(self.x)
         for j in range(c.groups - 1):
-            self.x.copy_(self.emb)
             self._layers(self.cp, self.cp_kc, self.cp_vc, self.cp_pos[j + 1:j + 2], self.cp_scr,
                          c.cp_inter, stream)
-            lai.rmsnorm(self.x, self.cp_norm, c.eps, y=self.hidden, stream=stream)
-            lai.gemv(self.hidden, self.cp_heads[j], y=self.cp_logits, stream=stream)
+            # final RMSNorm of the row folded into lm_head[j]'s GEMV
+            lai.gemv(self.x, self.cp_heads[j], self.cp_norm, c.eps, y=self.cp_logits,
+                     stream=stream)
             sub = self._sample(self.cp_logits, j + 1, False, stream)
             self._gather(self.cp_embed[j], sub, stream)
-            lai.add(self.codec_sum, self.emb, stream=stream)
+            lai.add(self.codec_sum, self.x, stream=stream)
         lai.add(self.codec_sum, self.trail_frame, stream=stream)
         self.pos.add_(1)
 
     def launches_per_frame(self) -> int:
+        """Library kernels per frame (the 2 tensor copies and the position add not counted)."""
         c = self.cfg
         per_layer = 6
-        return (c.layers * per_layer + 5 + (c.groups) * c.cp_layers * per_layer
-                + (c.groups - 1) * 5 + 1 + 1)
+        return (c.layers * per_layer + 2 + 3 + c.groups * c.cp_layers * per_layer + 1
+                + (c.groups - 1) * 4 + 1)
 
     def weight_bytes_per_frame(self) -> int:
         """Weights streamed from HBM per frame: every talker layer once, every code-predictor
