@@ -247,6 +247,19 @@ LAI_API int lai_decode_attention_f32(float *out, const float *q, const float *k_
                                      const int32_t *pos, int n_seqs, int n_heads, int n_kv_heads,
                                      int head_dim, int max_seq, float scale, void *scratch,
                                      int *err, lai_stream_t stream);
+/* The same launch with the decode step's per-head q/k RMSNorm and NeoX RoPE folded in
+ * (qwen_rms_norm_per_head + qwen_apply_rope_neox at the cache row, src/tts_native.c:644-648,
+ * then :650-656): q and k_new are read raw and left unmodified, the attention uses the
+ * normed, rotated q, and cache row pos receives the normed, rotated key. wq / wk [128] may be
+ * NULL (no norm); cos_t / sin_t [table_rows, 128] both NULL (no RoPE) or both given, row pos
+ * used; pos >= table_rows sets LAI_DEVERR_POSITION. */
+LAI_API int lai_decode_attention_qk_f32(float *out, const float *q, const float *k_new,
+                                        const float *v_new, float *k_cache, float *v_cache,
+                                        const int32_t *pos, int n_seqs, int n_heads,
+                                        int n_kv_heads, int head_dim, int max_seq, float scale,
+                                        const float *wq, const float *wk, const float *cos_t,
+                                        const float *sin_t, int64_t table_rows, float eps,
+                                        void *scratch, int *err, lai_stream_t stream);
 
 /* ---- token sampling on device logits ------------------------------------------------------
  * Per row r of logits [rows, vocab]: tts_apply_repetition_penalty(logits, vocab, history,

@@ -39,15 +39,56 @@ constexpr float kNegBig = -1e30f;  // finite "minus infinity": merges of empty s
 
 __device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
 
-template <int G>
+// Per-head q/k transform of the fused entry (lai_decode_attention_qk_f32): the decode step's
+// qwen_rms_norm_per_head then qwen_apply_rope_neox at the cache row (src/tts_native.c:644-648)
+// on this lane's 8 dims d0..d0+7 of a 128-dim head spread over a half-warp (lanes differ in
+// bits 0-3). Sum of squares by an xor tree over the half-warp; the NeoX partner d +- 64 lives
+// in lane ^ 8. The arithmetic per element is that of qk_norm_rope.cu's FP32 path (separately
+// rounded products; only the sum of squares adds in another order).
+__host__ __device__ constexpr int kv_dim_of(int n_kv) { return n_kv * kHD; }
+
+struct QkArgs {
+    const float *wq, *wk;       // per-head norm weights [128], or null (no norm)
+    const float *cos_t, *sin_t;  // [table_rows, 128] RoPE tables, or null (no RoPE)
+    int64_t table_rows;
+    float eps;
+};
+
+__device__ __forceinline__ void norm_rope8(float (&a)[8], const float *w, const float (&cs)[8],
+                                           const float (&sn)[8], bool rope, float eps,
+                                           int d0) {
+    if (w) {
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; e++) ss = fmaf(a[e], a[e], ss);
+#pragma unroll
+        for (int o = 8; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = 1.0f / sqrtf(ss / (float)kHD + eps);
+        const float4 w0 = ld4(w + d0), w1 = ld4(w + d0 + 4);
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int e = 0; e < 8; e++) a[e] = __fmul_rn(__fmul_rn(a[e], inv), wv[e]);
+    }
+    if (rope) {
+        const bool first = d0 < kHD / 2;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const float pa = __shfl_xor_sync(0xffffffffu, a[e], 8);
+            a[e] = first ? __fsub_rn(__fmul_rn(a[e], cs[e]), __fmul_rn(pa, sn[e]))
+                         : __fadd_rn(__fmul_rn(pa, sn[e]), __fmul_rn(a[e], cs[e]));
+        }
+    }
+}
+
+template <int G, bool QK>
 __global__ void __launch_bounds__(kThreads)
 decode_attn_kernel(float *out, const float *__restrict__ q, const float *__restrict__ k_new,
                    const float *__restrict__ v_new, float *k_cache, float *v_cache,
                    const int32_t *__restrict__ pos, int n_kv, int max_seq, float scale_log2,
-                   float *partials, int *counters, int max_splits, int *err) {
+                   float *partials, int *counters, int max_splits, int *err, const QkArgs qa) {
     const int split = blockIdx.x, kvh = blockIdx.y, s = blockIdx.z;
     const int p = pos[s];
-    if (p < 0 || p >= max_seq) {
+    if (p < 0 || p >= max_seq || (QK && qa.cos_t && p >= qa.table_rows)) {
         if (split == 0 && kvh == 0 && threadIdx.x == 0 && err) atomicOr(err, LAI_DEVERR_POSITION);
         return;
     }
@@ -59,15 +100,35 @@ decode_attn_kernel(float *out, const float *__restrict__ q, const float *__restr
     const int slot = lane >> 4;  // which half-warp: its own key stream
     const int d0 = (lane & 15) * 8;
 
+    float cs[8], sn[8];  // RoPE row p for this lane's dims (fused entry)
+    const bool rope = QK && qa.cos_t != nullptr;
+    if (rope) {
+        const float4 c0 = ld4(qa.cos_t + (size_t)p * kHD + d0), c1 = ld4(qa.cos_t + (size_t)p * kHD + d0 + 4);
+        const float4 s0 = ld4(qa.sin_t + (size_t)p * kHD + d0), s1 = ld4(qa.sin_t + (size_t)p * kHD + d0 + 4);
+        cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w;
+        cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
+        sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w;
+        sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+    }
     float qr[G][8];
 #pragma unroll
     for (int g = 0; g < G; g++) {
         const float *qp = q + (size_t)s * n_heads * kHD + (size_t)(kvh * G + g) * kHD + d0;
         const float4 a = ld4(qp), b = ld4(qp + 4);
-        qr[g][0] = a.x * scale_log2; qr[g][1] = a.y * scale_log2;
-        qr[g][2] = a.z * scale_log2; qr[g][3] = a.w * scale_log2;
-        qr[g][4] = b.x * scale_log2; qr[g][5] = b.y * scale_log2;
-        qr[g][6] = b.z * scale_log2; qr[g][7] = b.w * scale_log2;
+        float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        if (QK) norm_rope8(x, qa.wq, cs, sn, rope, qa.eps, d0);
+#pragma unroll
+        for (int e = 0; e < 8; e++) qr[g][e] = x[e] * scale_log2;
+    }
+    // fused entry: this token's key, normed and rotated, in registers (both half-warps hold
+    // the same 8 dims); it stands in for the row at j == p and is what the cache receives
+    float kn[8];
+    if (QK) {
+        const float *kp = k_new + (size_t)s * kv_dim_of(n_kv) + (size_t)kvh * kHD + d0;
+        const float4 a = ld4(kp), b = ld4(kp + 4);
+        kn[0] = a.x; kn[1] = a.y; kn[2] = a.z; kn[3] = a.w;
+        kn[4] = b.x; kn[5] = b.y; kn[6] = b.z; kn[7] = b.w;
+        norm_rope8(kn, qa.wk, cs, sn, rope, qa.eps, d0);
     }
     float m[G], l[G], acc[G][8];
 #pragma unroll
@@ -96,6 +157,10 @@ decode_attn_kernel(float *out, const float *__restrict__ q, const float *__restr
                 const float4 a = ld4(kr), b = ld4(kr + 4), c = ld4(vr), d = ld4(vr + 4);
                 kv[u][0] = a.x; kv[u][1] = a.y; kv[u][2] = a.z; kv[u][3] = a.w;
                 kv[u][4] = b.x; kv[u][5] = b.y; kv[u][6] = b.z; kv[u][7] = b.w;
+                if (QK && j == p) {
+#pragma unroll
+                    for (int e = 0; e < 8; e++) kv[u][e] = kn[e];
+                }
                 kv[u][8] = c.x; kv[u][9] = c.y; kv[u][10] = c.z; kv[u][11] = c.w;
                 kv[u][12] = d.x; kv[u][13] = d.y; kv[u][14] = d.z; kv[u][15] = d.w;
             } else {
@@ -181,8 +246,15 @@ decode_attn_kernel(float *out, const float *__restrict__ q, const float *__restr
     if (split == n_splits - 1 && threadIdx.x < 32) {  // append the token's k/v to the cache
         const size_t row = (size_t)s * max_seq * kv_dim + (size_t)p * kv_dim + (size_t)kvh * kHD;
         const size_t src = (size_t)s * kv_dim + (size_t)kvh * kHD;
-        reinterpret_cast<float4 *>(k_cache + row)[threadIdx.x] =
-            reinterpret_cast<const float4 *>(k_new + src)[threadIdx.x];
+        if (QK) {
+            if (threadIdx.x < 16) {  // lanes 0-15 hold all 128 dims of the transformed key
+                *reinterpret_cast<float4 *>(k_cache + row + d0) = make_float4(kn[0], kn[1], kn[2], kn[3]);
+                *reinterpret_cast<float4 *>(k_cache + row + d0 + 4) = make_float4(kn[4], kn[5], kn[6], kn[7]);
+            }
+        } else {
+            reinterpret_cast<float4 *>(k_cache + row)[threadIdx.x] =
+                reinterpret_cast<const float4 *>(k_new + src)[threadIdx.x];
+        }
         reinterpret_cast<float4 *>(v_cache + row)[threadIdx.x] =
             reinterpret_cast<const float4 *>(v_new + src)[threadIdx.x];
     }
@@ -230,11 +302,17 @@ decode_attn_kernel(float *out, const float *__restrict__ q, const float *__restr
 template <int G>
 void launch(float *out, const float *q, const float *k_new, const float *v_new, float *kc,
             float *vc, const int32_t *pos, int n_seqs, int n_kv, int max_seq, float scale_log2,
-            float *partials, int *counters, int max_splits, int *err, cudaStream_t st) {
+            float *partials, int *counters, int max_splits, int *err, const QkArgs *qa,
+            cudaStream_t st) {
     const dim3 grid((unsigned)max_splits, (unsigned)n_kv, (unsigned)n_seqs);
-    decode_attn_kernel<G><<<grid, kThreads, 0, st>>>(out, q, k_new, v_new, kc, vc, pos, n_kv,
-                                                     max_seq, scale_log2, partials, counters,
-                                                     max_splits, err);
+    if (qa)
+        decode_attn_kernel<G, true><<<grid, kThreads, 0, st>>>(
+            out, q, k_new, v_new, kc, vc, pos, n_kv, max_seq, scale_log2, partials, counters,
+            max_splits, err, *qa);
+    else
+        decode_attn_kernel<G, false><<<grid, kThreads, 0, st>>>(
+            out, q, k_new, v_new, kc, vc, pos, n_kv, max_seq, scale_log2, partials, counters,
+            max_splits, err, QkArgs{});
 }
 
 inline int splits_for(int max_seq) { return (max_seq + kChunk - 1) / kChunk; }
@@ -249,12 +327,12 @@ extern "C" size_t lai_decode_attention_scratch_bytes(int n_seqs, int n_heads, in
     return partials * sizeof(float) + (size_t)n_seqs * n_kv_heads * sizeof(int);
 }
 
-extern "C" int lai_decode_attention_f32(float *out, const float *q, const float *k_new,
-                                        const float *v_new, float *k_cache, float *v_cache,
-                                        const int32_t *pos, int n_seqs, int n_heads,
-                                        int n_kv_heads, int head_dim, int max_seq, float scale,
-                                        void *scratch, int *err, lai_stream_t stream) {
-    using namespace lai;
+namespace lai {
+namespace {
+int attention_entry(float *out, const float *q, const float *k_new, const float *v_new,
+                    float *k_cache, float *v_cache, const int32_t *pos, int n_seqs, int n_heads,
+                    int n_kv_heads, int head_dim, int max_seq, float scale, void *scratch,
+                    int *err, const QkArgs *qa, lai_stream_t stream) {
     if (!out || !q || !k_new || !v_new || !k_cache || !v_cache || !pos || !scratch ||
         n_seqs < 0 || n_heads <= 0 || n_kv_heads <= 0 || max_seq <= 0)
         return LAI_ERR_INVALID;
@@ -265,6 +343,11 @@ extern "C" int lai_decode_attention_f32(float *out, const float *q, const float 
     if (n_seqs > 65535 || n_kv_heads > 65535) return LAI_ERR_RANGE;
     if (!aligned16(out) || !aligned16(q) || !aligned16(k_new) || !aligned16(v_new) ||
         !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(scratch))
+        return LAI_ERR_INVALID;
+    if (qa && ((qa->wq && !aligned16(qa->wq)) || (qa->wk && !aligned16(qa->wk)) ||
+               ((qa->cos_t == nullptr) != (qa->sin_t == nullptr)) ||
+               (qa->cos_t && (!aligned16(qa->cos_t) || !aligned16(qa->sin_t) ||
+                              qa->table_rows <= 0))))
         return LAI_ERR_INVALID;
     const size_t cache_bytes = (size_t)n_seqs * max_seq * n_kv_heads * kHD * sizeof(float);
     const size_t out_bytes = (size_t)n_seqs * n_heads * kHD * sizeof(float);
@@ -278,10 +361,34 @@ extern "C" int lai_decode_attention_f32(float *out, const float *q, const float 
     const float sl2 = scale * kLog2e;
     const cudaStream_t st = as_stream(stream);
     switch (G) {
-        case 1: launch<1>(out, q, k_new, v_new, k_cache, v_cache, pos, n_seqs, n_kv_heads, max_seq, sl2, partials, counters, max_splits, err, st); break;
-        case 2: launch<2>(out, q, k_new, v_new, k_cache, v_cache, pos, n_seqs, n_kv_heads, max_seq, sl2, partials, counters, max_splits, err, st); break;
-        case 4: launch<4>(out, q, k_new, v_new, k_cache, v_cache, pos, n_seqs, n_kv_heads, max_seq, sl2, partials, counters, max_splits, err, st); break;
-        default: launch<8>(out, q, k_new, v_new, k_cache, v_cache, pos, n_seqs, n_kv_heads, max_seq, sl2, partials, counters, max_splits, err, st); break;
+        case 1: launch<1>(out, q, k_new, v_new, k_cache, v_cache, pos, n_seqs, n_kv_heads, max_seq, sl2, partials, counters, max_splits, err, qa, st); break;
+        case 2: launch<2>(out, q, k_new, v_new, k_cache, v_cache, pos, n_seqs, n_kv_heads, max_seq, sl2, partials, counters, max_splits, err, qa, st); break;
+        case 4: launch<4>(out, q, k_new, v_new, k_cache, v_cache, pos, n_seqs, n_kv_heads, max_seq, sl2, partials, counters, max_splits, err, qa, st); break;
+        default: launch<8>(out, q, k_new, v_new, k_cache, v_cache, pos, n_seqs, n_kv_heads, max_seq, sl2, partials, counters, max_splits, err, qa, st); break;
     }
     return launch_status();
+}
+}  // namespace
+}  // namespace lai
+
+extern "C" int lai_decode_attention_f32(float *out, const float *q, const float *k_new,
+                                        const float *v_new, float *k_cache, float *v_cache,
+                                        const int32_t *pos, int n_seqs, int n_heads,
+                                        int n_kv_heads, int head_dim, int max_seq, float scale,
+                                        void *scratch, int *err, lai_stream_t stream) {
+    return lai::attention_entry(out, q, k_new, v_new, k_cache, v_cache, pos, n_seqs, n_heads,
+                                n_kv_heads, head_dim, max_seq, scale, scratch, err, nullptr,
+                                stream);
+}
+
+extern "C" int lai_decode_attention_qk_f32(float *out, const float *q, const float *k_new,
+                                           const float *v_new, float *k_cache, float *v_cache,
+                                           const int32_t *pos, int n_seqs, int n_heads,
+                                           int n_kv_heads, int head_dim, int max_seq, float scale,
+                                           const float *wq, const float *wk, const float *cos_t,
+                                           const float *sin_t, int64_t table_rows, float eps,
+                                           void *scratch, int *err, lai_stream_t stream) {
+    const lai::QkArgs qa{wq, wk, cos_t, sin_t, table_rows, eps};
+    return lai::attention_entry(out, q, k_new, v_new, k_cache, v_cache, pos, n_seqs, n_heads,
+                                n_kv_heads, head_dim, max_seq, scale, scratch, err, &qa, stream);
 }

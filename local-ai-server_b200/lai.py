@@ -62,6 +62,9 @@ SIGNATURES: dict[str, tuple] = {
     "lai_decode_attention_scratch_bytes": (ctypes.c_size_t, [_i32, _i32, _i32, _i32]),
     "lai_decode_attention_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32,
                                         _i32, _i32, _f32, _vp, _vp, _vp]),
+    "lai_decode_attention_qk_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32,
+                                           _i32, _i32, _f32, _vp, _vp, _vp, _vp, _i64, _f32,
+                                           _vp, _vp, _vp]),
     "lai_sample_topk_f32": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp, _i32, _f32, _f32, _i32, _vp,
                                    _vp]),
     "lai_voc_bigvgan_block_f32": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp,
@@ -336,18 +339,28 @@ def decode_attention_scratch(n_seqs, n_heads, n_kv_heads, max_seq, device="cuda"
 
 
 def decode_attention(q, k_new, v_new, k_cache, v_cache, pos, n_heads, n_kv_heads, scratch=None,
-                     scale=None, out=None, err=None, stream=None):
+                     scale=None, out=None, err=None, stream=None, qk=None):
     """One token per sequence: append k_new/v_new at pos[s] and attend over keys 0..pos[s].
-    q [S, H*128]; k_new/v_new [S, Hkv*128]; caches [S, max_seq, Hkv*128]."""
+    q [S, H*128]; k_new/v_new [S, Hkv*128]; caches [S, max_seq, Hkv*128].
+    qk = (wq, wk, cos_t, sin_t, eps): fold the per-head q/k RMSNorm + NeoX RoPE at pos into the
+    same launch (q and k_new are then read raw; the cache receives the transformed key)."""
     import torch
     S, max_seq = k_cache.shape[0], k_cache.shape[1]
     hd = q.shape[1] // n_heads
     if scratch is None:
         scratch = decode_attention_scratch(S, n_heads, n_kv_heads, max_seq, q.device)
     out = torch.empty_like(q) if out is None else out
-    call("lai_decode_attention_f32", _p(out), _p(q), _p(k_new), _p(v_new), _p(k_cache),
-         _p(v_cache), _p(pos), S, n_heads, n_kv_heads, hd, max_seq,
-         hd ** -0.5 if scale is None else scale, _p(scratch), _p(err), _s(stream))
+    sc = hd ** -0.5 if scale is None else scale
+    if qk is None:
+        call("lai_decode_attention_f32", _p(out), _p(q), _p(k_new), _p(v_new), _p(k_cache),
+             _p(v_cache), _p(pos), S, n_heads, n_kv_heads, hd, max_seq, sc, _p(scratch),
+             _p(err), _s(stream))
+    else:
+        wq, wk, cos_t, sin_t, eps = qk
+        call("lai_decode_attention_qk_f32", _p(out), _p(q), _p(k_new), _p(v_new), _p(k_cache),
+             _p(v_cache), _p(pos), S, n_heads, n_kv_heads, hd, max_seq, sc, _p(wq), _p(wk),
+             _p(cos_t), _p(sin_t), 0 if cos_t is None else cos_t.shape[0], eps, _p(scratch),
+             _p(err), _s(stream))
     return out
 
 

@@ -745,7 +745,8 @@ class TtsFrame:
     library call on one stream and every sampled token kept in device memory:
 
       talker_forward(codec_sum) (:608-686): per layer RMSNorm + fused q|k|v GEMV, per-head
-        q/k RMSNorm + RoPE at the cache position, cache append + attention, o GEMV + residual,
+        q/k RMSNorm + RoPE at the cache position + cache append + attention (one launch),
+        o GEMV + residual,
         RMSNorm + gate/up GEMV + SwiGLU, down GEMV + residual; final RMSNorm (the hidden state
         the code predictor starts from) and the codec head GEMV -> 3072 logits;
       logits [2048, 3072) except EOS -> -1e9, repetition penalty over the cb0 history, top-k
@@ -840,10 +841,10 @@ class TtsFrame:
         act = self.act[:, :inter]
         for i, L in enumerate(layers):
             lai.gemv(self.x, L["wqkv"], L["in_norm"], c.eps, y=self.qkv, stream=stream)
-            lai.qk_norm_rope(q, k, L["q_norm"], L["k_norm"], self.cos, self.sin, pos, c.n_q,
-                             c.n_kv, c.head_dim, c.eps, err=self.err, stream=stream)
+            # per-head q/k RMSNorm + RoPE at pos, cache append and attention: one launch
             lai.decode_attention(q, k, v, kc[i], vc[i], pos, c.n_q, c.n_kv, scratch=scr,
-                                 out=self.attn, err=self.err, stream=stream)
+                                 out=self.attn, err=self.err, stream=stream,
+                                 qk=(L["q_norm"], L["k_norm"], self.cos, self.sin, c.eps))
             lai.gemv_residual(self.x, self.attn, L["wo"], stream=stream)
             lai.gemv_swiglu(self.x, L["wgu"], L["post_norm"], c.eps, out=act, stream=stream)
             lai.gemv_residual(self.x, act, L["wd"], stream=stream)
@@ -921,7 +922,7 @@ class TtsFrame:
     def launches_per_frame(self) -> int:
         """Library kernels per frame (the 2 tensor copies and the position add not counted)."""
         c = self.cfg
-        per_layer = 6
+        per_layer = 5
         return (c.layers * per_layer + 2 + 3 + c.groups * c.cp_layers * per_layer + 1
                 + (c.groups - 1) * 4 + 1)
 

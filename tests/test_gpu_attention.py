@@ -112,3 +112,38 @@ def test_decode_attention_argument_checks():
     assert f(P, P, P, P, P, P, P, 1, 16, 6, 128, 100, 0.1, P, None, None) == lai.LAI_ERR_INVALID
     assert f(P, P, P, P, P, P, P, 1, 12, 4, 128, 100, 0.1, P, None, None) == lai.LAI_ERR_INVALID
     assert f(P, P, P, P, P, P, P, 0, 16, 8, 128, 100, 0.1, P, None, None) == lai.LAI_OK
+
+
+# ---- the fused entry: per-head q/k RMSNorm + NeoX RoPE at pos folded into the launch -------
+def rope_tables(rows, theta=1e6):
+    inv = 1.0 / theta ** (np.arange(0, HD, 2, dtype=np.float64) / HD)
+    ang = np.arange(rows)[:, None] * inv[None, :]
+    c = np.concatenate([np.cos(ang), np.cos(ang)], 1).astype(np.float32)
+    s = np.concatenate([np.sin(ang), np.sin(ang)], 1).astype(np.float32)
+    return c, s
+
+
+@pytest.mark.parametrize("S,H,Hkv,max_seq,pos", CASES[:4] + [(2, 16, 8, 300, [7, 299])])
+@pytest.mark.parametrize("norm,rope", [(True, True), (True, False), (False, True)])
+def test_decode_attention_qk_fused(S, H, Hkv, max_seq, pos, norm, rope):
+    q, kn, vn, kc, vc = make(S, H, Hkv, max_seq, S * 7 + max_seq)
+    rng = np.random.default_rng(max_seq)
+    wq = (1 + 0.1 * rng.standard_normal(HD)).astype(np.float32) if norm else None
+    wk = (1 + 0.1 * rng.standard_normal(HD)).astype(np.float32) if norm else None
+    cos_t, sin_t = rope_tables(max_seq) if rope else (None, None)
+    t = lambda a: None if a is None else torch.from_numpy(np.ascontiguousarray(a)).to(DEV)  # noqa: E731
+    kcd, vcd = t(kc), t(vc)
+    qd, knd = t(q), t(kn)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = lai.decode_attention(qd, knd, t(vn), kcd, vcd, t(np.asarray(pos, np.int32)), H, Hkv,
+                               err=err, qk=(t(wq), t(wk), t(cos_t), t(sin_t), 1e-6))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(qd.cpu(), torch.from_numpy(q)) and torch.equal(knd.cpu(), torch.from_numpy(kn))
+    # oracle: the separate per-head norm + RoPE at each sequence's pos, then attention
+    qn, kn2 = oracle.qk_norm_rope(q, kn, wq, wk, cos_t, sin_t, np.asarray(pos, np.int32), H, Hkv,
+                                  HD, 1e-6, bf16=False)
+    want, kc2, vc2 = expected(qn, kn2, vn, kc, vc, pos, H, Hkv)
+    assert max_rel_err(out.cpu().numpy(), want) <= TOL_F32
+    assert max_rel_err(kcd.cpu().numpy(), kc2) <= TOL_F32  # the transformed key in the cache
+    assert np.array_equal(vcd.cpu().numpy(), vc2)
