@@ -87,6 +87,10 @@ decode_attn_kernel(float *out, const float *__restrict__ q, const float *__restr
                    const int32_t *__restrict__ pos, int n_kv, int max_seq, float scale_log2,
                    float *partials, int *counters, int max_splits, int *err, const QkArgs qa) {
     const int split = blockIdx.x, kvh = blockIdx.y, s = blockIdx.z;
+    // launched with programmatic dependent launch: q / k / v come from the kernel before,
+    // and the kernel after (the o-projection GEMV) may start streaming its weights now
+    pdl_wait_prior();
+    pdl_launch_dependents();
     const int p = pos[s];
     if (p < 0 || p >= max_seq || (QK && qa.cos_t && p >= qa.table_rows)) {
         if (split == 0 && kvh == 0 && threadIdx.x == 0 && err) atomicOr(err, LAI_DEVERR_POSITION);
@@ -306,13 +310,13 @@ void launch(float *out, const float *q, const float *k_new, const float *v_new, 
             cudaStream_t st) {
     const dim3 grid((unsigned)max_splits, (unsigned)n_kv, (unsigned)n_seqs);
     if (qa)
-        decode_attn_kernel<G, true><<<grid, kThreads, 0, st>>>(
-            out, q, k_new, v_new, kc, vc, pos, n_kv, max_seq, scale_log2, partials, counters,
-            max_splits, err, *qa);
+        launch_pdl(decode_attn_kernel<G, true>, grid, dim3(kThreads), 0, st, out, q, k_new,
+                   v_new, kc, vc, pos, n_kv, max_seq, scale_log2, partials, counters, max_splits,
+                   err, *qa);
     else
-        decode_attn_kernel<G, false><<<grid, kThreads, 0, st>>>(
-            out, q, k_new, v_new, kc, vc, pos, n_kv, max_seq, scale_log2, partials, counters,
-            max_splits, err, QkArgs{});
+        launch_pdl(decode_attn_kernel<G, false>, grid, dim3(kThreads), 0, st, out, q, k_new,
+                   v_new, kc, vc, pos, n_kv, max_seq, scale_log2, partials, counters, max_splits,
+                   err, QkArgs{});
 }
 
 inline int splits_for(int max_seq) { return (max_seq + kChunk - 1) / kChunk; }

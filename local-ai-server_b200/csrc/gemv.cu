@@ -111,13 +111,6 @@ struct WF32 {
     static __device__ __forceinline__ float to_f(T w) { return w; }
 };
 
-// Programmatic dependent launch: let the next kernel on the stream start launching
-// now, and wait for the previous kernel's results only where they are first read.
-// Without the launch attribute both are no-ops.
-__device__ __forceinline__ void pdl_launch_dependents() {
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-__device__ __forceinline__ void pdl_wait_prior() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // Stage x[M,K] in shared memory as FP32, normalised by RMSNorm when norm_w != NULL.
 template <int M>

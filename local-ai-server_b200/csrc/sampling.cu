@@ -77,6 +77,8 @@ sample_topk_kernel(int32_t *out, float *logits, int vocab, int64_t ld, const int
     float *srow = reinterpret_cast<float *>(seen + (vocab + 31) / 32);
     const int row = blockIdx.x, tid = threadIdx.x;
     float *lg = logits + (size_t)row * ld;
+    pdl_wait_prior();  // the logits come from the kernel before (programmatic launch)
+    pdl_launch_dependents();
 
     if (penalty > 1.0f && history && hist_len) {
         const int words = (vocab + 31) / 32;
@@ -172,9 +174,9 @@ extern "C" int lai_sample_topk_f32(int32_t *out_tokens, float *logits, int vocab
         cudaFuncSetAttribute(sample_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem) != cudaSuccess)
         return LAI_ERR_CUDA;
-    sample_topk_kernel<<<rows, kThreads, smem, as_stream(stream)>>>(
-        out_tokens, logits, vocab, (int64_t)vocab, history, history_len, history_stride, penalty,
-        temperature, k, u, staged ? 1 : 0);
+    launch_pdl(sample_topk_kernel, dim3(rows), dim3(kThreads), smem, as_stream(stream),
+               out_tokens, logits, vocab, (int64_t)vocab, history, history_len, history_stride,
+               penalty, temperature, k, u, staged ? 1 : 0);
     return launch_status();
 }
 
@@ -183,6 +185,8 @@ namespace {
 
 __global__ void mask_range_kernel(float *logits, int64_t vocab, int rows, int lo, int hi,
                                   int keep, float value) {
+    pdl_wait_prior();
+    pdl_launch_dependents();
     const int64_t n = (int64_t)rows * (hi - lo);
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
@@ -194,6 +198,8 @@ __global__ void mask_range_kernel(float *logits, int64_t vocab, int rows, int lo
 
 __global__ void history_append_kernel(int32_t *history, int32_t *len, const int32_t *tokens,
                                       int rows, int stride, int *err) {
+    pdl_wait_prior();
+    pdl_launch_dependents();
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= rows) return;
     const int n = len[r];
@@ -217,8 +223,8 @@ extern "C" int lai_logits_mask_range_f32(float *logits, int vocab, int rows, int
         return LAI_ERR_INVALID;
     if (rows == 0 || lo == hi) return LAI_OK;
     const int64_t n = (int64_t)rows * (hi - lo);
-    mask_range_kernel<<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(logits, vocab, rows, lo,
-                                                                        hi, keep, value);
+    launch_pdl(mask_range_kernel, dim3(grid_for(n, 256)), dim3(256), 0, as_stream(stream),
+               logits, (int64_t)vocab, rows, lo, hi, keep, value);
     return launch_status();
 }
 
@@ -230,7 +236,7 @@ extern "C" int lai_history_append_i32(int32_t *history, int32_t *history_len,
     if (!history || !history_len || !tokens || rows < 0 || history_stride <= 0)
         return LAI_ERR_INVALID;
     if (rows == 0) return LAI_OK;
-    history_append_kernel<<<(rows + 127) / 128, 128, 0, as_stream(stream)>>>(
-        history, history_len, tokens, rows, history_stride, err);
+    launch_pdl(history_append_kernel, dim3((rows + 127) / 128), dim3(128), 0, as_stream(stream),
+               history, history_len, tokens, rows, history_stride, err);
     return launch_status();
 }
