@@ -11,7 +11,11 @@
 // scan exactly: warp 0 tests 32 tokens per ballot against the current minimum, applies
 // the qualifying tokens one at a time in index order (the lowest set lane first, the
 // minimum re-found by a warp-wide first-argmin over the slots after each), and re-tests
-// the rest of the chunk against the new minimum. One thread then runs the softmax and the
+// the rest of the chunk against the new minimum. For top_k <= 64 the slots live in
+// registers, two per lane, and the first-argmin is two hardware warp min-reductions (an
+// order-preserving integer key of the value, then the lowest slot among the lanes holding
+// it) instead of a shuffle tree over shared memory; larger top_k keep the slots in shared
+// memory. Either way the replacements happen in the same order. One thread then runs the softmax and the
 // cumulative walk sequentially so the float sums round in the reference's order. The
 // uniform draw the reference takes from libc rand() comes in as u[row].
 //
@@ -66,6 +70,35 @@ __host__ __device__ inline size_t sample_smem_bytes(int vocab, int k, bool stage
     return (size_t)k * 8 + words * 4 + (staged ? (size_t)vocab * 4 : 0);
 }
 
+// Order-preserving 32-bit key of a float (smaller value <-> smaller key; -0 and +0 equal, as
+// they compare equal), for the warp's hardware min-reduction.
+__device__ __forceinline__ uint32_t order_key(float v) {
+    const uint32_t u = __float_as_uint(v == 0.0f ? 0.0f : v);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// First minimum over the k <= 64 slots held two per lane (lane L: slots L and L + 32):
+// min key over the warp, then the lowest slot index among the slots holding it.
+__device__ __forceinline__ void reg_argmin_first(const float (&v)[2], int k, float &mv, int &mi) {
+    const int lane = threadIdx.x & 31;
+    uint32_t kb = 0xffffffffu;
+    int ib = INT_MAX;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const int slot = lane + 32 * h;
+        if (slot < k) {
+            const uint32_t key = order_key(v[h]);
+            if (key < kb) {  // strict: slot L before slot L + 32 on a tie
+                kb = key;
+                ib = slot;
+            }
+        }
+    }
+    const uint32_t kmin = __reduce_min_sync(0xffffffffu, kb);
+    mi = (int)__reduce_min_sync(0xffffffffu, kb == kmin ? (uint32_t)ib : 0xffffffffu);
+    mv = __shfl_sync(0xffffffffu, mi < 32 ? v[0] : v[1], mi & 31);
+}
+
 __global__ void __launch_bounds__(kThreads)
 sample_topk_kernel(int32_t *out, float *logits, int vocab, int64_t ld, const int32_t *history,
                    const int32_t *hist_len, int hist_stride, float penalty, float temperature,
@@ -108,7 +141,46 @@ sample_topk_kernel(int32_t *out, float *logits, int vocab, int64_t ld, const int
         si[i] = i;
     }
     __syncthreads();
-    if (tid < 32) {
+    if (tid < 32 && k <= 64) {
+        // the slots in registers, two per lane; the same scan and replacements as below
+        const int lane = tid;
+        float rv[2];
+        int ri[2];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int slot = lane + 32 * h;
+            rv[h] = slot < k ? sv[slot] : 0.0f;
+            ri[h] = slot;
+        }
+        float mv;
+        int mi;
+        reg_argmin_first(rv, k, mv, mi);
+        for (int i0 = k; i0 < vocab; i0 += 32) {
+            const int i = i0 + lane;
+            const bool valid = i < vocab;
+            const float v = valid ? scan[i] : 0.0f;
+            uint32_t mask = __ballot_sync(0xffffffffu, valid && v > mv);
+            while (mask) {
+                const int f = __ffs(mask) - 1;
+                const float vf = __shfl_sync(0xffffffffu, v, f);
+                if (lane == (mi & 31)) {  // the lane holding the minimum slot replaces it
+                    rv[mi >> 5] = vf;
+                    ri[mi >> 5] = i0 + f;
+                }
+                reg_argmin_first(rv, k, mv, mi);
+                mask = __ballot_sync(0xffffffffu, valid && lane > f && v > mv);
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int slot = lane + 32 * h;
+            if (slot < k) {
+                sv[slot] = rv[h];
+                si[slot] = ri[h];
+            }
+        }
+        __syncwarp();
+    } else if (tid < 32) {
         const int lane = tid;
         float mv;
         int mi;
@@ -130,27 +202,27 @@ sample_topk_kernel(int32_t *out, float *logits, int vocab, int64_t ld, const int
                 mask = __ballot_sync(0xffffffffu, valid && lane > f && v > mv);
             }
         }
-        if (lane == 0) {
-            float mx = sv[0];
-            for (int j = 1; j < k; j++)
-                if (sv[j] > mx) mx = sv[j];
-            float sum = 0.0f;
-            for (int j = 0; j < k; j++) {
-                sv[j] = expf((sv[j] - mx) / temperature);
-                sum += sv[j];
-            }
-            const float r = u[row] * sum;
-            float cum = 0.0f;
-            int sel = si[0];
-            for (int j = 0; j < k; j++) {
-                cum += sv[j];
-                if (cum >= r) {
-                    sel = si[j];
-                    break;
-                }
-            }
-            out[row] = sel;
+    }
+    if (tid == 0) {  // softmax and cumulative walk over the slots in their order
+        float mx = sv[0];
+        for (int j = 1; j < k; j++)
+            if (sv[j] > mx) mx = sv[j];
+        float sum = 0.0f;
+        for (int j = 0; j < k; j++) {
+            sv[j] = expf((sv[j] - mx) / temperature);
+            sum += sv[j];
         }
+        const float r = u[row] * sum;
+        float cum = 0.0f;
+        int sel = si[0];
+        for (int j = 0; j < k; j++) {
+            cum += sv[j];
+            if (cum >= r) {
+                sel = si[j];
+                break;
+            }
+        }
+        out[row] = sel;
     }
 }
 
