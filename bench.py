@@ -416,7 +416,8 @@ def run_resunits(args) -> None:
     torch.cuda.synchronize()
     sampler.start()
     time.sleep(0.3)
-    total_ms, per = time_launches(launches, args.steps, False, work.kernel_names)
+    # v4's front is ~100 launches of a few microseconds: one CUDA graph per step
+    total_ms, per = time_launches(launches, args.steps, args.config == "v4", work.kernel_names)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -763,6 +764,76 @@ def cpu_decoder_rate(t0: int, batch: int, min_seconds: float, t0_sample: int = 4
             "passes": n, "seconds": el, "t0_sample": t0_sample, "samples_sample": out.shape[1]}
 
 
+def cpu_front_seconds(t_frames: int, min_seconds: float = 1.0, steps: int | None = None) -> dict:
+    """tts_vocoder_run stages 1-3 (RVQ decode, pre_conv, the 8-layer pre-transformer,
+    src/tts_vocoder.c:589-640) on host cores as the reference's USE_BLAS build runs them: every
+    linear (the 16 RVQ projections, input/q/k/v/o/gate/up/down/output projections) and the
+    pre_conv taps as SGEMMs through numpy's OpenBLAS on all cores; RMSNorm, NeoX RoPE, causal
+    attention, SwiGLU and the residual adds from the oracle's timed C build (float sums,
+    OpenMP). Runs the full t_frames (attention is T^2). Returns seconds per run."""
+    import numpy as np
+    from threadpoolctl import threadpool_limits
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle
+    import runner
+    lib = oracle.load("liblai_cpuref.so")
+    nthreads = len(os.sched_getaffinity(0))
+    rng = np.random.default_rng(21)
+    f = lambda a: np.ascontiguousarray(a, dtype=np.float32)  # noqa: E731
+    T, H, A, I = t_frames, runner.XFMR_HIDDEN, runner.XFMR_ATTN, runner.XFMR_INTER
+    books = f(rng.standard_normal((runner.RVQ_CODEBOOKS, runner.RVQ_SIZE, runner.RVQ_DIM)))
+    proj = [f(rng.standard_normal((runner.RVQ_OUT, runner.RVQ_DIM)) / 64)
+            for _ in range(runner.RVQ_CODEBOOKS)]
+    codes = rng.integers(0, runner.RVQ_SIZE, (T, runner.RVQ_CODEBOOKS))
+    pre_taps = [f(rng.standard_normal((1024, 512)) / np.sqrt(1536)) for _ in range(3)]
+    pre_b = f(rng.normal(0, .01, (1024, 1)))
+    lin_w = lambda n, k: f(rng.standard_normal((n, k)) / np.sqrt(k))  # noqa: E731
+    in_w, in_b, out_w, out_b = lin_w(H, 1024), f(rng.normal(0, .01, H)), lin_w(1024, H), f(
+        rng.normal(0, .01, 1024))
+    layers = [{"n1": f(1 + rng.normal(0, .1, H)), "wq": lin_w(A, H), "wk": lin_w(A, H),
+               "wv": lin_w(A, H), "wo": lin_w(H, A), "g1": f(rng.normal(0, .1, H)),
+               "n2": f(1 + rng.normal(0, .1, H)), "wg": lin_w(I, H), "wu": lin_w(I, H),
+               "wd": lin_w(H, I), "g2": f(rng.normal(0, .1, H))}
+              for _ in range(runner.XFMR_LAYERS)]
+    fnorm = f(1 + rng.normal(0, .1, H))
+    cos_t, sin_t = oracle.compute_rope_neox(np.arange(T, dtype=np.int32), runner.XFMR_HD,
+                                            runner.XFMR_THETA, lib=lib)
+
+    def run():
+        rvq = np.zeros((runner.RVQ_OUT, T), np.float32)  # [512, T] as the reference
+        for cb in range(runner.RVQ_CODEBOOKS):
+            rvq += proj[cb] @ books[cb][codes[:, cb]].T
+        pad = np.zeros((512, T + 2), np.float32)
+        pad[:, 2:] = rvq
+        pre = pre_taps[0] @ pad[:, :T]
+        for k in range(1, 3):
+            pre += pre_taps[k] @ pad[:, k:k + T]
+        pre += pre_b
+        x = f(pre.T) @ in_w.T + in_b  # the reference transposes to [T, 1024] first
+        for L in layers:
+            xn = oracle.rms_norm(x, L["n1"], 1e-5, lib=lib)
+            q = oracle.apply_rope_neox(xn @ L["wq"].T, cos_t, sin_t, 16, 64, lib=lib)
+            k = oracle.apply_rope_neox(xn @ L["wk"].T, cos_t, sin_t, 16, 64, lib=lib)
+            a = oracle.causal_attention(q, k, xn @ L["wv"].T, 16, 16, 64, lib=lib)
+            x = oracle.add_inplace(x, (a @ L["wo"].T) * L["g1"], lib=lib)
+            xn = oracle.rms_norm(x, L["n2"], 1e-5, lib=lib)
+            ffn = oracle.swiglu_separate(xn @ L["wg"].T, xn @ L["wu"].T, lib=lib)
+            x = oracle.add_inplace(x, (ffn @ L["wd"].T) * L["g2"], lib=lib)
+        x = oracle.rms_norm(x, fnorm, 1e-5, lib=lib)
+        return f((x @ out_w.T + out_b).T)  # back to [1024, T]
+
+    with threadpool_limits(nthreads):
+        run()
+        n, t0 = 0, time.perf_counter()
+        while True:
+            run()
+            n += 1
+            el = time.perf_counter() - t0
+            if (steps is not None and n >= steps) or (steps is None and el >= min_seconds):
+                break
+    return {"seconds": el / n, "passes": n, "threads": nthreads}
+
+
 def cpu_sampling_rate(rows: int, vocab: int, top_k: int, temperature: float, penalty: float,
                       hist: int, min_seconds: float, steps: int | None = None) -> dict:
     """The reference's own tts_apply_repetition_penalty + tts_sample_topk (oracle/_ref, built
@@ -923,7 +994,7 @@ def run_single(args) -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     seed = args.seed + 1000 * rank
-    tensor = args.config in ("n1", "v2", "v3")
+    tensor = args.config in ("n1", "v2", "v3", "v4")
     tf32 = tf32_peak_tflops() if tensor else None
     if args.config == "a3":
         work = runner.DecodeAttention(seqs=args.rows or 256, seed=seed)
@@ -934,6 +1005,8 @@ def run_single(args) -> None:
         work = runner.VocDecoder(t0=2000 // args.t_div, passes=args.passes, seed=seed)
     elif args.config == "v3":
         work = runner.VocFullDecoder(t_frames=500 // args.t_div, passes=args.passes, seed=seed)
+    elif args.config == "v4":
+        work = runner.VocCodesToAudio(t_frames=500 // args.t_div, passes=args.passes, seed=seed)
     elif args.config == "d1":
         work = runner.TtsDecode(frames=args.warmup + args.steps + args.e2e_steps + 2, seed=seed)
     else:
@@ -1015,6 +1088,14 @@ def run_single(args) -> None:
             outs = [(pin(work.audio), work.audio)]
             api = ("the 10 vocoder-decoder calls with the pre-transformer output copied in from and "
                    "the audio copied back to pinned host memory each step")
+        elif args.config == "v4":
+            ins = [(work.codes, pin(work.codes))]
+            outs = [(pin(work.audio), work.audio)]
+            launches = [lambda: work.run(graph=True)]
+            api = ("VocCodesToAudio.run(graph=True): the whole tts_vocoder_run as one CUDA graph "
+                   "of library calls (RVQ gather + GEMM, pre_conv, 8 pre-transformer layers, "
+                   "the decoder's 10 calls) with the int64 codes copied in from and the audio "
+                   "copied back to pinned host memory each step")
         elif args.config == "d1":
             tf = work.tf
             ins = [(tf.u_frame, pin(tf.draws[:1])), (tf.trail_frame, pin(tf.trailing[:1]))]
@@ -1064,6 +1145,19 @@ def run_single(args) -> None:
                              f"scaled to {work.t_frames} frames: the reference's USE_BLAS path "
                              "(its compiled SnakeBeta, depthwise conv, LayerNorm, GELU and final "
                              f"conv + OpenBLAS SGEMMs), host {cpu_model()}"}
+        elif args.config == "v4":
+            fr = cpu_front_seconds(work.t_frames, min_seconds=min(2.0, args.cpu_seconds / 4))
+            r = cpu_decoder_rate(work.dec.t_dec, 1, args.cpu_seconds, full=True)
+            step_s = fr["seconds"] + r["step_seconds"]
+            cpu = {"value": round(work.rows_step / step_s, 1), "unit": "rows/s",
+                   "cores": r["threads"], "kind": "port",
+                   "sample": f"the front (RVQ decode, pre_conv, 8-layer pre-transformer) at the "
+                             f"full {work.t_frames} frames, {fr['passes']} runs "
+                             f"({fr['seconds'] * 1000:.0f} ms each: OpenBLAS SGEMM linears, the "
+                             "oracle's timed C build for norms, RoPE, attention, SwiGLU), plus "
+                             f"the decoder path as config v3 times it ({r['passes']} runs from "
+                             f"{r['t0_sample'] // 4} frames scaled to {work.t_frames}: "
+                             f"{r['step_seconds'] * 1000:.0f} ms), host {cpu_model()}"}
         elif args.config == "d1":
             r = cpu_tts_frame_rate(args.cpu_seconds)
             cpu = {"value": round(r["rows_per_s"], 3), "unit": "rows/s", "cores": r["threads"],
@@ -1117,6 +1211,14 @@ def run_single(args) -> None:
                "frames": getattr(work, "t_frames", None), "batch": getattr(work, "batch", None),
                "audio_samples": getattr(work, "t_final", None), "passes": args.passes,
                "rows": "audio samples (24 kHz) per step"},
+        "v4": {"workload": "the whole tts_vocoder_run, codec codes to audio: RVQ decode (16 "
+                           "codebooks, one gather + one GEMM), pre_conv k=3, 8-layer "
+                           "pre-transformer (fused q|k|v and gate|up GEMMs, causal attention "
+                           "with RoPE, LayerScale residual epilogues), then the v3 decoder "
+                           "path; FP32 channels-last, linears and convs on tcgen05 (3xTF32)",
+               "frames": getattr(work, "t_frames", None), "batch": 1,
+               "audio_samples": getattr(work, "rows_step", None), "passes": args.passes,
+               "rows": "audio samples (24 kHz) per step"},
         "d1": {"workload": "run_decode_loop frames of Qwen3-TTS 0.6B: talker step (28 layers, "
                            "fused GEMVs, q/k norm + RoPE, KV-cache attention, codec head), "
                            "cb0 suppression + penalty + top-k, 15 code-predictor sub-codes (5 "
@@ -1142,6 +1244,9 @@ def run_single(args) -> None:
         "per_kernel": per_kernel, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
         "gpu_launches": args.steps * {"n1": 3 * len(launches), "v2": 8 * len(launches),
                                       "v3": 2 + 2 * 3 + 2 + 4 * 8 + 1,
+                                      # front: gather, 3 convs x (split + GEMM), 8 x (2 norms,
+                                      # attention, SwiGLU, 4 x (split + GEMM)), norm + conv
+                                      "v4": 1 + 6 + 8 * 12 + 3 + 2 + 2 * 3 + 2 + 4 * 8 + 1,
                                       "d1": work.tf.launches_per_frame()
                                       if args.config == "d1" else 0}.get(args.config,
                                                                          len(launches)),
@@ -1223,6 +1328,22 @@ def run_reference(args) -> None:
                     ms_per_step=1000.0 * r["step_seconds"], scaling="weak", dtype="f32",
                     config={"workload": "tts_vocoder_run from the pre-transformer output to audio",
                             "config": "v3", "frames": 500, "batch": 1})
+    elif args.config == "v4":
+        fr = cpu_front_seconds(500, steps=1)
+        r = cpu_decoder_rate(2000, 1, 0.0, t0_sample=40, steps=args.steps, warmup=args.warmup,
+                             full=True)
+        step_s = fr["seconds"] + r["step_seconds"]
+        value = r["rows_per_s"] * r["step_seconds"] / step_s
+        cb = {"value": value, "unit": "rows/s", "cores": r["threads"], "kind": "port",
+              "sample": f"the front at the full 500 frames ({fr['seconds'] * 1000:.0f} ms: "
+                        "OpenBLAS SGEMM linears + the oracle's timed C build for norms, RoPE, "
+                        "attention, SwiGLU) plus the decoder path from 10 frames per step "
+                        "scaled to 500 frames (the reference's USE_BLAS path, its compiled "
+                        f"SnakeBeta, depthwise conv, LayerNorm, GELU, final conv), host {cpu_model()}"}
+        line = dict(common, value=value, unit="rows/s", ms_per_step=1000.0 * step_s,
+                    scaling="weak", dtype="f32",
+                    config={"workload": "the whole tts_vocoder_run, codec codes to audio",
+                            "config": "v4", "frames": 500, "batch": 1})
     elif args.config == "d1":
         r = cpu_tts_frame_rate(0.0, frames=max(1, min(args.steps, int(args.ref_budget / 2))))
         cb = {"value": r["rows_per_s"], "unit": "rows/s", "cores": r["threads"], "kind": "port",
@@ -1720,7 +1841,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "d1", "g1", "g2", "v1", "v2", "v3",
-                                         "a3", "n1", "s3"],
+                                         "v4", "a3", "n1", "s3"],
                     default="c2")
     ap.add_argument("--t-div", type=int, default=1,
                     help="v1: divide every stage's length (small profiling cases)")
@@ -1752,13 +1873,14 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)  # timing rule: at least 3 untimed warm-up steps
     if args.steps is None:
-        args.steps = {"v1": 20, "v2": 20, "v3": 20, "n1": 50, "a3": 200, "d1": 50}.get(
+        args.steps = {"v1": 20, "v2": 20, "v3": 20, "v4": 20, "n1": 50, "a3": 200,
+                      "d1": 50}.get(
             args.config, 2000)
     if args.impl == "reference":
         run_reference(args)
     elif args.config == "v1":
         run_resunits(args)
-    elif args.config in ("a3", "d1", "n1", "s3", "v2", "v3"):
+    elif args.config in ("a3", "d1", "n1", "s3", "v2", "v3", "v4"):
         run_single(args)
     else:
         run_ours(args)

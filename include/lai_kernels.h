@@ -261,6 +261,25 @@ LAI_API int lai_decode_attention_qk_f32(float *out, const float *q, const float 
                                         const float *sin_t, int64_t table_rows, float eps,
                                         void *scratch, int *err, lai_stream_t stream);
 
+/* ---- causal self-attention over a whole sequence ------------------------------------------
+ * qwen_causal_attention(out, q, k, v, T, T, n_heads, n_kv_heads, head_dim, scale, 0) as the
+ * vocoder's pre-transformer calls it (src/tts_vocoder_xfmr.c:172-180): row t of q attends
+ * keys 0..t. q / out [T, n_heads*head_dim], k / v [T, n_kv_heads*head_dim], F32, head_dim 64
+ * or 128; query head h reads kv head h / (n_heads / n_kv_heads). */
+LAI_API int lai_prefill_attention_f32(float *out, const float *q, const float *k, const float *v,
+                                      int T, int n_heads, int n_kv_heads, int head_dim,
+                                      float scale, lai_stream_t stream);
+/* The same with the pre-transformer's NeoX RoPE (qwen_apply_rope_neox on q and k,
+ * src/tts_vocoder_xfmr.c:172-175) folded in and row strides, so q / k / v can be the three
+ * column blocks of one fused q|k|v projection output: q row t at q + t*ld_q, k / v rows at
+ * + t*ld_kv; cos_t / sin_t [table_rows >= T, head_dim] give position t's row (both NULL:
+ * no RoPE). out stays [T, n_heads*head_dim]. */
+LAI_API int lai_prefill_attention_rope_f32(float *out, const float *q, const float *k,
+                                           const float *v, int ld_q, int ld_kv, int T,
+                                           int n_heads, int n_kv_heads, int head_dim, float scale,
+                                           const float *cos_t, const float *sin_t,
+                                           int64_t table_rows, lai_stream_t stream);
+
 /* ---- token sampling on device logits ------------------------------------------------------
  * Per row r of logits [rows, vocab]: tts_apply_repetition_penalty(logits, vocab, history,
  * history_len, penalty) (src/tts_sampling.c:19-36; history [rows, history_stride] int32,
@@ -366,6 +385,25 @@ LAI_API int lai_voc_conv_transpose1d_f32(float *out, const float *x, float *scra
 LAI_API int lai_voc_final_f32(float *audio, const float *x, const float *exp_alpha,
                               const float *inv_exp_beta, const float *w, const float *bias,
                               int batch, int channels, int T, lai_stream_t stream);
+
+/* The vocoder's front (tts_vocoder_run stages 1 and 3, src/tts_vocoder.c:589-640):
+ *   lai_voc_rvq_gather_f32: RVQ decode's lookups (rvq_decode, :428-455) as one gather,
+ *     out [T, n_codebooks*dim] = row t holds codebooks[cb][codes[t, cb]] for cb in order;
+ *     codebooks packed [n_codebooks*codebook_size, dim] F32, codes int64 [T, n_codebooks] as
+ *     the reference passes them (out-of-range: zero row, LAI_DEVERR_TOKEN_ID). One GEMM
+ *     against the n_codebooks projections laid side by side ([512, n_codebooks*dim], e.g. via
+ *     lai_voc_conv1d_f32 with kernel 1) then sums the codebooks.
+ *   lai_voc_linear_scale_residual_f32: x_res [rows, c_out] += gamma * (in [rows, c_in] . W^T
+ *     + bias), the pre-transformer's o / down projection with LayerScale and residual
+ *     (src/tts_vocoder_xfmr.c:182-186, 203-207); W packed by lai_voc_pack_conv_f32 (kernel 1);
+ *     scratch 2*rows*c_in floats; c_in, c_out multiples of 32; passes 1 or 3 as for the convs. */
+LAI_API int lai_voc_rvq_gather_f32(float *out, const float *codebooks, const int64_t *codes,
+                                   int T, int n_codebooks, int codebook_size, int dim, int *err,
+                                   lai_stream_t stream);
+LAI_API int lai_voc_linear_scale_residual_f32(float *x_res, const float *in, float *scratch,
+                                              const float *w, const float *bias,
+                                              const float *gamma, int rows, int c_in, int c_out,
+                                              int passes, int *err, lai_stream_t stream);
 
 /* ---- vocoder ConvNeXt block (upsample stages) --------------------------------------------
  * run_convnext(x, C, T, cn) (src/tts_vocoder.c:463-533): depthwise causal conv k=7 + bias,

@@ -28,6 +28,8 @@
 // a timeout sets LAI_DEVERR_TIMEOUT in *err and the CTA still releases its TMEM.
 #pragma once
 
+#include <cooperative_groups.h>
+
 #include <mutex>
 
 #include "lai_common.cuh"
@@ -104,6 +106,9 @@ struct Tile {
                   "shared memory beyond the SM's capacity for kMinBlocks CTAs");
     static_assert(2 * kStages + 4 <= kBarBytes / 8 - 1, "barrier area too small");
     static_assert(kHalf % 16 == 0, "drain warps read 16-column groups");
+    // split-K partial tile [128][BN + 4] in the ring (float4 rows, conflict-free by rows)
+    static constexpr int kPartPitch = BN + 4;
+    static_assert(kRing >= (uint32_t)kBM * kPartPitch * 4, "partial tile must fit the ring");
 };
 
 __device__ __forceinline__ void store4(float *p, float a, float b, float c, float d) {
@@ -182,8 +187,15 @@ __device__ __forceinline__ void epilogue4(const ConvArgs &a, const EpiParams &q,
 // other buffer. Chunk errors then carry each chunk's own sign and largely cancel.
 //
 // act_map: [2 planes][batch][T][c_in] (hi, lo); w_map: [2 * taps][c_out][c_in] (hi taps,
-// then lo taps). Grid: ceil(T / 128) x (c_out / BN) x phases x batch tiles, one dimension.
-template <int BN, int PASSES, int EPI>
+// then lo taps). Grid: ceil(T / 128) x (c_out / BN) x phases x batch tiles, one dimension,
+// times `splits` when a GEMM has too few tiles to fill the SMs (a short sequence: the
+// pre-transformer's 500-row linears make 8-48 tiles). Split-K runs the `splits` CTAs of a
+// tile as one cluster, each over a contiguous 1/splits of the K chunks; each writes its F32
+// partial tile into its own (then idle) operand ring, and after a cluster barrier the CTA
+// of rank r sums rows/columns unit r of every CTA's partial through distributed shared
+// memory in rank order 0..splits-1 (deterministic, no global workspace, no waits on
+// flags) and runs the epilogue for them.
+template <int BN, int PASSES, int EPI, bool SPLITK>
 __global__ void __launch_bounds__(kThreads, (BN <= 128 ? 2 : 1))
 conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
                  const __grid_constant__ CUtensorMap w_map, const ConvArgs a) {
@@ -204,13 +216,16 @@ conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    // split-K: the cluster's CTAs share one tile; S = cluster size, split = rank in it
+    const int S = SPLITK ? (int)cooperative_groups::this_cluster().num_blocks() : 1;
+    const int split = SPLITK ? (int)cooperative_groups::this_cluster().block_rank() : 0;
     // Tile order (fastest first): output-channel tile, phase, time tile, batch. The CTAs
     // that read the same input rows (every channel tile and phase of one time tile) run
     // side by side, so an input larger than L2 comes from HBM once, not once per channel
     // tile or phase.
     const int P = a.phases > 1 ? a.phases : 1;
     const int n_nt = a.c_out / BN, n_tt = (a.T + kBM - 1) / kBM;
-    int rest = (int)blockIdx.x;
+    int rest = SPLITK ? (int)(blockIdx.x / (unsigned)S) : (int)blockIdx.x;
     const int nt = rest % n_nt;
     rest /= n_nt;
     const int phase = rest % P;
@@ -225,8 +240,14 @@ conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
         return (int64_t)b * a.T_out + (int64_t)(t - a.row_trim) * P + phase;
     };
     const int kblocks = a.c_in / kBK;
-    const int n_iter = a.taps * kblocks;
-    const int n_chunks = (n_iter + L::kChunk - 1) / L::kChunk;
+    const int n_iter_all = a.taps * kblocks;
+    const int n_chunks_all = (n_iter_all + L::kChunk - 1) / L::kChunk;
+    // this CTA's contiguous share of the K chunks: iterations [it0, it0 + n_iter)
+    const int c_lo = SPLITK ? (int)((int64_t)split * n_chunks_all / S) : 0;
+    const int c_hi = SPLITK ? (int)((int64_t)(split + 1) * n_chunks_all / S) : n_chunks_all;
+    const int it0 = SPLITK ? c_lo * L::kChunk : 0;
+    const int n_iter = SPLITK ? min(n_iter_all, c_hi * L::kChunk) - it0 : n_iter_all;
+    const int n_chunks = SPLITK ? c_hi - c_lo : n_chunks_all;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < L::kStages; s++) {
@@ -260,7 +281,7 @@ conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
                     ok = false;
                     break;
                 }
-                const int tap = it / kblocks, kb = it - tap * kblocks;
+                const int tap = (it0 + it) / kblocks, kb = (it0 + it) - tap * kblocks;
                 const int c = kb * kBK;
                 const int row = t0 - (a.taps - 1 - tap) * a.dilation;
                 uint8_t *st = tiles + s * L::kStage;
@@ -342,7 +363,51 @@ conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
             __syncwarp();
             if (lane == 0) bulk::mbar_arrive(&acc_empty[j & 1]);
         }
-        if (ok) {
+        // Split-K: every CTA of the cluster writes its partial tile into its own ring; then
+        // rank r finishes rows [r * 128 / S, (r + 1) * 128 / S) of the tile with all 256
+        // drain threads (float4 items, partials summed in rank order 0..S-1, the same
+        // epilogue4 per item) and skips the per-warp epilogue below.
+        bool mine = true;
+        if (SPLITK) {
+            namespace cg = cooperative_groups;
+            cg::cluster_group cluster = cg::this_cluster();
+            float *part = reinterpret_cast<float *>(tiles);  // the ring: every MMA has completed
+            if (ok) {
+                const int row = q * 32 + lane;
+#pragma unroll
+                for (int i = 0; i < L::kHalf; i += 4)
+                    *reinterpret_cast<float4 *>(part + row * L::kPartPitch + half * L::kHalf +
+                                                i) = make_float4(sum[i], sum[i + 1], sum[i + 2],
+                                                                 sum[i + 3]);
+            }
+            cluster.sync();  // every partial written (release / acquire across the cluster)
+            mine = false;
+            const int rows_per = kBM / S, n4 = rows_per * (BN / 4);
+            const int row_lo = split * rows_per;
+            for (int i = (int)threadIdx.x - 64; ok && i < n4; i += 32 * kEpiWarps) {
+                const int rr = i / (BN / 4), c4 = (i - rr * (BN / 4)) * 4;
+                const int row = row_lo + rr;
+                const int64_t orow = out_row(t0 + row);
+                float v[4] = {0.f, 0.f, 0.f, 0.f};
+                for (int r = 0; r < S; r++) {
+                    const float4 pv = *reinterpret_cast<const float4 *>(
+                        cluster.map_shared_rank(part, r) + row * L::kPartPitch + c4);
+                    v[0] += pv.x;
+                    v[1] += pv.y;
+                    v[2] += pv.z;
+                    v[3] += pv.w;
+                }
+                if (orow < 0) continue;
+                const int c = n0 + c4;
+                const EpiParams prm = epi_params<EPI>(a, c);
+                float4 xr = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (EPI == kEpiResidual || EPI == kEpiScaleResidual)
+                    xr = *reinterpret_cast<const float4 *>(a.x + (size_t)orow * a.c_out + c);
+                epilogue4<PASSES, EPI>(a, prm, v, xr, (size_t)orow, c);
+            }
+            cluster.sync();  // no CTA exits while its partial is still being read
+        }
+        if (ok && mine) {
             // Coalesced epilogue: the warp's 32 rows x GW columns of sums go through a
             // padded shared-memory buffer (row per lane in, conflict-free) and come back
             // as GW/4 lanes per row, 4 consecutive channels each, so every global load and
@@ -391,6 +456,10 @@ conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
                 __syncwarp();
             }
         }
+    }
+    if (SPLITK && warp < 2) {  // the producer and MMA warps join the drain warps' two barriers
+        cooperative_groups::this_cluster().sync();
+        cooperative_groups::this_cluster().sync();
     }
     if (!ok && a.err) atomicOr(a.err, LAI_DEVERR_TIMEOUT);
     umma::fence_before_sync();
@@ -447,6 +516,21 @@ bool weight_map(CUtensorMap *m, const float *w, int taps, int c_out, int c_in, i
                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// SMs of the current device (cached per device; 148 on B200).
+int sm_count() {
+    static int cached[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (cached[dev] == 0) {
+        int n = 0;
+        cached[dev] = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) ==
+                                  cudaSuccess && n > 0
+                          ? n
+                          : 148;
+    }
+    return cached[dev];
+}
+
 int pick_bn(int c_out) {
     if (c_out <= 384) {  // narrow outputs: tiles that fit two CTAs per SM
         for (int bn : {128, 96, 64, 32})
@@ -461,14 +545,40 @@ template <int BN, int PASSES, int EPI>
 int launch_conv_t(const CUtensorMap &am, const CUtensorMap &wm, const ConvArgs &a, int batch,
                   cudaStream_t st) {
     using L = Tile<BN, PASSES>;
-    auto kern = conv_umma_kernel<BN, PASSES, EPI>;
+    auto kern = conv_umma_kernel<BN, PASSES, EPI, false>;
+    auto kern_split = conv_umma_kernel<BN, PASSES, EPI, true>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kSmem) !=
         cudaSuccess)
         return LAI_ERR_CUDA;
     const unsigned phases = a.phases > 1 ? (unsigned)a.phases : 1u;
     const long long tiles = (long long)((a.T + kBM - 1) / kBM) * (a.c_out / BN) * phases * batch;
     if (tiles > 0x7fffffffLL) return LAI_ERR_TOOBIG;
-    kern<<<(unsigned)tiles, kThreads, L::kSmem, st>>>(am, wm, a);
+    // Split-K while the grid stays within one wave of resident CTAs and every split keeps
+    // at least two K chunks (64 input channels).
+    const int chunks = (a.taps * (a.c_in / kBK) + L::kChunk - 1) / L::kChunk;
+    const long long slots = (long long)L::kMinBlocks * sm_count();
+    int S = 1;
+    while (S < 8 && tiles * 2 * S <= slots && chunks / (2 * S) >= 2) S *= 2;
+    if (S == 1) {
+        kern<<<(unsigned)tiles, kThreads, L::kSmem, st>>>(am, wm, a);
+        return launch_status();
+    }
+    if (cudaFuncSetAttribute(kern_split, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)L::kSmem) != cudaSuccess)
+        return LAI_ERR_CUDA;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(tiles * S));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = L::kSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)S;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern_split, am, wm, a) != cudaSuccess) return LAI_ERR_CUDA;
     return launch_status();
 }
 

@@ -123,8 +123,81 @@ int launch_final(float *audio, const float *x, const float *ea, const float *ieb
     return launch_status();
 }
 
+// RVQ decode's gather: row t of out is the 16 codebook rows codes[t, 0..n_cb) laid side by
+// side, [T, n_cb * dim]; one GEMM against the packed projections then sums the codebooks.
+__global__ void rvq_gather_kernel(float4 *__restrict__ out, const float4 *__restrict__ books,
+                                  const int64_t *__restrict__ codes, int64_t T, int n_cb,
+                                  int cb_size, int dim4, int *err) {
+    const int64_t n = T * n_cb * dim4;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t tc = i / dim4;  // (t, cb)
+        const int d = (int)(i - tc * dim4);
+        const int cb = (int)(tc % n_cb);
+        const int64_t code = codes[tc];
+        if (code < 0 || code >= cb_size) {
+            out[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (d == 0 && err) atomicOr(err, LAI_DEVERR_TOKEN_ID);
+            continue;
+        }
+        out[i] = books[((int64_t)cb * cb_size + code) * dim4 + d];
+    }
+}
+
 }  // namespace
 }  // namespace lai
+
+extern "C" int lai_voc_rvq_gather_f32(float *out, const float *codebooks, const int64_t *codes,
+                                      int T, int n_codebooks, int codebook_size, int dim,
+                                      int *err, lai_stream_t stream) {
+    using namespace lai;
+    if (!out || !codebooks || !codes || T < 0 || n_codebooks <= 0 || codebook_size <= 0 ||
+        dim <= 0 || dim % 4 != 0 || !aligned16(out) || !aligned16(codebooks))
+        return LAI_ERR_INVALID;
+    if (T == 0) return LAI_OK;
+    const size_t ob = (size_t)T * n_codebooks * dim * 4;
+    if (overlaps(out, ob, codebooks, (size_t)n_codebooks * codebook_size * dim * 4))
+        return LAI_ERR_ALIAS;
+    const int64_t n = (int64_t)T * n_codebooks * (dim / 4);
+    rvq_gather_kernel<<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(
+        reinterpret_cast<float4 *>(out), reinterpret_cast<const float4 *>(codebooks), codes, T,
+        n_codebooks, codebook_size, dim / 4, err);
+    return launch_status();
+}
+
+// x_res[rows, c_out] += gamma * (in[rows, c_in] . W^T + bias): the pre-transformer's o / down
+// projection with its LayerScale and residual (src/tts_vocoder_xfmr.c:182-186, 203-207), on
+// the same tcgen05 kernel as the convolutions (k = 1), F32 through the 3xTF32 split.
+extern "C" int lai_voc_linear_scale_residual_f32(float *x_res, const float *in, float *scratch,
+                                                 const float *w, const float *bias,
+                                                 const float *gamma, int rows, int c_in,
+                                                 int c_out, int passes, int *err,
+                                                 lai_stream_t stream) {
+    using namespace lai;
+    if (!x_res || !in || !scratch || !w || !bias || !gamma || rows < 0 ||
+        (passes != 1 && passes != 3))
+        return LAI_ERR_INVALID;
+    if (rows == 0) return LAI_OK;
+    if (c_in % 32 != 0 || c_out % 32 != 0 || !aligned16(x_res) || !aligned16(in) ||
+        !aligned16(scratch) || !aligned16(w))
+        return LAI_ERR_INVALID;
+    const size_t in_plane = (size_t)rows * c_in, out_plane = (size_t)rows * c_out;
+    if (overlaps(x_res, out_plane * 4, in, in_plane * 4) ||
+        overlaps(x_res, out_plane * 4, scratch, 2 * in_plane * 4) ||
+        overlaps(in, in_plane * 4, scratch, 2 * in_plane * 4))
+        return LAI_ERR_ALIAS;
+    if (!encode_fn()) return LAI_ERR_CUDA;
+    const cudaStream_t st = as_stream(stream);
+    int rc = launch_split(in, scratch, scratch + in_plane, in_plane, passes, st);
+    if (rc != LAI_OK) return rc;
+    CUtensorMap am, wm;
+    if (!act_map(&am, scratch, 1, rows, c_in) ||
+        !weight_map(&wm, w, 1, c_out, c_in, pick_bn(c_out)))
+        return LAI_ERR_INVALID;
+    const ConvArgs a{nullptr, nullptr, x_res, bias, nullptr, nullptr, gamma,
+                     rows, c_in, c_out, 1, 1, err, 1, rows, 0};
+    return launch_conv<kEpiScaleResidual>(passes, am, wm, a, 1, st);
+}
 
 extern "C" int lai_voc_conv1d_f32(float *out, const float *x, float *scratch, const float *w,
                                   const float *bias, int batch, int c_in, int c_out, int T,

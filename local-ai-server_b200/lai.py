@@ -57,6 +57,12 @@ SIGNATURES: dict[str, tuple] = {
     "lai_gemv_swiglu_f32w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
     "lai_quantize_rows_i8_bf16": (_i32, [_vp, _vp, _vp, _i32, _i32, _vp]),
     "lai_logits_mask_range_f32": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _f32, _vp]),
+    "lai_prefill_attention_f32": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _f32, _vp]),
+    "lai_prefill_attention_rope_f32": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
+                                              _i32, _f32, _vp, _vp, _i64, _vp]),
+    "lai_voc_rvq_gather_f32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp]),
+    "lai_voc_linear_scale_residual_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32,
+                                                 _i32, _vp, _vp]),
     "lai_history_append_i32": (_i32, [_vp, _vp, _vp, _i32, _i32, _vp, _vp]),
     "lai_convert_bf16_to_f16": (_i32, [_vp, _vp, _i64, _vp]),
     "lai_decode_attention_scratch_bytes": (ctypes.c_size_t, [_i32, _i32, _i32, _i32]),
@@ -329,6 +335,57 @@ def history_append(history, history_len, tokens, err=None, stream=None):
     rows, stride = (1, history.shape[0]) if history.dim() == 1 else history.shape
     call("lai_history_append_i32", _p(history), _p(history_len), _p(tokens), rows, stride,
          _p(err), _s(stream))
+
+
+def prefill_attention(q, k, v, n_heads, n_kv_heads, head_dim, scale=None, out=None,
+                      stream=None):
+    """Causal self-attention: q [T, H*hd], k / v [T, Hkv*hd] -> out [T, H*hd]."""
+    import torch
+    T = q.shape[0]
+    out = torch.empty_like(q) if out is None else out
+    call("lai_prefill_attention_f32", _p(out), _p(q), _p(k), _p(v), T, n_heads, n_kv_heads,
+         head_dim, head_dim ** -0.5 if scale is None else scale, _s(stream))
+    return out
+
+
+def prefill_attention_rope(qkv, n_heads, n_kv_heads, head_dim, cos_t, sin_t, scale=None,
+                           out=None, stream=None):
+    """Causal self-attention with NeoX RoPE on q and k, read from a fused projection output
+    qkv [T, (H + 2 Hkv) hd] (q | k | v column blocks) -> out [T, H*hd]."""
+    import torch
+    T = qkv.shape[0]
+    qd, kvd = n_heads * head_dim, n_kv_heads * head_dim
+    out = torch.empty((T, qd), dtype=torch.float32, device=qkv.device) if out is None else out
+    base, ld = qkv.data_ptr(), qkv.stride(0)
+    call("lai_prefill_attention_rope_f32", _p(out), base, base + 4 * qd, base + 4 * (qd + kvd), ld,
+         ld, T, n_heads, n_kv_heads, head_dim, head_dim ** -0.5 if scale is None else scale,
+         _p(cos_t), _p(sin_t), 0 if cos_t is None else cos_t.shape[0], _s(stream))
+    return out
+
+
+def voc_rvq_gather(codebooks, codes, out=None, err=None, stream=None):
+    """codebooks [n_cb, size, dim] F32, codes [T, n_cb] int64 -> [T, n_cb*dim]."""
+    import torch
+    n_cb, size, dim = codebooks.shape
+    T = codes.shape[0]
+    out = torch.empty((T, n_cb * dim), dtype=torch.float32, device=codes.device) if out is None else out
+    call("lai_voc_rvq_gather_f32", _p(out), _p(codebooks), _p(codes), T, n_cb, size, dim, _p(err),
+         _s(stream))
+    return out
+
+
+def voc_linear_scale_residual(x_res, inp, w_packed, bias, gamma, scratch=None, passes=3, err=None,
+                              stream=None):
+    """x_res [rows, c_out] += gamma * (inp [rows, c_in] . W^T + bias); w_packed from
+    voc_pack_conv(W[c_out, c_in, 1])."""
+    import torch
+    rows, c_in = inp.shape
+    c_out = x_res.shape[1]
+    if scratch is None:
+        scratch = torch.empty(2 * rows * c_in, dtype=torch.float32, device=inp.device)
+    call("lai_voc_linear_scale_residual_f32", _p(x_res), _p(inp), _p(scratch), _p(w_packed),
+         _p(bias), _p(gamma), rows, c_in, c_out, passes, _p(err), _s(stream))
+    return x_res
 
 
 def decode_attention_scratch(n_seqs, n_heads, n_kv_heads, max_seq, device="cuda"):

@@ -372,7 +372,7 @@ class VocFullDecoder:
     Every step recomputes from the same input."""
 
     def __init__(self, t_frames: int = 500, batch: int = 1, passes: int = 3, seed: int = 88,
-                 device="cuda"):
+                 device="cuda", x_in=None):
         import torch
         self.batch, self.passes, self.t_frames = batch, passes, t_frames
         k = 0
@@ -385,7 +385,7 @@ class VocFullDecoder:
             return t
 
         C = 1024
-        self.x_in = normal((batch, t_frames, C))
+        self.x_in = normal((batch, t_frames, C)) if x_in is None else x_in
         self.ups = []
         t = t_frames
         for _ in range(2):
@@ -469,6 +469,208 @@ class VocFullDecoder:
         r += self.dec.rows_per_launch()
         r.append(B * self.t_final)
         return r
+
+
+RVQ_CODEBOOKS, RVQ_SIZE, RVQ_DIM, RVQ_OUT = 16, 2048, 256, 512
+PRE_CONV_OUT, PRE_CONV_KERNEL = 1024, 3
+XFMR_LAYERS, XFMR_HIDDEN, XFMR_ATTN, XFMR_HEADS, XFMR_HD, XFMR_INTER = 8, 512, 1024, 16, 64, 1024
+XFMR_EPS, XFMR_THETA = 1e-5, 10000.0
+
+
+class VocFront:
+    """tts_vocoder_run stages 1-3 (src/tts_vocoder.c:589-640) on the device, channels-last:
+    codes [T, 16] int64 -> RVQ decode (rvq_decode, :428-455: 16 codebook lookups [2048, 256]
+    each projected 256 -> 512 and summed) -> pre_conv CausalConv1d 512 -> 1024, k = 3
+    (:612-616) -> the 8-layer pre-transformer (voc_pre_transformer,
+    src/tts_vocoder_xfmr.c:126-225: input_proj 1024 -> 512 + bias; per layer RMSNorm, q/k/v
+    512 -> 1024, NeoX RoPE (theta 1e4), causal attention over 16 heads of 64, o 1024 -> 512
+    with LayerScale + residual, RMSNorm, SwiGLU MLP 512 -> 1024 -> 512 with LayerScale +
+    residual; final RMSNorm, output_proj 512 -> 1024 + bias) -> y [T, 1024], the layout
+    VocFullDecoder takes. The reference transposes [C, T] <-> [T, C] around the transformer;
+    channels-last throughout needs no transpose.
+
+    Device form: RVQ is one gather of the 16 codebook rows of a frame side by side ([T, 4096])
+    and one GEMM against the 16 projections laid side by side (K = 4096), which sums the
+    codebooks inside the accumulator; q|k|v and gate|up are each one GEMM over the
+    concatenated (gate/up row-interleaved) weights; attention reads q, k, v out of the q|k|v
+    output with RoPE folded in; o and down add their LayerScale'd output into the residual in
+    the GEMM epilogue. All linears are 3xTF32 tcgen05 GEMMs (F32 parity). Weights in the
+    reference's layouts are kept in `ref` for the checker."""
+
+    def __init__(self, t_frames: int = 500, passes: int = 3, seed: int = 99, device="cuda"):
+        import torch
+        self.t, self.passes = t_frames, passes
+        T = t_frames
+        k = 0
+
+        def normal(shape, std=1.0, mean=0.0):
+            nonlocal k
+            t = torch.empty(shape, dtype=torch.float32, device=device)
+            lai.synth_normal(t, seed=seed + k, mean=mean, std=std)
+            k += 1
+            return t
+
+        f32 = dict(dtype=torch.float32, device=device)
+        codes = torch.empty((T, RVQ_CODEBOOKS), dtype=torch.int32, device=device)
+        lai.synth_uniform_i32(codes, seed + 500, 0, RVQ_SIZE)
+        self.codes = codes.to(torch.int64)
+        H, A, I = XFMR_HIDDEN, XFMR_ATTN, XFMR_INTER
+        ref = {"codebooks": normal((RVQ_CODEBOOKS, RVQ_SIZE, RVQ_DIM)),
+               "proj": normal((RVQ_CODEBOOKS, RVQ_OUT, RVQ_DIM), RVQ_DIM ** -0.5 / 4),
+               "pre_w": normal((PRE_CONV_OUT, RVQ_OUT, PRE_CONV_KERNEL), (3 * RVQ_OUT) ** -0.5),
+               "pre_b": normal(PRE_CONV_OUT, 0.01),
+               "in_w": normal((H, PRE_CONV_OUT), PRE_CONV_OUT ** -0.5), "in_b": normal(H, 0.01),
+               "final_norm": normal(H, 0.1, 1.0),
+               "out_w": normal((PRE_CONV_OUT, H), H ** -0.5), "out_b": normal(PRE_CONV_OUT, 0.01),
+               "layers": []}
+        for _ in range(XFMR_LAYERS):
+            ref["layers"].append({
+                "in_norm": normal(H, 0.1, 1.0), "wq": normal((A, H), H ** -0.5),
+                "wk": normal((A, H), H ** -0.5), "wv": normal((A, H), H ** -0.5),
+                "wo": normal((H, A), A ** -0.5), "attn_ls": normal(H, 0.1),
+                "post_norm": normal(H, 0.1, 1.0), "gate": normal((I, H), H ** -0.5),
+                "up": normal((I, H), H ** -0.5), "down": normal((H, I), I ** -0.5),
+                "mlp_ls": normal(H, 0.1)})
+        self.ref = ref
+        pk = lambda w: lai.voc_pack_conv(w if w.dim() == 3 else w.unsqueeze(-1))  # noqa: E731
+        # the 16 projections side by side: W[o, cb*256 + d] = proj[cb][o, d]
+        self.rvq_w = pk(ref["proj"].permute(1, 0, 2).reshape(RVQ_OUT, RVQ_CODEBOOKS * RVQ_DIM))
+        self.pre_w, self.in_w, self.out_w = pk(ref["pre_w"]), pk(ref["in_w"]), pk(ref["out_w"])
+        self.layers = []
+        for L in ref["layers"]:
+            gu = torch.stack([L["gate"], L["up"]], dim=1).reshape(2 * I, H)  # rows g0,u0,g1,u1..
+            self.layers.append({"qkv": pk(torch.cat([L["wq"], L["wk"], L["wv"]])), "gu": pk(gu),
+                                "o": pk(L["wo"]), "down": pk(L["down"])})
+        self.zeros = torch.zeros(3 * A, **f32)
+        pos = torch.arange(T, dtype=torch.int32, device=device)
+        self.cos, self.sin = lai.rope_table(pos, T, XFMR_HD, XFMR_THETA, device=device)
+        self.g = torch.empty((T, RVQ_CODEBOOKS * RVQ_DIM), **f32)
+        self.rvq = torch.empty((1, T, RVQ_OUT), **f32)
+        self.pre = torch.empty((1, T, PRE_CONV_OUT), **f32)
+        self.x = torch.empty((T, H), **f32)
+        self.xn = torch.empty((T, H), **f32)
+        self.qkv = torch.empty((T, 3 * A), **f32)
+        self.attn = torch.empty((T, A), **f32)
+        self.gu = torch.empty((T, 2 * I), **f32)
+        self.ffn = torch.empty((T, I), **f32)
+        self.y = torch.empty((1, T, PRE_CONV_OUT), **f32)
+        self.scratch = torch.empty(2 * T * RVQ_CODEBOOKS * RVQ_DIM, **f32)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.kernel_names = ("rvq_gather", "rvq_proj", "pre_conv", "input_proj") + tuple(
+            f"layer{i}_{n}" for i in range(XFMR_LAYERS)
+            for n in ("norm1", "qkv", "attention", "o_scale_residual", "norm2", "gate_up",
+                      "swiglu", "down_scale_residual")) + ("final_norm", "output_proj")
+        self.rows_step = T
+
+    def _conv(self, out, x, w, bias, c_in, c_out, kernel, stream):
+        lai.call("lai_voc_conv1d_f32", lai._p(out), lai._p(x), lai._p(self.scratch), lai._p(w),
+                 lai._p(bias), 1, c_in, c_out, self.t, kernel, 1, self.passes, lai._p(self.err),
+                 lai._s(stream))
+
+    def _scale_res(self, inp, w, gamma, c_in, stream):
+        lai.call("lai_voc_linear_scale_residual_f32", lai._p(self.x), lai._p(inp),
+                 lai._p(self.scratch), lai._p(w), lai._p(self.zeros), lai._p(gamma), self.t, c_in,
+                 XFMR_HIDDEN, self.passes, lai._p(self.err), lai._s(stream))
+
+    def launches(self, stream=None):
+        T, H, A, I = self.t, XFMR_HIDDEN, XFMR_ATTN, XFMR_INTER
+        r = self.ref
+        L = [lambda: lai.call("lai_voc_rvq_gather_f32", lai._p(self.g), lai._p(r["codebooks"]),
+                              lai._p(self.codes), T, RVQ_CODEBOOKS, RVQ_SIZE, RVQ_DIM,
+                              lai._p(self.err), lai._s(stream)),
+             lambda: self._conv(self.rvq, self.g, self.rvq_w, self.zeros,
+                                RVQ_CODEBOOKS * RVQ_DIM, RVQ_OUT, 1, stream),
+             lambda: self._conv(self.pre, self.rvq, self.pre_w, r["pre_b"], RVQ_OUT,
+                                PRE_CONV_OUT, PRE_CONV_KERNEL, stream),
+             lambda: self._conv(self.x, self.pre, self.in_w, r["in_b"], PRE_CONV_OUT, H, 1,
+                                stream)]
+        for R, W in zip(r["layers"], self.layers):
+            L += [lambda R=R: lai.rmsnorm(self.x, R["in_norm"], XFMR_EPS, y=self.xn, stream=stream),
+                  lambda W=W: self._conv(self.qkv, self.xn, W["qkv"], self.zeros, H, 3 * A, 1,
+                                         stream),
+                  lambda: lai.prefill_attention_rope(self.qkv, XFMR_HEADS, XFMR_HEADS, XFMR_HD,
+                                                     self.cos, self.sin, out=self.attn,
+                                                     stream=stream),
+                  lambda R=R, W=W: self._scale_res(self.attn, W["o"], R["attn_ls"], A, stream),
+                  lambda R=R: lai.rmsnorm(self.x, R["post_norm"], XFMR_EPS, y=self.xn,
+                                          stream=stream),
+                  lambda W=W: self._conv(self.gu, self.xn, W["gu"], self.zeros, H, 2 * I, 1,
+                                         stream),
+                  lambda: lai.swiglu(self.gu, I, out=self.ffn, stream=stream),
+                  lambda R=R, W=W: self._scale_res(self.ffn, W["down"], R["mlp_ls"], I, stream)]
+        L += [lambda: lai.rmsnorm(self.x, r["final_norm"], XFMR_EPS, y=self.xn, stream=stream),
+              lambda: self._conv(self.y, self.xn, self.out_w, r["out_b"], H, PRE_CONV_OUT, 1,
+                                 stream)]
+        return L
+
+    def flops_per_launch(self) -> list[float]:
+        T, H, A, I = self.t, XFMR_HIDDEN, XFMR_ATTN, XFMR_INTER
+        f = [0.0, 2.0 * T * RVQ_CODEBOOKS * RVQ_DIM * RVQ_OUT,
+             2.0 * T * RVQ_OUT * PRE_CONV_OUT * PRE_CONV_KERNEL, 2.0 * T * PRE_CONV_OUT * H]
+        attn = 2.0 * 2 * XFMR_HEADS * XFMR_HD * T * (T + 1) / 2  # q.k and p.v over keys <= t
+        f += [0.0, 2.0 * T * H * 3 * A, attn, 2.0 * T * A * H, 0.0, 2.0 * T * H * 2 * I, 0.0,
+              2.0 * T * I * H] * XFMR_LAYERS
+        return f + [0.0, 2.0 * T * H * PRE_CONV_OUT]
+
+    def bytes_per_launch(self) -> list[int]:
+        T, H, A, I = self.t, XFMR_HIDDEN, XFMR_ATTN, XFMR_INTER
+        G = RVQ_CODEBOOKS * RVQ_DIM
+        conv = lambda ci, co, k: 4 * (T * ci + T * co + 2 * k * co * ci + co)  # noqa: E731
+        b = [T * RVQ_CODEBOOKS * 8 + 2 * 4 * T * G, conv(G, RVQ_OUT, 1),
+             conv(RVQ_OUT, PRE_CONV_OUT, PRE_CONV_KERNEL), conv(PRE_CONV_OUT, H, 1)]
+        b += [4 * (2 * T * H + H), conv(H, 3 * A, 1), 4 * (T * 3 * A + 2 * T * XFMR_HD + T * A),
+              conv(A, H, 1) + 4 * (T * H + H), 4 * (2 * T * H + H), conv(H, 2 * I, 1),
+              4 * (T * 2 * I + T * I), conv(I, H, 1) + 4 * (T * H + H)] * XFMR_LAYERS
+        return b + [4 * (2 * T * H + H), conv(H, PRE_CONV_OUT, 1)]
+
+    def rows_per_launch(self) -> list[int]:
+        return [self.t] * len(self.kernel_names)
+
+
+class VocCodesToAudio:
+    """The whole tts_vocoder_run on the device (config v4, src/tts_vocoder.c:589-758):
+    VocFront (codes -> pre-transformer output) then VocFullDecoder (-> audio) on the front's
+    output buffer; for 500 codec frames (40 s of audio) 500 x 16 codes in, 959445 samples
+    out. Every step recomputes from the same codes."""
+
+    def __init__(self, t_frames: int = 500, passes: int = 3, seed: int = 99, device="cuda"):
+        self.front = VocFront(t_frames, passes=passes, seed=seed, device=device)
+        self.dec = VocFullDecoder(t_frames, batch=1, passes=passes, seed=seed + 5000,
+                                  device=device, x_in=self.front.y)
+        self.codes, self.audio, self.t_frames = self.front.codes, self.dec.audio, t_frames
+        self.kernel_names = self.front.kernel_names + self.dec.kernel_names
+        self.rows_step = self.dec.rows_step
+        self.err = self.front.err
+        self.graph = None
+
+    def launches(self, stream=None):
+        return self.front.launches(stream) + self.dec.launches(stream)
+
+    def run(self, graph: bool = False):
+        """codes -> audio once. graph: replay the ~150 launches as one CUDA graph (captured on
+        first use; the codes and audio buffers stay where they are, so new codes copied into
+        `codes` are picked up by the next replay)."""
+        import torch
+        if not graph:
+            for f in self.launches():
+                f()
+            return self.audio
+        if self.graph is None:
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph):
+                for f in self.launches():
+                    f()
+        self.graph.replay()
+        return self.audio
+
+    def flops_per_launch(self) -> list[float]:
+        return self.front.flops_per_launch() + self.dec.flops_per_launch()
+
+    def bytes_per_launch(self) -> list[int]:
+        return self.front.bytes_per_launch() + self.dec.bytes_per_launch()
+
+    def rows_per_launch(self) -> list[int]:
+        return self.front.rows_per_launch() + self.dec.rows_per_launch()
 
 
 class VocConvNeXt:

@@ -357,6 +357,45 @@ void oracle_linear_bf16(float *out, const float *in, const uint16_t *W, int M, i
 }
 
 /* ---------------------------------------------------------------------------
+ * Causal self-attention over a sequence: qwen_causal_attention(out, q, k, v, T, T, heads,
+ * kv_heads, hd, scale, 0) as the vocoder's pre-transformer calls it
+ * (src/tts_vocoder_xfmr.c:172-180); the math of tools/verify_xfmr.py:57-77: scores
+ * q.k * scale over keys 0..t, max-subtracted softmax, weighted sum of v. The function body is
+ * in the un-vendored qwen-asr sources, so this follows the spec, in acc_t.
+ * ------------------------------------------------------------------------- */
+void oracle_causal_attention(float *out, const float *q, const float *k, const float *v, int T,
+                             int n_heads, int n_kv_heads, int head_dim, float scale) {
+    const int group = n_heads / n_kv_heads;
+    const int ldq = n_heads * head_dim, ldk = n_kv_heads * head_dim;
+#pragma omp parallel for schedule(dynamic)
+    for (int th = 0; th < T * n_heads; th++) {
+        const int t = th / n_heads, h = th % n_heads, kvh = h / group;
+        const float *qr = q + (size_t)t * ldq + (size_t)h * head_dim;
+        acc_t *sc = (acc_t *)malloc(sizeof(acc_t) * (size_t)(t + 1));
+        acc_t mx = -1e300;
+        for (int j = 0; j <= t; j++) {
+            const float *kr = k + (size_t)j * ldk + (size_t)kvh * head_dim;
+            acc_t s = 0;
+            for (int d = 0; d < head_dim; d++) s += (acc_t)qr[d] * (acc_t)kr[d];
+            sc[j] = s * (acc_t)scale;
+            if (sc[j] > mx) mx = sc[j];
+        }
+        acc_t den = 0;
+        for (int j = 0; j <= t; j++) {
+            sc[j] = (acc_t)exp((double)(sc[j] - mx));
+            den += sc[j];
+        }
+        float *o = out + (size_t)t * ldq + (size_t)h * head_dim;
+        for (int d = 0; d < head_dim; d++) {
+            acc_t a = 0;
+            for (int j = 0; j <= t; j++) a += sc[j] * (acc_t)v[(size_t)j * ldk + (size_t)kvh * head_dim + d];
+            o[d] = (float)(a / den);
+        }
+        free(sc);
+    }
+}
+
+/* ---------------------------------------------------------------------------
  * The reference's other GPU weight formats for the same linears: FP16 (its fp16 mode),
  * INT8 with a per-row scale (its int8 mode) and F32 (src/tts_pipeline.h:37-40,
  * src/tts_native.c:1185-1240). The INT8 recipe is tools/asr_benchmarks.md:342-352:

@@ -70,6 +70,12 @@ void oracle_add_bf16(uint16_t *x, const uint16_t *y, int64_t n);
 /* ---- linear_bf16 (src/tts_native.c:66-79): out[M,N] = in[M,K] @ W[N,K]^T, W BF16 ---- */
 void oracle_linear_bf16(float *out, const float *in, const uint16_t *W, int M, int K, int N);
 
+/* ---- causal self-attention over a sequence (qwen_causal_attention with T queries, as
+ * src/tts_vocoder_xfmr.c:172-180 calls it; math tools/verify_xfmr.py:57-77) ----
+ * q / out [T, H*hd], k / v [T, Hkv*hd]; row t attends keys 0..t; sums in acc_t. */
+void oracle_causal_attention(float *out, const float *q, const float *k, const float *v, int T,
+                             int n_heads, int n_kv_heads, int head_dim, float scale);
+
 /* ---- the reference's other GPU weight formats (src/tts_pipeline.h:37-40,
  * src/tts_native.c:1185-1240; INT8 recipe tools/asr_benchmarks.md:342-352) ----
  * FP16 weights; INT8 weights with per-row scales, out = (sum_k q[n,k] x[m,k]) * scale[n];

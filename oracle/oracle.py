@@ -103,6 +103,7 @@ def _declare(lib: ctypes.CDLL) -> None:
                                    _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float],
         "oracle_linear_bf16": [_F, _F, _U16, _c_int, _c_int, _c_int],
         "oracle_linear_f16": [_F, _F, _U16, _c_int, _c_int, _c_int],
+        "oracle_causal_attention": [_F, _F, _F, _F, _c_int, _c_int, _c_int, _c_int, _c_float],
         "oracle_linear_i8": [_F, _F, _I8, _F, _c_int, _c_int, _c_int],
         "oracle_linear_f32": [_F, _F, _F, _c_int, _c_int, _c_int],
         "oracle_quantize_rows_i8_bf16": [_I8, _F, _U16, _c_int, _c_int],
@@ -342,6 +343,16 @@ def linear_bf16(x, W, lib=None):
     N = W.shape[0]
     out = np.empty((M, N), np.float32)
     lib.oracle_linear_bf16(ptr(out), ptr(x), ptr(W, _U16), M, K, N)
+    return out
+
+
+def causal_attention(q, k, v, n_heads, n_kv_heads, head_dim, scale=None, lib=None):
+    """Row t of q [T, H*hd] attends keys 0..t of k / v [T, Hkv*hd]."""
+    lib = lib or load()
+    q, k, v = (np.ascontiguousarray(a, np.float32) for a in (q, k, v))
+    out = np.empty_like(q)
+    lib.oracle_causal_attention(ptr(out), ptr(q), ptr(k), ptr(v), q.shape[0], n_heads,
+                                n_kv_heads, head_dim, head_dim ** -0.5 if scale is None else scale)
     return out
 
 
@@ -624,3 +635,40 @@ def voc_bigvgan_block(x, blk, lib=None):
             h = voc_resunit(h, {k: v for k, v in u.items() if k != "dilation"}, u["dilation"], lib)
         outs.append(h)
     return np.stack(outs)
+
+
+# ---- the vocoder's front: RVQ decode -> pre_conv -> pre-transformer ----
+
+def voc_front(p, codes, lib=None, linear=None):
+    """tts_vocoder_run stages 1-3 (src/tts_vocoder.c:589-640) restated from the oracle's
+    functions: rvq_decode (:428-455, the 16 projected codebook rows summed in codebook order),
+    voc_conv1d_causal pre_conv (:612-616, channels-first as the reference runs it), then
+    voc_pre_transformer (src/tts_vocoder_xfmr.c:126-225) in [T, C]. p: numpy arrays in the
+    reference's layouts (codebooks [16, 2048, 256], proj [16, 512, 256], pre_w [1024, 512, 3],
+    pre_b, in_w [512, 1024], in_b, layers: in_norm, wq / wk / wv [1024, 512], wo [512, 1024],
+    attn_ls, post_norm, gate / up [1024, 512], down [512, 1024], mlp_ls; final_norm,
+    out_w [1024, 512], out_b); codes [T, 16]. linear(x, W) defaults to linear_f32 (the
+    reference's linear_f32: out = x . W^T). Returns [T, 1024]."""
+    lib = lib or load()
+    lin = linear or (lambda x, W: linear_f32(x, W, lib=lib))
+    codes = np.asarray(codes)
+    T = codes.shape[0]
+    rvq = np.zeros((T, p["proj"].shape[1]), np.float32)
+    for cb in range(p["codebooks"].shape[0]):
+        rvq += lin(p["codebooks"][cb][codes[:, cb]], p["proj"][cb])
+    pre = voc_conv1d_causal(np.ascontiguousarray(rvq.T), p["pre_w"], p["pre_b"], lib=lib)
+    x = lin(np.ascontiguousarray(pre.T), p["in_w"]) + p["in_b"]
+    hd = 64
+    heads = p["layers"][0]["wq"].shape[0] // hd
+    cos_t, sin_t = compute_rope_neox(np.arange(T, dtype=np.int32), hd, 10000.0, lib=lib)
+    for L in p["layers"]:
+        xn = rms_norm(x, L["in_norm"], 1e-5, lib=lib)
+        q = apply_rope_neox(lin(xn, L["wq"]), cos_t, sin_t, heads, hd, lib=lib)
+        k = apply_rope_neox(lin(xn, L["wk"]), cos_t, sin_t, heads, hd, lib=lib)
+        a = causal_attention(q, k, lin(xn, L["wv"]), heads, heads, hd, lib=lib)
+        x = add_inplace(x, lin(a, L["wo"]) * L["attn_ls"], lib=lib)
+        xn = rms_norm(x, L["post_norm"], 1e-5, lib=lib)
+        ffn = swiglu_separate(lin(xn, L["gate"]), lin(xn, L["up"]), lib=lib)
+        x = add_inplace(x, lin(ffn, L["down"]) * L["mlp_ls"], lib=lib)
+    x = rms_norm(x, p["final_norm"], 1e-5, lib=lib)
+    return lin(x, p["out_w"]) + p["out_b"]
