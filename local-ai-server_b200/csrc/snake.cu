@@ -8,7 +8,9 @@
 //
 // Roofline: HBM, 8 bytes per element (read + write). With a full-range sinf the
 // kernel was issue-bound (ncu: 85% issue-active, ~41 instructions per element);
-// sin2_fast brings the arithmetic well under the HBM rate.
+// sin2_fast brought that to ~20, still ~60% of the issue rate the HBM rate needs at the
+// 1.7 GHz the power cap allows over a long sweep, so the vector body runs two elements per
+// instruction (snake2, Blackwell's packed FP32 FMA / MUL / ADD; same bits as snake1).
 //
 // Layout: snake_flat_kernel treats [batch*C rows, T] as one run of float4 vectors
 // and recovers each vector's row and channel by multiply-high division, so short
@@ -48,10 +50,10 @@ snake_kernel(float *x, const float *__restrict__ ea, const float *__restrict__ i
         for (int i = 0; i < kUnroll; i++) {
             const int64_t k = v0 + (int64_t)i * kThreads;
             if (k < nv) {
-                float4 r;
-                r.x = snake1(v[i].x, a, b); r.y = snake1(v[i].y, a, b);
-                r.z = snake1(v[i].z, a, b); r.w = snake1(v[i].w, a, b);
-                xv[k] = r;
+                const float2 a2 = make_float2(a, a), b2 = make_float2(b, b);
+                const float2 lo = snake2(make_float2(v[i].x, v[i].y), a2, b2);
+                const float2 hi = snake2(make_float2(v[i].z, v[i].w), a2, b2);
+                xv[k] = make_float4(lo.x, lo.y, hi.x, hi.y);
             }
         }
         if (blockIdx.x == 0) {
@@ -105,8 +107,10 @@ snake_flat_kernel(float *x, const float *__restrict__ ea, const float *__restric
         const float a = __ldg(ea + c), b = __ldg(ieb + c);
         float4 r;
         if (col + 3 < T) {
-            r.x = snake1(v[i].x, a, b); r.y = snake1(v[i].y, a, b);
-            r.z = snake1(v[i].z, a, b); r.w = snake1(v[i].w, a, b);
+            const float2 a2 = make_float2(a, a), b2 = make_float2(b, b);
+            const float2 lo = snake2(make_float2(v[i].x, v[i].y), a2, b2);
+            const float2 hi = snake2(make_float2(v[i].z, v[i].w), a2, b2);
+            r = make_float4(lo.x, lo.y, hi.x, hi.y);
         } else {  // the vector crosses into the next row (T % 4 != 0)
             const uint32_t c2 = c + 1 == C ? 0 : c + 1;
             const float a2 = __ldg(ea + c2), b2 = __ldg(ieb + c2);
