@@ -141,7 +141,11 @@ __device__ __forceinline__ EpiParams epi_params(const ConvArgs &a, int c) {
 
 // Epilogue for 4 finished sums of output row `row` (global index), channels [c, c + 4).
 // `xr` holds x[row, c..c+3] for the residual epilogues, loaded earlier.
-template <int PASSES, int EPI>
+// PACK: SnakeBeta two channels per instruction (snake2, same bits as snake1). Used by the
+// narrow tiles (BN <= 128, two CTAs per SM), where a shorter epilogue leaves the SM's other
+// CTA its shared-memory-bound mainloop alone for longer (the 96/128/192-channel blocks 2-3%
+// faster, the final step 14%); the one-CTA-per-SM BN = 256 tiles were 11% slower with it.
+template <int PASSES, int EPI, bool PACK>
 __device__ __forceinline__ void epilogue4(const ConvArgs &a, const EpiParams &q, float (&v)[4],
                                           const float4 &xr, size_t row, int c) {
     const size_t off = row * (size_t)a.c_out + c;
@@ -164,11 +168,20 @@ __device__ __forceinline__ void epilogue4(const ConvArgs &a, const EpiParams &q,
         if (a.ea == nullptr) return;
     }
     float hi[4];
+    if (PACK && EPI != kEpiGelu) {
+#pragma unroll
+        for (int i = 0; i < 4; i += 2) {
+            const float2 r = snake2(make_float2(v[i], v[i + 1]), make_float2(q.p1[i], q.p1[i + 1]),
+                                    make_float2(q.p2[i], q.p2[i + 1]));
+            v[i] = r.x;
+            v[i + 1] = r.y;
+        }
+    }
 #pragma unroll
     for (int i = 0; i < 4; i++) {
         if (EPI == kEpiGelu)
             v[i] = 0.5f * v[i] * (1.0f + erff(v[i] * 0.7071067811865475f));  // voc_gelu
-        else
+        else if (!PACK)
             v[i] = snake1(v[i], q.p1[i], q.p2[i]);
         hi[i] = umma::tf32_round(v[i]);
     }
@@ -403,7 +416,7 @@ conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
                 float4 xr = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (EPI == kEpiResidual || EPI == kEpiScaleResidual)
                     xr = *reinterpret_cast<const float4 *>(a.x + (size_t)orow * a.c_out + c);
-                epilogue4<PASSES, EPI>(a, prm, v, xr, (size_t)orow, c);
+                epilogue4<PASSES, EPI, (BN <= 128)>(a, prm, v, xr, (size_t)orow, c);
             }
             cluster.sync();  // no CTA exits while its partial is still being read
         }
@@ -447,7 +460,7 @@ conv_umma_kernel(const __grid_constant__ CUtensorMap act_map,
                         for (int i = 0; i < 4; i++) v[i] = buf[r * kEpiPitch + c4 + i];
                         const int64_t orow = out_row(row0 + r);
                         if (orow >= 0)
-                            epilogue4<PASSES, EPI>(
+                            epilogue4<PASSES, EPI, (BN <= 128)>(
                                 a, prm, v,
                                 EPI == kEpiResidual || EPI == kEpiScaleResidual ? xr[p] : xr[0],
                                 (size_t)orow, c);

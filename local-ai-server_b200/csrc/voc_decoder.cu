@@ -87,10 +87,16 @@ final_kernel(float *audio, const float *__restrict__ x, const float *__restrict_
                 const int r = i / V, c = 4 * (i - r * V), t = t0 - 6 + r;
                 const bool in = t >= 0 && t < T;
                 float *dst = s + r * pitch + c;
-                dst[0] = in ? snake1(v[u].x, sa[c], sb[c]) : 0.f;
-                dst[1] = in ? snake1(v[u].y, sa[c + 1], sb[c + 1]) : 0.f;
-                dst[2] = in ? snake1(v[u].z, sa[c + 2], sb[c + 2]) : 0.f;
-                dst[3] = in ? snake1(v[u].w, sa[c + 3], sb[c + 3]) : 0.f;
+                // two channels per instruction (snake2: same bits as snake1)
+                const float2 p0 = snake2(make_float2(v[u].x, v[u].y), make_float2(sa[c], sa[c + 1]),
+                                         make_float2(sb[c], sb[c + 1]));
+                const float2 p1 = snake2(make_float2(v[u].z, v[u].w),
+                                         make_float2(sa[c + 2], sa[c + 3]),
+                                         make_float2(sb[c + 2], sb[c + 3]));
+                dst[0] = in ? p0.x : 0.f;
+                dst[1] = in ? p0.y : 0.f;
+                dst[2] = in ? p1.x : 0.f;
+                dst[3] = in ? p1.y : 0.f;
             }
         }
     }

@@ -30,12 +30,15 @@ snake_split_kernel(const float *__restrict__ x, const float *__restrict__ ea,
          i += (int64_t)gridDim.x * blockDim.x) {
         const float4 v = reinterpret_cast<const float4 *>(x)[i];
         const int c = (int)((i * 4) % C);  // C % 4 == 0: the 4 lanes share a row
-        float y[4] = {v.x, v.y, v.z, v.w}, h[4];
+        // SnakeBeta two channels per instruction (snake2: same bits as snake1)
+        const float2 lo2 = snake2(make_float2(v.x, v.y), make_float2(__ldg(ea + c), __ldg(ea + c + 1)),
+                                  make_float2(__ldg(ieb + c), __ldg(ieb + c + 1)));
+        const float2 hi2 = snake2(make_float2(v.z, v.w),
+                                  make_float2(__ldg(ea + c + 2), __ldg(ea + c + 3)),
+                                  make_float2(__ldg(ieb + c + 2), __ldg(ieb + c + 3)));
+        float y[4] = {lo2.x, lo2.y, hi2.x, hi2.y}, h[4];
 #pragma unroll
-        for (int k = 0; k < 4; k++) {
-            y[k] = snake1(y[k], __ldg(ea + c + k), __ldg(ieb + c + k));
-            h[k] = umma::tf32_round(y[k]);
-        }
+        for (int k = 0; k < 4; k++) h[k] = umma::tf32_round(y[k]);
         reinterpret_cast<float4 *>(hi)[i] = make_float4(h[0], h[1], h[2], h[3]);
         if (PASSES == 3)
             reinterpret_cast<float4 *>(lo)[i] =
