@@ -177,16 +177,17 @@ prefill_attn_kernel(float *__restrict__ out, const float *__restrict__ q,
 #pragma unroll
             for (int jj = 0; jj < kGroup; jj++) {
                 const float4 *kr = reinterpret_cast<const float4 *>(sm.tile.k[jb + jj]);
-                float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+                // four partial sums as two packed pairs (FFMA2: the same per-lane FMAs)
+                float2 s01 = make_float2(0.f, 0.f), s23 = make_float2(0.f, 0.f);
 #pragma unroll
                 for (int d4 = 0; d4 < HD / 4; d4++) {
                     const float4 kk = kr[d4];
-                    s0 = fmaf(qr[4 * d4], kk.x, s0);
-                    s1 = fmaf(qr[4 * d4 + 1], kk.y, s1);
-                    s2 = fmaf(qr[4 * d4 + 2], kk.z, s2);
-                    s3 = fmaf(qr[4 * d4 + 3], kk.w, s3);
+                    s01 = __ffma2_rn(make_float2(qr[4 * d4], qr[4 * d4 + 1]),
+                                     make_float2(kk.x, kk.y), s01);
+                    s23 = __ffma2_rn(make_float2(qr[4 * d4 + 2], qr[4 * d4 + 3]),
+                                     make_float2(kk.z, kk.w), s23);
                 }
-                sc[jj] = (s0 + s1) + (s2 + s3);
+                sc[jj] = (s01.x + s01.y) + (s23.x + s23.y);
                 if (jj < nk) mn = fmaxf(mn, sc[jj]);
             }
             const float corr = exp2f(m - mn);
@@ -200,20 +201,20 @@ prefill_attn_kernel(float *__restrict__ out, const float *__restrict__ q,
             l = fmaf(l, corr, psum);
 #pragma unroll
             for (int d4 = 0; d4 < HD / 4; d4++) {
-                float a0 = acc[4 * d4] * corr, a1 = acc[4 * d4 + 1] * corr;
-                float a2 = acc[4 * d4 + 2] * corr, a3 = acc[4 * d4 + 3] * corr;
+                const float2 c2 = make_float2(corr, corr);
+                float2 a01 = __fmul2_rn(make_float2(acc[4 * d4], acc[4 * d4 + 1]), c2);
+                float2 a23 = __fmul2_rn(make_float2(acc[4 * d4 + 2], acc[4 * d4 + 3]), c2);
 #pragma unroll
                 for (int jj = 0; jj < kGroup; jj++) {
                     const float4 vv = reinterpret_cast<const float4 *>(sm.tile.v[jb + jj])[d4];
-                    a0 = fmaf(sc[jj], vv.x, a0);
-                    a1 = fmaf(sc[jj], vv.y, a1);
-                    a2 = fmaf(sc[jj], vv.z, a2);
-                    a3 = fmaf(sc[jj], vv.w, a3);
+                    const float2 p2 = make_float2(sc[jj], sc[jj]);
+                    a01 = __ffma2_rn(p2, make_float2(vv.x, vv.y), a01);
+                    a23 = __ffma2_rn(p2, make_float2(vv.z, vv.w), a23);
                 }
-                acc[4 * d4] = a0;
-                acc[4 * d4 + 1] = a1;
-                acc[4 * d4 + 2] = a2;
-                acc[4 * d4 + 3] = a3;
+                acc[4 * d4] = a01.x;
+                acc[4 * d4 + 1] = a01.y;
+                acc[4 * d4 + 2] = a23.x;
+                acc[4 * d4 + 3] = a23.y;
             }
         }
     }
