@@ -1,6 +1,9 @@
 // umma.cuh - 5th-generation tensor core (tcgen05) and TMA tensor-copy helpers, sm_100a.
 //
-// One CTA (cta_group::1), no clusters, no multicast. Operands are K-major tiles that a
+// Each MMA is issued for one CTA (cta_group::1) on operands in that CTA's own shared memory,
+// and every TMA copy fills only its own CTA's shared memory (no multicast). (Split-K GEMMs
+// group CTAs in clusters only to add their finished partial tiles through distributed
+// shared memory; see voc_conv.cuh.) Operands are K-major tiles that a
 // TMA tensor copy wrote into shared memory with the 64-byte swizzle; accumulators
 // live in tensor memory (TMEM) and come back to registers with tcgen05.ld.
 //
