@@ -149,8 +149,14 @@ template <int PASSES, int EPI, bool PACK>
 __device__ __forceinline__ void epilogue4(const ConvArgs &a, const EpiParams &q, float (&v)[4],
                                           const float4 &xr, size_t row, int c) {
     const size_t off = row * (size_t)a.c_out + c;
+    if (PACK) {  // two-wide FP32 adds: the same per-lane additions
+        const float2 b01 = __fadd2_rn(make_float2(v[0], v[1]), make_float2(q.bias[0], q.bias[1]));
+        const float2 b23 = __fadd2_rn(make_float2(v[2], v[3]), make_float2(q.bias[2], q.bias[3]));
+        v[0] = b01.x; v[1] = b01.y; v[2] = b23.x; v[3] = b23.y;
+    } else {
 #pragma unroll
-    for (int i = 0; i < 4; i++) v[i] += q.bias[i];
+        for (int i = 0; i < 4; i++) v[i] += q.bias[i];
+    }
     if (EPI == kEpiScaleResidual) {  // x = (W h + b) * gamma + x  (run_convnext order)
         const float r[4] = {xr.x, xr.y, xr.z, xr.w};
 #pragma unroll
@@ -159,7 +165,13 @@ __device__ __forceinline__ void epilogue4(const ConvArgs &a, const EpiParams &q,
         return;
     }
     if (EPI == kEpiResidual) {
-        v[0] += xr.x; v[1] += xr.y; v[2] += xr.z; v[3] += xr.w;
+        if (PACK) {
+            const float2 r01 = __fadd2_rn(make_float2(v[0], v[1]), make_float2(xr.x, xr.y));
+            const float2 r23 = __fadd2_rn(make_float2(v[2], v[3]), make_float2(xr.z, xr.w));
+            v[0] = r01.x; v[1] = r01.y; v[2] = r23.x; v[3] = r23.y;
+        } else {
+            v[0] += xr.x; v[1] += xr.y; v[2] += xr.z; v[3] += xr.w;
+        }
         store4(a.x + off, v[0], v[1], v[2], v[3]);
         if (a.ea == nullptr) return;
     }
@@ -187,7 +199,13 @@ __device__ __forceinline__ void epilogue4(const ConvArgs &a, const EpiParams &q,
     }
     store4(a.out_hi + off, hi[0], hi[1], hi[2], hi[3]);
     if (PASSES == 3)
-        store4(a.out_lo + off, v[0] - hi[0], v[1] - hi[1], v[2] - hi[2], v[3] - hi[3]);
+        if (PACK) {
+            const float2 l01 = __fadd2_rn(make_float2(v[0], v[1]), make_float2(-hi[0], -hi[1]));
+            const float2 l23 = __fadd2_rn(make_float2(v[2], v[3]), make_float2(-hi[2], -hi[3]));
+            store4(a.out_lo + off, l01.x, l01.y, l23.x, l23.y);
+        } else {
+            store4(a.out_lo + off, v[0] - hi[0], v[1] - hi[1], v[2] - hi[2], v[3] - hi[3]);
+        }
 }
 
 // Accumulation. The tensor core's F32 accumulation does not round to nearest: measured
