@@ -47,10 +47,13 @@ LAI_API void qwen_rms_norm(float *out, const float *x, const float *w, int seq, 
  * synchronisation. It stages through a fixed 8 MiB array compiled into the
  * library (held on every GPU that loads it) and calls no allocator: seq*dim*4
  * plus dim*4 bytes (each rounded up to 256) must fit in 8 MiB, else
- * LAI_ERR_TOOBIG. The first call on a device looks up the array's address, so
- * make it before any stream capture. Calls share the array: calls whose GPU work
- * overlaps (several threads or streams on one device) race; the call
- * synchronises `stream` before it returns. Returns a LAI_* status. */
+ * LAI_ERR_TOOBIG. With CUDA's default lazy module loading the array is claimed
+ * when the library's device code first loads on a device, which is inside the
+ * first call there: make that first call (or set CUDA_MODULE_LOADING=EAGER)
+ * before a pool allocator reserves the device's memory, and before any stream
+ * capture. Calls share the array: calls whose GPU work overlaps (several threads
+ * or streams on one device) race; the call synchronises `stream` before it
+ * returns, on error paths too. Returns a LAI_* status. */
 LAI_API int lai_rmsnorm_f32_host_noalloc(float *out, const float *x, const float *w, int seq,
                                          int dim, float eps, void *stream);
 /* src/tts_native.c:562-563, 644-645, 724-725 (in place) */

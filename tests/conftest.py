@@ -47,3 +47,28 @@ def max_rel_err(got, ref) -> float:
     if got.size == 0:
         return 0.0
     return float(np.max(np.abs(got - ref) / np.maximum(1.0, np.abs(ref))))
+
+
+# ---- real memory for argument-check tests ----
+# Calls that must be rejected by a host-side check still get pointers into a real,
+# zeroed allocation (on the GPU when there is one), large enough for every size those
+# tests pass, so that a regressed check would launch on owned memory, not on a made-up
+# address.
+ARENA_BYTES = 64 << 20
+_arena = None
+
+
+def arena_ptr(offset: int = 0):
+    """ctypes pointer `offset` bytes into the shared argument-check arena."""
+    import ctypes
+    global _arena
+    assert 0 <= offset < ARENA_BYTES
+    if _arena is None:
+        import torch
+        if torch.cuda.is_available():
+            _arena = torch.zeros(ARENA_BYTES, dtype=torch.uint8, device="cuda")
+        else:
+            import numpy as np
+            _arena = np.zeros(ARENA_BYTES, np.uint8)
+    base = _arena.data_ptr() if hasattr(_arena, "data_ptr") else _arena.ctypes.data
+    return ctypes.c_void_p(base + offset)

@@ -47,7 +47,10 @@ def extract_functions(path: str, names: list[str]) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("LAI_REFERENCE", "/root/reference"))
+    beside = os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", "..", "..", "reference")
+    ap.add_argument("--ref", default=os.environ.get("LAI_REFERENCE", os.path.normpath(beside)),
+                    help="the reference checkout (default: $LAI_REFERENCE, else a reference/ "
+                         "directory beside this repository)")
     args = ap.parse_args()
     ref = args.ref
     xf = extract_functions(os.path.join(ref, "tools", "verify_xfmr.py"),

@@ -9,6 +9,7 @@ import subprocess
 import pytest
 
 import lai
+from conftest import arena_ptr
 
 V = ctypes.c_void_p
 
@@ -45,23 +46,41 @@ def test_oracle_is_not_linked_into_the_product():
     assert "lai_oracle" not in deps and "cpuref" not in deps
 
 
-P = V(16)  # a non-NULL dummy pointer: never dereferenced, the checks fail first
+class _Arena:
+    """A(off): a pointer `off` bytes into a real, zeroed 64 MiB allocation (conftest)."""
+
+    def __call__(self, off):
+        return arena_ptr(off)
+
+
+A = _Arena()
+
+
+class _P:
+    """P: a non-NULL pointer into the arena; the checks below fail before any use."""
+
+    @property
+    def _as_parameter_(self):
+        return arena_ptr(16)
+
+
+P = _P()
 
 
 @pytest.mark.parametrize("call, want", [
     (lambda l: l.lai_rmsnorm_bf16(P, P, P, -1, 1024, 1e-6, None), lai.LAI_ERR_INVALID),
     (lambda l: l.lai_rmsnorm_f32(P, None, P, 4, 1024, 1e-6, None), lai.LAI_ERR_INVALID),
     (lambda l: l.lai_rmsnorm_f32(P, P, P, 4, 0, 1e-6, None), lai.LAI_ERR_INVALID),
-    (lambda l: l.lai_add_rmsnorm_bf16(V(4096), P, P, V(4096), 4, 256, 1e-6, None), lai.LAI_ERR_ALIAS),
+    (lambda l: l.lai_add_rmsnorm_bf16(A(4096), P, P, A(4096), 4, 256, 1e-6, None), lai.LAI_ERR_ALIAS),
     (lambda l: l.lai_qk_norm_rope_bf16(P, None, None, None, None, None, None, 0, 4, 16, 8, 128,
                                        1e-6, None, None), lai.LAI_ERR_INVALID),
     (lambda l: l.lai_qk_norm_rope_f32(P, None, P, None, None, None, None, 0, 4, 16, 8, 127,
                                       1e-6, None, None), lai.LAI_ERR_INVALID),
     (lambda l: l.lai_qk_norm_rope_f32(P, None, None, None, P, None, None, 8, 4, 16, 8, 128,
                                       1e-6, None, None), lai.LAI_ERR_INVALID),
-    (lambda l: l.lai_swiglu_bf16(V(4096 + 2), V(4096), 4, 64, None), lai.LAI_ERR_ALIAS),
+    (lambda l: l.lai_swiglu_bf16(A(4096 + 2), A(4096), 4, 64, None), lai.LAI_ERR_ALIAS),
     (lambda l: l.lai_swiglu_f32(P, P, 4, 0, None), lai.LAI_ERR_INVALID),
-    (lambda l: l.lai_add_f32(V(4096), V(4096 + 4), 64, None), lai.LAI_ERR_ALIAS),
+    (lambda l: l.lai_add_f32(A(4096), A(4096 + 4), 64, None), lai.LAI_ERR_ALIAS),
     (lambda l: l.lai_embed_gather_bf16(P, P, P, 4, 1024, 0, None, None), lai.LAI_ERR_INVALID),
     (lambda l: l.lai_snake_beta_f32(P, P, None, 1, 4, 16, None), lai.LAI_ERR_INVALID),
     (lambda l: l.lai_rope_table_f32(P, P, None, 4, 1024, 1e6, None), lai.LAI_ERR_INVALID),
@@ -71,7 +90,7 @@ P = V(16)  # a non-NULL dummy pointer: never dereferenced, the checks fail first
                                           None), lai.LAI_ERR_INVALID),
     (lambda l: l.lai_decode_attention_f32(P, P, P, P, P, P, P, 1, 12, 4, 128, 100, 0.1, P, None,
                                           None), lai.LAI_ERR_INVALID),
-    (lambda l: l.lai_decode_attention_f32(V(4096), P, P, P, V(4096), P, P, 1, 16, 8, 128, 100,
+    (lambda l: l.lai_decode_attention_f32(A(4096), P, P, P, A(4096), P, P, 1, 16, 8, 128, 100,
                                           0.1, P, None, None), lai.LAI_ERR_ALIAS),
     # sampling: empty vocab; history without lengths; shared memory beyond 200 KiB
     (lambda l: l.lai_sample_topk_f32(P, P, 0, 1, None, None, 0, 1.0, 1.0, 5, P, None),
@@ -94,22 +113,22 @@ P = V(16)  # a non-NULL dummy pointer: never dereferenced, the checks fail first
     (lambda l: l.lai_voc_conv_transpose1d_f32(P, P, P, P, P, 1, 64, 64, 10, 3, 2, 3, None, None),
      lai.LAI_ERR_INVALID),
     (lambda l: l.lai_voc_final_f32(P, P, P, P, P, None, 1, 96, 100, None), lai.LAI_ERR_INVALID),
-    (lambda l: l.lai_voc_transpose_f32(V(4096), V(4096 + 8), 1, 4, 4, None), lai.LAI_ERR_ALIAS),
+    (lambda l: l.lai_voc_transpose_f32(A(4096), A(4096 + 8), 1, 4, 4, None), lai.LAI_ERR_ALIAS),
     # decode GEMVs: output overlapping input; K beyond the staged maximum
-    (lambda l: l.lai_gemv_bf16w_f32(V(256), V(256), None, 1e-6, P, 1, 64, 8, None),
+    (lambda l: l.lai_gemv_bf16w_f32(A(256), A(256), None, 1e-6, P, 1, 64, 8, None),
      lai.LAI_ERR_ALIAS),
-    (lambda l: l.lai_gemv_bf16w_f32(V(256), V(1 << 30), None, 1e-6, P, 1, 60000, 8, None),
+    (lambda l: l.lai_gemv_bf16w_f32(A(256), A(1 << 24), None, 1e-6, P, 1, 60000, 8, None),
      lai.LAI_ERR_TOOBIG),
     # other weight formats: INT8 needs its scales; odd SwiGLU width; quantizer / converter
-    (lambda l: l.lai_gemv_i8w_f32(P, V(1 << 20), None, 1e-6, P, None, 1, 64, 8, None),
+    (lambda l: l.lai_gemv_i8w_f32(P, A(1 << 20), None, 1e-6, P, None, 1, 64, 8, None),
      lai.LAI_ERR_INVALID),
-    (lambda l: l.lai_gemv_swiglu_f16w_f32(P, V(1 << 20), None, 1e-6, P, 1, 64, 0, None),
+    (lambda l: l.lai_gemv_swiglu_f16w_f32(P, A(1 << 20), None, 1e-6, P, 1, 64, 0, None),
      lai.LAI_ERR_INVALID),
-    (lambda l: l.lai_gemv_residual_f32w_f32(V(256), V(256), P, 1, 64, 8, None), lai.LAI_ERR_ALIAS),
+    (lambda l: l.lai_gemv_residual_f32w_f32(A(256), A(256), P, 1, 64, 8, None), lai.LAI_ERR_ALIAS),
     (lambda l: l.lai_quantize_rows_i8_bf16(P, P, P, 4, 0, None), lai.LAI_ERR_INVALID),
-    (lambda l: l.lai_quantize_rows_i8_bf16(V(4096), V(1 << 20), V(4096 + 16), 4, 64, None),
+    (lambda l: l.lai_quantize_rows_i8_bf16(A(4096), A(1 << 20), A(4096 + 16), 4, 64, None),
      lai.LAI_ERR_ALIAS),
-    (lambda l: l.lai_convert_bf16_to_f16(V(4096), V(4096 + 2), 64, None), lai.LAI_ERR_ALIAS),
+    (lambda l: l.lai_convert_bf16_to_f16(A(4096), A(4096 + 2), 64, None), lai.LAI_ERR_ALIAS),
 ])
 def test_argument_checks(call, want):
     assert call(lai.load()) == want

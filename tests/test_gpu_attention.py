@@ -105,7 +105,8 @@ def test_decode_attention_position_out_of_range_flags_and_skips():
 def test_decode_attention_argument_checks():
     L = lai.load()
     import ctypes
-    P = ctypes.c_void_p(1 << 20)
+    from conftest import arena_ptr
+    P = arena_ptr(1 << 20)  # real memory: a regressed check would still stay in bounds
     f = L.lai_decode_attention_f32
     # head_dim other than 128; heads not a multiple of kv heads; group of 3
     assert f(P, P, P, P, P, P, P, 1, 16, 8, 64, 100, 0.1, P, None, None) == lai.LAI_ERR_INVALID

@@ -100,11 +100,12 @@ def test_gemv_decode_layer_equals_unfused_sequence():
 def test_gemv_argument_checks():
     L = lai.load()
     import ctypes
-    P = ctypes.c_void_p(256)
+    from conftest import arena_ptr
+    P = arena_ptr(256)  # real memory: a regressed check would still stay in bounds
     assert L.lai_gemv_bf16w_f32(P, P, None, 1e-6, P, 1, 64, 8, None) == lai.LAI_ERR_ALIAS
-    assert L.lai_gemv_swiglu_bf16w_f32(P, ctypes.c_void_p(1 << 20), None, 1e-6, P, 1, 64, 0,
+    assert L.lai_gemv_swiglu_bf16w_f32(P, arena_ptr(1 << 20), None, 1e-6, P, 1, 64, 0,
                                        None) == lai.LAI_ERR_INVALID
-    assert L.lai_gemv_bf16w_f32(P, ctypes.c_void_p(1 << 30), None, 1e-6, P, 1, 60000, 8,
+    assert L.lai_gemv_bf16w_f32(P, arena_ptr(1 << 24), None, 1e-6, P, 1, 60000, 8,
                                 None) == lai.LAI_ERR_TOOBIG
 
 

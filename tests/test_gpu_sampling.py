@@ -73,7 +73,8 @@ def test_sample_topk_matches_reference_build():
 def test_sample_topk_argument_checks():
     L = lai.load()
     import ctypes
-    P = ctypes.c_void_p(1 << 20)
+    from conftest import arena_ptr
+    P = arena_ptr(1 << 20)  # real memory: a regressed check would still stay in bounds
     f = L.lai_sample_topk_f32
     assert f(P, P, 0, 1, None, None, 0, 1.0, 1.0, 5, P, None) == lai.LAI_ERR_INVALID
     assert f(P, P, 100, 1, P, None, 4, 1.0, 1.0, 5, P, None) == lai.LAI_ERR_INVALID
