@@ -2,16 +2,21 @@
 """Benchmark of the B200 per-layer kernels (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c1|c3|c4|c5|g1|g2|v1] [--graph auto|on|off]
+                    [--config c5|c1|c2|c3|c4|g1|g2|v1|...] [--graph auto|on|off]
 
 A step is one decoder layer's elementwise chain over one batch (runner.LayerChain):
 fused residual-add+RMSNorm, fused q/k RMSNorm+RoPE, fused residual-add+RMSNorm,
 SwiGLU -- BF16 storage, FP32 math -- on inputs resident in HBM. The default
-workload is config c2 (Qwen3-ASR-1.7B layer ops, 64 x 1024 tokens, hidden 2048,
-FFN 6144), per GPU: N GPUs each run their own 65536-token batch, no collective
-("scaling": "weak"). --config c5 runs the 2M-token chain split across the N GPUs
-instead ("strong"). `value` is tokens/s over all GPUs; the roofline object
-reports the dominant kernel's achieved HBM GB/s from live CUDA events.
+workload is config c5: the Qwen3-1.7B chain (hidden 2048, FFN 6144, 16/8 heads of
+128) over 2 097 152 tokens, row-sharded in contiguous blocks across the N GPUs with
+no collective ("scaling": "strong"; N = 1 holds all of it, ~116 GB). `value` is
+tokens/s over all GPUs (the slowest rank's CUDA-event time); `per_rank` has every
+rank's per-kernel GB/s; the roofline object reports the dominant kernel's achieved
+HBM GB/s from live CUDA events. At N = 1 the line also carries `other_shapes`: the
+c2 chain (64 x 1024 tokens) with both SwiGLU call forms, the L2-resident c1 and c3
+(decode at random positions, CUDA graph) and the c4 SnakeBeta stages, each with its
+own per-kernel table and roofline. --config c2 runs the 65536-token batch per GPU
+("weak").
 
 --config g1/g2 time the decode step's fused linear path (GEMVs with RMSNorm prologue
 and residual / SwiGLU epilogues) through 28 layers; --config v1 times the vocoder's
@@ -125,16 +130,17 @@ class ClockSampler:
 
 # ----------------------------------------------------------------- CPU side
 def cpu_chain_rate(cfg, rows: int, min_seconds: float, steps: int | None = None,
-                   warmup: int = 1) -> dict:
+                   warmup: int = 1, threads: int | None = None) -> dict:
     """The reference's FP32 chain on host cores (oracle/_build/liblai_cpuref.so).
 
     Returns rows/s. Either `steps` timed passes, or passes until `min_seconds`.
+    threads: OpenMP threads (default: every core this process may run on).
     """
     import numpy as np
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     import oracle
     lib = oracle.load("liblai_cpuref.so")
-    lib.oracle_set_threads(len(os.sched_getaffinity(0)))  # all host cores, whatever OMP_* says
+    lib.oracle_set_threads(threads or len(os.sched_getaffinity(0)))  # whatever OMP_* says
     rng = np.random.default_rng(5)
     D, I, hd = cfg.dim, cfg.inter, cfg.head_dim
     f = lambda *s: rng.standard_normal(s, dtype=np.float32)  # noqa: E731
@@ -1387,7 +1393,7 @@ def run_reference(args) -> None:
     else:
         cfg = runner.CONFIGS[args.config]
         probe = cpu_chain_rate(cfg, min(cfg.tokens, 1024), 0.0, steps=2, warmup=1)
-        rows = int(max(64, min(cfg.tokens, args.cpu_rows, probe["rows_per_s"] * per_step_s)))
+        rows = int(max(64, min(cfg.tokens, args.ref_rows, probe["rows_per_s"] * per_step_s)))
         r = cpu_chain_rate(cfg, rows, 0.0, steps=args.steps, warmup=args.warmup)
         cb = {"value": r["rows_per_s"], "unit": "rows/s", "cores": r["threads"], "kind": "port",
               "sample": f"{rows} of {cfg.tokens} tokens of {cfg.name} per step, FP32, "
@@ -1614,6 +1620,206 @@ def time_launches(launches, steps: int, graph: bool, names=None):
     return total, per
 
 
+def summarize_kernels(names, per, bpl, rows_pl, peak) -> tuple[dict, str]:
+    """Per kernel name: mean CUDA-event time over its launches, algorithmic GB/s, fraction
+    of `peak`, rows/s. Returns (table, name of the kernel with the largest total time)."""
+    kernels = {}
+    for j, name in enumerate(names):
+        k = kernels.setdefault(name, {"ms": [], "bytes": bpl[j], "rows": rows_pl[j]})
+        k["ms"] += per[j]
+    table, dominant, dom_total = {}, None, -1.0
+    for name, k in kernels.items():
+        avg_ms = statistics.mean(k["ms"])
+        gbs = k["bytes"] / (avg_ms / 1000.0) / 1e9
+        table[name] = {"avg_us": round(avg_ms * 1000, 2), "gbs": round(gbs, 1),
+                       "frac_of_peak": round(gbs / peak, 4),
+                       "rows_per_s": round(k["rows"] / (avg_ms / 1000.0), 1),
+                       "bytes_per_launch": k["bytes"], "launches": len(k["ms"])}
+        if sum(k["ms"]) > dom_total:
+            dominant, dom_total = name, sum(k["ms"])
+    return table, dominant
+
+
+def roofline_of(table, dominant, peak, peak_kind, traffic_key) -> dict:
+    d = table[dominant]
+    return {"bound": "hbm", "kernel": dominant, "achieved": d["gbs"], "peak": peak,
+            "unit": "GB/s", "frac": round(d["gbs"] / peak, 4),
+            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                           else "fallback 6650 GB/s",
+            "traffic": load_traffic().get(traffic_key),
+            "algorithmic_bytes_per_launch": d["bytes_per_launch"]}
+
+
+def time_swiglu_forms(work, steps: int, warmup: int, peak: float) -> dict:
+    """SwiGLU on a LayerChain's gate_up in both call forms, each launch restored from a
+    pristine copy first (untimed): out of place into `act` (the chain's form) and in
+    place, out == gate_up (the reference's qwen_swiglu_multiply(out, out, ...) form,
+    src/tts_native.c:588, 665, 744). CUDA events bracket the call: the in-place form's
+    whole wave schedule is inside them."""
+    import torch
+    import lai
+    gu, inter = work.gate_up, work.cfg.inter
+    pristine = gu.clone()
+    stream = torch.cuda.current_stream()
+    nbytes = work.cfg.bytes_per_token(work.elem)["swiglu"] * work.rows
+    out = {}
+    for form in ("out_of_place", "inplace"):
+        evs = []
+        for i in range(warmup + steps):
+            gu.copy_(pristine)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            if form == "inplace":
+                lai.swiglu_inplace(gu, inter)
+            else:
+                lai.swiglu(gu, inter, out=work.act)
+            b.record(stream)
+            if i >= warmup:
+                evs.append((a, b))
+        torch.cuda.synchronize()
+        avg_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+        gbs = nbytes / (avg_ms / 1000.0) / 1e9
+        out[form] = {"avg_us": round(avg_ms * 1000, 2), "gbs": round(gbs, 1),
+                     "frac_of_peak": round(gbs / peak, 4), "bytes_per_launch": nbytes,
+                     "launches": len(evs)}
+    del pristine
+    out["inplace_over_out_of_place"] = round(out["inplace"]["avg_us"]
+                                             / out["out_of_place"]["avg_us"], 4)
+    return out
+
+
+def measure_chain_extra(name: str, steps: int, warmup: int, seed: int, peak: float,
+                        peak_kind: str, swiglu_forms: bool = False) -> dict:
+    """One more named shape on this GPU (N = 1): its whole chain timed per launch (CUDA
+    graph replay for the launch-bound L2-resident shapes), per-kernel GB/s, roofline."""
+    import torch
+    import runner
+    cfg = runner.CONFIGS[name]
+    rows = cfg.tokens
+    work = runner.LayerChain(cfg, rows, row0=0, seed=seed)
+    launches = work.launches(None)
+    graph = rows <= 4096
+    for _ in range(warmup):
+        for f in launches:
+            f()
+    torch.cuda.synchronize()
+    total_ms, per = time_launches(launches, steps, graph, work.kernel_names)
+    torch.cuda.synchronize()
+    assert int(work.err.item()) == 0, f"an id or position was out of range in {name}"
+    bpl = work.bytes_per_launch()
+    table, dominant = summarize_kernels(work.kernel_names, per, bpl, [rows] * len(bpl), peak)
+    step_bytes = sum(bpl)
+    res = {"workload": f"{cfg.name} layer chain", "rows": rows, "dim": cfg.dim,
+           "ffn": cfg.inter, "positions": f"{cfg.pos_mode} < {cfg.pos_period}",
+           "value": round(rows * steps / (total_ms / 1000.0), 1), "unit": "rows/s",
+           "ms_per_step": round(total_ms / steps, 4), "steps": steps,
+           "timing": "CUDA graph replay" if graph else "direct launches",
+           "l2": (f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB per step)"
+                  if step_bytes > 126e6 else
+                  f"L2-resident working set ({step_bytes / 1e6:.1f} MB per step): hot-cache, "
+                  "launch-latency-bound numbers"),
+           "per_kernel": table,
+           "roofline": roofline_of(table, dominant, peak, peak_kind, f"{dominant}@{name}")}
+    if swiglu_forms:
+        res["swiglu_forms"] = time_swiglu_forms(work, min(steps, 20), 3, peak)
+    del work, launches
+    torch.cuda.empty_cache()
+    return res
+
+
+def measure_snake_extra(steps: int, warmup: int, seed: int, peak: float, peak_kind: str) -> dict:
+    """Config c4 on this GPU (N = 1): SnakeBeta over the five BigVGAN stages x batch 8, one
+    launch per stage, per-stage GB/s and its fraction of the measured HBM bandwidth."""
+    import torch
+    import runner
+    work = runner.SnakeSweep(seed=seed)
+    launches = work.launches(None)
+    for _ in range(warmup):
+        for f in launches:
+            f()
+    torch.cuda.synchronize()
+    total_ms, per = time_launches(launches, steps, False, work.kernel_names)
+    bpl = work.bytes_per_launch()
+    table, dominant = summarize_kernels(work.kernel_names, per, bpl, work.rows_per_launch(), peak)
+    res = {"workload": "vocoder SnakeBeta over the BigVGAN stages, FP32 in place",
+           "stages": runner.SNAKE_STAGES, "batch": runner.SNAKE_BATCH,
+           "value": round(sum(work.rows_per_launch()) * steps / (total_ms / 1000.0), 1),
+           "unit": "channel rows/s", "ms_per_step": round(total_ms / steps, 4), "steps": steps,
+           "sweep_gbs": round(sum(bpl) * steps / (total_ms / 1000.0) / 1e9, 1),
+           "per_kernel": table,
+           "roofline": roofline_of(table, dominant, peak, peak_kind, f"{dominant}@c4"),
+           "min_stage_frac": min(v["frac_of_peak"] for v in table.values())}
+    del work, launches
+    torch.cuda.empty_cache()
+    return res
+
+
+def pcie_peaks(nbytes: int = 1 << 30, reps: int = 3) -> dict:
+    """Pinned host <-> device copy rates of this GPU, measured in this run: H2D alone, D2H
+    alone, and both directions at once on two streams (GB/s, best of `reps`)."""
+    import torch
+    h_in = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    h_out = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    d_a = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    d_b = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def timed(fn):
+        best = float("inf")
+        for _ in range(reps):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            fn()
+            torch.cuda.synchronize()
+            best = min(best, time.perf_counter() - t0)
+        return best
+
+    def both():
+        with torch.cuda.stream(s1):
+            d_a.copy_(h_in, non_blocking=True)
+        with torch.cuda.stream(s2):
+            h_out.copy_(d_b, non_blocking=True)
+
+    t_h2d = timed(lambda: d_a.copy_(h_in, non_blocking=True))
+    t_d2h = timed(lambda: h_out.copy_(d_b, non_blocking=True))
+    t_both = timed(both)
+    del h_in, h_out, d_a, d_b
+    torch.cuda.empty_cache()
+    return {"h2d_gbs": round(nbytes / t_h2d / 1e9, 2), "d2h_gbs": round(nbytes / t_d2h / 1e9, 2),
+            "duplex_gbs": round(2 * nbytes / t_both / 1e9, 2), "bytes": nbytes}
+
+
+def pcie_fields(h2d: int, d2h: int, seconds_per_step: float, peaks: dict) -> dict:
+    """Achieved bus rate of a host-buffer path and its fraction of the fastest the measured
+    copy rates allow for the same bytes. With both directions busy each runs at half the
+    measured duplex rate (below its solo rate), so the fastest schedule overlaps all of the
+    smaller direction with the larger and moves the larger one's excess alone:
+    min(H2D, D2H) / (duplex / 2) + the excess at that direction's solo rate."""
+    if not peaks:
+        return {}
+    both = min(h2d, d2h)
+    solo = (h2d - both) / (peaks["h2d_gbs"] * 1e9) + (d2h - both) / (peaks["d2h_gbs"] * 1e9)
+    bound_s = both / (peaks["duplex_gbs"] * 1e9 / 2) + solo
+    # never below a direction's own solo time (a duplex rate above twice a solo rate)
+    bound_s = max(bound_s, h2d / (peaks["h2d_gbs"] * 1e9), d2h / (peaks["d2h_gbs"] * 1e9))
+    return {"pcie_gbs": round((h2d + d2h) / seconds_per_step / 1e9, 2),
+            "pcie_bound_ms": round(bound_s * 1000, 3),
+            "pcie_frac": round(bound_s / seconds_per_step, 4)}
+
+
+def cpu_chain_baseline(cfg, rows_all: int, rows_1t: int, seconds: float) -> dict:
+    """The FP32 chain on the host: all cores and one thread, each the median of 3 runs of
+    about seconds / 6 (the reference's vocoder_bench convention: tools/vocoder_bench.c:190,
+    476)."""
+    runs_all = [cpu_chain_rate(cfg, rows_all, seconds / 6) for _ in range(3)]
+    runs_1t = [cpu_chain_rate(cfg, rows_1t, seconds / 6, threads=1) for _ in range(3)]
+    med = lambda rs: statistics.median(r["rows_per_s"] for r in rs)  # noqa: E731
+    return {"value": round(med(runs_all), 1), "value_1t": round(med(runs_1t), 1),
+            "threads": runs_all[0]["threads"], "rows_all": rows_all, "rows_1t": rows_1t,
+            "passes": sum(r["passes"] for r in runs_all),
+            "passes_1t": sum(r["passes"] for r in runs_1t)}
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -1689,20 +1895,23 @@ def run_ours(args) -> None:
     value = total_rows * args.steps / (max_ms / 1000.0)
     bpl = work.bytes_per_launch()
     rows_pl = work.rows_per_launch() if (snake or decode) else [rows] * len(bpl)
-    kernels = {}
-    for j, name in enumerate(work.kernel_names):
-        k = kernels.setdefault(name, {"ms": [], "bytes": bpl[j], "rows": rows_pl[j]})
-        k["ms"] += per[j]
-    per_kernel, dominant, dom_total = {}, None, -1.0
-    for name, k in kernels.items():
-        avg_ms = statistics.mean(k["ms"])
-        gbs = k["bytes"] / (avg_ms / 1000.0) / 1e9
-        per_kernel[name] = {"avg_us": round(avg_ms * 1000, 2), "gbs": round(gbs, 1),
-                            "frac_of_peak": round(gbs / peak, 4),
-                            "rows_per_s": round(k["rows"] / (avg_ms / 1000.0), 1),
-                            "bytes_per_launch": k["bytes"], "launches": len(k["ms"])}
-        if sum(k["ms"]) > dom_total:
-            dominant, dom_total = name, sum(k["ms"])
+    per_kernel, dominant = summarize_kernels(work.kernel_names, per, bpl, rows_pl, peak)
+
+    # every rank's own step time and per-kernel GB/s (the slowest rank sets `value`)
+    per_rank = None
+    if world > 1:
+        names = list(per_kernel)
+        mine = torch.tensor([total_ms / args.steps, float(rows)]
+                            + [per_kernel[n]["gbs"] for n in names],
+                            device="cuda", dtype=torch.float64)
+        allr = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allr, mine)
+        per_rank = [{"rank": r, "ms_per_step": round(float(v[0]), 4), "rows": int(v[1]),
+                     "gbs": {n: round(float(v[2 + j]), 1) for j, n in enumerate(names)},
+                     "frac_of_peak": {n: round(float(v[2 + j]) / peak, 4)
+                                      for j, n in enumerate(names)}}
+                    for r, v in enumerate(allr)]
+
     # each distinct kernel also timed alone: `steps` back-to-back launches of it (outside
     # the chain, so no neighbour's leftover L2 write-back is charged to it)
     isolated = {}
@@ -1718,14 +1927,8 @@ def run_ours(args) -> None:
                               "frac_of_peak": round(bpl[j] / (avg_ms / 1000.0) / 1e9 / peak, 4)}
     step_bytes = sum(bpl)
     step_gbs = step_bytes * args.steps / (total_ms / 1000.0) / 1e9
-    d = per_kernel[dominant]
-    roofline = {"bound": "hbm", "kernel": dominant, "achieved": d["gbs"], "peak": peak,
-                "unit": "GB/s", "frac": round(d["gbs"] / peak, 4),
-                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
-                               else "fallback 6650 GB/s",
-                "traffic": load_traffic().get(f"{dominant}@{args.config}"),
-                "algorithmic_bytes_per_launch": d["bytes_per_launch"],
-                "step_gbs": round(step_gbs, 1), "step_frac": round(step_gbs / peak, 4)}
+    roofline = roofline_of(per_kernel, dominant, peak, peak_kind, f"{dominant}@{args.config}")
+    roofline.update(step_gbs=round(step_gbs, 1), step_frac=round(step_gbs / peak, 4))
 
     def max_time(sec):
         et = torch.tensor([sec], device="cuda", dtype=torch.float64)
@@ -1733,31 +1936,50 @@ def run_ours(args) -> None:
             dist.all_reduce(et, op=dist.ReduceOp.MAX)
         return float(et.item())
 
-    e2e = e2e_f32 = None
+    del work, launches  # free the device-resident workload before the other measurements
+    torch.cuda.empty_cache()
+
+    # the other named shapes, one GPU only (the scaling runs time the headline shape alone)
+    extras = {}
+    if world == 1 and not args.no_extras and args.config == "c5":
+        ew = max(3, min(args.warmup, 10))
+        es = max(args.steps, 20)
+        extras["c2"] = measure_chain_extra("c2", es, ew, args.seed, peak, peak_kind,
+                                           swiglu_forms=True)
+        extras["c1"] = measure_chain_extra("c1", max(es, 200), ew, args.seed, peak, peak_kind)
+        extras["c3"] = measure_chain_extra("c3", max(es, 200), ew, args.seed, peak, peak_kind)
+        extras["c4"] = measure_snake_extra(es, ew, args.seed, peak, peak_kind)
+
+    e2e = e2e_f32 = pcie = None
     if not args.no_e2e and not decode:
-        del work, launches  # free the device-resident workload before the staged runs
-        torch.cuda.empty_cache()
+        pcie = pcie_peaks()
         if snake:
             r = e2e_snake_dropin(runner.SNAKE_STAGES, runner.SNAKE_BATCH, args.e2e_steps, 1)
-            e2e = {"value": round(rows * world * r["steps"] / max_time(r["seconds"]), 1),
+            sec = max_time(r["seconds"])
+            e2e = {"value": round(rows * world * r["steps"] / sec, 1),
                    "unit": "rows/s", "h2d_bytes_per_step": r["h2d"],
                    "d2h_bytes_per_step": r["d2h"], "dtype": "f32",
-                   "api": "voc_snake_beta drop-in on pinned host buffers, one call per item and stage"}
+                   "api": "voc_snake_beta drop-in on pinned host buffers, one call per item and stage",
+                   **pcie_fields(r["h2d"], r["d2h"], sec / r["steps"], pcie)}
         else:
             er = min(rows, args.e2e_rows_bf16)
             r = e2e_staged_bf16(cfg, er, args.e2e_steps, 1)
-            e2e = {"value": round(er * world * r["steps"] / max_time(r["seconds"]), 1),
+            sec = max_time(r["seconds"])
+            e2e = {"value": round(er * world * r["steps"] / sec, 1),
                    "unit": "rows/s", "h2d_bytes_per_step": r["h2d"],
                    "d2h_bytes_per_step": r["d2h"], "rows_per_step": er, "dtype": "bf16",
                    "api": "lai_staged_{add_rmsnorm,qk_norm_rope,swiglu}_bf16 on pinned host "
-                          "buffers, 4 synchronous calls/step"}
+                          "buffers, 4 synchronous calls/step",
+                   **pcie_fields(r["h2d"], r["d2h"], sec / r["steps"], pcie)}
             fr = min(rows, args.e2e_rows)
             r = e2e_dropin_f32(cfg, fr, args.e2e_steps, 1)
-            e2e_f32 = {"value": round(fr * world * r["steps"] / max_time(r["seconds"]), 1),
+            sec = max_time(r["seconds"])
+            e2e_f32 = {"value": round(fr * world * r["steps"] / sec, 1),
                        "unit": "rows/s", "h2d_bytes_per_step": r["h2d"],
                        "d2h_bytes_per_step": r["d2h"], "rows_per_step": fr, "dtype": "f32",
                        "api": "reference-named qwen_* drop-ins on pinned host FP32 buffers, "
-                              "9 calls/step"}
+                              "9 calls/step",
+                       **pcie_fields(r["h2d"], r["d2h"], sec / r["steps"], pcie)}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -1776,11 +1998,15 @@ def run_ours(args) -> None:
                              f"({r['seconds']:.1f} s) through the reference's voc_snake_beta "
                              f"(AVX2 build), host {cpu_model()}"}
         else:
-            r = cpu_chain_rate(cfg, min(rows, args.cpu_rows), args.cpu_seconds)
-            cpu = {"value": round(r["rows_per_s"], 1), "unit": "rows/s", "cores": r["threads"],
-                   "kind": "port",
-                   "sample": f"{min(rows, args.cpu_rows)} tokens x {r['passes']} passes "
-                             f"({r['seconds']:.1f} s) of the FP32 chain, host {cpu_model()}"}
+            ra, r1 = min(rows, args.cpu_rows), min(rows, max(64, args.cpu_rows // 8))
+            r = cpu_chain_baseline(cfg, ra, r1, args.cpu_seconds)
+            cpu = {"value": r["value"], "unit": "rows/s", "cores": r["threads"],
+                   "value_1t": r["value_1t"], "cores_1t": 1, "kind": "port",
+                   "sample": f"the FP32 chain (the oracle's timed build: add+RMSNorm, per-head "
+                             f"RMSNorm, RoPE, add+RMSNorm, SwiGLU): {ra} tokens on "
+                             f"{r['threads']} threads ({r['passes']} passes) and {r1} tokens "
+                             f"on 1 thread ({r['passes_1t']} passes), each the median of 3 "
+                             f"runs, host {cpu_model()}"}
 
     if world > 1:
         dist.barrier()
@@ -1807,9 +2033,12 @@ def run_ours(args) -> None:
     else:
         config = {"workload": f"{cfg.name} layer elementwise chain ("
                               + ", ".join(work_names := list(cfg.kernels())) + ")",
-                  "config": args.config, "rows_per_gpu": rows, "dim": cfg.dim, "ffn": cfg.inter,
+                  "config": args.config, "tokens": cfg.tokens if strong else rows * world,
+                  "rows_per_gpu": rows, "dim": cfg.dim, "ffn": cfg.inter,
                   "heads": [cfg.n_q, cfg.n_kv, cfg.head_dim], "positions": cfg.pos_mode,
-                  "parallelism": f"row-sharded x{world}, no collective",
+                  "parallelism": (f"row-sharded x{world} (contiguous blocks of the "
+                                  f"{cfg.tokens} tokens), no collective" if strong else
+                                  f"x{world} GPUs, each its own {rows} tokens, no collective"),
                   "timing": "CUDA graph replay" if graph else "direct launches",
                   "l2": (f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB per step per GPU)"
                          if step_bytes > 126e6 else
@@ -1825,8 +2054,9 @@ def run_ours(args) -> None:
         "data": "synthetic (seeded counter-based N(0,1) on device; norm weights 1+N(0,0.02))",
         "config": config,
         "hbm_gbs": round(step_gbs * (1 if strong else world), 1),
-        "per_kernel": per_kernel, "per_kernel_isolated": isolated, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-        "e2e_dropin_f32": e2e_f32,
+        "per_kernel": per_kernel, "per_kernel_isolated": isolated, "per_rank": per_rank,
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+        "e2e_dropin_f32": e2e_f32, "pcie_peaks": pcie, "other_shapes": extras or None,
         "gpu_launches": args.steps * launches_per_step,
         "clocks": clocks,
     }
@@ -1842,7 +2072,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "d1", "g1", "g2", "v1", "v2", "v3",
                                          "v4", "a3", "n1", "s3"],
-                    default="c2")
+                    default="c5")
     ap.add_argument("--t-div", type=int, default=1,
                     help="v1: divide every stage's length (small profiling cases)")
     ap.add_argument("--passes", type=int, choices=[1, 3], default=3,
@@ -1863,19 +2093,25 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-isolate", action="store_true",
                     help="skip timing each kernel alone after the chain")
-    ap.add_argument("--cpu-rows", type=int, default=8192)
+    ap.add_argument("--cpu-rows", type=int, default=8192,
+                    help="tokens of the in-run CPU baseline sample (all cores; 1/8 of it on 1 thread)")
+    ap.add_argument("--ref-rows", type=int, default=65536,
+                    help="--impl reference: most tokens per step of the CPU sample")
     ap.add_argument("--cpu-batch", type=int, default=2,
                     help="SnakeBeta batch items in the CPU baseline sample (c4)")
     ap.add_argument("--ref-budget", type=float, default=90.0,
                     help="seconds the --impl reference run should take in total")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="c5: skip timing the other named shapes (c1, c2 + SwiGLU in place, c3, "
+                         "c4) after the headline")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)  # timing rule: at least 3 untimed warm-up steps
     if args.steps is None:
         args.steps = {"v1": 20, "v2": 20, "v3": 20, "v4": 20, "n1": 50, "a3": 200,
                       "d1": 50}.get(
-            args.config, 2000)
+            args.config, 100 if args.config == "c5" else 2000)
     if args.impl == "reference":
         run_reference(args)
     elif args.config == "v1":
