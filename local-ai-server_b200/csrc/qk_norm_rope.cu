@@ -9,10 +9,11 @@
 // read once, written once in place); the [hd] weights and the table rows are
 // shared (L1/L2-resident) and not counted.
 //
-// Kernels. BF16 with hd=128 (every Qwen3 decoder shape) runs qk_pipe_kernel: a
-// persistent kernel that streams token tiles through a shared-memory ring filled
-// by bulk async copies (described at the kernel), used for every batch size so a
-// token's result never depends on the batch it arrives in. FP32 and hd=64/256 run
+// Kernels. BF16 with hd=128 (every Qwen3 decoder shape) runs qk_stream_kernel: a
+// persistent kernel whose warps each stream single tokens through their own
+// shared-memory stages filled by bulk async copies (described at the kernel); small
+// batches of the Qwen3 head layout run qk_reg_kernel with the same per-head
+// arithmetic, so a token's result never depends on the batch it arrives in. FP32 and hd=64/256 run
 // qk_warp_kernel: one warp owns one (token, q-or-k) segment; a head of hd elements
 // spans LPH = hd*s/16 lanes, each lane one 16-byte vector, all of the segment's
 // loads issued before any arithmetic; the per-head sum of squares is an xor-shuffle
@@ -121,214 +122,312 @@ qk_warp_kernel(T *q, T *k, const float *__restrict__ wq, const float *__restrict
     }
 }
 
-// ---- pipelined BF16 hd=128 kernel: bulk async copies through a shared-memory ring ----
+// ---- BF16 hd=128 kernels: shared per-head arithmetic -----------------------------
 //
-// Persistent CTAs (2 per SM). A tile is kTileTok consecutive tokens: their q rows
-// and their k rows are each one contiguous range, fetched by two bulk copies into
-// one of kStages shared-memory stages (completion counted on the stage's mbarrier),
-// computed in place in shared memory and written back by two bulk stores; a stage is
-// refilled only after its stores have finished reading it. Memory parallelism
-// therefore comes from the copy engine, not from registers.
-//
-// Each CTA runs as two independent groups of 4 warps that take alternate tiles (group g:
-// tiles g, g+2, ...; stages g and g+2), each with its own named barrier and its own
-// leader thread issuing its loads and stores. One group's barrier, stores and refill then
-// overlap the other group's arithmetic; with one CTA-wide barrier per tile (the previous
-// form) the whole CTA stalled at every tile boundary and the kernel reached 0.79 of the
-// measured copy bandwidth against 0.855 now (same bits out). Work split within a group:
-// 8 half-warps, 8/kTileTok per token, a half-warp per head (pipe_heads).
-__device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
+// A quarter-warp (8 lanes) holds one head; a lane owns elements d0..d0+7 of the first
+// half (d0 = 8 * (lane % 8)) and their RoPE partners 64+d0..64+d0+7, one 16-byte access
+// each, so the rotation needs no shuffle and the sum of squares is a 3-step xor tree.
+// Arithmetic runs on packed two-wide FP32 (FMUL2 / FFMA2). qk_stream_kernel (large
+// batches) and qk_reg_kernel (small batches) share head_math, so a token's bits do not
+// depend on which of them ran or on the batch it arrived in.
+__device__ __forceinline__ float2 bf16x2_to_f2(uint32_t w) { return make_float2(bf16_lo(w), bf16_hi(w)); }
+__device__ __forceinline__ uint32_t f2_to_bf16x2(float2 v) { return pack_bf16x2(v.x, v.y); }
 
-constexpr int kTileTok = 4;
-constexpr int kStages = 4;
-constexpr int kPipeThreads = 256;
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far beyond any real copy
+struct RopeRow {
+    float2 cl[4], ch[4], sl[4], sh[4];  // cos / sin of d0..d0+7 and 64+d0..64+d0+7
+};
 
-// One token's heads (q or k) in shared memory, BF16 hd=128: a half-warp per head,
-// lane owns elements d0..d0+3 (first half) and their RoPE partners 64+d0..64+d0+3,
-// so the rotation needs no shuffle; the sum of squares is a 4-step xor tree. The
-// trip count is the same in every half-warp (shuffles need the whole warp); `valid`
-// and h < nheads predicate the shared-memory traffic.
-template <int HW, int TRIPS>
-__device__ __forceinline__ void pipe_heads(uint16_t *base, int nheads, int sub, int d0, bool valid,
-                                           const float (&w)[8], bool norm, bool rope,
-                                           const float (&cs)[8], const float (&sn)[8], float eps) {
-    // TRIPS > 0: the trip count is known at compile time, the loop unrolls fully and
-    // independent heads interleave; TRIPS == 0: any head count.
-    const int trips = TRIPS > 0 ? TRIPS : (nheads + HW - 1) / HW;
+// All eight lanes of every quarter-warp must call it (3 xor shuffles).
+__device__ __forceinline__ void head_math(uint4 &lo, uint4 &hi, const float2 (&w)[8], bool norm,
+                                          bool rope, const RopeRow &t, float eps) {
+    float2 a[4] = {bf16x2_to_f2(lo.x), bf16x2_to_f2(lo.y), bf16x2_to_f2(lo.z), bf16x2_to_f2(lo.w)};
+    float2 b[4] = {bf16x2_to_f2(hi.x), bf16x2_to_f2(hi.y), bf16x2_to_f2(hi.z), bf16x2_to_f2(hi.w)};
+    if (norm) {
+        float2 s0 = __fmul2_rn(a[0], a[0]), s1 = __fmul2_rn(b[0], b[0]);
 #pragma unroll
-    for (int j = 0; j < (TRIPS > 0 ? TRIPS : trips); j++) {
-        const int h = sub + j * HW;
-        const bool hv = valid && h < nheads;
-        uint16_t *hp = base + (size_t)h * 128;
-        const uint2 lo = hv ? *reinterpret_cast<const uint2 *>(hp + d0) : make_uint2(0, 0);
-        const uint2 hi = hv ? *reinterpret_cast<const uint2 *>(hp + 64 + d0) : make_uint2(0, 0);
-        float a[8] = {bf16_lo(lo.x), bf16_hi(lo.x), bf16_lo(lo.y), bf16_hi(lo.y),
-                      bf16_lo(hi.x), bf16_hi(hi.x), bf16_lo(hi.y), bf16_hi(hi.y)};
-        // pairwise tree: 3 dependent levels instead of 8
-        float ss = ((a[0] * a[0] + a[1] * a[1]) + (a[2] * a[2] + a[3] * a[3])) +
-                   ((a[4] * a[4] + a[5] * a[5]) + (a[6] * a[6] + a[7] * a[7]));
-        ss = group_sum<16>(ss);
+        for (int e = 1; e < 4; e++) {
+            s0 = __ffma2_rn(a[e], a[e], s0);
+            s1 = __ffma2_rn(b[e], b[e], s1);
+        }
+        float ss = (s0.x + s0.y) + (s1.x + s1.y);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
         // BF16 output keeps 8 significant bits, so the approximate reciprocal square
-        // root and the fused multiply-adds (FP32 ulp-level departures from the
-        // separately rounded reference form) cannot show in the result.
-        if (norm) {
-            const float inv = rsqrtf(ss * (1.0f / 128) + eps);
+        // root and the packed products (ulp-level departures from the separately
+        // rounded reference form) cannot show in the result.
+        const float inv = rsqrtf(ss * (1.0f / 128) + eps);
+        const float2 inv2 = make_float2(inv, inv);
 #pragma unroll
-            for (int e = 0; e < 8; e++) a[e] = a[e] * inv * w[e];
+        for (int e = 0; e < 4; e++) {
+            a[e] = __fmul2_rn(__fmul2_rn(a[e], inv2), w[e]);
+            b[e] = __fmul2_rn(__fmul2_rn(b[e], inv2), w[4 + e]);
         }
-        if (rope) {
+    }
+    if (rope) {
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const float x1 = a[e], x2 = a[4 + e];
-                a[e] = fmaf(-x2, sn[e], x1 * cs[e]);         // x1*c - x2*s
-                a[4 + e] = fmaf(x1, sn[4 + e], x2 * cs[4 + e]);  // x1*s + x2*c
-            }
+        for (int e = 0; e < 4; e++) {
+            const float2 x1 = a[e], x2 = b[e];
+            const float2 nx2 = make_float2(-x2.x, -x2.y);
+            a[e] = __ffma2_rn(nx2, t.sl[e], __fmul2_rn(x1, t.cl[e]));  // x1*c - x2*s
+            b[e] = __ffma2_rn(x1, t.sh[e], __fmul2_rn(x2, t.ch[e]));   // x1*s + x2*c
         }
+    }
+    lo = make_uint4(f2_to_bf16x2(a[0]), f2_to_bf16x2(a[1]), f2_to_bf16x2(a[2]), f2_to_bf16x2(a[3]));
+    hi = make_uint4(f2_to_bf16x2(b[0]), f2_to_bf16x2(b[1]), f2_to_bf16x2(b[2]), f2_to_bf16x2(b[3]));
+}
+
+// A lane's cos / sin values from a table row (shared or global memory).
+__device__ __forceinline__ void load_rope_row(RopeRow &t, const float *c, const float *s, int d0) {
+    const float4 c0 = *reinterpret_cast<const float4 *>(c + d0);
+    const float4 c1 = *reinterpret_cast<const float4 *>(c + d0 + 4);
+    const float4 c2 = *reinterpret_cast<const float4 *>(c + 64 + d0);
+    const float4 c3 = *reinterpret_cast<const float4 *>(c + 64 + d0 + 4);
+    const float4 s0 = *reinterpret_cast<const float4 *>(s + d0);
+    const float4 s1 = *reinterpret_cast<const float4 *>(s + d0 + 4);
+    const float4 s2 = *reinterpret_cast<const float4 *>(s + 64 + d0);
+    const float4 s3 = *reinterpret_cast<const float4 *>(s + 64 + d0 + 4);
+    t.cl[0] = make_float2(c0.x, c0.y); t.cl[1] = make_float2(c0.z, c0.w);
+    t.cl[2] = make_float2(c1.x, c1.y); t.cl[3] = make_float2(c1.z, c1.w);
+    t.ch[0] = make_float2(c2.x, c2.y); t.ch[1] = make_float2(c2.z, c2.w);
+    t.ch[2] = make_float2(c3.x, c3.y); t.ch[3] = make_float2(c3.z, c3.w);
+    t.sl[0] = make_float2(s0.x, s0.y); t.sl[1] = make_float2(s0.z, s0.w);
+    t.sl[2] = make_float2(s1.x, s1.y); t.sl[3] = make_float2(s1.z, s1.w);
+    t.sh[0] = make_float2(s2.x, s2.y); t.sh[1] = make_float2(s2.z, s2.w);
+    t.sh[2] = make_float2(s3.x, s3.y); t.sh[3] = make_float2(s3.z, s3.w);
+}
+
+// A lane's weights: w[0..3] = pairs of d0..d0+7, w[4..7] = pairs of 64+d0..64+d0+7.
+__device__ __forceinline__ void load_head_weights(float2 (&w)[8], const float *src, int d0) {
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        w[e] = src ? make_float2(src[d0 + 2 * e], src[d0 + 2 * e + 1]) : make_float2(1.f, 1.f);
+        w[4 + e] = src ? make_float2(src[64 + d0 + 2 * e], src[64 + d0 + 2 * e + 1])
+                       : make_float2(1.f, 1.f);
+    }
+}
+
+// One token's heads (q or k) in shared memory: 4 heads per pass.
+// P > 0: the pass count is known at compile time (fully unrolled); P == 0: any count.
+template <int P>
+__device__ __forceinline__ void stream_heads(unsigned char *base, int nheads, int hsub, int d0,
+                                             const float2 (&w)[8], bool norm, bool rope,
+                                             const RopeRow &t, float eps) {
+    const int passes = P > 0 ? P : (nheads + 3) / 4;
+#pragma unroll
+    for (int j = 0; j < (P > 0 ? P : passes); j++) {
+        const int h = hsub + 4 * j;
+        const bool hv = P > 0 || h < nheads;
+        uint16_t *hp = reinterpret_cast<uint16_t *>(base) + (size_t)h * 128;
+        uint4 lo = hv ? *reinterpret_cast<const uint4 *>(hp + d0) : make_uint4(0, 0, 0, 0);
+        uint4 hi = hv ? *reinterpret_cast<const uint4 *>(hp + 64 + d0) : make_uint4(0, 0, 0, 0);
+        head_math(lo, hi, w, norm, rope, t, eps);
         if (hv) {
-            *reinterpret_cast<uint2 *>(hp + d0) = make_uint2(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]));
-            *reinterpret_cast<uint2 *>(hp + 64 + d0) =
-                make_uint2(pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
+            *reinterpret_cast<uint4 *>(hp + d0) = lo;
+            *reinterpret_cast<uint4 *>(hp + 64 + d0) = hi;
         }
     }
 }
 
-template <int QT, int KT>  // head trips per half-warp for q and k (0: runtime)
-__global__ void __launch_bounds__(kPipeThreads, 2)
-qk_pipe_kernel(uint16_t *q, uint16_t *k, const float *__restrict__ wq,
-               const float *__restrict__ wk, const float *__restrict__ cos_t,
-               const float *__restrict__ sin_t, const int32_t *__restrict__ pos,
-               int64_t table_rows, int64_t rows, int nq, int nkv, float eps, int *err) {
-    constexpr int HD = 128;
-    constexpr int kGroupThreads = kPipeThreads / 2;
-    constexpr int HWT = (kGroupThreads / 16) / kTileTok;  // half-warps per token in a group
-    static_assert(kStages % 2 == 0, "the two groups own alternate stages");
-    extern __shared__ __align__(128) unsigned char smem[];
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
-    int *stop_flag = reinterpret_cast<int *>(smem + 64);  // [2]: a group lost a copy
-    unsigned char *ring = smem + 128;
-    const uint32_t q_tok = (uint32_t)nq * HD * 2, k_tok = (uint32_t)nkv * HD * 2;
-    const uint32_t stage_bytes = kTileTok * (q_tok + k_tok);
-    const int64_t ntiles = (rows + kTileTok - 1) / kTileTok;
-    const int64_t my_n = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-    const int tid = threadIdx.x, lane = tid & 31;
-    const int g = tid / kGroupThreads, gtid = tid % kGroupThreads;
-    const bool leader = gtid == 0;
+// ---- streaming kernel: an independent bulk-copy pipeline per warp -------------------
+//
+// One CTA per SM, up to kStreamWarps warps, no CTA-wide barrier after set-up: every
+// warp runs its own pipeline over kStreamStages single-token stages. A stage holds the
+// token's q row, its k row and (with RoPE) its cos and sin table rows, fetched by bulk
+// async copies that complete on the stage's mbarrier; the warp normalises and rotates
+// the heads in place in shared memory and writes the q and k rows back with two bulk
+// stores. Warp w of the grid takes tokens w, w + W_total, ... After issuing token i's
+// stores the warp refills the stage of token i - 1 (whose stores have been read out by
+// then) with token i - 1 + S, so a token's stores drain while the next token loads and
+// the warp never waits for a store. Memory parallelism comes from the 16 independent
+// warps per SM (16 x 2 stages x 7 KB fill the shared memory): refilling a stage as soon
+// as its own store has been read out (waiting on it) measured 15% slower, and 3-stage
+// pipelines at 8-10 warps 5-10% slower. Positions are fetched 32 tokens at a time (lane
+// j holds the position of the warp's token 32b + j) one block ahead, so the issuing
+// lane never waits on them.
+constexpr int kStreamWarps = 16;
+constexpr int kStreamStages = 2;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far beyond any real copy
 
-    if (tid == 0) {
-        for (int s = 0; s < kStages; s++) bulk::mbar_init(&full[s], 1);
-        stop_flag[0] = stop_flag[1] = 0;
+// Shared memory of qk_stream_kernel: per warp S mbarriers and S validity words, then
+// per warp S stages of one token's q and k rows (+ its cos / sin rows with RoPE).
+__host__ __device__ inline size_t stream_header_bytes(int warps) {
+    return ((size_t)warps * kStreamStages * 12 + 127) / 128 * 128;
+}
+__host__ __device__ inline size_t stream_stage_bytes(int nq, int nkv, bool rope) {
+    return (size_t)(nq + nkv) * 256 + (rope ? 1024 : 0);
+}
+
+template <int QP, int KP>  // QP / KP: q / k passes of 4 heads (0: runtime)
+__global__ void __launch_bounds__(kStreamWarps * 32, 1)
+qk_stream_kernel(uint16_t *q, uint16_t *k, const float *__restrict__ wq,
+                 const float *__restrict__ wk, const float *__restrict__ cos_t,
+                 const float *__restrict__ sin_t, const int32_t *__restrict__ pos,
+                 int64_t table_rows, int64_t rows, int nq, int nkv, float eps, int *err) {
+    constexpr int S = kStreamStages;
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int W = blockDim.x >> 5;  // warps of this launch (fewer for wide head layouts)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool rope = cos_t != nullptr;
+    const uint32_t q_tok = (uint32_t)nq * 256u, k_tok = (uint32_t)nkv * 256u;
+    const uint32_t stage_bytes = (uint32_t)stream_stage_bytes(nq, nkv, rope);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem) + warp * S;
+    int *valid_slot = reinterpret_cast<int *>(smem + W * S * 8) + warp * S;
+    unsigned char *ring = smem + stream_header_bytes(W) + (size_t)warp * S * stage_bytes;
+
+    const int64_t wg = (int64_t)blockIdx.x * W + warp, nw = (int64_t)gridDim.x * W;
+    const int64_t my_n = wg < rows ? (rows - 1 - wg) / nw + 1 : 0;
+    if (my_n == 0) return;  // the whole warp; nothing below synchronises across warps
+    if (lane == 0) {
+        for (int s = 0; s < S; s++) bulk::mbar_init(&full[s], 1);
         bulk::fence_barrier_init();
     }
-    __syncthreads();
+    __syncwarp();
 
-    auto issue = [&](int64_t i) {  // tile i of this CTA into stage i % kStages (a leader)
-        const int64_t r0 = (blockIdx.x + i * gridDim.x) * kTileTok;
-        const uint32_t gt = (uint32_t)imin64((int64_t)kTileTok, rows - r0);
-        unsigned char *st = ring + (size_t)(i % kStages) * stage_bytes;
-        uint64_t *bar = &full[i % kStages];
-        bulk::mbar_arrive_expect_tx(bar, gt * (q_tok + k_tok));
-        bulk::load(st, q + (size_t)r0 * nq * HD, gt * q_tok, bar);
-        if (k_tok) bulk::load(st + kTileTok * q_tok, k + (size_t)r0 * nkv * HD, gt * k_tok, bar);
+    // positions of the warp's items, 32 per register block, one block ahead
+    auto load_pos_block = [&](int64_t b) -> int64_t {
+        const int64_t i = b * 32 + lane;
+        if (i >= my_n) return 0;
+        const int64_t r = wg + i * nw;
+        return pos ? (int64_t)pos[r] : r;
     };
-    int64_t issued = g;  // the group's next tile to issue
-    if (leader)
-        for (int n = 0; n < kStages / 2 && issued < my_n; n++, issued += 2) issue(issued);
+    int64_t pblk = load_pos_block(0), pnxt = load_pos_block(1), cur_b = 0;
+    auto pos_of = [&](int64_t i) -> int64_t {  // warp-collective; i never decreases
+        while (cur_b < (i >> 5)) {
+            pblk = pnxt;
+            cur_b++;
+            pnxt = load_pos_block(cur_b + 1);
+        }
+        return __shfl_sync(0xffffffffu, pblk, (int)(i & 31));
+    };
+    auto issue = [&](int64_t i, int64_t p) {  // lane 0: item i into stage i % S
+        const int s = (int)(i % S);
+        const int64_t r = wg + i * nw;
+        unsigned char *st = ring + (size_t)s * stage_bytes;
+        const bool ok = !rope || (p >= 0 && p < table_rows);
+        valid_slot[s] = ok ? 1 : 0;  // read by the warp after the stage's barrier completes
+        bulk::mbar_arrive_expect_tx(&full[s], stage_bytes);
+        bulk::load(st, q + (size_t)r * nq * 128, q_tok, &full[s]);
+        if (k_tok) bulk::load(st + q_tok, k + (size_t)r * nkv * 128, k_tok, &full[s]);
+        if (rope) {
+            const int64_t pr = ok ? p : 0;  // an out-of-range row loads row 0 and is skipped
+            bulk::load(st + q_tok + k_tok, cos_t + (size_t)pr * 128, 512, &full[s]);
+            bulk::load(st + q_tok + k_tok + 512, sin_t + (size_t)pr * 128, 512, &full[s]);
+        }
+    };
 
-    const int hw = gtid >> 4;   // half-warp 0..7 of the group
-    const int tok = hw / HWT;   // token within the tile
-    const int sub = hw % HWT;   // this half-warp's share of the token's heads
-    const int d0 = (lane & 15) * 4;  // lane owns elements d0..d0+3 and 64+d0..64+d0+3
-    const bool rope = cos_t != nullptr;
-    float wqv[8], wkv[8];  // [0..3] first half, [4..7] second half
-#pragma unroll
-    for (int e = 0; e < 4; e++) {
-        wqv[e] = wq ? wq[d0 + e] : 1.f;
-        wqv[4 + e] = wq ? wq[64 + d0 + e] : 1.f;
-        wkv[e] = wk ? wk[d0 + e] : 1.f;
-        wkv[4 + e] = wk ? wk[64 + d0 + e] : 1.f;
+    int64_t issued = 0;
+    for (; issued < S && issued < my_n; issued++) {
+        const int64_t p = pos_of(issued);
+        if (lane == 0) issue(issued, p);
     }
-    // Table position of this half-warp's token in tile t (-1 when there is no token).
-    auto tile_pos = [&](int64_t t) -> int64_t {
-        if (t >= my_n) return -1;
-        const int64_t row = (blockIdx.x + t * gridDim.x) * kTileTok + tok;
-        if (row >= rows) return -1;
-        return pos ? (int64_t)pos[row] : row;
-    };
-    auto load_table = [&](int64_t p, float (&c)[8], float (&sgn)[8]) {
-        if (!rope || p < 0 || p >= table_rows) return;
-        const float *cr = cos_t + (size_t)p * HD, *sr = sin_t + (size_t)p * HD;
-        const float4 c1 = ld_f4(cr + d0), c2 = ld_f4(cr + 64 + d0);
-        const float4 s1 = ld_f4(sr + d0), s2 = ld_f4(sr + 64 + d0);
-        c[0] = c1.x; c[1] = c1.y; c[2] = c1.z; c[3] = c1.w;
-        c[4] = c2.x; c[5] = c2.y; c[6] = c2.z; c[7] = c2.w;
-        sgn[0] = s1.x; sgn[1] = s1.y; sgn[2] = s1.z; sgn[3] = s1.w;
-        sgn[4] = s2.x; sgn[5] = s2.y; sgn[6] = s2.z; sgn[7] = s2.w;
-    };
-    // positions run two of the group's tiles ahead and table rows one ahead of the
-    // compute, so their global-load latency overlaps the wait for the tile's copy
-    int64_t p_cur = tile_pos(g), p_nxt = tile_pos(g + 2);
-    float cs[8] = {}, sn[8] = {}, csn[8] = {}, snn[8] = {};
-    load_table(p_cur, cs, sn);
+
+    const int hsub = lane >> 3;     // head within a pass of 4
+    const int d0 = (lane & 7) * 8;  // elements d0..d0+7 and 64+d0..64+d0+7
+    float2 wq2[8], wk2[8];
+    load_head_weights(wq2, wq, d0);
+    load_head_weights(wk2, wk, d0);
 
     bool stopped = false;
-    int64_t i = g;
-    for (; i < my_n; i += 2) {
-        const int s = (int)(i % kStages);
-        const uint32_t parity = (uint32_t)((i / kStages) & 1);
-        const int64_t r0 = (blockIdx.x + i * gridDim.x) * kTileTok;
-        const int gt = (int)imin64((int64_t)kTileTok, rows - r0);
+    int64_t i = 0;
+    for (; i < my_n; i++) {
+        const int s = (int)(i % S);
+        const uint32_t parity = (uint32_t)((i / S) & 1);
         unsigned char *st = ring + (size_t)s * stage_bytes;
-        load_table(p_nxt, csn, snn);
-        const int64_t p_far = tile_pos(i + 4);
-        const bool ok = bulk::mbar_wait_bounded(&full[s], parity, kWaitLimitNs);
-        if (!ok) atomicOr(&stop_flag[g], 1);
-        if (ok) {
-            bool valid = tok < gt;
-            if (rope && valid && (p_cur < 0 || p_cur >= table_rows)) {
-                valid = false;
-                if (sub == 0 && (lane & 15) == 0 && err) atomicOr(err, LAI_DEVERR_POSITION);
-            }
-            uint16_t *qb = reinterpret_cast<uint16_t *>(st + (size_t)tok * q_tok);
-            uint16_t *kb = reinterpret_cast<uint16_t *>(st + (size_t)kTileTok * q_tok + (size_t)tok * k_tok);
-            pipe_heads<HWT, QT>(qb, nq, sub, d0, valid, wqv, wq != nullptr, rope, cs, sn, eps);
-            pipe_heads<HWT, KT>(kb, nkv, sub, d0, valid, wkv, wk != nullptr, rope, cs, sn, eps);
-        }
-        p_cur = p_nxt;
-        p_nxt = p_far;
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-            cs[e] = csn[e];
-            sn[e] = snn[e];
-        }
-        bulk::fence_proxy_async_smem();
-        // the group's barrier (ids 1 and 2; 0 is __syncthreads); a lost copy in any of the
-        // group's threads ends the group's work, uniformly
-        asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(kGroupThreads) : "memory");
-        if (*reinterpret_cast<volatile int *>(&stop_flag[g])) {
+        if (!__all_sync(0xffffffffu, bulk::mbar_wait_bounded(&full[s], parity, kWaitLimitNs))) {
             stopped = true;
             break;
         }
-        if (leader) {
-            bulk::store(q + (size_t)r0 * nq * HD, st, (uint32_t)gt * q_tok);
-            if (k_tok)
-                bulk::store(k + (size_t)r0 * nkv * HD, st + kTileTok * q_tok, (uint32_t)gt * k_tok);
-            bulk::commit();
-            if (issued < my_n) {
-                bulk::wait_read<0>();  // this stage has been read out by its stores
-                issue(issued);
-                issued += 2;
+        if (valid_slot[s]) {
+            RopeRow t = {};
+            if (rope) {
+                const float *ct = reinterpret_cast<const float *>(st + q_tok + k_tok);
+                load_rope_row(t, ct, ct + 128, d0);
             }
+            stream_heads<QP>(st, nq, hsub, d0, wq2, wq != nullptr, rope, t, eps);
+            if (k_tok) stream_heads<KP>(st + q_tok, nkv, hsub, d0, wk2, wk != nullptr, rope, t, eps);
+        } else if (lane == 0 && err) {
+            atomicOr(err, LAI_DEVERR_POSITION);  // row left as it was (stored back unchanged)
+        }
+        bulk::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            const int64_t r = wg + i * nw;
+            bulk::store(q + (size_t)r * nq * 128, st, q_tok);
+            if (k_tok) bulk::store(k + (size_t)r * nkv * 128, st + q_tok, k_tok);
+            bulk::commit();
+        }
+        // refill the previous item's stage: its store was committed one iteration ago
+        if (i >= 1 && issued < my_n) {
+            const int64_t p = pos_of(issued);
+            if (lane == 0) {
+                bulk::wait_read<1>();
+                issue(issued, p);
+            }
+            issued++;
         }
     }
-    if (leader) {
+    if (lane == 0) {
         bulk::wait_all();
         if (stopped) {
             if (err) atomicOr(err, LAI_DEVERR_TIMEOUT);
-            // drain loads still in flight into this group's stages, each bounded
-            for (int64_t j = i; j < issued; j += 2)
-                bulk::mbar_wait_bounded(&full[j % kStages], (uint32_t)((j / kStages) & 1), kWaitLimitNs);
+            // drain loads still in flight into this warp's stages, each bounded
+            for (int64_t j = i; j < issued; j++)
+                bulk::mbar_wait_bounded(&full[j % S], (uint32_t)((j / S) & 1), kWaitLimitNs);
         }
+    }
+}
+
+// ---- small batches: one warp per token straight from global memory -----------------
+// Launch- and latency-bound sizes: every q / k load of the token is issued before its
+// position's table row is needed; the same lane mapping and head_math as the stream
+// kernel, so the same bits.
+constexpr int kRegWarps = 4;
+
+template <int QP, int KP>  // q / k passes of 4 heads; the token's rows held in registers
+__global__ void __launch_bounds__(kRegWarps * 32)
+qk_reg_kernel(uint16_t *q, uint16_t *k, const float *__restrict__ wq, const float *__restrict__ wk,
+              const float *__restrict__ cos_t, const float *__restrict__ sin_t,
+              const int32_t *__restrict__ pos, int64_t table_rows, int64_t rows, float eps,
+              int *err) {
+    constexpr int NQ = 4 * QP, NKV = 4 * KP;
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * kRegWarps + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const bool rope = cos_t != nullptr;
+    const int hsub = lane >> 3, d0 = (lane & 7) * 8;
+    uint16_t *qr = q + (size_t)row * NQ * 128;
+    uint16_t *kr = KP ? k + (size_t)row * NKV * 128 : nullptr;
+    uint4 lo[QP + KP], hi[QP + KP];
+#pragma unroll
+    for (int j = 0; j < QP + KP; j++) {
+        const uint16_t *hp = (j < QP ? qr + (size_t)(hsub + 4 * j) * 128
+                                     : kr + (size_t)(hsub + 4 * (j - QP)) * 128);
+        lo[j] = *reinterpret_cast<const uint4 *>(hp + d0);
+        hi[j] = *reinterpret_cast<const uint4 *>(hp + 64 + d0);
+    }
+    const int64_t p = pos ? (int64_t)pos[row] : row;
+    if (rope && (p < 0 || p >= table_rows)) {
+        if (lane == 0 && err) atomicOr(err, LAI_DEVERR_POSITION);
+        return;  // row left as it was
+    }
+    RopeRow t = {};
+    if (rope) load_rope_row(t, cos_t + (size_t)p * 128, sin_t + (size_t)p * 128, d0);
+    float2 w2[8];
+    load_head_weights(w2, wq, d0);
+#pragma unroll
+    for (int j = 0; j < QP; j++) head_math(lo[j], hi[j], w2, wq != nullptr, rope, t, eps);
+    if (KP) {
+        load_head_weights(w2, wk, d0);
+#pragma unroll
+        for (int j = QP; j < QP + KP; j++) head_math(lo[j], hi[j], w2, wk != nullptr, rope, t, eps);
+    }
+#pragma unroll
+    for (int j = 0; j < QP + KP; j++) {
+        uint16_t *hp = (j < QP ? qr + (size_t)(hsub + 4 * j) * 128
+                               : kr + (size_t)(hsub + 4 * (j - QP)) * 128);
+        *reinterpret_cast<uint4 *>(hp + d0) = lo[j];
+        *reinterpret_cast<uint4 *>(hp + 64 + d0) = hi[j];
     }
 }
 
@@ -401,53 +500,68 @@ bool try_fast(T *q, T *k, const float *wq, const float *wk, const float *cos_t,
     }
 }
 
-// Shared memory of the pipelined kernel, and whether it fits two CTAs per SM.
-inline size_t pipe_smem_bytes(int nq, int nkv) {
-    return 128 + (size_t)kStages * kTileTok * (size_t)(nq + nkv) * 128 * 2;
-}
-
 struct DeviceInfo {
     int sms = 0;
     bool attr_set = false;
 };
 
-bool try_pipe(uint16_t *q, uint16_t *k, const float *wq, const float *wk, const float *cos_t,
-              const float *sin_t, const int32_t *pos, int64_t table_rows, int64_t rows, int nq,
-              int nkv, float eps, int *err, cudaStream_t s) {
-    constexpr size_t kMaxSmem = 110 * 1024;  // two CTAs per SM
-    const size_t smem = pipe_smem_bytes(nq, nkv);
-    if (smem > kMaxSmem || !aligned16(q) || (k && !aligned16(k)) ||
-        (cos_t && (!aligned16(cos_t) || !aligned16(sin_t))))
+#ifndef LAI_QK_REG_ROWS
+#define LAI_QK_REG_ROWS 4096
+#endif
+#ifndef LAI_QK_CTAS_PER_SM
+#define LAI_QK_CTAS_PER_SM 1
+#endif
+
+// BF16, hd = 128: qk_reg_kernel for small Qwen3-shaped batches, qk_stream_kernel
+// otherwise (the same bits either way). false when neither applies.
+bool try_bf16_hd128(uint16_t *q, uint16_t *k, const float *wq, const float *wk,
+                    const float *cos_t, const float *sin_t, const int32_t *pos, int64_t table_rows,
+                    int64_t rows, int nq, int nkv, float eps, int *err, cudaStream_t s) {
+    constexpr size_t kMaxSmem = 227 * 1024;
+    constexpr int kCtasPerSm = LAI_QK_CTAS_PER_SM;
+    const bool rope = cos_t != nullptr;
+    if (!aligned16(q) || (k && !aligned16(k)) || (rope && (!aligned16(cos_t) || !aligned16(sin_t))))
         return false;
+    // Qwen3's 16 q / 8 kv heads get fully unrolled head loops; other counts the generic one.
+    const bool qwen = nq == 16 && (nkv == 8 || nkv == 0);
+    if (qwen && rows <= LAI_QK_REG_ROWS) {
+        auto kern = nkv ? qk_reg_kernel<4, 2> : qk_reg_kernel<4, 0>;
+        kern<<<grid_for(rows, kRegWarps), kRegWarps * 32, 0, s>>>(q, k, wq, wk, cos_t, sin_t, pos,
+                                                                   table_rows, rows, eps, err);
+        return true;
+    }
+    // as many warps (up to kStreamWarps per SM) as fit their stages in shared memory
+    const size_t per_warp = (size_t)kStreamStages * stream_stage_bytes(nq, nkv, rope);
+    int warps = kStreamWarps / kCtasPerSm;
+    while (warps > 0 && stream_header_bytes(warps) + warps * per_warp > kMaxSmem / kCtasPerSm)
+        warps--;
+    if (warps == 0) return false;
+    const size_t smem = stream_header_bytes(warps) + warps * per_warp;
     static DeviceInfo info[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
     DeviceInfo &d = info[dev];
-    // Qwen3's 16 q / 8 kv heads get fully unrolled head loops; other counts the generic one.
-    constexpr int HW = 8 / kTileTok;  // half-warps per token within a warp group
-    const bool qwen = nq == 8 * HW && (nkv == 4 * HW || nkv == 0);
-    auto kern = qwen ? (nkv ? qk_pipe_kernel<8, 4> : qk_pipe_kernel<8, 0>) : qk_pipe_kernel<0, 0>;
+    auto kern = qwen ? (nkv ? qk_stream_kernel<4, 2> : qk_stream_kernel<4, 0>)
+                     : qk_stream_kernel<0, 0>;
     if (!d.attr_set) {
         if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
             cudaGetLastError();
             return false;
         }
-        for (auto f : {qk_pipe_kernel<8, 4>, qk_pipe_kernel<8, 0>, qk_pipe_kernel<0, 0>}) {
+        for (auto f : {qk_stream_kernel<4, 2>, qk_stream_kernel<4, 0>, qk_stream_kernel<0, 0>}) {
             if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)kMaxSmem) != cudaSuccess ||
-                // the largest carveout, so that two CTAs' rings are resident per SM
-                cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, 100) !=
-                    cudaSuccess) {
+                                     (int)kMaxSmem) != cudaSuccess) {
                 cudaGetLastError();
                 return false;
             }
         }
         d.attr_set = true;
     }
-    const int64_t ntiles = (rows + kTileTok - 1) / kTileTok;
-    const int64_t grid = ntiles < 2 * (int64_t)d.sms ? ntiles : 2 * (int64_t)d.sms;
-    kern<<<(unsigned)grid, kPipeThreads, smem, s>>>(q, k, wq, wk, cos_t, sin_t, pos, table_rows,
-                                                    rows, nq, nkv, eps, err);
+    const int64_t ctas = (rows + warps - 1) / warps;
+    const int64_t cap = (int64_t)kCtasPerSm * d.sms;
+    const int64_t grid = ctas < cap ? ctas : cap;
+    kern<<<(unsigned)grid, warps * 32, smem, s>>>(q, k, wq, wk, cos_t, sin_t, pos, table_rows,
+                                                  rows, nq, nkv, eps, err);
     return true;
 }
 
@@ -464,8 +578,8 @@ int run(T *q, T *k, const float *wq, const float *wk, const float *cos_t, const 
     cudaStream_t s = as_stream(stream);
     bool done = false;
     if constexpr (sizeof(T) == 2) {
-        if (hd == 128) done = try_pipe(q, k, wq, wk, cos_t, sin_t, pos, table_rows, rows, nq,
-                                       k ? nkv : 0, eps, err, s);
+        if (hd == 128) done = try_bf16_hd128(q, k, wq, wk, cos_t, sin_t, pos, table_rows, rows,
+                                             nq, k ? nkv : 0, eps, err, s);
     }
     if (!done) switch (hd) {
         case 64: done = try_fast<T, 64>(q, k, wq, wk, cos_t, sin_t, pos, table_rows, rows, nq, nkv, eps, err, s); break;

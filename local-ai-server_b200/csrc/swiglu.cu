@@ -13,11 +13,20 @@
 // In place without scratch. Unit k reads input bytes [16k, 16k+16) and writes
 // output bytes [8k, 8k+8), which hold the input of unit k/2. Units are therefore
 // processed in waves [L, 2L): a wave reads [16L, 32L) and writes [8L, 16L) --
-// disjoint -- and its writes only clobber inputs of the previous wave. Wave 0
-// ([0, kHeadUnits)) runs inside one CTA as sub-waves [0,1), [1,2), [2,4), ...
-// separated by __syncthreads; every later wave is one launch, ordered by the
-// stream. The ragged tail (inter*rows not a multiple of the unit width) is one
-// final serial step. log2(units / kHeadUnits) + 2 launches in total.
+// disjoint -- and its writes only clobber inputs of the previous wave, so a wave's
+// writes may start once every read of the previous wave is done. One cooperative
+// launch (every CTA resident) runs the whole schedule: a head of H units (H = the
+// grid's threads x kHeadRegs) is read into registers, one grid-wide barrier, then
+// written; the waves [H, 2H), [2H, 4H), ... follow, each separated from the next by
+// one grid-wide barrier (the wave right after the head needs none: its writes
+// clobber head inputs, all read before the head's barrier). The ragged tail
+// (inter*rows not a multiple of the unit width) is one serial step after a last
+// barrier: log2(units / H) + 2 barriers in one launch. (One launch per wave, with a
+// one-CTA head, cost 19% over the out-of-place form at 65536 x 6144: launch gaps and
+// tails of ~15 dependent launches.) Unaligned buffers keep that per-launch wave form
+// with scalar units.
+#include <cooperative_groups.h>
+
 #include "lai_common.cuh"
 
 namespace lai {
@@ -72,6 +81,64 @@ swiglu_units_kernel(uint2 *out, const uint4 *in, int64_t u0, int64_t u1) {
     }
 }
 
+// The whole in-place schedule in one cooperative launch (described at the top).
+constexpr int kCoopThreads = 256;
+constexpr int kCoopMinCtas = 6;  // 1536 threads per SM without spills
+constexpr int kHeadRegs = 4;     // head units held in registers per thread
+
+__device__ __forceinline__ uint4 ld_l2(const uint4 *p) {  // L2 only: bytes change under us
+    uint4 v;
+    asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kCoopThreads, kCoopMinCtas)
+swiglu_inplace_coop_kernel(T *buf, int64_t units, int64_t tail0, int64_t n) {
+    namespace cg = cooperative_groups;
+    cg::grid_group grid = cg::this_grid();
+    uint2 *out = reinterpret_cast<uint2 *>(buf);
+    const uint4 *in = reinterpret_cast<const uint4 *>(buf);
+    const int64_t nt = (int64_t)gridDim.x * kCoopThreads;
+    const int64_t t = (int64_t)blockIdx.x * kCoopThreads + threadIdx.x;
+    const int64_t head = units < nt * kHeadRegs ? units : nt * kHeadRegs;
+    {
+        uint4 v[kHeadRegs];
+#pragma unroll
+        for (int r = 0; r < kHeadRegs; r++)
+            if (t + r * nt < head) v[r] = ld_l2(in + t + r * nt);
+        grid.sync();  // every head unit read before any is written
+#pragma unroll
+        for (int r = 0; r < kHeadRegs; r++)
+            if (t + r * nt < head) out[t + r * nt] = unit_op<T>(v[r]);
+    }
+    // waves: each CTA takes contiguous blocks of kCoopThreads * kUnroll units (16 KB read)
+    constexpr int64_t kBlock = (int64_t)kCoopThreads * kUnroll;
+    for (int64_t lo = head; lo < units;) {
+        const int64_t hi = 2 * lo < units ? 2 * lo : units;
+        if (lo > head) grid.sync();  // the previous wave's reads before this wave's writes
+        for (int64_t b0 = lo + (int64_t)blockIdx.x * kBlock + threadIdx.x; b0 < hi;
+             b0 += (int64_t)gridDim.x * kBlock) {
+            uint4 v[kUnroll];
+#pragma unroll
+            for (int i = 0; i < kUnroll; i++)
+                if (b0 + i * kCoopThreads < hi) v[i] = ld_l2(in + b0 + i * kCoopThreads);
+#pragma unroll
+            for (int i = 0; i < kUnroll; i++)
+                if (b0 + i * kCoopThreads < hi) out[b0 + i * kCoopThreads] = unit_op<T>(v[i]);
+        }
+        lo = hi;
+    }
+    if (tail0 < n) {
+        grid.sync();  // the last wave's reads before the tail's writes
+        if (t == 0)
+            for (int64_t k = tail0; k < n; k++)
+                buf[k] = from_f<T>(silu_mul<T>(to_f(buf[2 * k]), to_f(buf[2 * k + 1])));
+    }
+}
+
 // Scalar elements [k0, k1) in increasing order by one thread: the ragged tail,
 // in place or not (the serial order is the reference's own).
 template <typename T>
@@ -80,30 +147,9 @@ __global__ void swiglu_serial_kernel(T *out, const T *in, int64_t k0, int64_t k1
     for (int64_t k = k0; k < k1; k++) out[k] = from_f<T>(silu_mul<T>(to_f(in[2 * k]), to_f(in[2 * k + 1])));
 }
 
-// Wave 0 of the in-place schedule in one CTA: sub-waves [0,1), [1,2), [2,4), ...
-// up to `u1` units, then (if `tail_k1` > `tail_k0`) the serial tail.
-template <typename T>
-__global__ void __launch_bounds__(1024)
-swiglu_inplace_head_kernel(T *buf, int64_t u1, int64_t tail_k0, int64_t tail_k1) {
-    uint2 *out = reinterpret_cast<uint2 *>(buf);
-    const uint4 *in = reinterpret_cast<const uint4 *>(buf);
-    int64_t lo = 0, hi = u1 < 1 ? u1 : 1;
-    while (lo < u1) {
-        for (int64_t k = lo + threadIdx.x; k < hi; k += blockDim.x) {
-            const uint4 v = ld_rw(in + k);  // written earlier in this kernel? never: reads run ahead
-            out[k] = unit_op<T>(v);
-        }
-        __syncthreads();
-        lo = hi;
-        hi = 2 * hi < u1 ? 2 * hi : u1;
-    }
-    if (threadIdx.x == 0)
-        for (int64_t k = tail_k0; k < tail_k1; k++)
-            buf[k] = from_f<T>(silu_mul<T>(to_f(buf[2 * k]), to_f(buf[2 * k + 1])));
-}
-
-// Scalar-unit variant of the wave schedule for unaligned in-place buffers:
-// unit = one output element (reads 2 elements, writes 1); same wave algebra.
+// Scalar-unit wave schedule for unaligned in-place buffers: unit = one output element
+// (reads 2 elements, writes 1); the same wave algebra, wave 0 as sub-waves inside one
+// CTA separated by __syncthreads, every later wave one launch ordered by the stream.
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
 swiglu_scalar_units_kernel(T *out, const T *in, int64_t u0, int64_t u1) {
@@ -125,6 +171,27 @@ __global__ void __launch_bounds__(1024) swiglu_scalar_head_kernel(T *buf, int64_
         lo = hi;
         hi = 2 * hi < u1 ? 2 * hi : u1;
     }
+}
+
+// CTAs of a cooperative launch of `kern` for `units` units: every SM's resident
+// share (cached per device), no more than the units need. 0 on error.
+template <typename K>
+int coop_grid(K kern, int64_t units) {
+    static int resident[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    if (resident[dev] == 0) {
+        int sms = 0, per_sm = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kCoopThreads, 0) !=
+                cudaSuccess || per_sm <= 0) {
+            cudaGetLastError();
+            return 0;
+        }
+        resident[dev] = sms * per_sm;
+    }
+    const int64_t need = (units + kCoopThreads - 1) / kCoopThreads;
+    return (int)(need < resident[dev] ? need : resident[dev]);
 }
 
 template <typename T>
@@ -149,16 +216,19 @@ int run(T *out, const T *in, int64_t rows, int inter, lai_stream_t stream) {
             if (tail0 < n) swiglu_serial_kernel<T><<<1, 32, 0, s>>>(out, in, tail0, n);
             return launch_status();
         }
-        const int64_t head = units < kHeadUnits ? units : kHeadUnits;
-        const bool tail_in_head = head == units;
-        swiglu_inplace_head_kernel<T><<<1, 1024, 0, s>>>(out, head, tail_in_head ? tail0 : 0,
-                                                         tail_in_head ? n : 0);
-        for (int64_t lo = head; lo < units;) {
-            const int64_t hi = 2 * lo < units ? 2 * lo : units;
-            swiglu_units_kernel<T><<<grid_for(hi - lo, kThreads * kUnroll), kThreads, 0, s>>>(o, iv, lo, hi);
-            lo = hi;
+        if (units == 0) {
+            swiglu_serial_kernel<T><<<1, 32, 0, s>>>(out, in, 0, n);
+            return launch_status();
         }
-        if (!tail_in_head && tail0 < n) swiglu_serial_kernel<T><<<1, 32, 0, s>>>(out, in, tail0, n);
+        const int grid = coop_grid(swiglu_inplace_coop_kernel<T>, units);
+        if (grid <= 0) return LAI_ERR_CUDA;
+        int64_t units_a = units, tail_a = tail0, n_a = n;
+        void *args[] = {&out, &units_a, &tail_a, &n_a};
+        if (cudaLaunchCooperativeKernel((const void *)swiglu_inplace_coop_kernel<T>, grid,
+                                        kCoopThreads, args, 0, s) != cudaSuccess) {
+            cudaGetLastError();
+            return LAI_ERR_CUDA;
+        }
         return launch_status();
     }
 
