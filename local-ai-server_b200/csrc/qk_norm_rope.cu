@@ -9,11 +9,12 @@
 // read once, written once in place); the [hd] weights and the table rows are
 // shared (L1/L2-resident) and not counted.
 //
-// Kernels. BF16 with hd=128 (every Qwen3 decoder shape) runs qk_stream_kernel: a
-// persistent kernel whose warps each stream single tokens through their own
-// shared-memory stages filled by bulk async copies (described at the kernel); small
-// batches of the Qwen3 head layout run qk_reg_kernel with the same per-head
-// arithmetic, so a token's result never depends on the batch it arrives in. FP32 and hd=64/256 run
+// Kernels. BF16 with hd=128 and the Qwen3 head layout (16 q / 8 kv heads, every Qwen3
+// decoder shape) runs qk_reg_kernel: one warp per token, the token's rows held in
+// registers; other head counts run qk_stream_kernel, a persistent kernel whose warps
+// each stream single tokens through their own shared-memory stages filled by bulk
+// async copies. Both share the per-head arithmetic and are used for every batch size,
+// so a token's result never depends on the batch it arrives in. FP32 and hd=64/256 run
 // qk_warp_kernel: one warp owns one (token, q-or-k) segment; a head of hd elements
 // spans LPH = hd*s/16 lanes, each lane one 16-byte vector, all of the segment's
 // loads issued before any arithmetic; the per-head sum of squares is an xor-shuffle
@@ -231,6 +232,7 @@ __device__ __forceinline__ void stream_heads(unsigned char *base, int nheads, in
 
 // ---- streaming kernel: an independent bulk-copy pipeline per warp -------------------
 //
+// Any head count (qk_reg_kernel covers the Qwen3 layout, whose rows fit in registers).
 // One CTA per SM, up to kStreamWarps warps, no CTA-wide barrier after set-up: every
 // warp runs its own pipeline over kStreamStages single-token stages. A stage holds the
 // token's q row, its k row and (with RoPE) its cos and sin table rows, fetched by bulk
@@ -258,7 +260,7 @@ __host__ __device__ inline size_t stream_stage_bytes(int nq, int nkv, bool rope)
     return (size_t)(nq + nkv) * 256 + (rope ? 1024 : 0);
 }
 
-template <int QP, int KP>  // QP / KP: q / k passes of 4 heads (0: runtime)
+template <int QP, int KP>  // QP / KP: q / k passes of 4 heads (0: runtime count)
 __global__ void __launch_bounds__(kStreamWarps * 32, 1)
 qk_stream_kernel(uint16_t *q, uint16_t *k, const float *__restrict__ wq,
                  const float *__restrict__ wk, const float *__restrict__ cos_t,
@@ -378,10 +380,15 @@ qk_stream_kernel(uint16_t *q, uint16_t *k, const float *__restrict__ wq,
     }
 }
 
-// ---- small batches: one warp per token straight from global memory -----------------
-// Launch- and latency-bound sizes: every q / k load of the token is issued before its
-// position's table row is needed; the same lane mapping and head_math as the stream
-// kernel, so the same bits.
+// ---- Qwen3 head layout: one warp per token straight from global memory -------------
+// Every q / k load of the token (12 x 16 bytes per lane for 16 + 8 heads) is issued
+// before the position's table row is needed, so a warp keeps 6 KB in flight and the
+// ~16 resident warps per SM (126 registers each) keep ~100 KB per SM in flight. Same
+// lane mapping and head_math as qk_stream_kernel. Measured against it (same bits, B200,
+// 16 q / 8 kv heads): 125 vs 135 us at 65536 tokens (0.98 vs 0.91 of the measured copy
+// bandwidth), 3.82 vs 3.97 ms at 2M tokens, 16.5 vs 22.6 us at 8192 and 5.1 vs 5.0 us
+// at 512: the shared-memory staging of the stream kernel buys nothing when the whole
+// token fits in a warp's registers.
 constexpr int kRegWarps = 4;
 
 template <int QP, int KP>  // q / k passes of 4 heads; the token's rows held in registers
@@ -505,26 +512,18 @@ struct DeviceInfo {
     bool attr_set = false;
 };
 
-#ifndef LAI_QK_REG_ROWS
-#define LAI_QK_REG_ROWS 4096
-#endif
-#ifndef LAI_QK_CTAS_PER_SM
-#define LAI_QK_CTAS_PER_SM 1
-#endif
-
-// BF16, hd = 128: qk_reg_kernel for small Qwen3-shaped batches, qk_stream_kernel
-// otherwise (the same bits either way). false when neither applies.
+// BF16, hd = 128: qk_reg_kernel for the Qwen3 head layout (16 q / 8 or 0 kv heads),
+// qk_stream_kernel for any other head count (the same per-head bits either way).
+// false when neither applies.
 bool try_bf16_hd128(uint16_t *q, uint16_t *k, const float *wq, const float *wk,
                     const float *cos_t, const float *sin_t, const int32_t *pos, int64_t table_rows,
                     int64_t rows, int nq, int nkv, float eps, int *err, cudaStream_t s) {
     constexpr size_t kMaxSmem = 227 * 1024;
-    constexpr int kCtasPerSm = LAI_QK_CTAS_PER_SM;
     const bool rope = cos_t != nullptr;
     if (!aligned16(q) || (k && !aligned16(k)) || (rope && (!aligned16(cos_t) || !aligned16(sin_t))))
         return false;
-    // Qwen3's 16 q / 8 kv heads get fully unrolled head loops; other counts the generic one.
     const bool qwen = nq == 16 && (nkv == 8 || nkv == 0);
-    if (qwen && rows <= LAI_QK_REG_ROWS) {
+    if (qwen) {
         auto kern = nkv ? qk_reg_kernel<4, 2> : qk_reg_kernel<4, 0>;
         kern<<<grid_for(rows, kRegWarps), kRegWarps * 32, 0, s>>>(q, k, wq, wk, cos_t, sin_t, pos,
                                                                    table_rows, rows, eps, err);
@@ -532,33 +531,26 @@ bool try_bf16_hd128(uint16_t *q, uint16_t *k, const float *wq, const float *wk,
     }
     // as many warps (up to kStreamWarps per SM) as fit their stages in shared memory
     const size_t per_warp = (size_t)kStreamStages * stream_stage_bytes(nq, nkv, rope);
-    int warps = kStreamWarps / kCtasPerSm;
-    while (warps > 0 && stream_header_bytes(warps) + warps * per_warp > kMaxSmem / kCtasPerSm)
-        warps--;
+    int warps = kStreamWarps;
+    while (warps > 0 && stream_header_bytes(warps) + warps * per_warp > kMaxSmem) warps--;
     if (warps == 0) return false;
     const size_t smem = stream_header_bytes(warps) + warps * per_warp;
     static DeviceInfo info[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
     DeviceInfo &d = info[dev];
-    auto kern = qwen ? (nkv ? qk_stream_kernel<4, 2> : qk_stream_kernel<4, 0>)
-                     : qk_stream_kernel<0, 0>;
+    auto kern = qk_stream_kernel<0, 0>;
     if (!d.attr_set) {
-        if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kMaxSmem) != cudaSuccess) {
             cudaGetLastError();
             return false;
-        }
-        for (auto f : {qk_stream_kernel<4, 2>, qk_stream_kernel<4, 0>, qk_stream_kernel<0, 0>}) {
-            if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)kMaxSmem) != cudaSuccess) {
-                cudaGetLastError();
-                return false;
-            }
         }
         d.attr_set = true;
     }
     const int64_t ctas = (rows + warps - 1) / warps;
-    const int64_t cap = (int64_t)kCtasPerSm * d.sms;
+    const int64_t cap = (int64_t)d.sms;
     const int64_t grid = ctas < cap ? ctas : cap;
     kern<<<(unsigned)grid, warps * 32, smem, s>>>(q, k, wq, wk, cos_t, sin_t, pos, table_rows,
                                                   rows, nq, nkv, eps, err);

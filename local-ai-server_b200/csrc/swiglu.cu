@@ -14,17 +14,19 @@
 // output bytes [8k, 8k+8), which hold the input of unit k/2. Units are therefore
 // processed in waves [L, 2L): a wave reads [16L, 32L) and writes [8L, 16L) --
 // disjoint -- and its writes only clobber inputs of the previous wave, so a wave's
-// writes may start once every read of the previous wave is done. One cooperative
-// launch (every CTA resident) runs the whole schedule: a head of H units (H = the
-// grid's threads x kHeadRegs) is read into registers, one grid-wide barrier, then
-// written; the waves [H, 2H), [2H, 4H), ... follow, each separated from the next by
-// one grid-wide barrier (the wave right after the head needs none: its writes
-// clobber head inputs, all read before the head's barrier). The ragged tail
-// (inter*rows not a multiple of the unit width) is one serial step after a last
-// barrier: log2(units / H) + 2 barriers in one launch. (One launch per wave, with a
-// one-CTA head, cost 19% over the out-of-place form at 65536 x 6144: launch gaps and
-// tails of ~15 dependent launches.) Unaligned buffers keep that per-launch wave form
-// with scalar units.
+// writes may start once every read of the previous wave is done. A cooperative
+// launch (every CTA resident) runs the start of the schedule: a head of H units (H =
+// the grid's threads x kHeadRegs, ~0.9M) is read into registers, one grid-wide
+// barrier, then written; the small waves [H, 2H), [2H, 4H), ... follow, each separated
+// from the next by one grid-wide barrier (the wave right after the head needs none: its
+// writes clobber head inputs, all read before the head's barrier). Waves of
+// kCoopWaveMax units or more are ordinary launches ordered by the stream (the
+// persistent grid-stride loop streams them ~30% below a fresh grid). The ragged tail
+// (inter*rows not a multiple of the unit width) is one serial step at the end. At
+// 65536 x 6144 that is one cooperative launch and 4 wave launches; one launch per wave
+// with a one-CTA head, as before, cost 19% over the out-of-place form there (launch gaps
+// and tails of ~15 dependent launches), the whole schedule in the cooperative launch 43%.
+// Unaligned buffers keep the per-launch wave form with scalar units.
 #include <cooperative_groups.h>
 
 #include "lai_common.cuh"
@@ -85,6 +87,7 @@ swiglu_units_kernel(uint2 *out, const uint4 *in, int64_t u0, int64_t u1) {
 constexpr int kCoopThreads = 256;
 constexpr int kCoopMinCtas = 6;  // 1536 threads per SM without spills
 constexpr int kHeadRegs = 4;     // head units held in registers per thread
+constexpr int64_t kCoopWaveMax = 4 << 20;  // units: larger waves are ordinary launches
 
 __device__ __forceinline__ uint4 ld_l2(const uint4 *p) {  // L2 only: bytes change under us
     uint4 v;
@@ -94,9 +97,11 @@ __device__ __forceinline__ uint4 ld_l2(const uint4 *p) {  // L2 only: bytes chan
     return v;
 }
 
+// The head and every wave up to unit `u_stop` (a wave boundary); with u_stop == units
+// also the ragged tail [tail0, n).
 template <typename T>
 __global__ void __launch_bounds__(kCoopThreads, kCoopMinCtas)
-swiglu_inplace_coop_kernel(T *buf, int64_t units, int64_t tail0, int64_t n) {
+swiglu_inplace_coop_kernel(T *buf, int64_t units, int64_t u_stop, int64_t tail0, int64_t n) {
     namespace cg = cooperative_groups;
     cg::grid_group grid = cg::this_grid();
     uint2 *out = reinterpret_cast<uint2 *>(buf);
@@ -116,7 +121,7 @@ swiglu_inplace_coop_kernel(T *buf, int64_t units, int64_t tail0, int64_t n) {
     }
     // waves: each CTA takes contiguous blocks of kCoopThreads * kUnroll units (16 KB read)
     constexpr int64_t kBlock = (int64_t)kCoopThreads * kUnroll;
-    for (int64_t lo = head; lo < units;) {
+    for (int64_t lo = head; lo < u_stop;) {
         const int64_t hi = 2 * lo < units ? 2 * lo : units;
         if (lo > head) grid.sync();  // the previous wave's reads before this wave's writes
         for (int64_t b0 = lo + (int64_t)blockIdx.x * kBlock + threadIdx.x; b0 < hi;
@@ -131,7 +136,7 @@ swiglu_inplace_coop_kernel(T *buf, int64_t units, int64_t tail0, int64_t n) {
         }
         lo = hi;
     }
-    if (tail0 < n) {
+    if (u_stop == units && tail0 < n) {
         grid.sync();  // the last wave's reads before the tail's writes
         if (t == 0)
             for (int64_t k = tail0; k < n; k++)
@@ -222,13 +227,28 @@ int run(T *out, const T *in, int64_t rows, int inter, lai_stream_t stream) {
         }
         const int grid = coop_grid(swiglu_inplace_coop_kernel<T>, units);
         if (grid <= 0) return LAI_ERR_CUDA;
-        int64_t units_a = units, tail_a = tail0, n_a = n;
-        void *args[] = {&out, &units_a, &tail_a, &n_a};
+        // the same wave boundaries as the kernel: head, then doubling waves; the
+        // cooperative launch stops before the first wave of kCoopWaveMax units or more
+        const int64_t head_cap = (int64_t)grid * kCoopThreads * kHeadRegs;
+        int64_t u_stop = units < head_cap ? units : head_cap;
+        while (u_stop < units) {
+            const int64_t hi = 2 * u_stop < units ? 2 * u_stop : units;
+            if (hi - u_stop >= kCoopWaveMax) break;
+            u_stop = hi;
+        }
+        int64_t units_a = units, stop_a = u_stop, tail_a = tail0, n_a = n;
+        void *args[] = {&out, &units_a, &stop_a, &tail_a, &n_a};
         if (cudaLaunchCooperativeKernel((const void *)swiglu_inplace_coop_kernel<T>, grid,
                                         kCoopThreads, args, 0, s) != cudaSuccess) {
             cudaGetLastError();
             return LAI_ERR_CUDA;
         }
+        for (int64_t lo = u_stop; lo < units;) {
+            const int64_t hi = 2 * lo < units ? 2 * lo : units;
+            swiglu_units_kernel<T><<<grid_for(hi - lo, kThreads * kUnroll), kThreads, 0, s>>>(o, iv, lo, hi);
+            lo = hi;
+        }
+        if (u_stop < units && tail0 < n) swiglu_serial_kernel<T><<<1, 32, 0, s>>>(out, in, tail0, n);
         return launch_status();
     }
 
