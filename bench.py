@@ -2022,7 +2022,7 @@ def run_ours(args) -> None:
                   "timing": "CUDA graph replay" if graph else "direct launches",
                   "unfused_library_us_per_step": unfused_us,
                   "l2": f"weights larger than L2 ({step_bytes / 1e9:.2f} GB per step)"}
-        launches_per_step = 8 * cfg.layers  # 4 GEMVs + 4 L2 prefetches per layer
+        launches_per_step = 4 * cfg.layers
     elif snake:
         config = {"workload": "vocoder SnakeBeta over the BigVGAN stages, FP32 in place",
                   "config": "c4", "stages": runner.SNAKE_STAGES, "batch": runner.SNAKE_BATCH,

@@ -216,14 +216,6 @@ LAI_API int lai_gemv_swiglu_f32w_f32(float *out, const float *x, const float *no
                                      const float *W_gu, int64_t M, int K, int inter,
                                      lai_stream_t stream);
 
-/* No counterpart in the reference (a scheduling helper for the GEMV chain above): bring
- * [p, p + bytes) into L2 with bulk prefetches while the kernel before it on `stream`
- * runs, e.g. the next projection's weights during the current GEMV. Launched with
- * programmatic dependent launch; it completes only after the previous kernel on the
- * stream has, so ordering on the stream is unchanged. p 16-byte aligned; a ragged
- * tail under 16 bytes is not prefetched. Reads nothing into the SM, writes nothing. */
-LAI_API int lai_prefetch_l2(const void *p, int64_t bytes, lai_stream_t stream);
-
 /* Load-time weight preparation (the reference converts BF16 safetensors when it uploads
  * weights, src/tts_native.c:1185-1240):
  *   lai_quantize_rows_i8_bf16: W [N, K] BF16 -> q [N, K] INT8 and scales [N] F32 with

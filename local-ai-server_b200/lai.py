@@ -44,7 +44,6 @@ SIGNATURES: dict[str, tuple] = {
     "lai_embed_gather_bf16_to_f32": (_i32, [_vp, _vp, _vp, _i64, _i32, _i64, _vp, _vp]),
     "lai_snake_beta_f32": (_i32, [_vp, _vp, _vp, _i64, _i32, _i64, _vp]),
     "lai_gemv_bf16w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
-    "lai_prefetch_l2": (_i32, [_vp, _i64, _vp]),
     "lai_gemv_residual_bf16w_f32": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _vp]),
     "lai_gemv_swiglu_bf16w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
     "lai_gemv_f16w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
@@ -249,11 +248,6 @@ def embed_gather(table, ids, to_f32: bool, err=None, stream=None):
     fn = "lai_embed_gather_bf16_to_f32" if to_f32 else "lai_embed_gather_bf16"
     call(fn, _p(out), _p(table), _p(ids), n, dim, table.shape[0], _p(err), _s(stream))
     return out
-
-
-def prefetch_l2(t, stream=None):
-    """Bring tensor t's bytes into L2 while the previous kernel on the stream runs."""
-    call("lai_prefetch_l2", _p(t), t.numel() * t.element_size(), _s(stream))
 
 
 def snake_beta(x, ea, ieb, stream=None):

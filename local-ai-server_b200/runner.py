@@ -854,23 +854,15 @@ class DecodeLinear:
                                      seed=seed + 8)
         self.qkv = torch.empty((M, self.qkv_n), dtype=f32, device=device)
         self.act = torch.empty((M, I), dtype=f32, device=device)
-        names = ("rmsnorm_qkv_gemv", "o_gemv_residual", "rmsnorm_gate_up_gemv_swiglu",
-                 "down_gemv_residual")
-        # before every GEMV, the next GEMV's weights (wrapping to the next step's first)
-        # are prefetched into L2 while this one runs (lai_prefetch_l2)
-        self.kernel_names = tuple(n for g in names * L for n in ("l2_prefetch", g))
-
-    def weights_in_order(self) -> list:
-        """The step's weight matrices in launch order."""
-        return [W for l in range(self.cfg.layers)
-                for W in (self.Wqkv[l], self.Wo[l], self.Wgu[l], self.Wd[l])]
+        self.kernel_names = ("rmsnorm_qkv_gemv", "o_gemv_residual", "rmsnorm_gate_up_gemv_swiglu",
+                             "down_gemv_residual") * L
 
     def launches(self, stream=None):
         c = self.cfg
         sc = lambda W: self.scales.get(id(W))  # noqa: E731
-        gemvs = []
+        out = []
         for l in range(c.layers):
-            gemvs += [
+            out += [
                 lambda l=l: lai.gemv(self.x, self.Wqkv[l], self.w_in, c.eps, y=self.qkv,
                                      stream=stream, scales=sc(self.Wqkv[l])),
                 lambda l=l: lai.gemv_residual(self.x, self.attn, self.Wo[l], stream=stream,
@@ -880,11 +872,6 @@ class DecodeLinear:
                 lambda l=l: lai.gemv_residual(self.x, self.act, self.Wd[l], stream=stream,
                                               scales=sc(self.Wd[l])),
             ]
-        ws = self.weights_in_order()
-        out = []
-        for j, g in enumerate(gemvs):
-            nxt = ws[(j + 1) % len(ws)]
-            out += [lambda nxt=nxt: lai.prefetch_l2(nxt, stream=stream), g]
         return out
 
     def unfused_library_launches(self):
@@ -919,16 +906,13 @@ class DecodeLinear:
         c, M, e = self.cfg, self.cfg.m, self.wbytes
         D, I = c.dim, c.inter
         s = 4 if self.wfmt == "i8" else 0
-        gemv = [self.qkv_n * (D * e + s) + M * D * 4 + M * self.qkv_n * 4 + D * 4,
+        return [self.qkv_n * (D * e + s) + M * D * 4 + M * self.qkv_n * 4 + D * 4,
                 D * (c.q_dim * e + s) + M * c.q_dim * 4 + 2 * M * D * 4,
                 2 * I * (D * e + s) + M * D * 4 + M * I * 4 + D * 4,
                 D * (I * e + s) + M * I * 4 + 2 * M * D * 4] * c.layers
-        # a prefetch moves the next GEMV's weights HBM -> L2 on that GEMV's behalf: its
-        # bytes are that GEMV's, counted there once
-        return [b for g in gemv for b in (0, g)]
 
     def rows_per_launch(self) -> list[int]:
-        return [self.cfg.m] * 8 * self.cfg.layers
+        return [self.cfg.m] * 4 * self.cfg.layers
 
 
 @dataclasses.dataclass(frozen=True)

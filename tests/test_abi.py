@@ -129,10 +129,6 @@ P = _P()
     (lambda l: l.lai_quantize_rows_i8_bf16(A(4096), A(1 << 20), A(4096 + 16), 4, 64, None),
      lai.LAI_ERR_ALIAS),
     (lambda l: l.lai_convert_bf16_to_f16(A(4096), A(4096 + 2), 64, None), lai.LAI_ERR_ALIAS),
-    # L2 prefetch: NULL, unaligned start, negative size
-    (lambda l: l.lai_prefetch_l2(None, 64, None), lai.LAI_ERR_INVALID),
-    (lambda l: l.lai_prefetch_l2(A(4096 + 8), 64, None), lai.LAI_ERR_INVALID),
-    (lambda l: l.lai_prefetch_l2(A(4096), -1, None), lai.LAI_ERR_INVALID),
 ])
 def test_argument_checks(call, want):
     assert call(lai.load()) == want
