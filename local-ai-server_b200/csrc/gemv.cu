@@ -48,6 +48,12 @@ constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxM = 8;
 constexpr int kUnrollK = 8;  // 16-byte weight vectors in flight per lane per row (K <= 2048: one trip)
+// M = 1 rows longer than one trip of kUnrollK vectors (BF16 K > 2048, e.g. the down
+// projection's K = 3072): 16 in flight, so the whole row (or two trips for K = 6144) is
+// requested before the kernel waits for its predecessor instead of a second trip's loads
+// waiting behind that dependency: talker step (g1) 483 -> 451 us, 1.7B step (g2) 966 ->
+// 921 us. With 16 for every shape the K = 1024 projections were slower and K = 2048 mixed.
+constexpr int kUnrollDeep = 16;
 constexpr size_t kMaxSmem = 200 * 1024;
 
 enum Epi { kStore = 0, kResidual = 1, kSwiglu = 2 };
@@ -159,7 +165,7 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 }
 
 // K % (elements per vector) == 0 and W 16-byte aligned: 16-byte weight vectors.
-template <typename WF, int M, int EPI>
+template <typename WF, int M, int EPI, int U>
 __global__ void __launch_bounds__(kThreads)
 gemv_vec_kernel(float *y, const float *x, const float *norm_w, float eps,
                 const typename WF::T *__restrict__ W, const float *__restrict__ scales, int K,
@@ -177,9 +183,9 @@ gemv_vec_kernel(float *y, const float *x, const float *norm_w, float eps,
     for (int r = 0; r < RPW; r++) wr[r] = W + (size_t)(active ? row0 + r : 0) * K;
     // the weights depend on nothing earlier on the stream: their first chunk is in
     // flight before this kernel waits for the previous one and stages its inputs
-    uint4 wv[kUnrollK][RPW];
+    uint4 wv[U][RPW];
 #pragma unroll
-    for (int u = 0; u < kUnrollK; u++) {
+    for (int u = 0; u < U; u++) {
         const int k0 = u * S + lane * E;
 #pragma unroll
         for (int r = 0; r < RPW; r++)
@@ -205,10 +211,10 @@ gemv_vec_kernel(float *y, const float *x, const float *norm_w, float eps,
 #pragma unroll
         for (int m = 0; m < M; m++) acc[r][m] = 0.f;
 
-    for (int kb = 0; kb < K; kb += S * kUnrollK) {
+    for (int kb = 0; kb < K; kb += S * U) {
         if (kb > 0) {
 #pragma unroll
-            for (int u = 0; u < kUnrollK; u++) {
+            for (int u = 0; u < U; u++) {
                 const int k0 = kb + u * S + lane * E;
 #pragma unroll
                 for (int r = 0; r < RPW; r++)
@@ -216,7 +222,7 @@ gemv_vec_kernel(float *y, const float *x, const float *norm_w, float eps,
             }
         }
 #pragma unroll
-        for (int u = 0; u < kUnrollK; u++) {
+        for (int u = 0; u < U; u++) {
             const int k0 = kb + u * S + lane * E;
             if (k0 >= K) break;
             float wf[RPW][E];
@@ -302,7 +308,9 @@ int launch(float *y, const float *x, const float *norm_w, float eps, const typen
            const float *scales, int K, int N, int ldy, bool vec, cudaStream_t s) {
     constexpr int RPW = EPI == kSwiglu ? 2 : 1;
     const size_t smem = (size_t)M * K * sizeof(float);
-    auto kern = vec ? gemv_vec_kernel<WF, M, EPI> : gemv_scalar_kernel<WF, M, EPI>;
+    const bool deep = M == 1 && K > kUnrollK * 32 * WF::kEpv;
+    auto kern = !vec ? gemv_scalar_kernel<WF, M, EPI>
+                     : deep ? gemv_vec_kernel<WF, M, EPI, kUnrollDeep> : gemv_vec_kernel<WF, M, EPI, kUnrollK>;
     // opt in above 47 KiB: the default 48 KiB limit also covers the kernel's small static array
     if (smem > 47 * 1024 &&
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
