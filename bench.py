@@ -1929,6 +1929,8 @@ def run_ours(args) -> None:
     step_gbs = step_bytes * args.steps / (total_ms / 1000.0) / 1e9
     roofline = roofline_of(per_kernel, dominant, peak, peak_kind, f"{dominant}@{args.config}")
     roofline.update(step_gbs=round(step_gbs, 1), step_frac=round(step_gbs / peak, 4))
+    if strong and roofline["traffic"] is not None:  # the committed figure is for all the tokens
+        roofline["traffic"] = int(roofline["traffic"] * rows / cfg.tokens)
 
     def max_time(sec):
         et = torch.tensor([sec], device="cuda", dtype=torch.float64)
