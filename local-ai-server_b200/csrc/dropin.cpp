@@ -4,12 +4,15 @@
 // or whole size, in/out) plus a launcher that runs one lai_* kernel on a row
 // range. If every pointer is device-accessible the launcher runs once on the
 // drop-in stream. Otherwise host rows are staged: rows are cut into chunks of
-// about kChunkBytes host bytes, chunk c runs on pipeline stream c % 3 as
-// copy-in -> kernel -> copy-out using that stream's device slot, so the copy-in
-// of one chunk, the kernel of the next and the copy-out of a third overlap. When
-// a host output aliases a host input with another row size (SwiGLU compaction,
-// out == gate_up) the copy-out of chunk c first waits for the copy-in events of
-// every earlier chunk whose input bytes it overwrites.
+// about kChunkBytes host bytes that cycle through kSlots device slots, and three
+// streams carry them: copy-in (all host-to-device copies, in chunk order), kernel
+// and copy-out (all device-to-host copies). Chunk c's kernel waits for its copy-in,
+// its copy-out for its kernel, and the copy-in of chunk c + kSlots for that copy-out
+// (the slot is free again), so both copy directions stay busy back to back. When a
+// host output aliases a host input with another row size (SwiGLU compaction,
+// out == gate_up), the copy-out of chunk c overwrites input bytes of chunks <= c
+// only, all copied in before chunk c's own copy-in on the in-order copy-in stream:
+// no further ordering is needed.
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -23,12 +26,13 @@
 
 namespace {
 
-constexpr int kSlots = 3;
+constexpr int kSlots = 4;
 constexpr size_t kChunkBytes = 16u << 20;
+enum { kIn = 0, kKernel = 1, kOut = 2, kStreams = 3 };
 
 struct Ctx {
     int device = -1;
-    cudaStream_t pipe[kSlots] = {};
+    cudaStream_t pipe[kStreams] = {};  // copy-in, kernel, copy-out
     void *slot[kSlots] = {};
     size_t slot_cap[kSlots] = {};
     void *whole = nullptr;
@@ -36,7 +40,7 @@ struct Ctx {
     int *derr = nullptr;        // device error word of staged calls
     int *derr_direct = nullptr; // device error word of device-pointer calls
     int32_t *zero_id = nullptr; // a device int holding 0 (single-row gathers)
-    std::vector<cudaEvent_t> events;
+    cudaEvent_t in_done[kSlots] = {}, k_done[kSlots] = {}, out_done[kSlots] = {};
     cudaEvent_t start_ev = nullptr;
 };
 
@@ -64,8 +68,11 @@ Ctx *get_ctx(const char *fn) {
     Ctx &c = t_ctx[dev];
     if (c.device < 0) {
         c.device = dev;
-        for (int i = 0; i < kSlots; i++)
+        for (int i = 0; i < kStreams; i++)
             if ((e = cudaStreamCreateWithFlags(&c.pipe[i], cudaStreamNonBlocking)) != cudaSuccess) break;
+        for (int i = 0; i < kSlots && e == cudaSuccess; i++)
+            for (cudaEvent_t *ev : {&c.in_done[i], &c.k_done[i], &c.out_done[i]})
+                if (e == cudaSuccess) e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
         if (e == cudaSuccess) e = cudaMalloc(&c.derr, 4 * sizeof(int));
         if (e == cudaSuccess) e = cudaMemset(c.derr, 0, 4 * sizeof(int));
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c.start_ev, cudaEventDisableTiming);
@@ -174,38 +181,20 @@ int run_op(const char *fn, std::vector<Arg> &args, int64_t rows, const Launcher 
 
     // order after prior work on the drop-in stream (device-pointer args)
     if ((e = cudaEventRecord(c->start_ev, t_stream)) != cudaSuccess) return cuda_fail(fn, e);
-    for (int s = 0; s < kSlots; s++) cudaStreamWaitEvent(c->pipe[s], c->start_ev, 0);
-    cudaMemsetAsync(c->derr, 0, sizeof(int), c->pipe[0]);
+    for (int s = 0; s < kStreams; s++) cudaStreamWaitEvent(c->pipe[s], c->start_ev, 0);
+    cudaStream_t sin = c->pipe[kIn], sk = c->pipe[kKernel], sout = c->pipe[kOut];
+    cudaMemsetAsync(c->derr, 0, sizeof(int), sin);
     for (auto &a : args)
         if (a.host && a.row_bytes == 0 && a.in)
             cudaMemcpyAsync(static_cast<char *>(c->whole) + a.whole_off, a.ptr, a.whole_bytes,
-                            cudaMemcpyHostToDevice, c->pipe[0]);
-    // the other pipeline streams start after the whole-argument copies and the reset
-    if ((e = cudaEventRecord(c->start_ev, c->pipe[0])) != cudaSuccess) return cuda_fail(fn, e);
-    for (int s = 1; s < kSlots; s++) cudaStreamWaitEvent(c->pipe[s], c->start_ev, 0);
+                            cudaMemcpyHostToDevice, sin);
 
-    // aliasing host output/input pairs with different row sizes need ordering
-    bool alias = false;
-    for (auto &o : args)
-        for (auto &i : args)
-            if (&o != &i && o.host && i.host && o.out && i.in && o.row_bytes && i.row_bytes &&
-                o.row_bytes != i.row_bytes && o.ptr == i.ptr)
-                alias = true;
     const int64_t nchunks = (rows + chunk - 1) / chunk;
-    if (alias) {
-        while ((int64_t)c->events.size() < nchunks) {
-            cudaEvent_t ev;
-            if ((e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming)) != cudaSuccess)
-                return cuda_fail(fn, e);
-            c->events.push_back(ev);
-        }
-    }
-
     int status = LAI_OK;
     for (int64_t ci = 0; ci < nchunks && status == LAI_OK; ci++) {
         const int64_t r0 = ci * chunk, nr = (r0 + chunk <= rows) ? chunk : rows - r0;
         const int s = (int)(ci % kSlots);
-        cudaStream_t st = c->pipe[s];
+        if (ci >= kSlots) cudaStreamWaitEvent(sin, c->out_done[s], 0);  // slot read out
         for (size_t i = 0; i < args.size(); i++) {
             Arg &a = args[i];
             if (!a.ptr) { dptr[i] = nullptr; continue; }
@@ -221,32 +210,23 @@ int run_op(const char *fn, std::vector<Arg> &args, int64_t rows, const Launcher 
             dptr[i] = static_cast<char *>(c->slot[s]) + a.slot_off;
             if (a.in)
                 cudaMemcpyAsync(dptr[i], static_cast<const char *>(a.ptr) + (size_t)r0 * a.row_bytes,
-                                (size_t)nr * a.row_bytes, cudaMemcpyHostToDevice, st);
+                                (size_t)nr * a.row_bytes, cudaMemcpyHostToDevice, sin);
         }
-        if (alias) cudaEventRecord(c->events[ci], st);
-        status = launch(st, r0, nr, dptr.data(), c->derr);
+        cudaEventRecord(c->in_done[s], sin);
+        cudaStreamWaitEvent(sk, c->in_done[s], 0);
+        status = launch(sk, r0, nr, dptr.data(), c->derr);
+        cudaEventRecord(c->k_done[s], sk);
+        cudaStreamWaitEvent(sout, c->k_done[s], 0);
         for (size_t i = 0; i < args.size() && status == LAI_OK; i++) {
             Arg &a = args[i];
             if (!a.ptr || !a.host || !a.out || a.row_bytes == 0) continue;
             char *hdst = const_cast<char *>(static_cast<const char *>(a.ptr)) + (size_t)r0 * a.row_bytes;
-            const size_t nb = (size_t)nr * a.row_bytes;
-            if (alias) {
-                // wait for every earlier chunk whose host input bytes this copy-out overwrites
-                for (const Arg &b : args) {
-                    if (&b == &a || !b.host || !b.in || b.ptr != a.ptr || !b.row_bytes) continue;
-                    for (int64_t cj = 0; cj < ci; cj++) {
-                        const char *lo = static_cast<const char *>(b.ptr) + (size_t)(cj * chunk) * b.row_bytes;
-                        const int64_t nj = (cj * chunk + chunk <= rows) ? chunk : rows - cj * chunk;
-                        const char *hi = lo + (size_t)nj * b.row_bytes;
-                        if (lo < hdst + nb && hdst < hi) cudaStreamWaitEvent(st, c->events[cj], 0);
-                    }
-                }
-            }
-            cudaMemcpyAsync(hdst, dptr[i], nb, cudaMemcpyDeviceToHost, st);
+            cudaMemcpyAsync(hdst, dptr[i], (size_t)nr * a.row_bytes, cudaMemcpyDeviceToHost, sout);
         }
+        cudaEventRecord(c->out_done[s], sout);
     }
     cudaError_t sync_err = cudaSuccess;
-    for (int s = 0; s < kSlots; s++) {
+    for (int s = 0; s < kStreams; s++) {
         cudaError_t es = cudaStreamSynchronize(c->pipe[s]);
         if (es != cudaSuccess && sync_err == cudaSuccess) sync_err = es;
     }
@@ -488,13 +468,15 @@ void lai_shutdown(void) {
     for (auto &kv : t_ctx) {
         Ctx &c = kv.second;
         cudaSetDevice(c.device);
-        for (int s = 0; s < kSlots; s++) {
+        for (int s = 0; s < kStreams; s++)
             if (c.pipe[s]) cudaStreamSynchronize(c.pipe[s]), cudaStreamDestroy(c.pipe[s]);
+        for (int s = 0; s < kSlots; s++) {
             if (c.slot[s]) cudaFree(c.slot[s]);
+            for (cudaEvent_t ev : {c.in_done[s], c.k_done[s], c.out_done[s]})
+                if (ev) cudaEventDestroy(ev);
         }
         if (c.whole) cudaFree(c.whole);
         if (c.derr) cudaFree(c.derr);
-        for (cudaEvent_t ev : c.events) cudaEventDestroy(ev);
         if (c.start_ev) cudaEventDestroy(c.start_ev);
     }
     t_ctx.clear();
