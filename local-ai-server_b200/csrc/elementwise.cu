@@ -76,6 +76,7 @@ gather_kernel(void *out, const uint16_t *__restrict__ table, const int32_t *__re
     const int lane = threadIdx.x & 31;
     const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
     if (r >= n) return;
+    pdl_wait_prior();  // launched with programmatic dependent launch: inputs after this
     const int64_t id = ids[r];
     const bool ok = id >= 0 && id < vocab;
     if (!ok && lane == 0 && err) atomicOr(err, LAI_DEVERR_TOKEN_ID);
@@ -101,6 +102,7 @@ gather_kernel(void *out, const uint16_t *__restrict__ table, const int32_t *__re
                 static_cast<uint16_t *>(out)[(size_t)r * dim + i] = h;
         }
     }
+    pdl_launch_dependents();
 }
 
 template <bool OUT_F32>
@@ -111,9 +113,11 @@ int run_gather(void *out, const uint16_t *table, const int32_t *ids, int64_t n, 
     cudaStream_t s = as_stream(stream);
     const bool vec = dim % 8 == 0 && aligned16(out) && aligned16(table);
     if (vec)
-        gather_kernel<OUT_F32, true><<<grid_for(n, 8), 256, 0, s>>>(out, table, ids, n, dim, vocab, err);
+        launch_pdl(gather_kernel<OUT_F32, true>, dim3(grid_for(n, 8)), dim3(256), 0, s, out, table,
+                   ids, n, dim, vocab, err);
     else
-        gather_kernel<OUT_F32, false><<<grid_for(n, 8), 256, 0, s>>>(out, table, ids, n, dim, vocab, err);
+        launch_pdl(gather_kernel<OUT_F32, false>, dim3(grid_for(n, 8)), dim3(256), 0, s, out, table,
+                   ids, n, dim, vocab, err);
     return launch_status();
 }
 

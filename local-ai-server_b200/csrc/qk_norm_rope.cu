@@ -401,6 +401,7 @@ qk_reg_kernel(uint16_t *q, uint16_t *k, const float *__restrict__ wq, const floa
     const int lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * kRegWarps + (threadIdx.x >> 5);
     if (row >= rows) return;
+    pdl_wait_prior();  // launched with programmatic dependent launch: inputs after this
     const bool rope = cos_t != nullptr;
     const int hsub = lane >> 3, d0 = (lane & 7) * 8;
     uint16_t *qr = q + (size_t)row * NQ * 128;
@@ -436,6 +437,7 @@ qk_reg_kernel(uint16_t *q, uint16_t *k, const float *__restrict__ wq, const floa
         *reinterpret_cast<uint4 *>(hp + d0) = lo[j];
         *reinterpret_cast<uint4 *>(hp + 64 + d0) = hi[j];
     }
+    pdl_launch_dependents();
 }
 
 // Any even head_dim / alignment / head count: one warp per (token, head).
@@ -525,8 +527,8 @@ bool try_bf16_hd128(uint16_t *q, uint16_t *k, const float *wq, const float *wk,
     const bool qwen = nq == 16 && (nkv == 8 || nkv == 0);
     if (qwen) {
         auto kern = nkv ? qk_reg_kernel<4, 2> : qk_reg_kernel<4, 0>;
-        kern<<<grid_for(rows, kRegWarps), kRegWarps * 32, 0, s>>>(q, k, wq, wk, cos_t, sin_t, pos,
-                                                                   table_rows, rows, eps, err);
+        launch_pdl(kern, dim3(grid_for(rows, kRegWarps)), dim3(kRegWarps * 32), 0, s, q, k, wq, wk,
+                   cos_t, sin_t, pos, table_rows, rows, eps, err);
         return true;
     }
     // as many warps (up to kStreamWarps per SM) as fit their stages in shared memory

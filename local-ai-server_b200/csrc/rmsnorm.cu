@@ -28,6 +28,7 @@ rmsnorm_warp_kernel(T *__restrict__ y, T *x, const T *__restrict__ delta,
     const int lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
     if (row >= rows) return;
+    pdl_wait_prior();  // launched with programmatic dependent launch: inputs after this
 
     const size_t off = (size_t)row * dim;
     uint4 v[NV];
@@ -74,6 +75,7 @@ rmsnorm_warp_kernel(T *__restrict__ y, T *x, const T *__restrict__ delta,
         for (int e = 0; e < E; e++) a[e] = __fmul_rn(__fmul_rn(a[e], inv), wv[e]);
         st_vec(y + off + c, pack<T>(a));
     }
+    pdl_launch_dependents();  // this row is done: the next kernel may start launching
 }
 
 // Any width / alignment: one CTA per row (grid-stride over rows).
@@ -105,8 +107,8 @@ rmsnorm_block_kernel(T *y, T *x, const T *delta, const float *__restrict__ w, in
 template <typename T, bool ADD, int NV>
 void launch_warp(T *y, T *x, const T *delta, const float *w, int64_t rows, int dim, float eps,
                  cudaStream_t s) {
-    rmsnorm_warp_kernel<T, NV, ADD><<<grid_for(rows, kRowsPerCta), kRowsPerCta * 32, 0, s>>>(
-        y, x, delta, w, rows, dim, eps);
+    launch_pdl(rmsnorm_warp_kernel<T, NV, ADD>, dim3(grid_for(rows, kRowsPerCta)),
+               dim3(kRowsPerCta * 32), 0, s, y, x, delta, w, rows, dim, eps);
 }
 
 template <typename T, bool ADD>

@@ -70,6 +70,7 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads)
 swiglu_units_kernel(uint2 *out, const uint4 *in, int64_t u0, int64_t u1) {
     const int64_t base = u0 + (int64_t)blockIdx.x * (kThreads * kUnroll) + threadIdx.x;
+    pdl_wait_prior();  // launched with programmatic dependent launch: inputs after this
     uint4 v[kUnroll];
 #pragma unroll
     for (int i = 0; i < kUnroll; i++) {
@@ -81,6 +82,7 @@ swiglu_units_kernel(uint2 *out, const uint4 *in, int64_t u0, int64_t u1) {
         const int64_t k = base + (int64_t)i * kThreads;
         if (k < u1) out[k] = unit_op<T>(v[i]);
     }
+    pdl_launch_dependents();
 }
 
 // The whole in-place schedule in one cooperative launch (described at the top).
@@ -217,7 +219,8 @@ int run(T *out, const T *in, int64_t rows, int inter, lai_stream_t stream) {
         const uint4 *iv = reinterpret_cast<const uint4 *>(in);
         if (!inplace) {
             if (units > 0)
-                swiglu_units_kernel<T><<<grid_for(units, kThreads * kUnroll), kThreads, 0, s>>>(o, iv, 0, units);
+                launch_pdl(swiglu_units_kernel<T>, dim3(grid_for(units, kThreads * kUnroll)),
+                           dim3(kThreads), 0, s, o, iv, (int64_t)0, units);
             if (tail0 < n) swiglu_serial_kernel<T><<<1, 32, 0, s>>>(out, in, tail0, n);
             return launch_status();
         }
@@ -245,7 +248,8 @@ int run(T *out, const T *in, int64_t rows, int inter, lai_stream_t stream) {
         }
         for (int64_t lo = u_stop; lo < units;) {
             const int64_t hi = 2 * lo < units ? 2 * lo : units;
-            swiglu_units_kernel<T><<<grid_for(hi - lo, kThreads * kUnroll), kThreads, 0, s>>>(o, iv, lo, hi);
+            launch_pdl(swiglu_units_kernel<T>, dim3(grid_for(hi - lo, kThreads * kUnroll)),
+                       dim3(kThreads), 0, s, o, iv, lo, hi);
             lo = hi;
         }
         if (u_stop < units && tail0 < n) swiglu_serial_kernel<T><<<1, 32, 0, s>>>(out, in, tail0, n);
