@@ -90,6 +90,7 @@ snake_flat_kernel(float *x, const float *__restrict__ ea, const float *__restric
     const uint32_t nvec = total / 4;
     const uint32_t base = blockIdx.x * (uint32_t)kSegVec + threadIdx.x;
     float4 *xv = reinterpret_cast<float4 *>(x);
+    pdl_wait_prior();  // launched with programmatic dependent launch: inputs after this
     float4 v[kUnroll];
 #pragma unroll
     for (int i = 0; i < kUnroll; i++) {
@@ -127,6 +128,7 @@ snake_flat_kernel(float *x, const float *__restrict__ ea, const float *__restric
         const uint32_t c = row - fdiv(row, divC) * C;
         x[e] = snake1(x[e], __ldg(ea + c), __ldg(ieb + c));
     }
+    pdl_launch_dependents();
 }
 
 }  // namespace
@@ -142,10 +144,10 @@ extern "C" int lai_snake_beta_f32(float *x, const float *exp_alpha, const float 
     const int64_t total = rows * T;
     if (vec && T >= 4 && total < (int64_t)0xffffffffll) {
         const int64_t nvec = total / 4;
-        lai::snake_flat_kernel<<<lai::grid_for(nvec > 0 ? nvec : 1, lai::kSegVec), lai::kThreads, 0,
-                                 lai::as_stream(stream)>>>(
-            x, exp_alpha, inv_exp_beta, (uint32_t)total, (uint32_t)T, (uint32_t)channels,
-            lai::make_fastdiv((uint32_t)T), lai::make_fastdiv((uint32_t)channels));
+        lai::launch_pdl(lai::snake_flat_kernel, dim3(lai::grid_for(nvec > 0 ? nvec : 1, lai::kSegVec)),
+                        dim3(lai::kThreads), 0, lai::as_stream(stream), x, exp_alpha, inv_exp_beta,
+                        (uint32_t)total, (uint32_t)T, (uint32_t)channels,
+                        lai::make_fastdiv((uint32_t)T), lai::make_fastdiv((uint32_t)channels));
         return lai::launch_status();
     }
     const int64_t nv_max = vec ? T / 4 + 1 : 0;
