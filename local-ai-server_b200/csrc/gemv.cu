@@ -54,6 +54,11 @@ constexpr int kUnrollK = 8;  // 16-byte weight vectors in flight per lane per ro
 // waiting behind that dependency: talker step (g1) 483 -> 451 us, 1.7B step (g2) 966 ->
 // 921 us. With 16 for every shape the K = 1024 projections were slower and K = 2048 mixed.
 constexpr int kUnrollDeep = 16;
+// M = 1 rows of at most 4 vectors per lane (BF16 K <= 1024) hold only those: half the weight
+// registers of the 8-vector form, so more CTAs stay resident and the next GEMV's CTAs (and
+// their weight loads) fit beside this one's (the 0.6B talker's gate|up GEMV needed two waves
+// of CTAs at 96 registers)
+constexpr int kUnrollShort = 4;
 constexpr size_t kMaxSmem = 200 * 1024;
 
 enum Epi { kStore = 0, kResidual = 1, kSwiglu = 2 };
@@ -309,8 +314,11 @@ int launch(float *y, const float *x, const float *norm_w, float eps, const typen
     constexpr int RPW = EPI == kSwiglu ? 2 : 1;
     const size_t smem = (size_t)M * K * sizeof(float);
     const bool deep = M == 1 && K > kUnrollK * 32 * WF::kEpv;
+    const bool shallow = M == 1 && K <= kUnrollShort * 32 * WF::kEpv;
     auto kern = !vec ? gemv_scalar_kernel<WF, M, EPI>
-                     : deep ? gemv_vec_kernel<WF, M, EPI, kUnrollDeep> : gemv_vec_kernel<WF, M, EPI, kUnrollK>;
+                : deep ? gemv_vec_kernel<WF, M, EPI, (M == 1 ? kUnrollDeep : kUnrollK)>
+                : shallow ? gemv_vec_kernel<WF, M, EPI, (M == 1 ? kUnrollShort : kUnrollK)>
+                          : gemv_vec_kernel<WF, M, EPI, kUnrollK>;
     // opt in above 47 KiB: the default 48 KiB limit also covers the kernel's small static array
     if (smem > 47 * 1024 &&
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
