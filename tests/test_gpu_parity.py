@@ -122,6 +122,7 @@ def table(rows, hd, theta):
     (5003, 16, 8, 128, "random"),  # several tiles per persistent CTA, partial last tile
     (64, 16, 16, 64, "seq"),       # vocoder pre-transformer heads (hd 64)
     (7, 3, 1, 128, "random"),      # odd head counts -> generic kernel
+    (3001, 32, 8, 128, "random"),  # 32 q heads: the per-warp stream kernel, fewer warps per CTA
     (5, 2, 2, 96, "seq"),          # head_dim without a fast path
 ])
 def test_qk_norm_rope(dtype, rows, nq, nkv, hd, posmode):
@@ -146,6 +147,21 @@ def test_qk_norm_rope(dtype, rows, nq, nkv, hd, posmode):
     else:
         assert max_rel_err(f32(q), qr) <= TOL_F32
         assert max_rel_err(f32(k), kr) <= TOL_F32
+
+
+def test_qk_q_only_bf16_qwen_heads():
+    # k = NULL with the Qwen3 16-head q layout (the register kernel without k passes)
+    rows, nq, hd = 777, 16, 128
+    q = rand((rows, nq * hd), 35, torch.bfloat16)
+    wq = norm_w(hd, 36)
+    cos_t, sin_t = table(4096, hd, 1e6)
+    g = torch.Generator(device="cpu").manual_seed(37)
+    pos = torch.randint(0, 4096, (rows,), generator=g, dtype=torch.int32).to(DEV)
+    qh = bf16_bits(q)
+    lai.qk_norm_rope(q, None, wq, None, cos_t, sin_t, pos, nq, 0, hd, 1e-6)
+    qr, _ = oracle.qk_norm_rope(qh, None, f32(wq), None, f32(cos_t), f32(sin_t),
+                                pos.cpu().numpy(), nq, 0, hd, 1e-6, bf16=True)
+    assert max_rel_err(oracle.bf16_bits_to_f32(bf16_bits(q)), oracle.bf16_bits_to_f32(qr)) <= TOL_BF16
 
 
 def test_qk_result_does_not_depend_on_batch_size():
@@ -215,8 +231,11 @@ def test_swiglu_f32(rows, inter):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-@pytest.mark.parametrize("rows,inter", [(1, 4), (3, 5), (16, 3072), (257, 1000), (2048, 3072)])
+@pytest.mark.parametrize("rows,inter", [(1, 4), (3, 5), (16, 3072), (257, 1000), (2048, 3072),
+                                        (21000, 3071)])
 def test_swiglu_in_place_equals_out_of_place(dtype, rows, inter):
+    # (2048, 3072): the cooperative launch's head and waves only; (21000, 3071): waves of
+    # 4M+ units as ordinary launches after it, and a ragged tail
     gu = rand((rows, 2 * inter), 32, dtype, scale=2.0)
     ref = lai.swiglu(gu, inter)
     got = lai.swiglu_inplace(gu, inter)
