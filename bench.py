@@ -1964,7 +1964,10 @@ def run_ours(args) -> None:
                    "api": "voc_snake_beta drop-in on pinned host buffers, one call per item and stage",
                    **pcie_fields(r["h2d"], r["d2h"], sec / r["steps"], pcie)}
         else:
-            er = min(rows, args.e2e_rows_bf16)
+            # strong scaling: the same host-buffer rows in all, split over the ranks (one
+            # host's pinned memory and PCIe serve every rank)
+            share = world if strong else 1
+            er = min(rows, max(1024, args.e2e_rows_bf16 // share))
             r = e2e_staged_bf16(cfg, er, args.e2e_steps, 1)
             sec = max_time(r["seconds"])
             e2e = {"value": round(er * world * r["steps"] / sec, 1),
@@ -1973,7 +1976,7 @@ def run_ours(args) -> None:
                    "api": "lai_staged_{add_rmsnorm,qk_norm_rope,swiglu}_bf16 on pinned host "
                           "buffers, 4 synchronous calls/step",
                    **pcie_fields(r["h2d"], r["d2h"], sec / r["steps"], pcie)}
-            fr = min(rows, args.e2e_rows)
+            fr = min(rows, max(1024, args.e2e_rows // share))
             r = e2e_dropin_f32(cfg, fr, args.e2e_steps, 1)
             sec = max_time(r["seconds"])
             e2e_f32 = {"value": round(fr * world * r["steps"] / sec, 1),
