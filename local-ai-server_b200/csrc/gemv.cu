@@ -59,6 +59,11 @@ constexpr int kUnrollDeep = 16;
 // their weight loads) fit beside this one's (the 0.6B talker's gate|up GEMV needed two waves
 // of CTAs at 96 registers)
 constexpr int kUnrollShort = 4;
+// ... and for those rows a warp takes several consecutive row groups (16 weight vectors per
+// lane for plain rows: 4 rows; SwiGLU: 2 gate/up pairs), fewer CTAs each staging (and
+// normalising) the input row once for more rows: the talker's q|k|v GEMV 4.26 -> 3.80 us,
+// gate|up 4.68 -> 4.61 us (4 pairs per warp: 5.30 us).
+constexpr int kShortGroups = 4, kShortPairs = 2;
 constexpr size_t kMaxSmem = 200 * 1024;
 
 enum Epi { kStore = 0, kResidual = 1, kSwiglu = 2 };
@@ -170,49 +175,55 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 }
 
 // K % (elements per vector) == 0 and W 16-byte aligned: 16-byte weight vectors.
-template <typename WF, int M, int EPI, int U>
+template <typename WF, int M, int EPI, int U, int R>  // R: row groups (1 row, 2 for SwiGLU) per warp
 __global__ void __launch_bounds__(kThreads)
 gemv_vec_kernel(float *y, const float *x, const float *norm_w, float eps,
                 const typename WF::T *__restrict__ W, const float *__restrict__ scales, int K,
                 int N, int ldy) {
     using T = typename WF::T;
-    constexpr int RPW = EPI == kSwiglu ? 2 : 1;
+    constexpr int RW = (EPI == kSwiglu ? 2 : 1) * R;  // consecutive weight rows per warp
     constexpr int E = WF::kEpv;   // weight elements per 16-byte vector
     constexpr int S = 32 * E;     // elements one warp covers per vector step
     extern __shared__ __align__(16) float xs[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int row0 = (blockIdx.x * kWarps + warp) * RPW;
+    const int row0 = (blockIdx.x * kWarps + warp) * RW;
     const bool active = row0 < N;
-    const T *wr[RPW];
+    const T *wr[RW];
+    bool rv[RW];
 #pragma unroll
-    for (int r = 0; r < RPW; r++) wr[r] = W + (size_t)(active ? row0 + r : 0) * K;
+    for (int r = 0; r < RW; r++) {
+        rv[r] = row0 + r < N;
+        wr[r] = W + (size_t)(rv[r] ? row0 + r : 0) * K;
+    }
     // the weights depend on nothing earlier on the stream: their first chunk is in
     // flight before this kernel waits for the previous one and stages its inputs
-    uint4 wv[U][RPW];
+    uint4 wv[U][RW];
 #pragma unroll
     for (int u = 0; u < U; u++) {
         const int k0 = u * S + lane * E;
 #pragma unroll
-        for (int r = 0; r < RPW; r++)
-            if (active && k0 < K) wv[u][r] = ld_stream(wr[r] + k0);
+        for (int r = 0; r < RW; r++)
+            if (rv[r] && k0 < K) wv[u][r] = ld_stream(wr[r] + k0);
     }
     // the row scales are weights too (no dependency): in flight with them
-    float sc[RPW];
+    float sc[RW];
 #pragma unroll
-    for (int r = 0; r < RPW; r++) sc[r] = WF::kScaled && active ? __ldg(scales + row0 + r) : 1.0f;
+    for (int r = 0; r < RW; r++) sc[r] = WF::kScaled && rv[r] ? __ldg(scales + row0 + r) : 1.0f;
     pdl_wait_prior();
     // the residual this lane adds into (written by the previous kernel): read now, so the
     // epilogue does not wait on a load after the reduction
-    float res = 0.0f;
-    if (EPI == kResidual && active && lane < M) res = y[(size_t)lane * ldy + row0];
+    float res[RW];
+#pragma unroll
+    for (int r = 0; r < RW; r++)
+        res[r] = EPI == kResidual && rv[r] && lane < M ? y[(size_t)lane * ldy + row0 + r] : 0.0f;
     stage_inputs<M>(xs, x, norm_w, eps, K);
     if (!active) {
         pdl_launch_dependents();
         return;
     }
-    float acc[RPW][M];
+    float acc[RW][M];
 #pragma unroll
-    for (int r = 0; r < RPW; r++)
+    for (int r = 0; r < RW; r++)
 #pragma unroll
         for (int m = 0; m < M; m++) acc[r][m] = 0.f;
 
@@ -222,17 +233,17 @@ gemv_vec_kernel(float *y, const float *x, const float *norm_w, float eps,
             for (int u = 0; u < U; u++) {
                 const int k0 = kb + u * S + lane * E;
 #pragma unroll
-                for (int r = 0; r < RPW; r++)
-                    if (k0 < K) wv[u][r] = ld_stream(wr[r] + k0);
+                for (int r = 0; r < RW; r++)
+                    if (rv[r] && k0 < K) wv[u][r] = ld_stream(wr[r] + k0);
             }
         }
 #pragma unroll
         for (int u = 0; u < U; u++) {
             const int k0 = kb + u * S + lane * E;
             if (k0 >= K) break;
-            float wf[RPW][E];
+            float wf[RW][E];
 #pragma unroll
-            for (int r = 0; r < RPW; r++) WF::unpack(wv[u][r], wf[r]);
+            for (int r = 0; r < RW; r++) WF::unpack(wv[u][r], wf[r]);
 #pragma unroll
             for (int m = 0; m < M; m++) {
 #pragma unroll
@@ -240,7 +251,7 @@ gemv_vec_kernel(float *y, const float *x, const float *norm_w, float eps,
                     const float4 a = *reinterpret_cast<const float4 *>(xs + m * K + k0 + 4 * q);
                     const float xv[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
-                    for (int r = 0; r < RPW; r++)
+                    for (int r = 0; r < RW; r++)
 #pragma unroll
                         for (int e = 0; e < 4; e++)
                             acc[r][m] = fmaf(wf[r][4 * q + e], xv[e], acc[r][m]);
@@ -252,20 +263,29 @@ gemv_vec_kernel(float *y, const float *x, const float *norm_w, float eps,
     // stream their own weights, then wait for this grid before reading activations)
     pdl_launch_dependents();
 #pragma unroll
-    for (int r = 0; r < RPW; r++) {
+    for (int r = 0; r < RW; r++) {
 #pragma unroll
         for (int m = 0; m < M; m++) {
             acc[r][m] = group_sum<32>(acc[r][m]);
             if (WF::kScaled) acc[r][m] *= sc[r];
         }
     }
-    // lane m writes input m's result (all lanes hold every total after the tree)
+    // lane m writes input m's results (all lanes hold every total after the tree)
 #pragma unroll
     for (int m = 0; m < M; m++) {
         if (lane != m) continue;
-        if constexpr (EPI == kStore) y[(size_t)m * ldy + row0] = acc[0][m];
-        if constexpr (EPI == kResidual) y[(size_t)m * ldy + row0] = res + acc[0][m];
-        if constexpr (EPI == kSwiglu) y[(size_t)m * ldy + row0 / 2] = silu_mul(acc[0][m], acc[1][m]);
+        if constexpr (EPI == kSwiglu) {
+#pragma unroll
+            for (int r = 0; r < RW; r += 2)
+                if (rv[r]) y[(size_t)m * ldy + (row0 + r) / 2] = silu_mul(acc[r][m], acc[r + 1][m]);
+        } else {
+#pragma unroll
+            for (int r = 0; r < RW; r++) {
+                if (!rv[r]) continue;
+                if constexpr (EPI == kStore) y[(size_t)m * ldy + row0 + r] = acc[r][m];
+                if constexpr (EPI == kResidual) y[(size_t)m * ldy + row0 + r] = res[r] + acc[r][m];
+            }
+        }
     }
 }
 
@@ -315,10 +335,12 @@ int launch(float *y, const float *x, const float *norm_w, float eps, const typen
     const size_t smem = (size_t)M * K * sizeof(float);
     const bool deep = M == 1 && K > kUnrollK * 32 * WF::kEpv;
     const bool shallow = M == 1 && K <= kUnrollShort * 32 * WF::kEpv;
+    constexpr int RS = M != 1 ? 1 : EPI == kSwiglu ? kShortPairs : kShortGroups;
     auto kern = !vec ? gemv_scalar_kernel<WF, M, EPI>
-                : deep ? gemv_vec_kernel<WF, M, EPI, (M == 1 ? kUnrollDeep : kUnrollK)>
-                : shallow ? gemv_vec_kernel<WF, M, EPI, (M == 1 ? kUnrollShort : kUnrollK)>
-                          : gemv_vec_kernel<WF, M, EPI, kUnrollK>;
+                : deep ? gemv_vec_kernel<WF, M, EPI, (M == 1 ? kUnrollDeep : kUnrollK), 1>
+                : shallow ? gemv_vec_kernel<WF, M, EPI, (M == 1 ? kUnrollShort : kUnrollK), RS>
+                          : gemv_vec_kernel<WF, M, EPI, kUnrollK, 1>;
+    const int rows_per_cta = kWarps * RPW * ((vec && shallow) ? RS : 1);
     // opt in above 47 KiB: the default 48 KiB limit also covers the kernel's small static array
     if (smem > 47 * 1024 &&
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
@@ -326,7 +348,7 @@ int launch(float *y, const float *x, const float *norm_w, float eps, const typen
         return LAI_ERR_CUDA;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid_for(N, kWarps * RPW));
+    cfg.gridDim = dim3(grid_for(N, rows_per_cta));
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
