@@ -64,6 +64,9 @@ constexpr int kUnrollShort = 4;
 // normalising) the input row once for more rows: the talker's q|k|v GEMV 4.26 -> 3.80 us,
 // gate|up 4.68 -> 4.61 us (4 pairs per warp: 5.30 us).
 constexpr int kShortGroups = 4, kShortPairs = 2;
+// Plain M = 1 rows of 5-8 vectors per lane (BF16 K = 2048): 2 rows per warp, 16 vectors in all
+// (1.7B step: q|k|v 7.17 -> 5.69 us, o 4.10 -> 3.58 us; talker o 3.07 -> 2.84 us).
+constexpr int kMidGroups = 2;
 constexpr size_t kMaxSmem = 200 * 1024;
 
 enum Epi { kStore = 0, kResidual = 1, kSwiglu = 2 };
@@ -336,11 +339,12 @@ int launch(float *y, const float *x, const float *norm_w, float eps, const typen
     const bool deep = M == 1 && K > kUnrollK * 32 * WF::kEpv;
     const bool shallow = M == 1 && K <= kUnrollShort * 32 * WF::kEpv;
     constexpr int RS = M != 1 ? 1 : EPI == kSwiglu ? kShortPairs : kShortGroups;
+    constexpr int RM = M != 1 || EPI == kSwiglu ? 1 : kMidGroups;
     auto kern = !vec ? gemv_scalar_kernel<WF, M, EPI>
                 : deep ? gemv_vec_kernel<WF, M, EPI, (M == 1 ? kUnrollDeep : kUnrollK), 1>
                 : shallow ? gemv_vec_kernel<WF, M, EPI, (M == 1 ? kUnrollShort : kUnrollK), RS>
-                          : gemv_vec_kernel<WF, M, EPI, kUnrollK, 1>;
-    const int rows_per_cta = kWarps * RPW * ((vec && shallow) ? RS : 1);
+                          : gemv_vec_kernel<WF, M, EPI, kUnrollK, RM>;
+    const int rows_per_cta = kWarps * RPW * (!vec || deep ? 1 : shallow ? RS : RM);
     // opt in above 47 KiB: the default 48 KiB limit also covers the kernel's small static array
     if (smem > 47 * 1024 &&
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
