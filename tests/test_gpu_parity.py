@@ -243,6 +243,26 @@ def test_swiglu_in_place_equals_out_of_place(dtype, rows, inter):
     assert torch.equal(got, ref)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_swiglu_in_place_captured_in_a_graph(dtype):
+    # the in-place form is a cooperative launch (+ wave launches when large): it must capture
+    rows, inter = 4096, 3072
+    src = rand((rows, 2 * inter), 38, dtype, scale=2.0)
+    ref = lai.swiglu(src, inter)
+    buf = src.clone()
+    stream, graph = torch.cuda.Stream(), torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        lai.swiglu_inplace(buf.clone(), inter)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            lai.swiglu_inplace(buf, inter)
+    for _ in range(2):
+        buf.copy_(src)
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(buf.view(-1)[: rows * inter], ref.view(-1))
+
+
 def test_swiglu_in_place_unaligned_buffer():
     base = rand((2 * 300 * 7 + 1,), 33, scale=2.0)
     gu = base[1:].view(300, 14)
