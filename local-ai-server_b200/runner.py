@@ -59,7 +59,9 @@ class LayerConfig:
         return sum(b[k] for k in self.kernels())
 
 
-# BASELINE configs (SURVEY 8a naming: C1..C5).
+# The benchmark configurations C1..C5: ASR-0.6B layer ops (512 tokens), ASR-1.7B layer ops
+# (64 x 1024 tokens), TTS-0.6B talker decode (256 rows at random positions), and the
+# 2M-token 1.7B chain; C4 (SnakeBeta) is SNAKE_STAGES below.
 CONFIGS = {
     "c1": LayerConfig("qwen3-asr-0.6b-decoder-layer", tokens=512, dim=1024, inter=3072,
                       pos_period=512, vocab=151936),
