@@ -495,10 +495,12 @@ qk_generic_kernel(T *q, T *k, const float *wq, const float *wk, const float *cos
 // (d0 = 8 * (lane % 8)) and their RoPE partners 64+d0..64+d0+7 (four 16-byte loads per head),
 // every load of the segment issued before the position's table row is needed. The
 // arithmetic is the reference's: the sum of squares in FP32, inv = 1 / sqrtf(ss / hd + eps),
-// x * inv * w and the rotation's products rounded separately (packed FMUL2 / FADD2 round each
-// lane exactly as FMUL / FADD do), so RoPE alone is bit-exact with the reference's scalar C.
-// Measured against qk_warp_kernel (a warp per head, partner by shuffle): 65 536 tokens at
-// Qwen3-1.7B shapes 319 us (0.77 of measured HBM) before.
+// x * inv * w, and the rotation's products and sums rounded separately (scalar __fmul_rn /
+// __fadd_rn, which the compiler never contracts into FMAs), so RoPE alone is bit-exact with
+// the reference's scalar C.
+// At 65 536 tokens of Qwen3-1.7B shapes: 239 us (1.03 of measured HBM) against 319 us (0.77)
+// for qk_warp_kernel (a warp per head, the partner by shuffle). Packed FMUL2 / FADD2 for the
+// rotation did not reproduce the reference's bits; the scalar forms below do.
 template <int QP, int KP>  // passes of 4 heads for q and k
 __global__ void __launch_bounds__(kRegWarps * 32)
 qk_reg_f32_kernel(float *q, float *k, const float *__restrict__ wq, const float *__restrict__ wk,
@@ -563,13 +565,14 @@ qk_reg_f32_kernel(float *q, float *k, const float *__restrict__ wq, const float 
                 b[e] = __fmul2_rn(__fmul2_rn(b[e], inv2), w2[4 + e]);
             }
         }
-        if (rope) {
+        if (rope) {  // scalar, separately rounded (never contracted): the reference's bits
 #pragma unroll
             for (int e = 0; e < 4; e++) {
                 const float2 x1 = a[e], x2 = b[e];
-                const float2 m1 = __fmul2_rn(x2, t.sl[e]);
-                a[e] = __fadd2_rn(__fmul2_rn(x1, t.cl[e]), make_float2(-m1.x, -m1.y));  // x1*c - x2*s
-                b[e] = __fadd2_rn(__fmul2_rn(x1, t.sh[e]), __fmul2_rn(x2, t.ch[e]));   // x1*s + x2*c
+                a[e] = make_float2(rope_first(x1.x, x2.x, t.cl[e].x, t.sl[e].x),
+                                   rope_first(x1.y, x2.y, t.cl[e].y, t.sl[e].y));
+                b[e] = make_float2(rope_second(x2.x, x1.x, t.ch[e].x, t.sh[e].x),
+                                   rope_second(x2.y, x1.y, t.ch[e].y, t.sh[e].y));
             }
         }
         float *hp = base + (size_t)(hsub + 4 * j) * 128;
