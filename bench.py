@@ -1754,6 +1754,66 @@ def measure_snake_extra(steps: int, warmup: int, seed: int, peak: float, peak_ki
     return res
 
 
+def measure_ops_extra(steps: int, warmup: int, seed: int, peak: float) -> dict:
+    """The path's remaining entry points on their own at config-2 sizes (65 536 rows, hidden
+    2048, FFN 6144), each launch timed with CUDA events: RMSNorm without the residual add
+    (qwen_rms_norm), residual add (qwen_add_inplace) in BF16 and FP32, SiLU (qwen_silu) and
+    SiLU*up with separate gate/up (swiglu_separate) in FP32, and the BF16 embedding gather from
+    the 151 936-row text table, BF16 and widened to FP32. Algorithmic bytes per launch."""
+    import torch
+    import lai
+    T, D, I, V = 65536, 2048, 6144, 151936
+    f32, bf = torch.float32, torch.bfloat16
+    dev = "cuda"
+
+    def normal(shape, dt, k):
+        t = torch.empty(shape, dtype=dt, device=dev)
+        return lai.synth_normal(t, seed=seed + 500 + k)
+
+    x, y = normal((T, D), bf, 1), normal((T, D), bf, 2)
+    yo = torch.empty_like(x)
+    w = 1 + 0.02 * normal((D,), f32, 3)
+    xf, yf = normal((T, D), f32, 4), normal((T, D), f32, 5)
+    g, u, o = normal((T * I // 4,), f32, 6), normal((T * I // 4,), f32, 7), torch.empty(T * I // 4, device=dev)
+    table = normal((V, D), bf, 8)
+    ids = torch.randint(0, V, (T,), dtype=torch.int32, device=dev)
+    emb_bf = torch.empty((T, D), dtype=bf, device=dev)
+    emb_f = torch.empty((T, D), dtype=f32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    P, S = lai._p, lambda: lai._s(None)  # noqa: E731
+    n_act = T * I // 4
+    ops = {
+        "rmsnorm_bf16": (lambda: lai.call("lai_rmsnorm_bf16", P(yo), P(x), P(w), T, D, 1e-6, S()),
+                         T * D * 2 * 2),
+        "add_bf16": (lambda: lai.call("lai_add_bf16", P(x), P(y), T * D, S()), T * D * 2 * 3),
+        "add_f32": (lambda: lai.call("lai_add_f32", P(xf), P(yf), T * D, S()), T * D * 4 * 3),
+        "silu_f32": (lambda: lai.call("lai_silu_f32", P(g), n_act, S()), n_act * 4 * 2),
+        "swiglu_separate_f32": (lambda: lai.call("lai_swiglu_separate_f32", P(o), P(g), P(u), n_act,
+                                                 S()), n_act * 4 * 3),
+        "embed_gather_bf16": (lambda: lai.call("lai_embed_gather_bf16", P(emb_bf), P(table), P(ids), T,
+                                               D, V, P(err), S()), T * (2 * D * 2 + 4)),
+        "embed_gather_bf16_to_f32": (lambda: lai.call("lai_embed_gather_bf16_to_f32", P(emb_f),
+                                                      P(table), P(ids), T, D, V, P(err), S()),
+                                     T * (2 * D + 4 * D + 4)),
+    }
+    out = {}
+    for name, (f, nbytes) in ops.items():
+        for _ in range(warmup):
+            f()
+        torch.cuda.synchronize()
+        ms, _ = time_launches([f], steps, False)
+        avg = ms / steps
+        gbs = nbytes / (avg / 1000.0) / 1e9
+        out[name] = {"avg_us": round(avg * 1000, 2), "gbs": round(gbs, 1),
+                     "frac_of_peak": round(gbs / peak, 4), "bytes_per_launch": nbytes}
+    assert int(err.item()) == 0
+    del x, y, yo, xf, yf, g, u, o, table, emb_bf, emb_f
+    torch.cuda.empty_cache()
+    return {"workload": "the path's other entry points on their own, config-2 sizes",
+            "rows": T, "dim": D, "ffn": I, "vocab": V, "steps": steps,
+            "l2": "inputs larger than L2 for every op", "per_kernel": out}
+
+
 def pcie_peaks(nbytes: int = 1 << 30, reps: int = 3) -> dict:
     """Pinned host <-> device copy rates of this GPU, measured in this run: H2D alone, D2H
     alone, and both directions at once on two streams (GB/s, best of `reps`)."""
@@ -1951,6 +2011,7 @@ def run_ours(args) -> None:
         extras["c1"] = measure_chain_extra("c1", max(es, 200), ew, args.seed, peak, peak_kind)
         extras["c3"] = measure_chain_extra("c3", max(es, 200), ew, args.seed, peak, peak_kind)
         extras["c4"] = measure_snake_extra(es, ew, args.seed, peak, peak_kind)
+        extras["ops"] = measure_ops_extra(es, ew, args.seed, peak)
 
     e2e = e2e_f32 = pcie = None
     if not args.no_e2e and not decode:

@@ -13,6 +13,7 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kUnroll = 4;
+constexpr int kGatherVec = 8;  // gather: 16-byte vectors per lane in flight (2048 BF16 per warp)
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
@@ -82,15 +83,27 @@ gather_kernel(void *out, const uint16_t *__restrict__ table, const int32_t *__re
     if (!ok && lane == 0 && err) atomicOr(err, LAI_DEVERR_TOKEN_ID);
     const uint16_t *src = table + (size_t)(ok ? id : 0) * dim;
     if constexpr (VEC) {
+        // up to kGatherVec 16-byte vectors per lane (a 2048-wide row) loaded before any store,
+        // so a warp has its whole row in flight
         const int nv = dim / 8;
-        for (int v = lane; v < nv; v += 32) {
-            const uint4 t = ok ? ld_stream(src + (size_t)v * 8) : make_uint4(0, 0, 0, 0);
-            if constexpr (OUT_F32) {
-                uint4 *o = reinterpret_cast<uint4 *>(static_cast<float *>(out) + (size_t)r * dim) + 2 * v;
-                o[0] = make_uint4(t.x << 16, t.x & 0xffff0000u, t.y << 16, t.y & 0xffff0000u);
-                o[1] = make_uint4(t.z << 16, t.z & 0xffff0000u, t.w << 16, t.w & 0xffff0000u);
-            } else {
-                st_vec(static_cast<uint16_t *>(out) + (size_t)r * dim + (size_t)v * 8, t);
+        for (int v0 = 0; v0 < nv; v0 += 32 * kGatherVec) {
+            uint4 t[kGatherVec];
+#pragma unroll
+            for (int i = 0; i < kGatherVec; i++) {
+                const int v = v0 + i * 32 + lane;
+                t[i] = ok && v < nv ? ld_stream(src + (size_t)v * 8) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int i = 0; i < kGatherVec; i++) {
+                const int v = v0 + i * 32 + lane;
+                if (v >= nv) break;
+                if constexpr (OUT_F32) {
+                    uint4 *o = reinterpret_cast<uint4 *>(static_cast<float *>(out) + (size_t)r * dim) + 2 * v;
+                    o[0] = make_uint4(t[i].x << 16, t[i].x & 0xffff0000u, t[i].y << 16, t[i].y & 0xffff0000u);
+                    o[1] = make_uint4(t[i].z << 16, t[i].z & 0xffff0000u, t[i].w << 16, t[i].w & 0xffff0000u);
+                } else {
+                    st_vec(static_cast<uint16_t *>(out) + (size_t)r * dim + (size_t)v * 8, t[i]);
+                }
             }
         }
     } else {

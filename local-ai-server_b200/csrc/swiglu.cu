@@ -275,15 +275,27 @@ __device__ __forceinline__ float silu_f32(float g) {
     return __fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))));
 }
 
+// kUnroll float4 per thread, all loaded before any store; threads of block 0 also take
+// the 1-3 trailing elements.
 __global__ void __launch_bounds__(kThreads) silu_kernel(float *x, int64_t n) {
     const int64_t nv = n / 4;
-    const int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
-    if (i < nv) {
-        float4 v = reinterpret_cast<float4 *>(x)[i];
-        v.x = silu_f32(v.x); v.y = silu_f32(v.y); v.z = silu_f32(v.z); v.w = silu_f32(v.w);
-        reinterpret_cast<float4 *>(x)[i] = v;
+    const int64_t base = (int64_t)blockIdx.x * (kThreads * kUnroll) + threadIdx.x;
+    float4 v[kUnroll];
+#pragma unroll
+    for (int j = 0; j < kUnroll; j++) {
+        const int64_t i = base + (int64_t)j * kThreads;
+        if (i < nv) v[j] = reinterpret_cast<float4 *>(x)[i];
     }
-    if (i < n - nv * 4) x[nv * 4 + i] = silu_f32(x[nv * 4 + i]);
+#pragma unroll
+    for (int j = 0; j < kUnroll; j++) {
+        const int64_t i = base + (int64_t)j * kThreads;
+        if (i < nv) {
+            float4 t = v[j];
+            t.x = silu_f32(t.x); t.y = silu_f32(t.y); t.z = silu_f32(t.z); t.w = silu_f32(t.w);
+            reinterpret_cast<float4 *>(x)[i] = t;
+        }
+    }
+    if (blockIdx.x == 0 && threadIdx.x < n - nv * 4) x[nv * 4 + threadIdx.x] = silu_f32(x[nv * 4 + threadIdx.x]);
 }
 __global__ void __launch_bounds__(kThreads) silu_scalar_kernel(float *x, int64_t n) {
     const int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
@@ -329,7 +341,8 @@ int lai_silu_f32(float *x, int64_t n, lai_stream_t stream) {
     if (n == 0) return LAI_OK;
     cudaStream_t s = lai::as_stream(stream);
     if (lai::aligned16(x))
-        lai::silu_kernel<<<lai::grid_for(n / 4 > 4 ? n / 4 : 4, lai::kThreads), lai::kThreads, 0, s>>>(x, n);
+        lai::silu_kernel<<<lai::grid_for(n / 4 > 0 ? n / 4 : 1, lai::kThreads * lai::kUnroll),
+                           lai::kThreads, 0, s>>>(x, n);
     else
         lai::silu_scalar_kernel<<<lai::grid_for(n, lai::kThreads), lai::kThreads, 0, s>>>(x, n);
     return lai::launch_status();
