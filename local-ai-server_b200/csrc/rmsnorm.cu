@@ -19,80 +19,80 @@ namespace lai {
 namespace {
 
 constexpr int kRowsPerCta = 8;  // 8 warps, one row each
+// RMSNorm alone runs three CTAs per SM (<= 85 registers): 0.90 -> 0.92-0.93 of the measured
+// copy bandwidth at 65 536 x 2048 (ptxas otherwise settles at 96 registers, two CTAs per SM).
+// The fused add form keeps the default: at three CTAs per SM it was 1% slower.
+constexpr int kPlainMinCtas = 3;
 
-template <typename T, int NV, bool ADD, int ROWS>  // ROWS consecutive rows per warp
-__global__ void __launch_bounds__(kRowsPerCta * 32)
-rmsnorm_warp_kernel(T *__restrict__ y, T *x, const T *__restrict__ delta,
-                    const float *__restrict__ w, int64_t rows, int dim, float eps) {
+template <typename T, int NV, bool ADD>
+__device__ __forceinline__ void rmsnorm_warp_body(T *__restrict__ y, T *x, const T *__restrict__ delta,
+                                                  const float *__restrict__ w, int64_t rows, int dim,
+                                                  float eps) {
     constexpr int E = Elt<T>::N;
     const int lane = threadIdx.x & 31;
-    const int64_t row0 = ((int64_t)blockIdx.x * kRowsPerCta + (threadIdx.x >> 5)) * ROWS;
-    if (row0 >= rows) return;
+    const int64_t row = (int64_t)blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
+    if (row >= rows) return;
     pdl_wait_prior();  // launched with programmatic dependent launch: inputs after this
 
-    uint4 v[ROWS][NV];
+    const size_t off = (size_t)row * dim;
+    uint4 v[NV];
 #pragma unroll
-    for (int r = 0; r < ROWS; r++) {
-        if (row0 + r >= rows) break;
-        const size_t off = (size_t)(row0 + r) * dim;
-#pragma unroll
-        for (int i = 0; i < NV; i++) v[r][i] = ld_stream(x + off + (size_t)(i * 32 + lane) * E);
-    }
+    for (int i = 0; i < NV; i++) v[i] = ld_stream(x + off + (size_t)(i * 32 + lane) * E);
+
+    float ss = 0.f;
     if constexpr (ADD) {
-        uint4 d[ROWS][NV];
+        uint4 d[NV];
 #pragma unroll
-        for (int r = 0; r < ROWS; r++) {
-            if (row0 + r >= rows) break;
-            const size_t off = (size_t)(row0 + r) * dim;
+        for (int i = 0; i < NV; i++) d[i] = ld_stream(delta + off + (size_t)(i * 32 + lane) * E);
 #pragma unroll
-            for (int i = 0; i < NV; i++) d[r][i] = ld_stream(delta + off + (size_t)(i * 32 + lane) * E);
-        }
+        for (int i = 0; i < NV; i++) {
+            float a[E], b[E];
+            unpack<T>(v[i], a);
+            unpack<T>(d[i], b);
 #pragma unroll
-        for (int r = 0; r < ROWS; r++) {
-            if (row0 + r >= rows) break;
-            const size_t off = (size_t)(row0 + r) * dim;
-#pragma unroll
-            for (int i = 0; i < NV; i++) {
-                float a[E], b[E];
-                unpack<T>(v[r][i], a);
-                unpack<T>(d[r][i], b);
-#pragma unroll
-                for (int e = 0; e < E; e++) a[e] = __fadd_rn(a[e], b[e]);
-                v[r][i] = pack<T>(a);  // x' rounded to storage precision, then normalised
-                st_vec(x + off + (size_t)(i * 32 + lane) * E, v[r][i]);
-            }
+            for (int e = 0; e < E; e++) a[e] = __fadd_rn(a[e], b[e]);
+            v[i] = pack<T>(a);  // x' rounded to storage precision, then normalised
+            st_vec(x + off + (size_t)(i * 32 + lane) * E, v[i]);
         }
     }
 #pragma unroll
-    for (int r = 0; r < ROWS; r++) {
-        if (row0 + r >= rows) break;  // warp-uniform
-        float ss = 0.f;
+    for (int i = 0; i < NV; i++) {
+        float a[E];
+        unpack<T>(v[i], a);
 #pragma unroll
-        for (int i = 0; i < NV; i++) {
-            float a[E];
-            unpack<T>(v[r][i], a);
-#pragma unroll
-            for (int e = 0; e < E; e++) ss = fmaf(a[e], a[e], ss);
-        }
-        ss = group_sum<32>(ss);
-        const float inv = 1.0f / sqrtf(ss / (float)dim + eps);
-        const size_t off = (size_t)(row0 + r) * dim;
-#pragma unroll
-        for (int i = 0; i < NV; i++) {
-            const int c = (i * 32 + lane) * E;
-            float a[E], wv[E];
-            unpack<T>(v[r][i], a);
-#pragma unroll
-            for (int e = 0; e < E; e += 4) {
-                float4 t = ld_f4(w + c + e);
-                wv[e] = t.x; wv[e + 1] = t.y; wv[e + 2] = t.z; wv[e + 3] = t.w;
-            }
-#pragma unroll
-            for (int e = 0; e < E; e++) a[e] = __fmul_rn(__fmul_rn(a[e], inv), wv[e]);
-            st_vec(y + off + c, pack<T>(a));
-        }
+        for (int e = 0; e < E; e++) ss = fmaf(a[e], a[e], ss);
     }
-    pdl_launch_dependents();  // these rows are done: the next kernel may start launching
+    ss = group_sum<32>(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)dim + eps);
+
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+        const int c = (i * 32 + lane) * E;
+        float a[E], wv[E];
+        unpack<T>(v[i], a);
+#pragma unroll
+        for (int e = 0; e < E; e += 4) {
+            float4 t = ld_f4(w + c + e);
+            wv[e] = t.x; wv[e + 1] = t.y; wv[e + 2] = t.z; wv[e + 3] = t.w;
+        }
+#pragma unroll
+        for (int e = 0; e < E; e++) a[e] = __fmul_rn(__fmul_rn(a[e], inv), wv[e]);
+        st_vec(y + off + c, pack<T>(a));
+    }
+    pdl_launch_dependents();  // this row is done: the next kernel may start launching
+}
+
+template <typename T, int NV>
+__global__ void __launch_bounds__(kRowsPerCta * 32)
+rmsnorm_warp_add_kernel(T *__restrict__ y, T *x, const T *__restrict__ delta,
+                        const float *__restrict__ w, int64_t rows, int dim, float eps) {
+    rmsnorm_warp_body<T, NV, true>(y, x, delta, w, rows, dim, eps);
+}
+template <typename T, int NV>
+__global__ void __launch_bounds__(kRowsPerCta * 32, kPlainMinCtas)
+rmsnorm_warp_kernel(T *__restrict__ y, T *x, const T *__restrict__ delta,
+                    const float *__restrict__ w, int64_t rows, int dim, float eps) {
+    rmsnorm_warp_body<T, NV, false>(y, x, delta, w, rows, dim, eps);
 }
 
 // Any width / alignment: one CTA per row (grid-stride over rows).
@@ -121,15 +121,12 @@ rmsnorm_block_kernel(T *y, T *x, const T *delta, const float *__restrict__ w, in
     }
 }
 
-// One row per warp. (RMSNorm alone keeps half the loads of the fused form in flight per row;
-// two rows per warp for it measured the same, 0.90 of the measured copy bandwidth at 65 536 x
-// 2048, at 128 instead of 96 registers.)
 template <typename T, bool ADD, int NV>
 void launch_warp(T *y, T *x, const T *delta, const float *w, int64_t rows, int dim, float eps,
                  cudaStream_t s) {
-    constexpr int ROWS = 1;
-    launch_pdl(rmsnorm_warp_kernel<T, NV, ADD, ROWS>, dim3(grid_for(rows, kRowsPerCta * ROWS)),
-               dim3(kRowsPerCta * 32), 0, s, y, x, delta, w, rows, dim, eps);
+    launch_pdl(ADD ? rmsnorm_warp_add_kernel<T, NV> : rmsnorm_warp_kernel<T, NV>,
+               dim3(grid_for(rows, kRowsPerCta)), dim3(kRowsPerCta * 32), 0, s, y, x, delta, w,
+               rows, dim, eps);
 }
 
 template <typename T, bool ADD>
