@@ -1631,7 +1631,8 @@ def summarize_kernels(names, per, bpl, rows_pl, peak) -> tuple[dict, str]:
     for name, k in kernels.items():
         avg_ms = statistics.mean(k["ms"])
         gbs = k["bytes"] / (avg_ms / 1000.0) / 1e9
-        table[name] = {"avg_us": round(avg_ms * 1000, 2), "gbs": round(gbs, 1),
+        table[name] = {"avg_us": round(avg_ms * 1000, 2),
+                       "median_us": round(statistics.median(k["ms"]) * 1000, 2), "gbs": round(gbs, 1),
                        "frac_of_peak": round(gbs / peak, 4),
                        "rows_per_s": round(k["rows"] / (avg_ms / 1000.0), 1),
                        "bytes_per_launch": k["bytes"], "launches": len(k["ms"])}
