@@ -189,6 +189,17 @@ int run_op(const char *fn, std::vector<Arg> &args, int64_t rows, const Launcher 
             cudaMemcpyAsync(static_cast<char *>(c->whole) + a.whole_off, a.ptr, a.whole_bytes,
                             cudaMemcpyHostToDevice, sin);
 
+    // An aliased host output may only be a compaction of its input (rows no longer than the
+    // input's, as SwiGLU's): then chunk c's copy-out overwrites input bytes of chunks <= c
+    // only, all already copied in on the in-order copy-in stream (see the top of this file).
+    for (auto &o : args)
+        for (auto &i : args)
+            if (&o != &i && o.host && i.host && o.out && i.in && o.ptr == i.ptr &&
+                o.row_bytes > i.row_bytes) {
+                for (int s2 = 0; s2 < kStreams; s2++) cudaStreamSynchronize(c->pipe[s2]);
+                return fail(fn, LAI_ERR_ALIAS, "output rows longer than the input rows they alias");
+            }
+
     const int64_t nchunks = (rows + chunk - 1) / chunk;
     int status = LAI_OK;
     for (int64_t ci = 0; ci < nchunks && status == LAI_OK; ci++) {
