@@ -1728,6 +1728,33 @@ def measure_chain_extra(name: str, steps: int, warmup: int, seed: int, peak: flo
     return res
 
 
+def time_after_l2_scrub(launches, names, bpl, steps: int, peak: float) -> dict:
+    """Each launch timed alone (CUDA events on the launching stream around the launch only)
+    after a read-only pass over 256 MiB, twice the L2: the pass evicts, and so writes back,
+    the dirty lines the previous launch left, which a launch in a chain of in-place kernels
+    otherwise pays for. The same cache state as ncu's default cache control."""
+    import torch
+    stream = torch.cuda.current_stream()
+    scrub = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
+    sink = torch.empty((), dtype=torch.float32, device="cuda")
+    out = {}
+    for j, f in enumerate(launches):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(steps)]
+        for a, b in ev:
+            torch.sum(scrub, dim=0, out=sink)
+            a.record(stream)
+            f()
+            b.record(stream)
+        torch.cuda.synchronize()
+        avg_ms = sum(a.elapsed_time(b) for a, b in ev) / steps
+        gbs = bpl[j] / (avg_ms / 1000.0) / 1e9
+        out[names[j]] = {"avg_us": round(avg_ms * 1000, 2), "gbs": round(gbs, 1),
+                         "frac_of_peak": round(gbs / peak, 4)}
+    del scrub
+    return out
+
+
 def measure_snake_extra(steps: int, warmup: int, seed: int, peak: float, peak_kind: str) -> dict:
     """Config c4 on this GPU (N = 1): SnakeBeta over the five BigVGAN stages x batch 8, one
     launch per stage, per-stage GB/s and its fraction of the measured HBM bandwidth."""
@@ -1742,6 +1769,7 @@ def measure_snake_extra(steps: int, warmup: int, seed: int, peak: float, peak_ki
     total_ms, per = time_launches(launches, steps, False, work.kernel_names)
     bpl = work.bytes_per_launch()
     table, dominant = summarize_kernels(work.kernel_names, per, bpl, work.rows_per_launch(), peak)
+    clean = time_after_l2_scrub(launches, work.kernel_names, bpl, steps, peak)
     res = {"workload": "vocoder SnakeBeta over the BigVGAN stages, FP32 in place",
            "stages": runner.SNAKE_STAGES, "batch": runner.SNAKE_BATCH,
            "value": round(sum(work.rows_per_launch()) * steps / (total_ms / 1000.0), 1),
@@ -1749,7 +1777,9 @@ def measure_snake_extra(steps: int, warmup: int, seed: int, peak: float, peak_ki
            "sweep_gbs": round(sum(bpl) * steps / (total_ms / 1000.0) / 1e9, 1),
            "per_kernel": table,
            "roofline": roofline_of(table, dominant, peak, peak_kind, f"{dominant}@c4"),
-           "min_stage_frac": min(v["frac_of_peak"] for v in table.values())}
+           "min_stage_frac": min(v["frac_of_peak"] for v in table.values()),
+           "per_kernel_clean_l2": clean,
+           "min_stage_frac_clean_l2": min(v["frac_of_peak"] for v in clean.values())}
     del work, launches
     torch.cuda.empty_cache()
     return res
