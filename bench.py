@@ -1933,7 +1933,9 @@ def run_ours(args) -> None:
         cfg = None
     elif decode:
         cfg = runner.DECODE_CONFIGS[args.config]
-        work = runner.DecodeLinear(cfg, seed=args.seed + 1000 * rank, wfmt=args.wfmt)
+        can_chain = args.wfmt == "bf16" and cfg.m == 1 and args.gemv != "per-op"
+        work = runner.DecodeLinear(cfg, seed=args.seed + 1000 * rank, wfmt=args.wfmt,
+                                   chain=can_chain)
         rows = cfg.m
     else:
         cfg = runner.CONFIGS[args.config]
@@ -1944,8 +1946,22 @@ def run_ours(args) -> None:
             row0, row1 = rank * per, (rank + 1) * per
         rows = row1 - row0
         work = runner.LayerChain(cfg, rows, row0=row0, seed=args.seed, dtype=args.dtype)
-    launches = work.launches(None)  # each launch goes to the current stream when called
     graph = args.graph == "on" or (args.graph == "auto" and not snake and rows <= 4096)
+    form_us = None
+    if decode and work.chain is not None:
+        # both forms of the step timed briefly (same weights); `auto` measures the faster below
+        form_us = {}
+        for form in ("per-op", "chain"):
+            work.set_form(form)
+            ls = work.launches(None)
+            for _ in range(3):
+                for f in ls:
+                    f()
+            torch.cuda.synchronize()
+            ms, _ = time_launches(ls, 20, graph, list(work.kernel_names))
+            form_us[form] = round(1000.0 * ms / 20, 2)
+        work.set_form(args.gemv if args.gemv != "auto" else min(form_us, key=form_us.get))
+    launches = work.launches(None)  # each launch goes to the current stream when called
     unfused_us = None
     ul = work.unfused_library_launches() if decode else None
     if ul:  # the same step as separate kernels around cuBLAS GEMMs, for comparison
@@ -2029,6 +2045,8 @@ def run_ours(args) -> None:
             dist.all_reduce(et, op=dist.ReduceOp.MAX)
         return float(et.item())
 
+    gemv_form = work.form if decode else None
+    step_kernels = len(work.kernel_names)
     del work, launches  # free the device-resident workload before the other measurements
     torch.cuda.empty_cache()
 
@@ -2118,8 +2136,11 @@ def run_ours(args) -> None:
                   "layers": cfg.layers, "weights": args.wfmt, "bytes_per_step": step_bytes,
                   "timing": "CUDA graph replay" if graph else "direct launches",
                   "unfused_library_us_per_step": unfused_us,
+                  "gemv": ("one persistent GEMV-chain kernel per step" if gemv_form == "chain"
+                           else "one fused-GEMV launch per projection"),
+                  "gemv_forms_us_per_step": form_us,
                   "l2": f"weights larger than L2 ({step_bytes / 1e9:.2f} GB per step)"}
-        launches_per_step = 4 * cfg.layers
+        launches_per_step = step_kernels
     elif snake:
         config = {"workload": "vocoder SnakeBeta over the BigVGAN stages, FP32 in place",
                   "config": "c4", "stages": runner.SNAKE_STAGES, "batch": runner.SNAKE_BATCH,
@@ -2175,6 +2196,10 @@ def main():
     ap.add_argument("--passes", type=int, choices=[1, 3], default=3,
                     help="v1: 3 = F32-faithful 3xTF32 products, 1 = plain TF32")
     ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--gemv", choices=["auto", "chain", "per-op"], default="auto",
+                    help="decode configs (BF16 weights, M = 1): the step as one persistent "
+                         "GEMV-chain kernel or one fused-GEMV launch per projection; auto times "
+                         "both briefly and measures the faster")
     ap.add_argument("--wfmt", choices=["bf16", "f16", "i8", "f32"], default="bf16",
                     help="g1/g2: decode weight format (the reference's GPU modes: BF16 as stored, "
                          "FP16, INT8 + per-row scale, F32)")

@@ -227,6 +227,39 @@ LAI_API int lai_quantize_rows_i8_bf16(int8_t *q, float *scales, const lai_bf16 *
 LAI_API int lai_convert_bf16_to_f16(lai_f16 *dst, const lai_bf16 *src, int64_t n,
                                     lai_stream_t stream);
 
+/* ---- a decode step's chain of fused GEMVs in one persistent kernel ------------------------
+ * The M = 1 BF16 GEMVs above, run back to back as one cooperative launch (one CTA per SM):
+ * op j reads what op j-1 wrote, as the per-layer decode sequence does (src/tts_native.c:
+ * 637-668, each layer four ops: RMSNorm + q|k|v, o + residual, RMSNorm + gate|up + SwiGLU,
+ * down + residual). Every CTA owns a fixed slice of rows of every matrix and streams its
+ * slices of the coming ops into shared memory ahead of the dependency.
+ *   epilogue LAI_CHAIN_STORE:    out[n]   = W . in'              (in' = RMSNorm(in; norm_w, eps)
+ *            LAI_CHAIN_RESIDUAL: out[n]  += W . in'               when norm_w, else in)
+ *            LAI_CHAIN_SWIGLU:   out[n/2] = silu(W[2j] . in') * (W[2j+1] . in')  (rows interleaved)
+ * W [n, k] BF16, in/norm_w [k] FP32, all 16-byte aligned; k % 256 == 0 and k <= 6144
+ * (LAI_ERR_TOOBIG beyond), at most 512 rows of an op per SM; out must not overlap in.
+ * lai_gemv_chain_create validates the ops and copies the table to the device (synchronous, at
+ * load time); lai_gemv_chain_run launches the chain on `stream` (capturable in a CUDA graph)
+ * and sets *err (device int, never cleared) to 1 if a bounded wait in the kernel ran out.
+ * Runs of one chain must not overlap in time (they share its grid counter).
+ */
+enum { LAI_CHAIN_STORE = 0, LAI_CHAIN_RESIDUAL = 1, LAI_CHAIN_SWIGLU = 2 };
+typedef struct {
+    const lai_bf16 *w;
+    const float *in;
+    const float *norm_w; /* NULL: no RMSNorm */
+    float *out;
+    int32_t n, k;
+    int32_t epilogue; /* LAI_CHAIN_* */
+    float eps;
+} lai_gemv_chain_op_t;
+typedef struct lai_gemv_chain lai_gemv_chain_t;
+LAI_API int lai_gemv_chain_create(lai_gemv_chain_t **chain, const lai_gemv_chain_op_t *ops,
+                                  int n_ops);
+LAI_API int lai_gemv_chain_run(const lai_gemv_chain_t *chain, int *err, lai_stream_t stream);
+LAI_API int lai_gemv_chain_grid(const lai_gemv_chain_t *chain); /* CTAs per launch */
+LAI_API void lai_gemv_chain_destroy(lai_gemv_chain_t *chain);
+
 /* ---- decode attention over the KV cache ----------------------------------------------------
  * One query token per sequence: the decode step's cache append + qwen_causal_attention
  * (src/tts_native.c:650-656: memcpy of k, v into kv_k_at / kv_v_at at pos, then

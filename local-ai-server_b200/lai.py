@@ -46,6 +46,10 @@ SIGNATURES: dict[str, tuple] = {
     "lai_gemv_bf16w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
     "lai_gemv_residual_bf16w_f32": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _vp]),
     "lai_gemv_swiglu_bf16w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
+    "lai_gemv_chain_create": (_i32, [_vp, _vp, _i32]),
+    "lai_gemv_chain_run": (_i32, [_vp, _vp, _vp]),
+    "lai_gemv_chain_grid": (_i32, [_vp]),
+    "lai_gemv_chain_destroy": (None, [_vp]),
     "lai_gemv_f16w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
     "lai_gemv_residual_f16w_f32": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _vp]),
     "lai_gemv_swiglu_f16w_f32": (_i32, [_vp, _vp, _vp, _f32, _vp, _i64, _i32, _i32, _vp]),
@@ -302,6 +306,51 @@ def gemv_swiglu(x, W_gu, norm_w=None, eps=1e-6, out=None, stream=None, scales=No
     call(f"lai_gemv_swiglu_{fmt}_f32", _p(out), _p(x), _p(norm_w), eps, _p(W_gu), *sc, M, K,
          inter, _s(stream))
     return out
+
+
+CHAIN_STORE, CHAIN_RESIDUAL, CHAIN_SWIGLU = 0, 1, 2
+
+
+class GemvChainOp(ctypes.Structure):
+    """lai_gemv_chain_op_t: one fused M = 1 GEMV of a chain (device pointers)."""
+    _fields_ = [("w", _vp), ("in_", _vp), ("norm_w", _vp), ("out", _vp), ("n", ctypes.c_int32),
+                ("k", ctypes.c_int32), ("epilogue", ctypes.c_int32), ("eps", _f32)]
+
+
+class GemvChain:
+    """A decode step's GEMVs as one persistent kernel (lai_gemv_chain_*). `ops`: a list of
+    (kind, W [n, k] BF16, in [k] FP32, norm_w [k] or None, out, eps) with kind one of
+    CHAIN_STORE / CHAIN_RESIDUAL / CHAIN_SWIGLU; the tensors must stay alive (the chain
+    keeps references) and are read and written in place by every run()."""
+
+    def __init__(self, ops):
+        import torch
+        self._keep = []
+        arr = (GemvChainOp * max(1, len(ops)))()
+        for j, (kind, W, x, norm_w, out, eps) in enumerate(ops):
+            assert W.dtype == torch.bfloat16 and x.dtype == torch.float32
+            arr[j] = GemvChainOp(W.data_ptr(), x.data_ptr(),
+                                 norm_w.data_ptr() if norm_w is not None else None, out.data_ptr(),
+                                 W.shape[0], W.shape[1], kind, eps)
+            self._keep += [W, x, norm_w, out]
+        h = _vp()
+        call("lai_gemv_chain_create", ctypes.byref(h), arr, len(ops))
+        self._h = h
+        dev = ops[0][1].device if ops else "cuda"
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    @property
+    def grid(self) -> int:
+        return load().lai_gemv_chain_grid(self._h)
+
+    def run(self, stream=None):
+        call("lai_gemv_chain_run", self._h, _p(self.err), _s(stream))
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            load().lai_gemv_chain_destroy(h)
+            self._h = None
 
 
 def quantize_rows_i8(W, stream=None):

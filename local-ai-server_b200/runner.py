@@ -820,9 +820,10 @@ class DecodeLinear:
     WEIGHT_BYTES = {"bf16": 2, "f16": 2, "i8": 1, "f32": 4}
 
     def __init__(self, cfg: DecodeConfig, seed: int = 4321, device: str = "cuda",
-                 wfmt: str = "bf16"):
+                 wfmt: str = "bf16", chain: bool = False):
         import torch
         self.cfg, self.rows, self.wfmt = cfg, cfg.m, wfmt
+        self.chain, self.form = None, "per-op"
         self.wbytes = self.WEIGHT_BYTES[wfmt]
         D, I, M = cfg.dim, cfg.inter, cfg.m
         self.qkv_n = cfg.q_dim + 2 * cfg.kv_dim
@@ -856,10 +857,44 @@ class DecodeLinear:
                                      seed=seed + 8)
         self.qkv = torch.empty((M, self.qkv_n), dtype=f32, device=device)
         self.act = torch.empty((M, I), dtype=f32, device=device)
-        self.kernel_names = ("rmsnorm_qkv_gemv", "o_gemv_residual", "rmsnorm_gate_up_gemv_swiglu",
-                             "down_gemv_residual") * L
+        if chain:  # the step also as one persistent kernel (lai_gemv_chain_*)
+            if wfmt != "bf16" or M != 1:
+                raise ValueError("the GEMV chain takes BF16 weights at M = 1")
+            self.chain = lai.GemvChain(self.chain_ops())
+            self.form = "chain"
+
+    PER_OP_NAMES = ("rmsnorm_qkv_gemv", "o_gemv_residual", "rmsnorm_gate_up_gemv_swiglu",
+                    "down_gemv_residual")
+
+    @property
+    def kernel_names(self):
+        return ("gemv_chain",) if self.form == "chain" else self.PER_OP_NAMES * self.cfg.layers
+
+    def set_form(self, form: str):
+        """"chain" (one persistent kernel per step) or "per-op" (one launch per projection)."""
+        if form == "chain" and self.chain is None:
+            raise ValueError("built without the chain")
+        self.form = form
+
+    def chain_ops(self):
+        """The step's 4 * layers GEMVs as chain ops, in the order per_op_launches() runs them."""
+        c = self.cfg
+        x, a, qkv, act = self.x[0], self.attn[0], self.qkv[0], self.act[0]
+        ops = []
+        for l in range(c.layers):
+            ops += [(lai.CHAIN_STORE, self.Wqkv[l], x, self.w_in, qkv, c.eps),
+                    (lai.CHAIN_RESIDUAL, self.Wo[l], a, None, x, 0.0),
+                    (lai.CHAIN_SWIGLU, self.Wgu[l], x, self.w_post, act, c.eps),
+                    (lai.CHAIN_RESIDUAL, self.Wd[l], act, None, x, 0.0)]
+        return ops
 
     def launches(self, stream=None):
+        if self.form == "chain":
+            return [lambda: self.chain.run(stream)]
+        return self.per_op_launches(stream)
+
+    def per_op_launches(self, stream=None):
+        """One fused-GEMV launch per projection (4 per layer)."""
         c = self.cfg
         sc = lambda W: self.scales.get(id(W))  # noqa: E731
         out = []
@@ -908,13 +943,14 @@ class DecodeLinear:
         c, M, e = self.cfg, self.cfg.m, self.wbytes
         D, I = c.dim, c.inter
         s = 4 if self.wfmt == "i8" else 0
-        return [self.qkv_n * (D * e + s) + M * D * 4 + M * self.qkv_n * 4 + D * 4,
-                D * (c.q_dim * e + s) + M * c.q_dim * 4 + 2 * M * D * 4,
-                2 * I * (D * e + s) + M * D * 4 + M * I * 4 + D * 4,
-                D * (I * e + s) + M * I * 4 + 2 * M * D * 4] * c.layers
+        per = [self.qkv_n * (D * e + s) + M * D * 4 + M * self.qkv_n * 4 + D * 4,
+               D * (c.q_dim * e + s) + M * c.q_dim * 4 + 2 * M * D * 4,
+               2 * I * (D * e + s) + M * D * 4 + M * I * 4 + D * 4,
+               D * (I * e + s) + M * I * 4 + 2 * M * D * 4] * c.layers
+        return [sum(per)] if self.form == "chain" else per
 
     def rows_per_launch(self) -> list[int]:
-        return [self.cfg.m] * 4 * self.cfg.layers
+        return [self.cfg.m] * len(self.kernel_names)
 
 
 @dataclasses.dataclass(frozen=True)

@@ -197,3 +197,158 @@ def test_i8_decode_layer_tracks_bf16():
     torch.cuda.synchronize()
     bound = (s.cpu() / 2)[None, :] * x.abs().sum(1, keepdim=True)  # |sum (w - q s) x| bound
     assert ((y8 - y16).abs().cpu() <= bound + 1e-5).all()
+
+
+# ---- the decode step's GEMVs as one persistent chain kernel (lai_gemv_chain_*) -----------
+def chain_layers(L, D, QD, KV, I, seed):
+    """L decoder layers' weights and norms (q|k|v rows concatenated, gate/up interleaved)."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    mk = lambda n, k: (torch.randn(n, k, generator=g) / np.sqrt(k)).to(torch.bfloat16)  # noqa: E731
+    layers = [dict(qkv=mk(QD + 2 * KV, D), o=mk(D, QD), gu=mk(2 * I, D), down=mk(D, I),
+                   w_in=1 + 0.02 * torch.randn(D, generator=g),
+                   w_post=1 + 0.02 * torch.randn(D, generator=g)) for _ in range(L)]
+    x = torch.randn(D, generator=g)
+    attn = torch.randn(QD, generator=g)
+    return layers, x, attn
+
+
+def chain_oracle(layers, x, attn, eps):
+    """The reference's per-layer decode sequence (src/tts_native.c:637-668) in the oracle."""
+    x = x.numpy()[None].copy()
+    a = attn.numpy()[None]
+    for ly in layers:
+        qkv = oracle.linear_bf16(oracle.rms_norm(x, ly["w_in"].numpy(), eps), wbits(ly["qkv"]))
+        x = oracle.add_inplace(x, oracle.linear_bf16(a, wbits(ly["o"])))
+        gu = oracle.linear_bf16(oracle.rms_norm(x, ly["w_post"].numpy(), eps), wbits(ly["gu"]))
+        act = oracle.swiglu_multiply(gu, ly["gu"].shape[0] // 2)
+        x = oracle.add_inplace(x, oracle.linear_bf16(act, wbits(ly["down"])))
+    return x[0], qkv[0], act[0]
+
+
+def build_chain(layers, x, attn, eps):
+    xd, ad = x.to(DEV), attn.to(DEV)
+    qkv = torch.empty(layers[0]["qkv"].shape[0], device=DEV)
+    act = torch.empty(layers[0]["gu"].shape[0] // 2, device=DEV)
+    dev = [{k: v.to(DEV) for k, v in ly.items()} for ly in layers]
+    ops = []
+    for ly in dev:
+        ops += [(lai.CHAIN_STORE, ly["qkv"], xd, ly["w_in"], qkv, eps),
+                (lai.CHAIN_RESIDUAL, ly["o"], ad, None, xd, 0.0),
+                (lai.CHAIN_SWIGLU, ly["gu"], xd, ly["w_post"], act, eps),
+                (lai.CHAIN_RESIDUAL, ly["down"], act, None, xd, 0.0)]
+    return lai.GemvChain(ops), xd, qkv, act
+
+
+# (layers, hidden, q dim, kv dim, FFN): the 0.6B talker, the 1.7B shapes (down K = 6144), and
+# a narrow model (1-3 rows per SM)
+CHAIN_SHAPES = [(3, 1024, 2048, 1024, 3072), (2, 2048, 2048, 1024, 6144), (2, 256, 256, 64, 256)]
+
+
+@pytest.mark.parametrize("L,D,QD,KV,I", CHAIN_SHAPES)
+def test_gemv_chain_matches_oracle(L, D, QD, KV, I):
+    layers, x, attn = chain_layers(L, D, QD, KV, I, L + D)
+    chain, xd, qkv, act = build_chain(layers, x, attn, 1e-6)
+    chain.run()
+    torch.cuda.synchronize()
+    assert int(chain.err.item()) == 0
+    rx, rqkv, ract = chain_oracle(layers, x, attn, 1e-6)
+    assert max_rel_err(qkv.cpu().numpy(), rqkv) <= TOL_F32
+    assert max_rel_err(act.cpu().numpy(), ract) <= TOL_F32
+    assert max_rel_err(xd.cpu().numpy(), rx) <= TOL_F32
+
+
+def test_gemv_chain_ops_with_fewer_rows_than_ctas():
+    # most CTAs own no rows of these ops but still take part in every grid barrier
+    g = torch.Generator(device="cpu").manual_seed(9)
+    K = 512
+    x = torch.randn(K, generator=g)
+    w = 1 + 0.02 * torch.randn(K, generator=g)
+    Ws = (torch.randn(64, K, generator=g) / 23).to(torch.bfloat16)
+    Wg = (torch.randn(100, K, generator=g) / 23).to(torch.bfloat16)   # 50 gate/up pairs
+    Wr = (torch.randn(20, 256, generator=g) / 16).to(torch.bfloat16)   # residual: 20 rows of K = 256
+    r0 = torch.randn(20, generator=g)
+    a = torch.randn(256, generator=g)
+    xd, wd, ad = x.to(DEV), w.to(DEV), a.to(DEV)
+    ys, yg, rr = torch.empty(64, device=DEV), torch.empty(50, device=DEV), r0.to(DEV)
+    chain = lai.GemvChain([(lai.CHAIN_STORE, Ws.to(DEV), xd, wd, ys, 1e-5),
+                           (lai.CHAIN_SWIGLU, Wg.to(DEV), xd, None, yg, 0.0),
+                           (lai.CHAIN_RESIDUAL, Wr.to(DEV), ad, None, rr, 0.0)])
+    chain.run()
+    torch.cuda.synchronize()
+    assert int(chain.err.item()) == 0
+    xn = oracle.rms_norm(x.numpy()[None], w.numpy(), 1e-5)
+    assert max_rel_err(ys.cpu().numpy(), oracle.linear_bf16(xn, wbits(Ws))[0]) <= TOL_F32
+    gu = oracle.linear_bf16(x.numpy()[None], wbits(Wg))
+    assert max_rel_err(yg.cpu().numpy(), oracle.swiglu_multiply(gu, 50)[0]) <= TOL_F32
+    ref = oracle.add_inplace(r0.numpy()[None], oracle.linear_bf16(a.numpy()[None], wbits(Wr)))
+    assert max_rel_err(rr.cpu().numpy(), ref[0]) <= TOL_F32
+
+
+@pytest.mark.parametrize("name", ["g1", "g2"])
+def test_gemv_chain_equals_per_op_launches_over_28_layers(name):
+    # a full decode step's linear path: the chain kernel vs one fused-GEMV launch per projection
+    import runner
+    cfg = runner.DECODE_CONFIGS[name]
+    a = runner.DecodeLinear(cfg, seed=11, chain=True)
+    b = runner.DecodeLinear(cfg, seed=11)
+    for f in a.launches():
+        f()
+    for f in b.launches():
+        f()
+    torch.cuda.synchronize()
+    assert int(a.chain.err.item()) == 0
+    for u, v in [(a.x, b.x), (a.qkv, b.qkv), (a.act, b.act)]:
+        assert max_rel_err(u.cpu().numpy(), v.cpu().numpy()) <= 1e-4
+    assert torch.isfinite(a.x).all()
+
+
+def test_gemv_chain_captured_in_a_graph_repeats():
+    layers, x, attn = chain_layers(2, 1024, 2048, 1024, 3072, 5)
+    chain, xd, qkv, act = build_chain(layers, x, attn, 1e-6)
+    x0 = xd.clone()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        chain.run(s)  # warm up outside the capture
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    once = xd.clone()
+    xd.copy_(x0)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        chain.run(torch.cuda.current_stream())
+    xd.copy_(x0)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(xd, once)  # same partition, same order: the same bits
+    g.replay()  # a second replay re-zeroes the grid counter and continues from the new x
+    torch.cuda.synchronize()
+    assert int(chain.err.item()) == 0
+    del g
+
+
+def test_gemv_chain_argument_checks():
+    import ctypes
+    from conftest import arena_ptr
+    L = lai.load()
+    P = arena_ptr(0)
+
+    def create(**kw):
+        op = dict(w=arena_ptr(1 << 20), in_=arena_ptr(4096), norm_w=None, out=arena_ptr(1 << 16),
+                  n=8, k=256, epilogue=lai.CHAIN_STORE, eps=1e-6)
+        op.update(kw)
+        arr = (lai.GemvChainOp * 1)(lai.GemvChainOp(**{k: (v.value if isinstance(v, ctypes.c_void_p)
+                                                          else v) for k, v in op.items()}))
+        h = ctypes.c_void_p()
+        st = L.lai_gemv_chain_create(ctypes.byref(h), arr, 1)
+        if h.value:
+            L.lai_gemv_chain_destroy(h)
+        return st
+
+    assert create(k=100) == lai.LAI_ERR_INVALID         # k not a multiple of 256
+    assert create(k=8192) == lai.LAI_ERR_TOOBIG         # a row beyond one stage
+    assert create(epilogue=lai.CHAIN_SWIGLU, n=7) == lai.LAI_ERR_INVALID  # odd gate/up rows
+    assert create(out=arena_ptr(4096 + 16)) == lai.LAI_ERR_ALIAS  # output over the input
+    assert create(n=1 << 20) == lai.LAI_ERR_TOOBIG      # more rows per SM than staged results
+    assert create() == lai.LAI_OK
+    assert L.lai_gemv_chain_run(None, P, None) == lai.LAI_ERR_INVALID
