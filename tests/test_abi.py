@@ -67,6 +67,19 @@ class _P:
 P = _P()
 
 
+def chain_create(lib, **kw):
+    """lai_gemv_chain_create on one op (arena pointers) with fields overridden by kw."""
+    op = dict(w=A(1 << 20).value, in_=A(4096).value, norm_w=None, out=A(1 << 16).value, n=8,
+              k=256, epilogue=lai.CHAIN_STORE, eps=1e-6)
+    op.update(kw)
+    arr = (lai.GemvChainOp * 1)(lai.GemvChainOp(**op))
+    h = ctypes.c_void_p()
+    st = lib.lai_gemv_chain_create(ctypes.byref(h), arr, 1)
+    if h.value:
+        lib.lai_gemv_chain_destroy(h)
+    return st
+
+
 @pytest.mark.parametrize("call, want", [
     (lambda l: l.lai_rmsnorm_bf16(P, P, P, -1, 1024, 1e-6, None), lai.LAI_ERR_INVALID),
     (lambda l: l.lai_rmsnorm_f32(P, None, P, 4, 1024, 1e-6, None), lai.LAI_ERR_INVALID),
@@ -129,6 +142,14 @@ P = _P()
     (lambda l: l.lai_quantize_rows_i8_bf16(A(4096), A(1 << 20), A(4096 + 16), 4, 64, None),
      lai.LAI_ERR_ALIAS),
     (lambda l: l.lai_convert_bf16_to_f16(A(4096), A(4096 + 2), 64, None), lai.LAI_ERR_ALIAS),
+    # GEMV chain: NULL table; k not a multiple of 256; a row beyond one stage; odd SwiGLU
+    # rows; an output over its input (all rejected before any device call)
+    (lambda l: l.lai_gemv_chain_create(ctypes.byref(ctypes.c_void_p()), None, 1), lai.LAI_ERR_INVALID),
+    (lambda l: chain_create(l, k=100), lai.LAI_ERR_INVALID),
+    (lambda l: chain_create(l, k=8192), lai.LAI_ERR_TOOBIG),
+    (lambda l: chain_create(l, epilogue=lai.CHAIN_SWIGLU, n=7), lai.LAI_ERR_INVALID),
+    (lambda l: chain_create(l, out=A(4096 + 16).value), lai.LAI_ERR_ALIAS),
+    (lambda l: l.lai_gemv_chain_run(None, P, None), lai.LAI_ERR_INVALID),
 ])
 def test_argument_checks(call, want):
     assert call(lai.load()) == want
