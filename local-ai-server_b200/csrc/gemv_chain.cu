@@ -36,9 +36,10 @@
 // across the warp), the CTA's row results and the stage mbarriers. Consumer warp w computes
 // the op-local rows r = w (mod kConsumerWarps), a whole row per warp (one shuffle tree a row).
 //
-// Every wait is bounded (1 s): a wait that runs out sets *err, marks the CTA aborted, and
-// the producer waits (bounded) for its copies in flight before the CTA exits; the other
-// CTAs' next grid waits then run out in turn. The grid counter is zeroed before every launch.
+// Every wait is bounded (1 s): a wait that runs out sets *err, marks the CTA aborted (the
+// consumer threads act on it together, at a barrier that ORs the flag), and the producer waits
+// (bounded) for its copies in flight before the CTA exits; the other CTAs' next grid waits then
+// run out in turn. The grid counter is zeroed before every launch.
 #include "lai_common.cuh"
 #include "bulk_copy.cuh"
 
@@ -87,6 +88,21 @@ __host__ __device__ __forceinline__ int rows_per_stage(int k) { return kStageByt
 
 __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
+}
+// Consumer barrier that also ORs `v` over the consumer threads: every one gets the same
+// answer, so an abort flag the producer warp may set at any moment is acted on uniformly
+// (a thread that returned while others wait at the next barrier would leave them waiting).
+__device__ __forceinline__ bool consumer_sync_any(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, 1, %2, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(kConsumers)
+        : "memory");
+    return r != 0;
 }
 __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
     unsigned v;
@@ -264,8 +280,7 @@ __device__ void consume(const lai_gemv_chain_op_t *ops, int n_ops, ChainSmem &sm
         }
         if (j > 0) {  // op j-1 finished on every CTA: its outputs are this op's inputs
             if (tid == 0 && !grid_wait(sync, (unsigned)j * (unsigned)G)) set_abort(sm, err);
-            consumer_sync();
-            if (aborted(sm)) return;
+            if (consumer_sync_any(aborted(sm))) return;
         }
         // the residual rows this thread adds into, in flight with the input vector
         float res[kResPerThread];
@@ -294,8 +309,7 @@ __device__ void consume(const lai_gemv_chain_op_t *ops, int n_ops, ChainSmem &sm
             __syncwarp();
             if (lane == 0) bulk::mbar_arrive(&sm.empty[q]);
         }
-        consumer_sync();
-        if (aborted(sm)) return;
+        if (consumer_sync_any(aborted(sm))) return;
         if (op.epilogue == kSwiglu) {
             for (int t = tid; t < R / 2; t += kConsumers)
                 op.out[r0 / 2 + t] = silu_mul(sm.dot[2 * t], sm.dot[2 * t + 1]);
